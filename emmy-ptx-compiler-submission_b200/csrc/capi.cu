@@ -1,0 +1,84 @@
+// C-ABI plumbing shared by every family: version, thread-local error text,
+// launch checks and the device status word.
+
+#include "common.cuh"
+
+#include <string.h>
+
+namespace emmy {
+
+__device__ int g_device_status = 0;
+
+namespace {
+thread_local char t_error[512] = {0};
+}
+
+int set_error(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_error, sizeof(t_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+void clear_error() { t_error[0] = 0; }
+
+const char *last_error_text() { return t_error; }
+
+int *device_status_ptr() {
+  static int *cached[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!cached[dev]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
+    cached[dev] = static_cast<int *>(p);
+  }
+  return cached[dev];
+}
+
+int check_launch(const char *what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return set_error(EMMY_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return EMMY_OK;
+}
+
+}  // namespace emmy
+
+using namespace emmy;
+
+extern "C" int emmy_version(void) { return 100; }
+
+extern "C" const char *emmy_last_error(void) { return last_error_text(); }
+
+extern "C" int emmy_get_device_status(int *code, void *stream) {
+  clear_error();
+  if (!code) return set_error(EMMY_ERR_INVALID, "emmy_get_device_status: null output");
+  cudaStream_t st = as_stream(stream);
+  int host = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&host, g_device_status, sizeof(int), 0,
+                                            cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess)
+    return set_error(EMMY_ERR_CUDA, "emmy_get_device_status: %s", cudaGetErrorString(e));
+  *code = host;
+  if (host != 0) {
+    int zero = 0;
+    e = cudaMemcpyToSymbolAsync(g_device_status, &zero, sizeof(int), 0,
+                                cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess)
+      return set_error(EMMY_ERR_CUDA, "emmy_get_device_status: %s", cudaGetErrorString(e));
+  }
+  return EMMY_OK;
+}
+
+extern "C" int emmy_zero(void *ptr, size_t bytes, void *stream) {
+  clear_error();
+  if (bytes == 0) return EMMY_OK;
+  if (!ptr) return set_error(EMMY_ERR_INVALID, "emmy_zero: null pointer");
+  cudaError_t e = cudaMemsetAsync(ptr, 0, bytes, as_stream(stream));
+  if (e != cudaSuccess) return set_error(EMMY_ERR_CUDA, "emmy_zero: %s", cudaGetErrorString(e));
+  return EMMY_OK;
+}

@@ -1,0 +1,392 @@
+"""IR synthesiser: Kernel IR + meta.json for the family shapes at any size.
+
+The emmy generator that produced the reference's fixtures is not available,
+so the benchmark configurations (which have no fixture) are written here as
+IR of the same statement shapes the reference fixtures carry, scaled up:
+
+* row reductions, ``Tile(outer..., aK_co)`` + StridedLoop + WarpShuffle +
+  TreeHalve + ``Cond(co == 0)`` write (``tests/variants/v_r_*``, ``w_r_*``);
+* rmsnorm / l2norm / softmax: the same plus a second StridedLoop map pass
+  (``v_f_rms_512``, ``v_f_l2_256``, ``v_f_softmax_1024``, ``w_f_softmax_dim0``);
+* layernorm: a two-moment accumulator pair (sum, sum of squares) and an
+  affine map pass (no fixture exists; the formula is the reference spec
+  ``tools/specs/ln_specs.py:2-6``);
+* f64 matvec: the reduction shape with a second, row-invariant load.
+
+``make_inputs`` builds the seeded inputs as the reference harness does
+(``tools/localrun.py:111-118``: ``default_rng(seed).standard_normal``), plus an
+optional ``init`` field per argument for the benchmark distributions
+(``{"dist": "normal", "mean": m, "std": s}`` or
+``{"dist": "uniform", "low": a, "high": b}``, drawn from ``default_rng(seed)``).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from .nodes import (
+    Accum, Assign, Axis, BinaryExpr, Cond, DataType, Dim, ElementwiseImpl, KernelOp, Let,
+    Literal, Load, NpDType, Smem, StridedLoop, Sync, Tile, TreeHalve, Var, WarpShuffle, Write,
+)
+
+DT = {
+    "f32": DataType(name="f32", np=NpDType("float32"), nbytes=4),
+    "f16": DataType(name="f16", np=NpDType("float16"), nbytes=2),
+    "f64": DataType(name="f64", np=NpDType("float64"), nbytes=8),
+}
+C_NAME = {"f32": "float", "f16": "half", "f64": "double"}
+NP = {"f32": np.float32, "f16": np.float16, "f64": np.float64}
+
+
+def V(name):
+    return Var(name=name)
+
+
+def L(v):
+    return Literal(value=v, dtype="float" if isinstance(v, float) else "int")
+
+
+def E(op):
+    return ElementwiseImpl(op)
+
+
+def ax(name, ext):
+    return Axis(name=name, extent=Dim(int(ext)), window=None)
+
+
+def A(name, op, args, dt="f32"):
+    return Assign(name=name, op=E(op), args=tuple(args), dtype=DT[dt] if dt else None)
+
+
+def _combine(states, rule):
+    """Combine statements ``state <- rule(state, state__o)`` (sum / max / softmax pair)."""
+    if rule == "add":
+        return tuple(Assign(name=s, op=E("add"), args=(s, s + "__o"), dtype=None) for s in states)
+    if rule == "max":
+        return tuple(Assign(name=s, op=E("maximum"), args=(s, s + "__o"), dtype=None) for s in states)
+    if rule == "softmax":
+        m, s = states
+        o = m + "__o"
+        return (
+            Assign(name=o + "__gn", op=E("maximum"), args=(m, o), dtype=None),
+            Assign(name=o + "__dg", op=E("subtract"), args=(m, o + "__gn"), dtype=None),
+            Assign(name=o + "__alpha", op=E("exp"), args=(o + "__dg",), dtype=None),
+            Assign(name=o + "__dg_o", op=E("subtract"), args=(o, o + "__gn"), dtype=None),
+            Assign(name=o + "__beta", op=E("exp"), args=(o + "__dg_o",), dtype=None),
+            Assign(name=o + "__" + s + "_sa", op=E("multiply"), args=(o + "__alpha", s), dtype=None),
+            Assign(name=o + "__" + s + "_sb", op=E("multiply"), args=(o + "__beta", s + "__o"), dtype=None),
+            Assign(name=s, op=E("add"), args=(o + "__" + s + "_sa", o + "__" + s + "_sb"), dtype=None),
+            Assign(name=m, op=E("copy"), args=(o + "__gn",), dtype=None),
+        )
+    raise ValueError(rule)
+
+
+def _block_combine(states, rule, block, dt="f32"):
+    """WarpShuffle + shared slots + TreeHalve, as in every reference reduction fixture."""
+    out = [WarpShuffle(state=tuple(states), state_b=tuple(s + "__o" for s in states),
+                       combine_states=_combine(states, rule), length=min(32, block), dtype=DT[dt])]
+    if block > 32:
+        warps = block // 32
+        bufs = tuple(s + "_smem" for s in states)
+        out += [Smem(name=b, extents=(warps,), dtype=C_NAME[dt], align=0) for b in bufs]
+        out.append(Cond(cond=BinaryExpr(op="==", left=V("lane"), right=L(0)),
+                        body=tuple(Write(output=b, index=(V("warp"),), values=(s,), value_dtype=DT[dt],
+                                         atomic=False, swizzle="NONE") for b, s in zip(bufs, states)),
+                        else_body=()))
+        out.append(Sync(barrier_id=0, count=None, warp=False))
+        out.append(TreeHalve(bufs=bufs, state=tuple(states), state_b=tuple(s + "__o" for s in states),
+                             combine_states=_combine(states, rule), length=warps, tid_var="warp",
+                             dtype=DT[dt], barrier_id=0, barrier_count=None, inner=None))
+    return out
+
+
+def _arg(name, dtype, shape, **kw):
+    d = {"name": name, "dtype": dtype, "shape": [int(s) for s in shape]}
+    d.update(kw)
+    return d
+
+
+def _meta(entry, args, grid, block, zero=()):
+    return {"node": [a["name"] for a in args if a.get("output")][0], "entry": entry,
+            "arg_order": [a["name"] for a in args], "grid": [int(grid), 1, 1],
+            "block": [int(block), 1, 1], "smem_bytes": 0, "zero_outputs": list(zero),
+            "args": args, "final": True}
+
+
+def _tile(axes, body, block):
+    return Tile(axes=tuple(axes), body=tuple(body), block_threads=int(block), aux_threads=0,
+                raster_axes=None, raster_group=None, raster_orient="m")
+
+
+def _outer_axes(dims):
+    return [ax(f"a{i}", d) for i, d in enumerate(dims)]
+
+
+# ---------------------------------------------------------------------------
+# reductions over the last axis
+
+
+def rmsnorm(rows, cols, eps=1e-5, weight=True, block=128, entry="k_rmsnorm",
+            x_init=None, w_init=None):
+    """``v_f_rms_512`` shape: ``x * recip(sqrt(eps + sum(x*x)*recip(n))) * w``."""
+    co = "a1_co"
+    red = StridedLoop(axis=ax("a1", cols), start=V(co), step=L(block), body=(
+        Load(names=("in2",), input="x", index=(V("a0"), V("a1")), dtype=DT["f32"]),
+        A("v1", "multiply", ("in2", "in2")),
+        Accum(name="acc0", value="v1", op=E("add"), dtype=DT["f32"], axes=("a1",), base=None),
+    ), unroll=False, end=None, seed=True)
+    mp = [Load(names=("in3",), input="x", index=(V("a0"), V("a2")), dtype=DT["f32"]),
+          A("v6", "multiply", ("in3", "v5"))]
+    if weight:
+        mp += [Load(names=("in4",), input="w", index=(V("a2"),), dtype=DT["f32"]),
+               A("v7", "multiply", ("in4", "v6"))]
+    mp.append(Write(output="y", index=(V("a0"), V("a2")), values=("v7" if weight else "v6",),
+                    value_dtype=DT["f32"], atomic=False, swizzle="NONE"))
+    body = [red] + _block_combine(["acc0"], "add", block) + [
+        Load(names=("in1",), input="mean_count", index=(L(0),), dtype=DT["f32"]),
+        A("v0", "reciprocal", ("in1",)),
+        A("v2", "multiply", ("acc0", "v0")),
+        Load(names=("in0",), input="add_c1", index=(L(0),), dtype=DT["f32"]),
+        A("v3", "add", ("in0", "v2")),
+        A("v4", "sqrt", ("v3",)),
+        A("v5", "reciprocal", ("v4",)),
+        StridedLoop(axis=ax("a2", cols), start=V(co), step=L(block), body=tuple(mp),
+                    unroll=False, end=None, seed=True),
+    ]
+    kop = KernelOp(name=entry, body=(_tile([ax("a0", rows), ax(co, block)], body, block),))
+    args = [_arg("mean_count", "f32", [1], data=[float(cols)]),
+            _arg("add_c1", "f32", [1], data=[float(eps)]),
+            _arg("x", "f32", [rows, cols], seed=0, **({"init": x_init} if x_init else {}))]
+    if weight:
+        args.append(_arg("w", "f32", [cols], seed=1, **({"init": w_init} if w_init else {})))
+    args.append(_arg("y", "f32", [rows, cols], output=True))
+    return kop, _meta(entry, args, rows, block)
+
+
+def l2norm(rows, cols, block=128, entry="k_l2norm"):
+    """``v_f_l2_256`` shape: ``x * recip(sqrt(sum(x*x)))``."""
+    co = "a1_co"
+    body = [StridedLoop(axis=ax("a1", cols), start=V(co), step=L(block), body=(
+        Load(names=("in0",), input="x", index=(V("a0"), V("a1")), dtype=DT["f32"]),
+        A("v0", "multiply", ("in0", "in0")),
+        Accum(name="acc0", value="v0", op=E("add"), dtype=DT["f32"], axes=("a1",), base=None),
+    ), unroll=False, end=None, seed=True)] + _block_combine(["acc0"], "add", block) + [
+        A("v1", "sqrt", ("acc0",)), A("v2", "reciprocal", ("v1",)),
+        StridedLoop(axis=ax("a2", cols), start=V(co), step=L(block), body=(
+            Load(names=("in1",), input="x", index=(V("a0"), V("a2")), dtype=DT["f32"]),
+            A("v3", "multiply", ("in1", "v2")),
+            Write(output="y", index=(V("a0"), V("a2")), values=("v3",), value_dtype=DT["f32"],
+                  atomic=False, swizzle="NONE"),
+        ), unroll=False, end=None, seed=True)]
+    kop = KernelOp(name=entry, body=(_tile([ax("a0", rows), ax(co, block)], body, block),))
+    args = [_arg("x", "f32", [rows, cols], seed=0), _arg("y", "f32", [rows, cols], output=True)]
+    return kop, _meta(entry, args, rows, block)
+
+
+def _softmax_update(x, m, s, one="one"):
+    return (
+        Assign(name=x + "__gn", op=E("maximum"), args=(m, x), dtype=DT["f32"]),
+        Assign(name=x + "__dg", op=E("subtract"), args=(m, x + "__gn"), dtype=DT["f32"]),
+        Assign(name=x + "__alpha", op=E("exp"), args=(x + "__dg",), dtype=DT["f32"]),
+        Assign(name=x + "__dg_o", op=E("subtract"), args=(x, x + "__gn"), dtype=DT["f32"]),
+        Assign(name=x + "__beta", op=E("exp"), args=(x + "__dg_o",), dtype=DT["f32"]),
+        Assign(name=x + "__" + s + "_sa", op=E("multiply"), args=(s, x + "__alpha"), dtype=DT["f32"]),
+        Assign(name=x + "__" + s + "_sb", op=E("multiply"), args=(x + "__beta", one), dtype=DT["f32"]),
+    )
+
+
+def softmax(shape, dim=-1, block=128, entry="k_softmax", x_init=None):
+    """``v_f_softmax_1024`` (last axis, any rank) or ``w_f_softmax_dim0`` (2-D, dim 0) shape."""
+    shape = [int(s) for s in shape]
+    nd = len(shape)
+    dim = dim % nd
+    if dim == nd - 1:
+        outer = shape[:-1]
+        n = shape[-1]
+        k = len(outer)
+        co = f"a{k}_co"
+        r, m = f"a{k}", f"a{k + 1}"
+        idx_r = tuple(V(f"a{i}") for i in range(k)) + (V(r),)
+        idx_m = tuple(V(f"a{i}") for i in range(k)) + (V(m),)
+        axes = _outer_axes(outer) + [ax(co, block)]
+        grid = math.prod(outer) if outer else 1
+    elif nd == 2 and dim == 0:
+        n, cols = shape
+        co = "a2_co"
+        r = "a2"
+        idx_r = (V("a2"), V("a1"))
+        axes = [ax("a0", n), ax("a1", cols), ax(co, block)]
+        grid = n * cols
+    else:
+        raise ValueError("softmax synthesis covers the last axis, or dim 0 of a 2-D tensor")
+    red = StridedLoop(axis=ax(r, n), start=V(co), step=L(block), body=(
+        Let(name="one", value=L(1.0), dtype=DT["f32"]),
+        Load(names=("in0",), input="x", index=idx_r, dtype=DT["f32"]),
+    ) + _softmax_update("in0", "acc0", "acc1") + (
+        Accum(name="acc1", value="in0__acc1_sb", op=E("add"), dtype=DT["f32"], axes=(r,),
+              base="in0__acc1_sa"),
+        Accum(name="acc0", value="in0", op=E("maximum"), dtype=DT["f32"], axes=(r,), base=None),
+    ), unroll=False, end=None, seed=True)
+    tail_ops = [A("v3", "subtract", ("in2", "acc0")), A("v4", "exp", ("v3",)),
+                A("v5", "multiply", ("v2", "v4"))]
+    if dim == nd - 1:
+        out = [A("v2", "reciprocal", ("acc1",)),
+               StridedLoop(axis=ax(m, n), start=V(co), step=L(block), body=tuple(
+                   [Load(names=("in2",), input="x", index=idx_m, dtype=DT["f32"])] + tail_ops + [
+                       Write(output="y", index=idx_m, values=("v5",), value_dtype=DT["f32"],
+                             atomic=False, swizzle="NONE")]), unroll=False, end=None, seed=True)]
+    else:
+        out = [Cond(cond=BinaryExpr(op="==", left=V(co), right=L(0)), body=tuple(
+            [A("v2", "reciprocal", ("acc1",)),
+             Load(names=("in2",), input="x", index=(V("a0"), V("a1")), dtype=DT["f32"])] + tail_ops + [
+                Write(output="y", index=(V("a0"), V("a1")), values=("v5",), value_dtype=DT["f32"],
+                      atomic=False, swizzle="NONE")]), else_body=())]
+    body = [red] + _block_combine(["acc0", "acc1"], "softmax", block) + out
+    kop = KernelOp(name=entry, body=(_tile(axes, body, block),))
+    args = [_arg("x", "f32", shape, seed=0, **({"init": x_init} if x_init else {})),
+            _arg("y", "f32", shape, output=True)]
+    return kop, _meta(entry, args, grid, block)
+
+
+def layernorm(rows, cols, eps=1e-5, affine=True, block=128, entry="k_layernorm",
+              x_init=None, g_init=None, b_init=None):
+    """Two-moment layernorm: ``(x - mean) * recip(sqrt(E[x^2] - mean^2 + eps)) * g + b``."""
+    co = "a1_co"
+    red = StridedLoop(axis=ax("a1", cols), start=V(co), step=L(block), body=(
+        Load(names=("in0",), input="x", index=(V("a0"), V("a1")), dtype=DT["f32"]),
+        A("v0", "multiply", ("in0", "in0")),
+        Accum(name="acc0", value="in0", op=E("add"), dtype=DT["f32"], axes=("a1",), base=None),
+        Accum(name="acc1", value="v0", op=E("add"), dtype=DT["f32"], axes=("a1",), base=None),
+    ), unroll=False, end=None, seed=True)
+    mp = [Load(names=("in3",), input="x", index=(V("a0"), V("a2")), dtype=DT["f32"]),
+          A("v9", "subtract", ("in3", "v2")), A("v10", "multiply", ("v9", "v8"))]
+    last = "v10"
+    if affine:
+        mp += [Load(names=("in4",), input="gamma", index=(V("a2"),), dtype=DT["f32"]),
+               A("v11", "multiply", ("v10", "in4")),
+               Load(names=("in5",), input="beta", index=(V("a2"),), dtype=DT["f32"]),
+               A("v12", "add", ("v11", "in5"))]
+        last = "v12"
+    mp.append(Write(output="y", index=(V("a0"), V("a2")), values=(last,), value_dtype=DT["f32"],
+                    atomic=False, swizzle="NONE"))
+    body = [red] + _block_combine(["acc0", "acc1"], "add", block) + [
+        Load(names=("in1",), input="ln_count", index=(L(0),), dtype=DT["f32"]),
+        A("v1", "reciprocal", ("in1",)),
+        A("v2", "multiply", ("acc0", "v1")),
+        A("v3", "multiply", ("acc1", "v1")),
+        A("v4", "multiply", ("v2", "v2")),
+        A("v5", "subtract", ("v3", "v4")),
+        Load(names=("in2",), input="ln_eps", index=(L(0),), dtype=DT["f32"]),
+        A("v6", "add", ("v5", "in2")),
+        A("v7", "sqrt", ("v6",)),
+        A("v8", "reciprocal", ("v7",)),
+        StridedLoop(axis=ax("a2", cols), start=V(co), step=L(block), body=tuple(mp),
+                    unroll=False, end=None, seed=True),
+    ]
+    kop = KernelOp(name=entry, body=(_tile([ax("a0", rows), ax(co, block)], body, block),))
+    args = [_arg("ln_count", "f32", [1], data=[float(cols)]),
+            _arg("ln_eps", "f32", [1], data=[float(eps)]),
+            _arg("x", "f32", [rows, cols], seed=0, **({"init": x_init} if x_init else {}))]
+    if affine:
+        args.append(_arg("gamma", "f32", [cols], seed=1, **({"init": g_init} if g_init else {})))
+        args.append(_arg("beta", "f32", [cols], seed=2, **({"init": b_init} if b_init else {})))
+    args.append(_arg("y", "f32", [rows, cols], output=True))
+    return kop, _meta(entry, args, rows, block)
+
+
+def reduce(shape, axis=-1, op="sum", block=128, entry="k_reduce", dtype="f32"):
+    """Sum / mean / max over one axis (``v_r_*``, ``w_r_dim0``, ``w_r_mid`` shapes).
+
+    ``axis=None`` reduces a 1-D tensor to a scalar (``v_r_100000``).
+    """
+    shape = [int(s) for s in shape]
+    if axis is None:
+        assert len(shape) == 1
+        kept, n = [], shape[0]
+        co, r = "a0_co", "a0"
+        idx = (V(r),)
+    else:
+        axis = axis % len(shape)
+        kept = [d for i, d in enumerate(shape) if i != axis]
+        n = shape[axis]
+        k = len(kept)
+        co, r = f"a{k}_co", f"a{k}"
+        coords = [V(f"a{i}") for i in range(k)]
+        idx = tuple(coords[:axis]) + (V(r),) + tuple(coords[axis:])
+    fold = {"sum": "add", "mean": "add", "max": "maximum", "min": "minimum"}[op]
+    red = StridedLoop(axis=ax(r, n), start=V(co), step=L(block), body=(
+        Load(names=("in0",), input="x", index=idx, dtype=DT[dtype]),
+        Accum(name="acc0", value="in0", op=E(fold), dtype=DT[dtype], axes=(r,), base=None),
+    ), unroll=False, end=None, seed=True)
+    out_idx = tuple(V(f"a{i}") for i in range(len(kept)))
+    wbody = []
+    args = []
+    val = "acc0"
+    if op == "mean":
+        wbody = [Load(names=("in1",), input="mean_count", index=(L(0),), dtype=DT[dtype]),
+                 A("v0", "reciprocal", ("in1",), dtype), A("v1", "multiply", ("acc0", "v0"), dtype)]
+        val = "v1"
+        args.append(_arg("mean_count", dtype, [1], data=[float(n)]))
+    wbody.append(Write(output="y", index=out_idx, values=(val,), value_dtype=DT[dtype],
+                       atomic=False, swizzle="NONE"))
+    rule = "max" if fold == "maximum" else ("add" if fold == "add" else None)
+    if rule is None:
+        raise ValueError("min reductions have no synthesised combine")
+    body = [red] + _block_combine(["acc0"], rule, block, dtype) + [
+        Cond(cond=BinaryExpr(op="==", left=V(co), right=L(0)), body=tuple(wbody), else_body=())]
+    axes = _outer_axes(kept) + [ax(co, block)]
+    kop = KernelOp(name=entry, body=(_tile(axes, body, block),))
+    args += [_arg("x", dtype, shape, seed=0), _arg("y", dtype, kept if kept else [1], output=True)]
+    return kop, _meta(entry, args, math.prod(kept) if kept else 1, block)
+
+
+def matvec(rows, cols, dtype="f64", block=128, entry="k_matvec"):
+    """``y = A @ v``: the reduction shape with a row-invariant second load."""
+    co = "a1_co"
+    red = StridedLoop(axis=ax("a1", cols), start=V(co), step=L(block), body=(
+        Load(names=("in0",), input="A", index=(V("a0"), V("a1")), dtype=DT[dtype]),
+        Load(names=("in1",), input="v", index=(V("a1"),), dtype=DT[dtype]),
+        A("v0", "multiply", ("in0", "in1"), dtype),
+        Accum(name="acc0", value="v0", op=E("add"), dtype=DT[dtype], axes=("a1",), base=None),
+    ), unroll=False, end=None, seed=True)
+    body = [red] + _block_combine(["acc0"], "add", block, dtype) + [
+        Cond(cond=BinaryExpr(op="==", left=V(co), right=L(0)), body=(
+            Write(output="y", index=(V("a0"),), values=("acc0",), value_dtype=DT[dtype],
+                  atomic=False, swizzle="NONE"),), else_body=())]
+    kop = KernelOp(name=entry, body=(_tile([ax("a0", rows), ax(co, block)], body, block),))
+    args = [_arg("A", dtype, [rows, cols], seed=0), _arg("v", dtype, [cols], seed=1),
+            _arg("y", dtype, [rows], output=True)]
+    return kop, _meta(entry, args, rows, block)
+
+
+# ---------------------------------------------------------------------------
+# inputs
+
+
+def make_inputs(meta: dict, seed_offset: int = 0, only=None) -> dict:
+    """Seeded host inputs (numpy) for every argument, outputs zero-filled."""
+    out = {}
+    for a in meta["args"]:
+        if only is not None and a["name"] not in only:
+            continue
+        n = math.prod(a["shape"]) if a["shape"] else 1
+        dt = NP.get(a["dtype"], np.float32)
+        if a.get("output"):
+            out[a["name"]] = np.zeros(n, dtype=dt)
+        elif "data" in a:
+            out[a["name"]] = np.array(a["data"], dtype=dt).reshape(-1)
+        else:
+            rng = np.random.default_rng(a.get("seed", 0) + seed_offset)
+            init = a.get("init")
+            if init is None:
+                v = rng.standard_normal(n)
+            elif init.get("dist") == "normal":
+                v = rng.standard_normal(n) * float(init.get("std", 1.0)) + float(init.get("mean", 0.0))
+            elif init.get("dist") == "uniform":
+                v = rng.uniform(float(init.get("low", 0.0)), float(init.get("high", 1.0)), n)
+            else:
+                raise ValueError(f"unknown init {init!r}")
+            out[a["name"]] = v.astype(dt)
+    return out

@@ -1,0 +1,261 @@
+"""Execute a launch plan through ``libemmyb200.so`` (ctypes C-ABI).
+
+This replaces what the reference's harness does with the PTX it emits
+(``tools/localrun.py:102-142``: load the module, allocate, copy, launch under
+the meta geometry, copy back): here the plan names a C-ABI symbol of the
+prebuilt sm_100a library and its tensor roles, and the library picks its own
+launch geometry.  Device memory and streams come from PyTorch; the library
+itself allocates nothing.
+
+There is no fallback: if the library is missing or a call fails, this raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+from pathlib import Path
+
+_HERE = Path(__file__).resolve().parent
+DEFAULT_LIB = _HERE.parent / "libemmyb200.so"
+
+_i64 = ctypes.c_int64
+_vp = ctypes.c_void_p
+_int = ctypes.c_int
+_sz = ctypes.c_size_t
+
+# symbol -> argtypes (all return int status)
+SIGNATURES = {
+    "emmy_version": [],
+    "emmy_get_device_status": [ctypes.POINTER(_int), _vp],
+    "emmy_zero": [_vp, _sz, _vp],
+    "emmy_reduce_f32": [_vp, _vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _sz, _vp],
+    "emmy_reduce_workspace_bytes": [_i64, _i64, _i64],
+    "emmy_rownorm_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _int, _vp],
+    "emmy_softmax_f32": [_vp, _vp, _i64, _i64, _i64, _vp],
+    "emmy_matvec_f64": [_vp, _vp, _vp, _i64, _i64, _vp],
+    "emmy_gemm_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _int, _vp],
+    "emmy_gemm_f16": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _int, _vp],
+    "emmy_attention_f32": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _int, _vp],
+    "emmy_attention_f16": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _vp],
+}
+RESTYPES = {"emmy_reduce_workspace_bytes": _sz}
+
+REDUCE_OP = {"sum": 0, "max": 1, "min": 2}
+REDUCE_PRE = {"identity": 0, "square": 1, "abs": 2}
+NORM_MODE = {"rms": 0, "l2": 1, "layer": 2}
+
+
+class LibraryError(RuntimeError):
+    pass
+
+
+_LIB = None
+
+
+def library_path() -> Path:
+    return Path(os.environ.get("EMMY_B200_LIB", str(DEFAULT_LIB)))
+
+
+def load_library():
+    """Load ``libemmyb200.so`` once; raise ``LibraryError`` when it is absent."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    path = library_path()
+    if not path.exists():
+        raise LibraryError(
+            f"{path} is missing: build it with `python emmy-ptx-compiler-submission_b200/build.py` "
+            "(there is no CPU fallback)")
+    lib = ctypes.CDLL(str(path))
+    for name, argtypes in SIGNATURES.items():
+        fn = getattr(lib, name, None)
+        if fn is None:
+            continue
+        fn.argtypes = argtypes
+        fn.restype = RESTYPES.get(name, _int)
+    lib.emmy_last_error.argtypes = []
+    lib.emmy_last_error.restype = ctypes.c_char_p
+    _LIB = lib
+    return lib
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load_library().emmy_last_error()
+        raise RuntimeError(f"{what} failed (status {rc}): {msg.decode() if msg else ''}")
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream_handle(stream):
+    if stream is None:
+        import torch
+        return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    return ctypes.c_void_p(getattr(stream, "cuda_stream", stream))
+
+
+_TORCH_DT = None
+
+
+def torch_dtype(dt: str):
+    import torch
+    global _TORCH_DT
+    if _TORCH_DT is None:
+        _TORCH_DT = {"f32": torch.float32, "f16": torch.float16, "f64": torch.float64,
+                     "i32": torch.int32, "i64": torch.int64, "i8": torch.int8,
+                     "u8": torch.uint8, "bool": torch.bool, "i16": torch.int16}
+    return _TORCH_DT[dt]
+
+
+def check_tensors(plan: dict, tensors: dict) -> None:
+    """Every plan tensor present, on a CUDA device, contiguous, right dtype and size."""
+    for name, spec in plan["tensors"].items():
+        t = tensors.get(name)
+        if t is None:
+            raise ValueError(f"missing tensor {name!r}")
+        if not t.is_cuda:
+            raise ValueError(f"tensor {name!r} is not on a CUDA device")
+        if not t.is_contiguous():
+            raise ValueError(f"tensor {name!r} is not contiguous")
+        if t.dtype != torch_dtype(spec["dtype"]):
+            raise ValueError(f"tensor {name!r} has dtype {t.dtype}, plan says {spec['dtype']}")
+        numel = math.prod(spec["shape"]) if spec["shape"] else 1
+        if t.numel() != numel:
+            raise ValueError(f"tensor {name!r} has {t.numel()} elements, plan says {numel}")
+
+
+def workspace_bytes(plan: dict) -> int:
+    """Device scratch a plan wants (the caller allocates it)."""
+    if plan["family"] == "reduce":
+        v = plan["view"]
+        return int(load_library().emmy_reduce_workspace_bytes(v["outer"], v["n"], v["inner"]))
+    return 0
+
+
+def run(plan: dict, tensors: dict, stream=None, workspace=None, check: bool = True) -> int:
+    """Launch the plan's kernel(s) on ``stream``; returns the number of library launches."""
+    lib = load_library()
+    if check:
+        check_tensors(plan, tensors)
+    st = _stream_handle(stream)
+    launches = 0
+    for name in plan.get("zero_outputs", []):
+        t = tensors[name]
+        _check(lib.emmy_zero(_ptr(t), t.numel() * t.element_size(), st), "emmy_zero")
+        launches += 1
+    a = plan["args"]
+    p = plan.get("params", {})
+    fam = plan["family"]
+    T = lambda role: tensors[a[role]] if role in a else None  # noqa: E731
+    if fam == "reduce":
+        v = plan["view"]
+        ws = workspace
+        _check(lib.emmy_reduce_f32(_ptr(T("x")), _ptr(T("y")), v["outer"], v["n"], v["inner"],
+                                   REDUCE_OP[p["op"]], REDUCE_PRE[p["pre"]], _ptr(T("count")),
+                                   _ptr(ws), 0 if ws is None else ws.numel() * ws.element_size(),
+                                   st), "emmy_reduce_f32")
+        launches += 2 if ws is not None and workspace_bytes(plan) else 1
+    elif fam == "rownorm":
+        v = plan["view"]
+        _check(lib.emmy_rownorm_f32(_ptr(T("x")), _ptr(T("w")), _ptr(T("b")), _ptr(T("y")),
+                                    v["outer"], v["n"], _ptr(T("eps")), _ptr(T("count")),
+                                    NORM_MODE[p["mode"]], st), "emmy_rownorm_f32")
+        launches += 1
+    elif fam == "softmax":
+        v = plan["view"]
+        _check(lib.emmy_softmax_f32(_ptr(T("x")), _ptr(T("y")), v["outer"], v["n"], v["inner"], st),
+               "emmy_softmax_f32")
+        launches += 1
+    elif fam == "matvec":
+        v = plan["view"]
+        _check(lib.emmy_matvec_f64(_ptr(T("x")), _ptr(T("v")), _ptr(T("y")), v["outer"], v["n"], st),
+               "emmy_matvec_f64")
+        launches += 1
+    elif fam == "gemm_f32":
+        g = plan["gemm"]
+        _check(lib.emmy_gemm_f32(_ptr(T("a")), _ptr(T("b")), _ptr(T("bias")), _ptr(T("c")),
+                                 g["batch"], g["m"], g["n"], g["k"], g["a_batch_stride"],
+                                 g["b_batch_stride"], g["c_batch_stride"], g["splits"],
+                                 int(g["accumulate"]), g["epilogue"], st), "emmy_gemm_f32")
+        launches += 1
+    elif fam == "gemm_f16":
+        g = plan["gemm"]
+        _check(lib.emmy_gemm_f16(_ptr(T("a")), _ptr(T("b")), _ptr(T("bias")), _ptr(T("c")),
+                                 g["batch"], g["m"], g["n"], g["k"], g["out_dtype"],
+                                 g["epilogue"], int(g["accumulate"]), st), "emmy_gemm_f16")
+        launches += 1
+    elif fam == "attention_f32":
+        g = plan["attention"]
+        _check(lib.emmy_attention_f32(_ptr(T("q")), _ptr(T("k")), _ptr(T("v")), _ptr(T("o")),
+                                      _ptr(T("scale")), g["batch"], g["sq"], g["sk"], g["d"],
+                                      g["dv"], int(g["k_transposed"]), st), "emmy_attention_f32")
+        launches += 1
+    elif fam == "attention_f16":
+        g = plan["attention"]
+        _check(lib.emmy_attention_f16(_ptr(T("q")), _ptr(T("k")), _ptr(T("v")), _ptr(T("o")),
+                                      _ptr(T("scale")), g["batch"], g["sq"], g["sk"], g["d"],
+                                      g["out_dtype"], int(g["k_transposed"]), st),
+               "emmy_attention_f16")
+        launches += 1
+    else:
+        raise ValueError(f"plan family {fam!r} has no launcher")
+    return launches
+
+
+class Executor:
+    """Device buffers for one plan, reused across calls (H2D -> kernel -> D2H)."""
+
+    def __init__(self, plan: dict, device=None):
+        import torch
+        self.plan = plan
+        self.device = torch.device(device or "cuda")
+        self.tensors = {}
+        for name, spec in plan["tensors"].items():
+            numel = math.prod(spec["shape"]) if spec["shape"] else 1
+            self.tensors[name] = torch.empty(numel, dtype=torch_dtype(spec["dtype"]),
+                                             device=self.device)
+        nb = workspace_bytes(plan)
+        self.workspace = torch.empty(nb, dtype=torch.uint8, device=self.device) if nb else None
+
+    def upload(self, host: dict, stream=None) -> int:
+        """Copy host arrays/tensors (pinned for true async) into the device buffers; returns bytes."""
+        import torch
+        nbytes = 0
+        for name, arr in host.items():
+            src = arr if isinstance(arr, torch.Tensor) else torch.from_numpy(arr)
+            dst = self.tensors[name]
+            dst.copy_(src.reshape(-1), non_blocking=True)
+            nbytes += dst.numel() * dst.element_size()
+        return nbytes
+
+    def launch(self, stream=None) -> int:
+        return run(self.plan, self.tensors, stream=stream, workspace=self.workspace, check=False)
+
+    def download(self, names=None, out=None) -> dict:
+        names = list(names or self.plan["outputs"])
+        res = {}
+        for name in names:
+            if out is not None and name in out:
+                out[name].copy_(self.tensors[name], non_blocking=True)
+                res[name] = out[name]
+            else:
+                res[name] = self.tensors[name].cpu()
+        return res
+
+
+def run_host(plan: dict, host: dict) -> dict:
+    """Convenience: numpy inputs in, numpy outputs out (zero-initialised outputs)."""
+    import numpy as np
+    import torch
+    ex = Executor(plan)
+    for name, t in ex.tensors.items():
+        if name not in host:
+            t.zero_()
+    ex.upload({k: np.ascontiguousarray(v) for k, v in host.items()})
+    ex.launch()
+    torch.cuda.synchronize()
+    return {k: v.numpy() for k, v in ex.download().items()}

@@ -1,0 +1,611 @@
+"""Family matcher for the cooperative-reduction IR shape.
+
+Shape (reference fixtures ``v_r_*``, ``w_r_*``, ``v_f_*``, ``w_f_*``; lowering in
+``ptxc/stmts.py:728-773`` (StridedLoop), ``:564-611`` (Accum), ``:1441-1492``
+(WarpShuffle), ``:1495-1568`` (TreeHalve)):
+
+    Tile(outer axes ..., <x>_co : block_threads)
+      StridedLoop r : n  start=<x>_co step=block   -- per-lane folds (Accum)
+      WarpShuffle / Smem / Cond(lane==0) Write / Sync / TreeHalve  -- block combine
+      [scalar epilogue: constant loads, Assigns]
+      then one of
+        Cond(<x>_co == 0) { ...; Write y[outer] }          -- reduction output
+        StridedLoop m : n start=<x>_co step=block { Load x[.., m]; ...; Write y[.., m] }
+        Cond(<x>_co == 0) { Load x[.., q]; ...; Write y[.., q] }  (q a Tile axis, softmax dim0)
+
+What each phase computes is checked by evaluating its scalar statements at
+random points (``ptxc.scalar``) against the closed forms of sum / mean / max /
+min / sum of squares / dot with a vector / online max-sum (softmax) /
+two-moment (layernorm), and the tensor layouts are read off the affine
+address forms.  Anything else is ``NoMatch``.
+"""
+
+from __future__ import annotations
+
+import itertools
+import math
+import random
+
+from .affine import Affine, flat_affine
+from .common import CompileError, const_int, norm_dtype, op_name, stmt_name
+from .scalar import ProbeMismatch, close, run_scalar
+
+
+class NoMatch(Exception):
+    pass
+
+
+def need(cond, msg):
+    if not cond:
+        raise NoMatch(msg)
+
+
+_RNG_SEED = 20240917
+
+
+# ---------------------------------------------------------------------------
+# accumulator systems: name -> (update(state, x, v), combine(a, b), seeds)
+
+def _upd_sum(s, x, v):
+    return (s[0] + x,)
+
+
+def _upd_sumsq(s, x, v):
+    return (s[0] + x * x,)
+
+
+def _upd_sumabs(s, x, v):
+    return (s[0] + abs(x),)
+
+
+def _upd_max(s, x, v):
+    return (max(s[0], x),)
+
+
+def _upd_min(s, x, v):
+    return (min(s[0], x),)
+
+
+def _upd_dot(s, x, v):
+    return (s[0] + x * v,)
+
+
+def _upd_softmax(s, x, v):
+    m, t = s
+    g = max(m, x)
+    return (g, t * math.exp(m - g) + math.exp(x - g))
+
+
+def _upd_moments(s, x, v):
+    return (s[0] + x, s[1] + x * x)
+
+
+def _cmb_add(a, b):
+    return (a[0] + b[0],)
+
+
+def _cmb_max(a, b):
+    return (max(a[0], b[0]),)
+
+
+def _cmb_min(a, b):
+    return (min(a[0], b[0]),)
+
+
+def _cmb_softmax(a, b):
+    g = max(a[0], b[0])
+    return (g, a[1] * math.exp(a[0] - g) + b[1] * math.exp(b[0] - g))
+
+
+def _cmb_moments(a, b):
+    return (a[0] + b[0], a[1] + b[1])
+
+
+SYSTEMS = {
+    # name: (n_states, update, combine, needs_vector)
+    "sum": (1, _upd_sum, _cmb_add, False),
+    "sumsq": (1, _upd_sumsq, _cmb_add, False),
+    "sumabs": (1, _upd_sumabs, _cmb_add, False),
+    "max": (1, _upd_max, _cmb_max, False),
+    "min": (1, _upd_min, _cmb_min, False),
+    "dot": (1, _upd_dot, _cmb_add, True),
+    "softmax": (2, _upd_softmax, _cmb_softmax, False),
+    "moments": (2, _upd_moments, _cmb_moments, False),
+}
+
+
+# ---------------------------------------------------------------------------
+# output forms: (system, form) -> fn(states, consts, x, w, b) ; const roles
+
+def _recip(v):
+    return 1.0 / v
+
+
+OUT_FORMS = {
+    # reduction outputs (no map tensor)
+    ("sum", "sum"): ((), lambda s, c, x, w, b: s[0]),
+    ("sum", "mean"): (("count",), lambda s, c, x, w, b: s[0] * _recip(c["count"])),
+    ("sumsq", "sum"): ((), lambda s, c, x, w, b: s[0]),
+    ("sumsq", "mean"): (("count",), lambda s, c, x, w, b: s[0] * _recip(c["count"])),
+    ("sumabs", "sum"): ((), lambda s, c, x, w, b: s[0]),
+    ("sumabs", "mean"): (("count",), lambda s, c, x, w, b: s[0] * _recip(c["count"])),
+    ("max", "max"): ((), lambda s, c, x, w, b: s[0]),
+    ("min", "min"): ((), lambda s, c, x, w, b: s[0]),
+    ("dot", "dot"): ((), lambda s, c, x, w, b: s[0]),
+    # map outputs
+    ("sumsq", "rms_w"): (("eps", "count"), lambda s, c, x, w, b:
+                         x * _recip(math.sqrt(c["eps"] + s[0] * _recip(c["count"]))) * w),
+    ("sumsq", "rms"): (("eps", "count"), lambda s, c, x, w, b:
+                       x * _recip(math.sqrt(c["eps"] + s[0] * _recip(c["count"])))),
+    ("sumsq", "l2"): ((), lambda s, c, x, w, b: x * _recip(math.sqrt(s[0]))),
+    ("softmax", "softmax"): ((), lambda s, c, x, w, b: math.exp(x - s[0]) * _recip(s[1])),
+    ("moments", "ln"): (("eps", "count"), lambda s, c, x, w, b: _ln(s, c, x)),
+    ("moments", "ln_w"): (("eps", "count"), lambda s, c, x, w, b: _ln(s, c, x) * w),
+    ("moments", "ln_wb"): (("eps", "count"), lambda s, c, x, w, b: _ln(s, c, x) * w + b),
+}
+
+
+def _ln(s, c, x):
+    mean = s[0] * _recip(c["count"])
+    var = s[1] * _recip(c["count"]) - mean * mean
+    return (x - mean) * _recip(math.sqrt(var + c["eps"]))
+
+
+# ---------------------------------------------------------------------------
+
+
+def _is_var(e, name):
+    return stmt_name(e) == "Var" and e.name == name
+
+
+def match_reduction(kop, tile, meta) -> dict:
+    threads = meta.block[0] * meta.block[1] * meta.block[2]
+    axes = [(a.name, int(a.extent.value)) for a in tile.axes]
+    need(len(axes) >= 1, "empty Tile")
+    co_name, co_ext = axes[-1]
+    need(co_name.endswith("_co"), "last Tile axis is not a cooperative lane axis")
+    need(co_ext == threads, "lane axis does not span the thread block")
+    outer = [(n, e) for n, e in axes[:-1]]
+    stmts = list(tile.body)
+    need(stmts and any(stmt_name(s) == "StridedLoop" for s in stmts), "no StridedLoop")
+
+    # ---- phase 1: the reduction loop
+    i = 0
+    head = []
+    while stmt_name(stmts[i]) != "StridedLoop":
+        need(stmt_name(stmts[i]) in ("Let", "Load", "Assign"), "statements before the reduction loop")
+        head.append(stmts[i])
+        i += 1
+    red = stmts[i]
+    i += 1
+    need(_is_var(red.start, co_name), "reduction loop does not start at the lane index")
+    need(const_int(red.step) == co_ext, "reduction loop step is not the block size")
+    r = red.axis.name
+    n = int(red.axis.extent.value)
+    need(red.end is None or const_int(red.end) == n, "reduction loop end differs from its extent")
+
+    shapes, dtypes = meta.shapes, meta.dtypes
+    consts = {}            # tensor name -> None (1-element data / scalar buffers)
+    tloads = []            # (stmt, affine, numel) of loads that move with r
+    accs = []
+    for st in red.body:
+        k = stmt_name(st)
+        if k == "Load":
+            need(st.input in shapes, f"load from unknown buffer {st.input!r}")
+            aff = flat_affine(st.index, shapes[st.input])
+            need(aff is not None, "non-affine load index in the reduction loop")
+            numel = math.prod(shapes[st.input]) if shapes[st.input] else 1
+            need(len(st.names) == 1, "vector load in the reduction loop")
+            if not aff.vars() and numel == 1 and aff.const() == 0:
+                consts[st.input] = None
+            elif aff.coef(r):
+                tloads.append((st, aff, numel))
+            else:
+                raise NoMatch("loop-invariant tensor load in the reduction loop")
+        elif k == "Accum":
+            accs.append(st)
+        elif k in ("Let", "Assign"):
+            pass
+        else:
+            raise NoMatch(f"{k} inside the reduction loop")
+    need(tloads, "no tensor load in the reduction loop")
+    distinct = {}
+    for t in tloads:
+        distinct.setdefault((t[0].input, t[1].key()), []).append(t)
+    loads_v = []
+    if len(distinct) == 1:
+        loads_x = tloads
+    else:
+        need(len(distinct) == 2, "several different tensor loads in the reduction loop")
+        (k0, g0), (k1, g1) = distinct.items()
+        a0, a1 = g0[0][1], g1[0][1]
+        if a0.vars() == {r} and a0.coef(r) == 1 and (a1.vars() - {r} or a1.coef(r) != 1):
+            loads_x, loads_v = g1, g0
+        elif a1.vars() == {r} and a1.coef(r) == 1 and (a0.vars() - {r} or a0.coef(r) != 1):
+            loads_x, loads_v = g0, g1
+        else:
+            raise NoMatch("two tensor loads that are not a row and a vector")
+        need(len(loads_v) == 1, "vector loaded twice")
+    x_name = loads_x[0][0].input
+    x_aff = loads_x[0][1]
+    acc_names = []
+    for a in accs:
+        if a.name not in acc_names:
+            acc_names.append(a.name)
+    need(1 <= len(acc_names) <= 2, "unsupported accumulator count")
+    acc_dt = {norm_dtype(a.dtype) for a in accs}
+    need(len(acc_dt) == 1, "mixed accumulator dtypes")
+    acc_dt = acc_dt.pop()
+
+    # ---- classify the per-lane update by probing
+    def run_update(states, x, v):
+        env = dict(zip(acc_names, states))
+
+        def load(st):
+            if st.input in consts:
+                raise ProbeMismatch("constant inside the loop")
+            if loads_v and st.input == loads_v[0][0].input:
+                return [v]
+            return [x]
+
+        run_scalar(red.body, env, load=load)
+        return tuple(env[nm] for nm in acc_names)
+
+    system = None
+    order = None
+    for name, (ns, upd, _, needs_v) in SYSTEMS.items():
+        if ns != len(acc_names) or needs_v != bool(loads_v):
+            continue
+        for perm in itertools.permutations(range(ns)):
+            ok = True
+            rng = random.Random(_RNG_SEED)
+            for _ in range(6):
+                st = [rng.uniform(-3, 3) for _ in range(ns)]
+                if name == "softmax":
+                    st[1] = rng.uniform(0.1, 5.0)
+                x = rng.uniform(-3, 3)
+                v = rng.uniform(-3, 3)
+                # states in the IR's order, reference in the system's order
+                ir_states = [0.0] * ns
+                for k2, p in enumerate(perm):
+                    ir_states[p] = st[k2]
+                try:
+                    got = run_update(ir_states, x, v)
+                except (ProbeMismatch, KeyError):
+                    ok = False
+                    break
+                want = upd(tuple(st), x, v)
+                got_sys = tuple(got[p] for p in perm)
+                if not all(close(g, w) for g, w in zip(got_sys, want)):
+                    ok = False
+                    break
+            if ok:
+                system, order = name, perm
+                break
+        if system:
+            break
+    need(system is not None, "reduction loop update is not a known fold")
+    # sys_states[k] is the IR accumulator named acc_names[order[k]]
+    sys_names = [acc_names[p] for p in order]
+
+    # ---- phase 2: block combine
+    ws = th = None
+    combine_stmts = []
+    while i < len(stmts):
+        st = stmts[i]
+        k = stmt_name(st)
+        if k == "WarpShuffle":
+            need(ws is None, "two WarpShuffles")
+            ws = st
+        elif k == "TreeHalve":
+            need(th is None, "two TreeHalves")
+            th = st
+        elif k in ("Smem", "Sync"):
+            pass
+        elif k == "Cond" and stmt_name(st.cond) == "BinaryExpr" and st.cond.op == "==" and \
+                _is_var(st.cond.left, "lane") and const_int(st.cond.right) == 0:
+            for s2 in st.body:
+                need(stmt_name(s2) == "Write", "lane-0 branch does more than publish partials")
+        else:
+            break
+        combine_stmts.append(st)
+        i += 1
+    if co_ext > 1:
+        need(ws is not None, "no warp combine")
+        need(set(ws.state) == set(acc_names), "warp combine does not cover the accumulators")
+        need(int(ws.length) == min(32, co_ext), "warp combine length")
+    if co_ext > 32:
+        need(th is not None, "no cross-warp combine")
+        need(set(th.state) == set(acc_names), "tree combine does not cover the accumulators")
+        need(int(th.length) * 32 == co_ext, "tree combine length")
+        need(th.inner is None, "tree combine with an inner offset")
+    for node in (ws, th):
+        if node is None:
+            continue
+        ns, _, cmb, _ = SYSTEMS[system]
+
+        def run_cmb(a, b, node=node):
+            env = {}
+            for nm, val in zip(sys_names, a):
+                env[nm] = val
+            ob = dict(zip(node.state, node.state_b))
+            for nm, val in zip(sys_names, b):
+                env[ob[nm]] = val
+            run_scalar(node.combine_states, env)
+            return tuple(env[nm] for nm in sys_names)
+
+        rng = random.Random(_RNG_SEED + 1)
+        for _ in range(6):
+            a = [rng.uniform(-3, 3) for _ in range(ns)]
+            b = [rng.uniform(-3, 3) for _ in range(ns)]
+            if system == "softmax":
+                a[1], b[1] = rng.uniform(0.1, 5), rng.uniform(0.1, 5)
+            try:
+                got = run_cmb(a, b)
+            except (ProbeMismatch, KeyError):
+                raise NoMatch("combine statements are not the fold's combine")
+            need(all(close(g, w) for g, w in zip(got, cmb(tuple(a), tuple(b)))),
+                 "combine statements are not the fold's combine")
+
+    # ---- phase 3/4: epilogue and output
+    tail = stmts[i:]
+    need(len(tail) >= 1, "no output phase")
+    last = tail[-1]
+    post = tail[:-1]
+    for st in post:
+        need(stmt_name(st) in ("Let", "Load", "Assign"), f"{stmt_name(st)} in the epilogue")
+        if stmt_name(st) == "Load":
+            aff = flat_affine(st.index, shapes.get(st.input, ()))
+            numel = math.prod(shapes.get(st.input, ())) if shapes.get(st.input) else 1
+            need(aff is not None and not aff.vars() and numel == 1, "tensor load in the epilogue")
+            consts[st.input] = None
+    for st in head:
+        if stmt_name(st) == "Load":
+            aff = flat_affine(st.index, shapes.get(st.input, ()))
+            numel = math.prod(shapes.get(st.input, ())) if shapes.get(st.input) else 1
+            need(aff is not None and not aff.vars() and numel == 1, "tensor load before the loop")
+            consts[st.input] = None
+
+    view = _derive_view(x_aff, r, n, outer, math.prod(shapes[x_name]) if shapes[x_name] else 1)
+    if loads_v:
+        need(view["inner"] == 1, "dot with a vector needs contiguous rows")
+
+    kind = stmt_name(last)
+    map_var = None
+    body = None
+    if kind == "StridedLoop":
+        need(_is_var(last.start, co_name) and const_int(last.step) == co_ext, "map loop shape")
+        need(int(last.axis.extent.value) == n and (last.end is None or const_int(last.end) == n),
+             "map loop extent differs from the reduction")
+        map_var = last.axis.name
+        body = list(last.body)
+        form_kind = "map"
+    elif kind == "Cond":
+        c = last.cond
+        need(stmt_name(c) == "BinaryExpr" and c.op == "==" and _is_var(c.left, co_name)
+             and const_int(c.right) == 0 and not last.else_body, "output branch shape")
+        body = list(last.body)
+        has_x = any(stmt_name(s) == "Load" and s.input == x_name for s in body)
+        if has_x:
+            need(len(view["zero"]) == 1, "output branch reloads x without a free axis")
+            map_var = view["zero"][0][0]
+            need(view["zero"][0][1] == n, "free axis extent differs from the reduction")
+            form_kind = "map"
+        else:
+            need(not view["zero"], "Tile axis unused by the reduction")
+            form_kind = "reduce"
+    else:
+        raise NoMatch("no output phase")
+    if form_kind == "map" and kind == "StridedLoop":
+        need(not view["zero"], "Tile axis unused by the reduction")
+
+    writes = [s for s in body if stmt_name(s) == "Write"]
+    need(len(writes) == 1 and body[-1] is writes[0], "output phase must end in one write")
+    wr = writes[0]
+    need(not wr.atomic and len(wr.values) == 1, "atomic or vector output write")
+    y_name = wr.output
+    need(y_name in shapes and y_name != x_name, "output buffer")
+    rename = None
+    y_aff = flat_affine(wr.index, shapes[y_name], rename)
+    need(y_aff is not None and y_aff.const() == 0, "output index is not affine")
+    y_numel = math.prod(shapes[y_name]) if shapes[y_name] else 1
+
+    roles = {}             # load statement id -> role
+    map_loads = []
+    for st in body[:-1]:
+        k = stmt_name(st)
+        if k == "Load":
+            aff = flat_affine(st.index, shapes.get(st.input, ()))
+            need(aff is not None, "non-affine load in the output phase")
+            numel = math.prod(shapes[st.input]) if shapes[st.input] else 1
+            need(len(st.names) == 1, "vector load in the output phase")
+            if not aff.vars() and numel == 1 and aff.const() == 0:
+                consts[st.input] = None
+                roles[id(st)] = ("const", st.input)
+            elif st.input == x_name:
+                need(form_kind == "map", "x reloaded in a reduction output")
+                need(_same_layout(aff, x_aff, r, map_var), "map load of x uses another layout")
+                roles[id(st)] = ("x", st.input)
+            elif aff.key() == ((map_var, 1),) and numel == n:
+                need(view["inner"] == 1, "per-column vector with strided rows")
+                roles[id(st)] = ("vec", st.input)
+                map_loads.append(st.input)
+            else:
+                raise NoMatch(f"unexpected load of {st.input!r} in the output phase")
+        elif k not in ("Let", "Assign"):
+            raise NoMatch(f"{k} in the output phase")
+
+    if form_kind == "map":
+        need(_same_layout(y_aff, x_aff, r, map_var), "output layout differs from the input's")
+        need(y_numel == view["outer"] * n * view["inner"], "output size")
+    else:
+        for name, c in view["inner_coef"].items():
+            need(y_aff.coef(name) == c, "reduction output layout")
+        for name, c in view["outer_coef"].items():
+            need(c % n == 0 and y_aff.coef(name) == c // n, "reduction output layout")
+        need(y_aff.vars() <= set(view["inner_coef"]) | set(view["outer_coef"]), "output index")
+        need(y_numel == view["outer"] * view["inner"], "output size")
+
+    # ---- probe the output formula
+    const_names = sorted(consts)
+    vec_names = sorted(set(map_loads))
+
+    def run_out(states, cvals, x, vecs):
+        env = dict(zip(sys_names, states))
+
+        def load(st):
+            role = roles.get(id(st))
+            if role is None or stmt_name(st) != "Load":
+                if st.input in cvals:
+                    return [cvals[st.input]]
+                raise ProbeMismatch("load")
+            if role[0] == "const":
+                return [cvals[st.input]]
+            if role[0] == "x":
+                return [x]
+            return [vecs[st.input]]
+
+        run_scalar(head, env, load=lambda st: [cvals[st.input]])
+        run_scalar(post, env, load=lambda st: [cvals[st.input]])
+        run_scalar(body[:-1], env, load=load)
+        return env[wr.values[0]]
+
+    ns = SYSTEMS[system][0]
+    found = None
+    for (sysname, form), (croles, fn) in OUT_FORMS.items():
+        if sysname != system:
+            continue
+        if (form_kind == "reduce") != (form in ("sum", "mean", "max", "min", "dot")):
+            continue
+        if len(croles) != len(const_names):
+            continue
+        nvec = {"rms_w": 1, "ln_w": 1, "ln_wb": 2}.get(form, 0)
+        if nvec != len(vec_names):
+            continue
+        for cperm in itertools.permutations(const_names):
+            cmap = dict(zip(croles, cperm))
+            for vperm in itertools.permutations(vec_names):
+                ok = True
+                rng = random.Random(_RNG_SEED + 2)
+                for _ in range(6):
+                    st = [rng.uniform(0.5, 4.0) for _ in range(ns)]
+                    if system == "moments":
+                        st = [rng.uniform(-2, 2), 0.0]
+                        st[1] = st[0] * st[0] * rng.uniform(0.2, 0.9) + rng.uniform(8, 20)
+                        # keep the variance positive: s1/c - (s0/c)^2 > 0 for c in [2,4]
+                    cv = {nm: rng.uniform(2.0, 4.0) for nm in const_names}
+                    x = rng.uniform(-2, 2)
+                    vv = {nm: rng.uniform(-2, 2) for nm in vec_names}
+                    try:
+                        got = run_out(st, cv, x, vv)
+                    except (ProbeMismatch, KeyError, ValueError):
+                        ok = False
+                        break
+                    c_by_role = {role: cv[nm] for role, nm in cmap.items()}
+                    w = vv[vperm[0]] if len(vperm) > 0 else None
+                    b = vv[vperm[1]] if len(vperm) > 1 else None
+                    try:
+                        want = fn(st, c_by_role, x, w, b)
+                    except (ValueError, ZeroDivisionError):
+                        ok = False
+                        break
+                    if not close(got, want):
+                        ok = False
+                        break
+                if ok:
+                    found = (form, cmap, vperm)
+                    break
+            if found:
+                break
+        if found:
+            break
+    need(found is not None, f"output formula is not a known {system} epilogue")
+    form, cmap, vperm = found
+
+    xdt = meta.dtypes[x_name]
+    ydt = meta.dtypes[y_name]
+    plan = {
+        "view": {"outer": view["outer"], "n": n, "inner": view["inner"]},
+        "args": {"x": x_name, "y": y_name},
+        "dtypes": {"x": xdt, "y": ydt, "acc": acc_dt},
+    }
+    if form in ("sum", "mean", "max", "min"):
+        need(xdt == "f32" and ydt == "f32", "only f32 reductions have a B200 kernel")
+        plan["family"] = "reduce"
+        plan["symbol"] = "emmy_reduce_f32"
+        plan["params"] = {"op": {"sum": "sum", "mean": "sum", "max": "max", "min": "min"}[form],
+                          "pre": {"sumsq": "square", "sumabs": "abs"}.get(system, "identity"),
+                          "mean": form == "mean"}
+        if form == "mean":
+            plan["args"]["count"] = cmap["count"]
+    elif form == "dot":
+        need(xdt == "f64" and ydt == "f64" and meta.dtypes[loads_v[0][0].input] == "f64",
+             "only the f64 dot-with-vector (matvec) has a B200 kernel")
+        plan["family"] = "matvec"
+        plan["symbol"] = "emmy_matvec_f64"
+        plan["args"]["v"] = loads_v[0][0].input
+        plan["params"] = {}
+    elif form == "softmax":
+        need(xdt == "f32" and ydt == "f32", "only f32 softmax has a B200 kernel")
+        plan["family"] = "softmax"
+        plan["symbol"] = "emmy_softmax_f32"
+        plan["params"] = {}
+    else:
+        need(xdt == "f32" and ydt == "f32", "only f32 row normalisation has a B200 kernel")
+        need(view["inner"] == 1, "row normalisation over a strided axis")
+        plan["family"] = "rownorm"
+        plan["symbol"] = "emmy_rownorm_f32"
+        mode = {"rms": "rms", "rms_w": "rms", "l2": "l2", "ln": "layer", "ln_w": "layer",
+                "ln_wb": "layer"}[form]
+        plan["params"] = {"mode": mode}
+        if "eps" in cmap:
+            plan["args"]["eps"] = cmap["eps"]
+        if "count" in cmap:
+            plan["args"]["count"] = cmap["count"]
+        if len(vperm) >= 1:
+            plan["args"]["w"] = vperm[0]
+        if len(vperm) >= 2:
+            plan["args"]["b"] = vperm[1]
+    return plan
+
+
+def _same_layout(aff, x_aff, r, m):
+    """``aff`` equals ``x_aff`` with the reduction variable ``r`` renamed to ``m``."""
+    renamed = Affine()
+    for k, v in x_aff.items():
+        renamed[m if k == r else k] = renamed.get(m if k == r else k, 0) + v
+    return aff.key() == renamed.key()
+
+
+def _derive_view(x_aff, r, n, outer_axes, x_numel):
+    sr = x_aff.coef(r)
+    need(sr > 0, "reduction stride must be positive")
+    need(x_aff.const() == 0, "reduction load has a constant offset")
+    inner, outer, zero = [], [], []
+    for name, ext in outer_axes:
+        c = x_aff.coef(name)
+        if ext == 1:
+            continue
+        if c == 0:
+            zero.append((name, ext))
+        elif c < sr:
+            inner.append((c, ext, name))
+        elif c >= sr * n:
+            outer.append((c, ext, name))
+        else:
+            raise NoMatch("tile axis overlaps the reduction axis")
+    need(x_aff.vars() <= {r} | {a for a, _ in outer_axes}, "load uses an unknown variable")
+    run = 1
+    for c, ext, _ in sorted(inner):
+        need(c == run, "inner axes are not dense")
+        run *= ext
+    need(run == sr, "inner axes do not fill the reduction stride")
+    run = sr * n
+    for c, ext, _ in sorted(outer):
+        need(c == run, "outer axes are not dense")
+        run *= ext
+    n_outer = run // (sr * n)
+    need(n_outer * n * sr == x_numel, "the view does not cover the input")
+    return {"outer": n_outer, "inner": sr, "zero": zero,
+            "inner_coef": {name: c for c, _, name in inner},
+            "outer_coef": {name: c for c, _, name in outer}}

@@ -1,0 +1,741 @@
+"""TEST INFRASTRUCTURE ONLY -- torch-CPU evaluation of a Kernel IR.
+
+This is the parity oracle and the timed CPU baseline ("torch-CPU evaluation of
+the IR").  Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU
+legs may import it; the product path (``compile.py`` -> ``ptxc`` -> the CUDA
+library) never does.
+
+It restates, statement by statement, the semantics the reference compiler
+gives each IR statement when it lowers a KernelOp to PTX, and runs them over
+every thread of the launch at once: one tensor lane per flattened work id
+``gid``.  Lanes advance in lockstep, which is a legal schedule for
+barrier-synchronised code, so ``Sync`` needs no action.
+
+Semantics followed (reference file:line):
+
+* launch and Tile decode: ``gid = ctaid.x*ntid.x + tid.x`` (``ptxc/lower.py:828-848``);
+  ``idx_i = (gid / suffix_i) % extent_i`` with ``suffix_i`` the product of the
+  later extents, a single axis binds ``gid`` itself, lanes with ``gid >= N``
+  are inactive (``ptxc/lower.py:736-825``).
+* flat index: row-major strides over the buffer shape for as many
+  coordinates as given; a lone coordinate is already flat
+  (``ptxc/common.py:398-415``, ``ptxc/memory.py:150-186``).
+* ``Accum``: ``acc = op(base if base else acc, value)``; accumulators are
+  seeded at the entry of the loop instance named by ``axes[0]`` unless an
+  ``Init`` names them, top-level ones at kernel entry, others lazily on first
+  fold (``ptxc/stmts.py:564-611``, ``ptxc/lower.py:524-546,651-677``,
+  ``ptxc/common.py:87-112``); seeds are ``add->0``, ``max->-1e30``,
+  ``min->1e30`` (``ptxc/ops.py:67-75``).  A half accumulator is rounded
+  back to f16 after every fold (``ptxc/stmts.py:589-594``).
+* ``StridedLoop``: ``for a in start..end step s`` per lane (``ptxc/stmts.py:728-773``);
+  ``Loop``: ``for a in 0..extent`` (``ptxc/stmts.py:663-725``).
+* ``WarpShuffle``: XOR butterfly for ``offset = length/2 .. 1`` then the
+  combine statements (``ptxc/stmts.py:1441-1492``).
+* ``TreeHalve``: for ``s = length/2 .. 1`` threads ``tid < s`` fold slot
+  ``tid+s`` into slot ``tid``; afterwards every thread reads slot 0
+  (``ptxc/stmts.py:1495-1568``).
+* ``Load``/``Write``: f16 loads widen to f32; a write converts to the
+  destination dtype (``ptxc/stmts.py:434-487``); atomic writes add
+  (``red.global.add``).
+* ``CpAsyncCopy``: ``nbytes`` consecutive elements from ``src[src_index]`` to
+  ``smem[smem_index (+ lane_index over (.., cols))]`` (``ptxc/stmts.py:1590-1623``).
+  A coordinate written ``None + e`` in a copy inside a ``StridedLoop`` stands
+  for ``loop_var + step + e`` (the next pipeline stage; see the prefetch
+  copies of the reference fixture ``tests/variants/v_m_256``); source reads
+  past the end of the buffer are skipped, since their stage is never used.
+* elementwise ops: the f32 spellings of ``ptxc/expr.py:880-1089``
+  (``exp`` is ``2^(x*log2 e)``, ``reciprocal`` is ``1/x`` rounded once,
+  ``maximum`` is ``max``, ``add``/``sub``/``mul`` rounded per op).  Values
+  are float32 tensors for f32/f16 work and float64 for f64 work.
+"""
+
+from __future__ import annotations
+
+import math
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+_PKG = Path(__file__).resolve().parent.parent / "emmy-ptx-compiler-submission_b200"
+if str(_PKG) not in sys.path:
+    sys.path.insert(0, str(_PKG))
+
+from emmy_ir.nodes import (  # noqa: E402
+    BinaryExpr, Builtin, CastExpr, Dim, Literal, TernaryExpr, Var, dtype_name, iter_stmts,
+)
+
+TORCH_DT = {"f32": torch.float32, "f16": torch.float16, "f64": torch.float64,
+            "i32": torch.int32, "i64": torch.int64, "u8": torch.uint8, "i8": torch.int8,
+            "bool": torch.bool}
+NP_DT = {"f32": np.float32, "f16": np.float16, "f64": np.float64, "i32": np.int32,
+         "i64": np.int64, "u8": np.uint8, "i8": np.int8, "bool": np.bool_}
+
+IDENTITY = {"add": 0.0, "sum": 0.0, "multiply": 1.0, "prod": 1.0,
+            "maximum": -1e30, "amax": -1e30, "minimum": 1e30}
+
+
+class OracleError(RuntimeError):
+    pass
+
+
+def _op_name(op) -> str:
+    return getattr(op, "name", str(op))
+
+
+def _strides(shape, ncoords):
+    shape = tuple(int(s) for s in shape)
+    if ncoords <= 1 or not shape:
+        return [1] * ncoords
+    out = []
+    for i in range(ncoords):
+        s = 1
+        for d in shape[i + 1:]:
+            s *= d
+        out.append(s)
+    return out
+
+
+def _compute_kind(dt: str) -> str:
+    return "f64" if dt == "f64" else ("f32" if dt in ("f32", "f16") else dt)
+
+
+class IRInterpreter:
+    """Run one KernelOp under its meta launch over CPU tensors.
+
+    ``buffers`` maps every argument name to a 1-D CPU tensor of the argument's
+    dtype and ``prod(shape)`` elements (outputs must already hold their
+    initial contents; the caller zeroes them as the reference harness does).
+    ``blocks=(b0, b1)`` restricts the run to a range of thread blocks, which
+    ``bench.py`` uses to time a bounded sample of a large launch.
+    """
+
+    def __init__(self, kernel_op, meta: dict, buffers: dict, blocks=None):
+        self.op = kernel_op
+        self.meta = meta
+        self.buffers = buffers
+        self.shapes = {a["name"]: tuple(a["shape"]) for a in meta["args"]}
+        self.dtypes = {a["name"]: a["dtype"] for a in meta["args"]}
+        self.threads = int(np.prod(meta["block"]))
+        grid = int(np.prod(meta["grid"]))
+        b0, b1 = (0, grid) if blocks is None else blocks
+        self.gid = torch.arange(b0 * self.threads, b1 * self.threads, dtype=torch.int64)
+        self.L = self.gid.numel()
+        self.tid = self.gid % self.threads
+        self.blk = self.gid // self.threads - b0
+        self.nblk = b1 - b0
+        self.env = {}          # name -> (tensor, kind)
+        self.axes = {}         # axis name -> int64 tensor or int
+        self.smem = {}         # name -> (tensor [nblk, n], dtype, extents)
+        self.inits = set()
+        self.loop_stack = []   # (axis name, var tensor, step)
+        for st in iter_stmts(kernel_op.body):
+            if type(st).__name__ == "Init":
+                self.inits.add(st.name)
+
+    # -- entry ---------------------------------------------------------------
+
+    def run(self):
+        body = self.op.body
+        tiles = [s for s in body if type(s).__name__ == "Tile"]
+        if len(tiles) != 1:
+            raise OracleError("expected exactly one Tile at the top of the kernel")
+        pre = [s for s in body if type(s).__name__ != "Tile"]
+        mask = torch.ones(self.L, dtype=torch.bool)
+        self._seed_top(body)
+        self._walk(pre, mask)
+        tile = tiles[0]
+        axes = [(a.name, int(a.extent.value)) for a in tile.axes]
+        n = 1
+        for _, e in axes:
+            n *= e
+        suffix = [1] * len(axes)
+        for i in range(len(axes) - 2, -1, -1):
+            suffix[i] = suffix[i + 1] * axes[i + 1][1]
+        if len(axes) == 1 and axes[0][1] > 1:
+            self.axes[axes[0][0]] = self.gid
+        else:
+            for (name, ext), suf in zip(axes, suffix):
+                self.axes[name] = (self.gid // suf) % ext
+        active = self.gid < n
+        self._walk(tile.body, active)
+
+    def _seed_top(self, body):
+        seen = {}
+        for st in iter_stmts(body):
+            if type(st).__name__ == "Accum":
+                seen.setdefault(st.name, st)
+        for name, st in seen.items():
+            if name in self.inits or tuple(st.axes or ()):
+                continue
+            self._seed(st, torch.ones(self.L, dtype=torch.bool))
+
+    # -- helpers ---------------------------------------------------------------
+
+    def _set(self, name, value, kind, mask):
+        if isinstance(value, torch.Tensor) and value.dim() == 0:
+            value = value.expand(self.L)
+        old = self.env.get(name)
+        if old is not None and not bool(mask.all()):
+            ov = old[0]
+            if ov.dtype != value.dtype:
+                ov = ov.to(value.dtype)
+            if ov.dim() == 0:
+                ov = ov.expand(self.L)
+            value = torch.where(mask, value, ov)
+        self.env[name] = (value, kind)
+
+    def _const(self, v, kind):
+        if kind == "f64":
+            return torch.tensor(float(v), dtype=torch.float64)
+        if kind in ("f32", "f16"):
+            return torch.tensor(float(v), dtype=torch.float32)
+        if kind == "pred":
+            return torch.tensor(bool(v))
+        return torch.tensor(int(v), dtype=torch.int64)
+
+    def _value(self, name):
+        if isinstance(name, (int, float)) and not isinstance(name, bool):
+            return self._const(name, "f32" if isinstance(name, float) else "i64"), \
+                ("f32" if isinstance(name, float) else "i64")
+        if name in self.env:
+            return self.env[name]
+        if name in self.axes:
+            return self._as_tensor(self.axes[name]), "i64"
+        if name in ("lane", "lane_id"):
+            return self.tid % 32, "i64"
+        if name in ("warp", "warp_id"):
+            return self.tid // 32, "i64"
+        if name in ("tid", "thread_id", "thread_idx.x"):
+            return self.tid, "i64"
+        raise OracleError(f"unknown SSA value {name!r}")
+
+    def _as_tensor(self, v):
+        if isinstance(v, torch.Tensor):
+            return v
+        return torch.tensor(int(v), dtype=torch.int64)
+
+    def _seed(self, st, mask):
+        dt = dtype_name(st.dtype)
+        kind = _compute_kind(dt)
+        ident = IDENTITY.get(_op_name(st.op), 0.0)
+        v = self._const(ident, kind)
+        if dt == "f16":
+            v = v.to(torch.float16).to(torch.float32)
+        self._set(st.name, v.expand(self.L).clone(), kind, mask)
+
+    def _seed_loop(self, loop, mask):
+        axis = loop.axis.name
+        found = []
+
+        def walk(stmts, shadowed=False):
+            for s in stmts:
+                nm = type(s).__name__
+                if nm == "Accum" and not shadowed:
+                    ax = tuple(s.axes or ())
+                    if ax and ax[0] == axis and s.name not in self.inits:
+                        found.append(s)
+                child_sh = shadowed or (nm in ("Loop", "StridedLoop") and s.axis.name == axis)
+                for attr in ("body", "else_body"):
+                    ch = getattr(s, attr, None)
+                    if isinstance(ch, (tuple, list)) and ch:
+                        walk(ch, child_sh)
+
+        walk(loop.body)
+        done = set()
+        for s in found:
+            if s.name not in done:
+                done.add(s.name)
+                self._seed(s, mask)
+
+    # -- index expressions -------------------------------------------------------
+
+    def idx(self, e):
+        """An integer expression over axes, loop variables and builtins (int64)."""
+        if e is None:
+            raise OracleError("None in an index expression outside a pipelined copy")
+        if isinstance(e, Dim):
+            return torch.tensor(int(e.value), dtype=torch.int64)
+        if isinstance(e, (int,)) and not isinstance(e, bool):
+            return torch.tensor(e, dtype=torch.int64)
+        if isinstance(e, Literal):
+            return torch.tensor(int(e.value), dtype=torch.int64)
+        if isinstance(e, (Var, Builtin)):
+            if e.name in self.axes:
+                return self._as_tensor(self.axes[e.name])
+            v, kind = self._value(e.name)
+            if kind in ("f32", "f64", "f16"):
+                return torch.trunc(v).to(torch.int64)
+            return v.to(torch.int64)
+        if isinstance(e, BinaryExpr):
+            if e.left is None or e.right is None:
+                if not self.loop_stack:
+                    raise OracleError("None operand outside a loop")
+                _, var, step = self.loop_stack[-1]
+                nxt = var + step
+                other = e.right if e.left is None else e.left
+                return self._ibin(e.op, nxt, self.idx(other)) if e.left is None \
+                    else self._ibin(e.op, self.idx(other), nxt)
+            return self._ibin(e.op, self.idx(e.left), self.idx(e.right))
+        if isinstance(e, TernaryExpr):
+            return torch.where(self.pred(e.cond), self.idx(e.if_true), self.idx(e.if_false))
+        if isinstance(e, CastExpr):
+            return self.idx(e.expr)
+        raise OracleError(f"unsupported index expression {type(e).__name__}")
+
+    @staticmethod
+    def _ibin(op, a, b):
+        if op in ("+", "add"):
+            return a + b
+        if op in ("-", "subtract"):
+            return a - b
+        if op in ("*", "multiply"):
+            return a * b
+        if op in ("/", "//", "divide", "floor_divide"):
+            # s32 division truncates toward zero (div.s32); indices are non-negative
+            return torch.div(a, b, rounding_mode="trunc")
+        if op in ("%", "mod", "remainder"):
+            return torch.fmod(a, b)
+        if op in ("<<", "left_shift"):
+            return a << b
+        if op in (">>", "right_shift"):
+            return a >> b
+        if op == "&":
+            return a & b
+        if op == "|":
+            return a | b
+        if op == "^":
+            return a ^ b
+        raise OracleError(f"unsupported index op {op!r}")
+
+    def pred(self, e):
+        if isinstance(e, BinaryExpr):
+            op = e.op
+            rel = {"<": torch.lt, "<=": torch.le, ">": torch.gt, ">=": torch.ge,
+                   "==": torch.eq, "!=": torch.ne}.get(op)
+            if rel is not None:
+                return rel(self.idx(e.left), self.idx(e.right))
+            if op in ("and", "&&"):
+                return self.pred(e.left) & self.pred(e.right)
+            if op in ("or", "||"):
+                return self.pred(e.left) | self.pred(e.right)
+        if isinstance(e, Var):
+            v, kind = self._value(e.name)
+            return v != 0 if kind != "pred" else v
+        raise OracleError(f"unsupported predicate {e!r}")
+
+    def flat(self, index, shape):
+        if index is None or len(index) == 0:
+            return torch.tensor(0, dtype=torch.int64)
+        if len(index) == 1:
+            return self.idx(index[0])
+        acc = None
+        for coord, stride in zip(index, _strides(shape, len(index))):
+            t = self.idx(coord) * stride
+            acc = t if acc is None else acc + t
+        return acc
+
+    # -- statements --------------------------------------------------------------
+
+    def _walk(self, stmts, mask):
+        for st in stmts:
+            getattr(self, "s_" + type(st).__name__)(st, mask)
+
+    def s_Tile(self, st, mask):
+        raise OracleError("nested Tile")
+
+    def s_Smem(self, st, mask):
+        if st.name in self.smem:
+            return
+        dt = dtype_name(st.dtype)
+        n = int(np.prod([int(x) for x in st.extents])) if st.extents else 1
+        self.smem[st.name] = (torch.zeros((self.nblk, n), dtype=TORCH_DT[dt]), dt,
+                              tuple(int(x) for x in st.extents))
+
+    def s_Sync(self, st, mask):
+        pass
+
+    def s_CpAsyncCommit(self, st, mask):
+        pass
+
+    def s_CpAsyncWait(self, st, mask):
+        pass
+
+    def s_Let(self, st, mask):
+        dt = dtype_name(st.dtype)
+        kind = _compute_kind(dt)
+        value = getattr(st.value, "value", st.value)
+        self._set(st.name, self._const(value, kind).expand(self.L), kind, mask)
+
+    def s_Init(self, st, mask):
+        dt = dtype_name(st.dtype)
+        kind = _compute_kind(dt)
+        value = getattr(st.identity, "value", st.identity)
+        self._set(st.name, self._const(value, kind).expand(self.L).clone(), kind, mask)
+
+    def _gather(self, name, flat, mask):
+        """Read one element per lane from a global or shared buffer."""
+        flat = flat.expand(self.L) if flat.dim() == 0 else flat
+        if name in self.smem:
+            buf, dt, _ = self.smem[name]
+            n = buf.shape[1]
+            safe = torch.where(mask & (flat >= 0) & (flat < n), flat, torch.zeros_like(flat))
+            return buf[self.blk, safe], dt
+        buf = self.buffers[name]
+        dt = self.dtypes[name]
+        n = buf.numel()
+        if n == 0:
+            raise OracleError(f"load from empty buffer {name!r}")
+        bad = mask & ((flat < 0) | (flat >= n))
+        if bool(bad.any()):
+            raise OracleError(f"out-of-bounds load from {name!r}")
+        safe = torch.where(mask, flat, torch.zeros_like(flat))
+        return buf[safe], dt
+
+    def s_Load(self, st, mask):
+        if st.input in self.smem:
+            shape = self.smem[st.input][2]
+        else:
+            shape = self.shapes[st.input]
+        base = self.flat(st.index, shape)
+        for i, name in enumerate(st.names):
+            raw, dt = self._gather(st.input, base + i, mask)
+            kind = _compute_kind(dt)
+            if kind == "f32":
+                raw = raw.to(torch.float32)
+            elif kind == "f64":
+                raw = raw.to(torch.float64)
+            else:
+                raw = raw.to(torch.int64)
+            self._set(name, raw, kind, mask)
+
+    def _convert(self, v, kind, dt):
+        tdt = TORCH_DT[dt]
+        if dt in ("f32", "f16", "f64"):
+            return v.to(tdt)
+        if kind in ("f32", "f64"):
+            return torch.trunc(v).to(tdt)
+        return v.to(tdt)
+
+    def s_Write(self, st, mask):
+        if st.output in self.smem:
+            buf, dt, ext = self.smem[st.output]
+            base = self.flat(st.index, ext)
+            for i, vname in enumerate(st.values):
+                v, kind = self._value(vname)
+                v = v.expand(self.L) if v.dim() == 0 else v
+                f = (base + i)
+                f = f.expand(self.L) if f.dim() == 0 else f
+                if getattr(st, "swizzle", "NONE") not in (None, "NONE"):
+                    f = _swizzle(f, st.swizzle)
+                m = mask
+                buf[self.blk[m], f[m]] = self._convert(v[m], kind, dt)
+            return
+        buf = self.buffers[st.output]
+        dt = self.dtypes[st.output]
+        base = self.flat(st.index, self.shapes[st.output])
+        for i, vname in enumerate(st.values):
+            v, kind = self._value(vname)
+            v = v.expand(self.L) if v.dim() == 0 else v
+            f = base + i
+            f = f.expand(self.L) if f.dim() == 0 else f
+            m = mask
+            idx = f[m]
+            if idx.numel() and (int(idx.min()) < 0 or int(idx.max()) >= buf.numel()):
+                raise OracleError(f"out-of-bounds write to {st.output!r}")
+            val = self._convert(v[m], kind, dt)
+            if st.atomic:
+                if dt == "f16":
+                    # red.global.add.f16 rounds each add; emulate in f32 then round
+                    acc = buf.to(torch.float32)
+                    acc.index_put_((idx,), val.to(torch.float32), accumulate=True)
+                    buf.copy_(acc.to(torch.float16))
+                else:
+                    buf.index_put_((idx,), val, accumulate=True)
+            else:
+                buf[idx] = val
+
+    def s_Assign(self, st, mask):
+        opname = _op_name(st.op)
+        vals = [self._value(a) for a in st.args]
+        dt = dtype_name(st.dtype) if st.dtype is not None else None
+        kinds = [k for _, k in vals]
+        if dt is None:
+            kind = "f64" if "f64" in kinds else ("f32" if any(k in ("f32", "f16") for k in kinds) else kinds[0])
+        else:
+            kind = _compute_kind(dt)
+        out = _elementwise(opname, [v for v, _ in vals], kinds, kind)
+        if isinstance(out, tuple):
+            out, kind = out
+        if dt == "f16":
+            out = out.to(torch.float16).to(torch.float32)
+        self._set(st.name, out, kind, mask)
+
+    def s_Accum(self, st, mask):
+        opname = _op_name(st.op)
+        dt = dtype_name(st.dtype)
+        kind = _compute_kind(dt)
+        if st.name not in self.env:
+            self._seed(st, mask)
+        left = self._value(st.base)[0] if st.base is not None else self.env[st.name][0]
+        right = self._value(st.value)[0]
+        out = _elementwise(opname, [left, right], [kind, kind], kind)
+        if isinstance(out, tuple):
+            out = out[0]
+        if dt == "f16":
+            out = out.to(torch.float16).to(torch.float32)
+        self._set(st.name, out, kind, mask)
+
+    def s_Cond(self, st, mask):
+        p = self.pred(st.cond)
+        p = p.expand(self.L) if p.dim() == 0 else p
+        m1 = mask & p
+        if bool(m1.any()):
+            self._walk(st.body, m1)
+        if st.else_body:
+            m2 = mask & ~p
+            if bool(m2.any()):
+                self._walk(st.else_body, m2)
+
+    def s_Loop(self, st, mask):
+        name = st.axis.name
+        ext = int(st.axis.extent.value)
+        saved = self.axes.get(name)
+        self._seed_loop(st, mask)
+        for i in range(ext):
+            var = torch.tensor(i, dtype=torch.int64)
+            self.axes[name] = var
+            self.loop_stack.append((name, var, 1))
+            self._walk(st.body, mask)
+            self.loop_stack.pop()
+        if saved is None:
+            self.axes.pop(name, None)
+        else:
+            self.axes[name] = saved
+
+    def s_StridedLoop(self, st, mask):
+        name = st.axis.name
+        start = self.idx(st.start)
+        start = start.expand(self.L) if start.dim() == 0 else start
+        end = self.idx(st.end if st.end is not None else st.axis.extent)
+        step = int(st.step.value)
+        if step <= 0:
+            raise OracleError("StridedLoop step must be positive")
+        saved = self.axes.get(name)
+        self._seed_loop(st, mask)
+        span = (end - start).clamp(min=0)
+        trips = torch.div(span + step - 1, step, rounding_mode="floor")
+        tmax = int(trips[mask].max()) if bool(mask.any()) else 0
+        for t in range(tmax):
+            var = start + t * step
+            m = mask & (var < end)
+            self.axes[name] = var
+            self.loop_stack.append((name, var, step))
+            self._walk(st.body, m)
+            self.loop_stack.pop()
+        if saved is None:
+            self.axes.pop(name, None)
+        else:
+            self.axes[name] = saved
+
+    def s_WarpShuffle(self, st, mask):
+        length = int(st.length)
+        lane = self.tid % 32
+        offset = length // 2
+        while offset >= 1:
+            partner_tid = (self.tid - lane) + (lane ^ offset)
+            if bool((partner_tid >= self.threads).any()):
+                raise OracleError("shuffle partner outside the block")
+            # lanes are laid out block-major, so the partner's lane index is
+            # this lane's index plus the tid difference
+            pidx = torch.arange(self.L) + (partner_tid - self.tid)
+            for s, sb in zip(st.state, st.state_b):
+                v, kind = self.env[s]
+                v = v.expand(self.L) if v.dim() == 0 else v
+                self._set(sb, v[pidx], kind, mask)
+            self._walk(st.combine_states, mask)
+            offset //= 2
+
+    def s_TreeHalve(self, st, mask):
+        if st.inner:
+            raise OracleError("TreeHalve with an inner offset is not restated")
+        length = int(st.length)
+        tid = self._value(st.tid_var)[0]
+        tid = tid.expand(self.L) if tid.dim() == 0 else tid
+        s = length // 2
+        while s >= 1:
+            m = mask & (tid < s)
+            for state, sb, bufname in zip(st.state, st.state_b, st.bufs):
+                buf, dt, _ = self.smem[bufname]
+                kind = _compute_kind(dt)
+                a = buf[self.blk, torch.where(m, tid, torch.zeros_like(tid))]
+                b = buf[self.blk, torch.where(m, tid + s, torch.zeros_like(tid))]
+                conv = torch.float64 if kind == "f64" else torch.float32
+                self._set(state, a.to(conv), kind, m)
+                self._set(sb, b.to(conv), kind, m)
+            self._walk(st.combine_states, m)
+            for state, bufname in zip(st.state, st.bufs):
+                buf, dt, _ = self.smem[bufname]
+                v, kind = self.env[state]
+                buf[self.blk[m], tid[m]] = self._convert(v[m], kind, dt)
+            s //= 2
+        for state, bufname in zip(st.state, st.bufs):
+            buf, dt, _ = self.smem[bufname]
+            kind = _compute_kind(dt)
+            conv = torch.float64 if kind == "f64" else torch.float32
+            self._set(state, buf[self.blk, 0].to(conv), kind, mask)
+
+    def s_CpAsyncCopy(self, st, mask):
+        buf, dt, ext = self.smem[st.smem]
+        esize = torch.empty((), dtype=TORCH_DT[dt]).element_size()
+        count = int(st.nbytes) // esize
+        dst = self.flat(st.smem_index, ext)
+        if st.lane_index is not None:
+            cols = ext[-1]
+            dst = dst + self.flat(st.lane_index, (0, cols))
+            if getattr(st, "swizzle", "NONE") not in (None, "NONE"):
+                dst = _swizzle(dst, st.swizzle)
+        src = self.flat(st.src_index, self.shapes[st.src])
+        dst = dst.expand(self.L) if dst.dim() == 0 else dst
+        src = src.expand(self.L) if src.dim() == 0 else src
+        sbuf = self.buffers[st.src]
+        for i in range(count):
+            s = src + i
+            ok = mask & (s >= 0) & (s < sbuf.numel())
+            if not bool(ok.any()):
+                continue
+            buf[self.blk[ok], (dst + i)[ok]] = sbuf[s[ok]].to(buf.dtype)
+
+    def s_ZeroPrologue(self, st, mask):
+        buf = self.buffers[st.dst]
+        nbytes = int(st.words) * 4
+        view = buf.view(torch.uint8)
+        view[:nbytes] = 0
+
+
+def _swizzle(flat, mode):
+    base, _, sh = str(mode).partition("@")
+    shift, msk = {"B32": (1, 1), "B64": (1, 3), "B128": (1, 7)}.get(base, (0, 0))
+    if sh:
+        shift = int(sh)
+    if not msk:
+        return flat
+    return flat ^ (((flat >> shift) & msk) << 3)
+
+
+def _f(v, kind):
+    return v
+
+
+def _elementwise(opname, args, kinds, kind):
+    """One elementwise op in the compute kind (f32 or f64 tensors, int64 or bool)."""
+    fl = kind in ("f32", "f64")
+    tdt = torch.float64 if kind == "f64" else torch.float32
+    if fl:
+        args = [a.to(tdt) if a.dtype != tdt and a.dtype != torch.bool else a for a in args]
+    a = args[0] if args else None
+    b = args[1] if len(args) > 1 else None
+    if opname in ("add", "sum"):
+        return a + b
+    if opname in ("subtract", "sub"):
+        return a - b
+    if opname in ("multiply", "prod"):
+        return a * b
+    if opname in ("divide", "true_divide", "divide_rn_f32"):
+        return a / b if fl else torch.div(a, b, rounding_mode="trunc")
+    if opname in ("maximum", "amax", "max"):
+        return torch.maximum(a, b)
+    if opname in ("minimum", "min"):
+        return torch.minimum(a, b)
+    if opname == "fma":
+        return (a.double() * b.double() + args[2].double()).to(tdt)
+    if opname in ("exp", "exp_fast"):
+        if kind == "f64":
+            return torch.exp(a)
+        return torch.exp2(a * torch.tensor(1.4426950408889634, dtype=torch.float32))
+    if opname == "exp2":
+        return torch.exp2(a)
+    if opname == "log":
+        return torch.log(a)
+    if opname == "sqrt":
+        return torch.sqrt(a)
+    if opname == "rsqrt":
+        return torch.rsqrt(a)
+    if opname == "reciprocal":
+        return torch.reciprocal(a)
+    if opname == "relu":
+        return torch.clamp_min(a, 0)
+    if opname in ("copy", "pad", "bitcast"):
+        return a.clone()
+    if opname in ("negative", "negate"):
+        return -a
+    if opname in ("abs", "fabs"):
+        return torch.abs(a)
+    if opname == "tanh":
+        return torch.tanh(a)
+    if opname == "sigmoid":
+        return torch.sigmoid(a)
+    if opname == "pow":
+        return torch.pow(a, b)
+    if opname in ("greater", "gt"):
+        return (a > b), "pred"
+    if opname in ("less", "lt"):
+        return (a < b), "pred"
+    if opname in ("greater_equal", "ge"):
+        return (a >= b), "pred"
+    if opname in ("less_equal", "le"):
+        return (a <= b), "pred"
+    if opname in ("equal", "eq"):
+        return (a == b), "pred"
+    if opname == "where":
+        c = args[0]
+        c = c if c.dtype == torch.bool else (c != 0)
+        x, y = args[1], args[2]
+        if x.dtype != y.dtype:
+            y = y.to(x.dtype)
+        return torch.where(c, x, y)
+    raise OracleError(f"unsupported elementwise op {opname!r}")
+
+
+def make_inputs(meta: dict, seed_offset: int = 0, rng_kind: str = "normal") -> dict:
+    """Seeded inputs exactly as the reference harness builds them.
+
+    ``tools/localrun.py:111-118``: outputs are zeros; ``data`` args are the
+    literal values; every other arg is
+    ``np.random.default_rng(seed).standard_normal(prod(shape)).astype(dtype)``,
+    or, when the argument carries an ``init`` field (benchmark inputs), a
+    normal/uniform draw from the same generator.  Returns numpy arrays keyed
+    by argument name.
+    """
+    out = {}
+    for a in meta["args"]:
+        n = int(np.prod(a["shape"])) if a["shape"] else 1
+        dt = NP_DT[a["dtype"]]
+        if a.get("output"):
+            out[a["name"]] = np.zeros(n, dtype=dt)
+        elif "data" in a:
+            out[a["name"]] = np.array(a["data"], dtype=dt).reshape(-1)
+        else:
+            rng = np.random.default_rng(a.get("seed", 0) + seed_offset)
+            init = a.get("init")
+            if init is None:
+                v = rng.standard_normal(n)
+            elif init.get("dist") == "normal":
+                v = rng.standard_normal(n) * float(init.get("std", 1.0)) + float(init.get("mean", 0.0))
+            elif init.get("dist") == "uniform":
+                v = rng.uniform(float(init.get("low", 0.0)), float(init.get("high", 1.0)), n)
+            else:
+                raise OracleError(f"unknown init {init!r}")
+            out[a["name"]] = v.astype(dt)
+    return out
+
+
+def run_ir(kernel_op, meta: dict, inputs: dict, blocks=None, threads=None) -> dict:
+    """Evaluate the IR on numpy inputs; returns every buffer as numpy (outputs filled)."""
+    if threads:
+        torch.set_num_threads(threads)
+    bufs = {k: torch.from_numpy(np.array(v, copy=True)) for k, v in inputs.items()}
+    with torch.no_grad():
+        IRInterpreter(kernel_op, meta, bufs, blocks=blocks).run()
+    return {k: v.numpy() for k, v in bufs.items()}

@@ -1,0 +1,69 @@
+"""The C-ABI library loads without a GPU and exports every symbol the header declares."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+
+import pytest
+
+from conftest import PKG, ROOT
+
+HEADER = ROOT / "include" / "emmy_b200.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(emmy_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    path = PKG / "libemmyb200.so"
+    if not path.exists():
+        import importlib.util
+        spec = importlib.util.spec_from_file_location("emmy_build", PKG / "build.py")
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        mod.build()
+    return ctypes.CDLL(str(path))
+
+
+def test_header_declares_the_families():
+    syms = declared_symbols()
+    for s in ("emmy_reduce_f32", "emmy_rownorm_f32", "emmy_softmax_f32", "emmy_matvec_f64",
+              "emmy_last_error", "emmy_get_device_status", "emmy_zero", "emmy_version"):
+        assert s in syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [s for s in declared_symbols() if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_version_and_error_text_need_no_gpu(lib):
+    assert lib.emmy_version() >= 100
+    lib.emmy_last_error.restype = ctypes.c_char_p
+    assert lib.emmy_last_error() is not None
+
+
+def test_host_side_argument_checks_run_before_any_cuda_call(lib):
+    # invalid sizes are rejected on the host with EMMY_ERR_INVALID (no device touched)
+    lib.emmy_softmax_f32.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                     ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p]
+    assert lib.emmy_softmax_f32(None, None, -1, 4, 1, None) == 1
+    lib.emmy_last_error.restype = ctypes.c_char_p
+    assert b"bad view" in lib.emmy_last_error()
+    lib.emmy_rownorm_f32.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int64] * 2 + \
+        [ctypes.c_void_p] * 2 + [ctypes.c_int, ctypes.c_void_p]
+    assert lib.emmy_rownorm_f32(None, None, None, None, 4, 4, None, None, 0, None) == 1
+    assert lib.emmy_rownorm_f32(None, None, None, None, 0, 4, None, None, 0, None) == 0
+
+
+def test_launcher_refuses_to_run_without_the_library(tmp_path, monkeypatch):
+    import ptxc.launch as L
+    monkeypatch.setattr(L, "_LIB", None)
+    monkeypatch.setenv("EMMY_B200_LIB", str(tmp_path / "missing.so"))
+    with pytest.raises(L.LibraryError):
+        L.load_library()
