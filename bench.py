@@ -42,7 +42,12 @@ for _p in (str(ROOT), str(PKG)):
 METRIC = "per-family HBM GB/s (K2: softmax4d + layernorm f32)"
 UNIT = "GB/s"
 FALLBACK_HBM_GBS = 6650.0
+# FP32 CUDA-core peak, nominal: 148 SMs x 128 FMA/clk x 2 flops x 1.965 GHz
+FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 L2_FLUSH_BYTES = 256 << 20
+# A short device spin queued before each timed region keeps the GPU busy while
+# the host enqueues the launches, so the CUDA events bracket device work only.
+SPIN_CYCLES = 200_000
 
 
 def hbm_peak():
@@ -146,6 +151,23 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+class L2Flush:
+    """Evict L2 between timed steps: write one 256 MiB buffer, then read another.
+
+    The read pass leaves L2 full of clean lines, so the next timed kernel does
+    not pay for writing back the flush's dirty lines.
+    """
+
+    def __init__(self, device):
+        import torch
+        self.w = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+        self.r = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=device)
+
+    def __call__(self):
+        self.w.zero_()
+        self.sink = self.r.sum()
+
+
 def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -245,12 +267,14 @@ def family_extras(device, peak):
     from ptxc import Lowerer
     from ptxc.launch import Executor
     out = {}
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    flush = L2Flush(device)
     cases = {
         "K1_rmsnorm_4096x512": synth.rmsnorm(4096, 512, eps=1e-6),
         "K2a_softmax_32x16x512x512": synth.softmax([32, 16, 512, 512]),
         "K2b_layernorm_16384x1024": synth.layernorm(16384, 1024),
         "K4b_matvec_f64_16384": synth.matvec(16384, 16384),
+        "K4a_splitk_f32_256x65536x256": synth.matmul(256, 256, 65536, splits=64, tm=128, tn=128,
+                                                     rm=8, rn=8),
     }
     for name, (kop, meta) in cases.items():
         plan = Lowerer(kop, meta).plan()
@@ -265,7 +289,8 @@ def family_extras(device, peak):
             ex.launch()
         times = []
         for _ in range(10):
-            flush.zero_()
+            flush()
+            torch.cuda._sleep(SPIN_CYCLES)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             ex.launch()
@@ -276,6 +301,13 @@ def family_extras(device, peak):
         gbs = plan_bytes(plan) / (ms * 1e-3) / 1e9
         out[name] = {"us": round(ms * 1000, 2), "gbs": round(gbs, 1), "frac_hbm": round(gbs / peak, 3),
                      "bytes": plan_bytes(plan)}
+        if "gemm" in plan:
+            g = plan["gemm"]
+            flops = 2.0 * g["batch"] * g["m"] * g["n"] * g["k"]
+            tf = flops / (ms * 1e-3) / 1e12
+            out[name]["tflops"] = round(tf, 2)
+            if plan["family"] == "gemm_f32":
+                out[name]["frac_fp32_nominal"] = round(tf / FP32_NOMINAL_TFLOPS, 3)
         del ex
     del flush
     torch.cuda.empty_cache()
@@ -317,7 +349,7 @@ def run_b200_arm(args):
     for ex, h in zip(execs, hosts):
         ex.upload(h)
     torch.cuda.synchronize()
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    flush = L2Flush(device)
 
     def barrier():
         if world > 1:
@@ -333,16 +365,17 @@ def run_b200_arm(args):
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     launches = 0
-    with ClockSampler(device.index) as clocks:
-        for i in range(args.steps):
-            flush.zero_()                       # L2 flush between steps (outside the events)
-            e0, e1, e2 = ev[i]
-            e0.record()
-            launches += execs[0].launch()       # softmax (dominant kernel)
-            e1.record()
-            launches += execs[1].launch()       # layernorm
-            e2.record()
-        torch.cuda.synchronize()
+    clocks = ClockSampler(device.index).__enter__()
+    for i in range(args.steps):
+        flush()                             # L2 flush between steps (outside the events)
+        torch.cuda._sleep(SPIN_CYCLES)
+        e0, e1, e2 = ev[i]
+        e0.record()
+        launches += execs[0].launch()       # softmax (dominant kernel)
+        e1.record()
+        launches += execs[1].launch()       # layernorm
+        e2.record()
+    torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
     step_ms = [a.elapsed_time(c) for a, b, c in ev]
@@ -383,6 +416,7 @@ def run_b200_arm(args):
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
+    clocks.__exit__(None, None, None)
     e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev)
     if world > 1:
         t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
@@ -449,6 +483,7 @@ PROFILE_CASES = {
     # name: (builder, launches) -- small cases (inputs above L2, a few hundred MB at most)
     # for one-kernel ncu captures: `python bench.py --case softmax_65536x512`
     "softmax_65536x512": lambda s: s.softmax([65536, 512], x_init={"dist": "normal", "std": 2.0}),
+    "softmax_K2a": lambda s: s.softmax([32, 16, 512, 512], x_init={"dist": "normal", "std": 2.0}),
     "layernorm_16384x1024": lambda s: s.layernorm(16384, 1024),
     "rmsnorm_65536x512": lambda s: s.rmsnorm(65536, 512, eps=1e-6),
     "matvec_f64_8192x4096": lambda s: s.matvec(8192, 4096),
@@ -478,7 +513,7 @@ def main():
     ap.add_argument("--case", choices=sorted(PROFILE_CASES), help="run one profiling case and exit")
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-families", action="store_true")

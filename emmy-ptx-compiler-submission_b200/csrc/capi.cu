@@ -2,6 +2,7 @@
 // launch checks and the device status word.
 
 #include "common.cuh"
+#include "tma.cuh"
 
 #include <string.h>
 
@@ -35,6 +36,35 @@ int *device_status_ptr() {
     cached[dev] = static_cast<int *>(p);
   }
   return cached[dev];
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+int make_tensor_map(CUtensorMap *map, CUtensorMapDataType dtype, int rank, const void *base,
+                    const uint64_t *dims, const uint64_t *strides_bytes, const uint32_t *box,
+                    CUtensorMapSwizzle swizzle) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return set_error(EMMY_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(map, dtype, (cuuint32_t)rank, const_cast<void *>(base),
+                   reinterpret_cast<const cuuint64_t *>(dims),
+                   reinterpret_cast<const cuuint64_t *>(strides_bytes),
+                   reinterpret_cast<const cuuint32_t *>(box), elem_strides,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(EMMY_ERR_INVALID, "tensor map encode failed (%d)", (int)r);
+  return EMMY_OK;
 }
 
 int check_launch(const char *what) {

@@ -1,0 +1,301 @@
+// f32 GEMM / batched GEMM / split-K on sm_100a CUDA cores.
+//
+// Replaces the entry the reference emits for its tiled-matmul IR shape: a
+// Tile over (m-block, n-block, m-lane, n-lane) axes, cp.async.cg 16-byte
+// copies into double-buffered _a_smem/_b_smem, an inner Loop over the smem
+// K-tile folding fma.rn into a per-thread register micro-tile, and direct (or,
+// with a split-K Tile axis, red.global.add) writes (reference
+// ptxc/stmts.py:663-725, 614-632, 1590-1623, 434-487; fixtures v_m_*, w_m_*).
+//
+// Here: a 128x128 CTA tile with BK = 16, 256 threads each owning an 8x8
+// register tile (rows ty + 16*i, columns 4*tx + {0..3} and 64 + 4*tx + {0..3},
+// which keeps every 128-bit shared load conflict-free), operands staged by TMA
+// (cp.async.bulk.tensor) into a 4-stage shared-memory ring whose stages
+// complete on mbarriers, one elected thread issuing the copies.  Products
+// accumulate with fma in f32, as the reference's fused accumulate does.  A
+// split-K launch gives each CTA a K range and combines partials with 128-bit
+// vector atomics (red.global.add.v4.f32), the reference's atomic Write.
+//
+// Shapes TMA cannot describe (K or N not a multiple of 4, unaligned bases)
+// take a plain shared-memory tiled kernel instead.
+
+#include "common.cuh"
+#include "tma.cuh"
+
+namespace emmy {
+
+namespace gemm32 {
+constexpr int BM = 128, BN = 128, BK = 16, STAGES = 4, THREADS = 256;
+constexpr int A_BYTES = BM * BK * 4, B_BYTES = BK * BN * 4, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+}  // namespace gemm32
+
+enum GemmMode { GEMM_STORE = 0, GEMM_ACCUMULATE = 1, GEMM_ATOMIC = 2 };
+
+__global__ void __launch_bounds__(gemm32::THREADS, 2)
+gemm_f32_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const float *__restrict__ bias, float *__restrict__ C, int M, int N, int K,
+                    int64_t c_batch_stride, int splits, int k_per_split, int epilogue, int mode,
+                    int *status) {
+  using namespace gemm32;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[STAGES];
+
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+  const int batch = blockIdx.z / splits, split = blockIdx.z - batch * splits;
+  const int kb = split * k_per_split;
+  const int ke = min(K, kb + k_per_split);
+  const int ntiles = ke > kb ? (ke - kb + BK - 1) / BK : 0;
+
+  if (tid == 0) {
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  auto issue = [&](int t) {
+    const int s = t % STAGES;
+    float *As = reinterpret_cast<float *>(smem + s * STAGE_BYTES);
+    float *Bs = reinterpret_cast<float *>(smem + s * STAGE_BYTES + A_BYTES);
+    mbar_expect_tx(&full[s], STAGE_BYTES);
+    const int k = kb + t * BK;
+    tma_load_3d(As, &tmA, &full[s], k, m0, batch);
+    tma_load_3d(Bs, &tmB, &full[s], n0, k, batch);
+  };
+  if (tid == 0)
+    for (int t = 0; t < STAGES - 1 && t < ntiles; ++t) issue(t);
+
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+  int failed_at = -1;
+  for (int t = 0; t < ntiles; ++t) {
+    const int s = t % STAGES;
+    if (tid == 0 && t + STAGES - 1 < ntiles) issue(t + STAGES - 1);
+    const bool ok = mbar_wait(&full[s], (t / STAGES) & 1, status, kStatusMbarTimeout);
+    const float *As = reinterpret_cast<const float *>(smem + s * STAGE_BYTES);
+    const float *Bs = reinterpret_cast<const float *>(smem + s * STAGE_BYTES + A_BYTES);
+#pragma unroll
+    for (int kk = 0; kk < BK; kk += 4) {
+      float a[8][4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 v = *reinterpret_cast<const float4 *>(As + (ty + 16 * i) * BK + kk);
+        a[i][0] = v.x; a[i][1] = v.y; a[i][2] = v.z; a[i][3] = v.w;
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 b0 = *reinterpret_cast<const float4 *>(Bs + (kk + q) * BN + 4 * tx);
+        const float4 b1 = *reinterpret_cast<const float4 *>(Bs + (kk + q) * BN + 64 + 4 * tx);
+        const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i][q], b[j], acc[i][j]);
+      }
+    }
+    // every thread is done with stage s before thread 0 refills it next trip;
+    // the vote makes a timed-out wait a block-uniform exit
+    if (__syncthreads_or(!ok)) {
+      failed_at = t;
+      break;
+    }
+  }
+  if (failed_at >= 0) {
+    // a copy never arrived: leave C untouched (the host sees EMMY_ERR_DEVICE);
+    // before exiting, wait (bounded) for this CTA's copies still in flight
+    if (tid == 0) {
+      const int issued = min(ntiles, failed_at + STAGES);
+      for (int u = failed_at; u < issued; ++u)
+        mbar_wait(&full[u % STAGES], (u / STAGES) & 1, nullptr, 0);
+    }
+    __syncthreads();
+    return;
+  }
+
+  float *Cb = C + (int64_t)batch * c_batch_stride;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int m = m0 + ty + 16 * i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int n = n0 + 64 * h + 4 * tx;
+      if (n >= N) continue;
+      float v[4] = {acc[i][4 * h], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]};
+      if ((epilogue & EMMY_EPI_BIAS) && bias && (mode != GEMM_ATOMIC || split == 0)) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] += (n + j < N) ? __ldg(bias + n + j) : 0.f;
+      }
+      if (epilogue & EMMY_EPI_RELU) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = fmaxf(v[j], 0.f);
+      }
+      float *dst = Cb + (int64_t)m * N + n;
+      if (n + 3 < N) {
+        if (mode == GEMM_ATOMIC) {
+          atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(v[0], v[1], v[2], v[3]));
+        } else if (mode == GEMM_ACCUMULATE) {
+          float4 o = *reinterpret_cast<float4 *>(dst);
+          *reinterpret_cast<float4 *>(dst) = make_float4(o.x + v[0], o.y + v[1], o.z + v[2], o.w + v[3]);
+        } else {
+          *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+      } else {
+        for (int j = 0; j < 4 && n + j < N; ++j) {
+          if (mode == GEMM_ATOMIC) atomicAdd(dst + j, v[j]);
+          else if (mode == GEMM_ACCUMULATE) dst[j] += v[j];
+          else dst[j] = v[j];
+        }
+      }
+    }
+  }
+}
+
+// Plain shared-memory tiled kernel for shapes TMA cannot describe.
+// 64x64 CTA tile, 256 threads, 4x4 outputs per thread, BK = 16.
+__global__ void __launch_bounds__(256)
+gemm_f32_plain_kernel(const float *__restrict__ A, const float *__restrict__ B,
+                      const float *__restrict__ bias, float *__restrict__ C, int M, int N, int K,
+                      int64_t sa, int64_t sb, int64_t sc, int splits, int k_per_split,
+                      int epilogue, int mode) {
+  __shared__ float As[16][64 + 1];
+  __shared__ float Bs[16][64 + 1];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int m0 = blockIdx.x * 64, n0 = blockIdx.y * 64;
+  const int batch = blockIdx.z / splits, split = blockIdx.z - batch * splits;
+  const int kb = split * k_per_split, ke = min(K, kb + k_per_split);
+  const float *Ab = A + (int64_t)batch * sa;
+  const float *Bb = B + (int64_t)batch * sb;
+  float acc[4][4] = {};
+  for (int k0 = kb; k0 < ke; k0 += 16) {
+    for (int i = tid; i < 16 * 64; i += 256) {
+      const int r = i / 16, c = i % 16;          // A tile: 64 rows x 16 k
+      const int m = m0 + r, k = k0 + c;
+      As[c][r] = (m < M && k < ke) ? Ab[(int64_t)m * K + k] : 0.f;
+      const int kr = i / 64, nc = i % 64;        // B tile: 16 k x 64 cols
+      const int kk = k0 + kr, n = n0 + nc;
+      Bs[kr][nc] = (kk < ke && n < N) ? Bb[(int64_t)kk * N + n] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(As[k][ty + 16 * i], Bs[k][tx + 16 * j], acc[i][j]);
+    __syncthreads();
+  }
+  float *Cb = C + (int64_t)batch * sc;
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty + 16 * i;
+    if (m >= M) continue;
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tx + 16 * j;
+      if (n >= N) continue;
+      float v = acc[i][j];
+      if ((epilogue & EMMY_EPI_BIAS) && bias && (mode != GEMM_ATOMIC || split == 0)) v += bias[n];
+      if (epilogue & EMMY_EPI_RELU) v = fmaxf(v, 0.f);
+      float *dst = Cb + (int64_t)m * N + n;
+      if (mode == GEMM_ATOMIC) atomicAdd(dst, v);
+      else if (mode == GEMM_ACCUMULATE) *dst += v;
+      else *dst = v;
+    }
+  }
+}
+
+}  // namespace emmy
+
+using namespace emmy;
+
+extern "C" int emmy_gemm_f32(const float *A, const float *B, const float *bias, float *C,
+                             int64_t batch, int64_t M, int64_t N, int64_t K, int64_t a_batch_stride,
+                             int64_t b_batch_stride, int64_t c_batch_stride, int splits,
+                             int accumulate, int epilogue, void *stream) {
+  using namespace gemm32;
+  clear_error();
+  if (batch < 0 || M < 0 || N < 0 || K < 0 || splits < 0)
+    return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32: negative size");
+  if (batch == 0 || M == 0 || N == 0) return EMMY_OK;
+  if (!A || !B || !C) return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32: null operand");
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || batch > 65535)
+    return set_error(EMMY_ERR_UNSUPPORTED, "emmy_gemm_f32: size beyond 32-bit tile indexing");
+  if ((epilogue & EMMY_EPI_RELU) && (splits > 1 || accumulate))
+    return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32: relu cannot follow a partial sum");
+  cudaStream_t st = as_stream(stream);
+  const int sms = sm_count();
+  const int64_t mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
+  // split count: the caller's, or enough K partitions to give every SM two tiles
+  int sp = splits;
+  if (sp <= 0) {
+    sp = 1;
+    const int64_t tiles = mt * nt * batch;
+    if (!accumulate && tiles < 2 * sms) {
+      sp = (int)((2 * sms + tiles - 1) / tiles);
+      const int64_t kt = (K + BK - 1) / BK;
+      if (sp > kt) sp = (int)(kt > 0 ? kt : 1);
+      if (sp > 256) sp = 256;
+    }
+  }
+  int64_t kps = (K + sp - 1) / sp;
+  kps = (kps + BK - 1) / BK * BK;
+  if (kps == 0) kps = BK;
+  sp = (int)((K + kps - 1) / kps);
+  if (sp < 1) sp = 1;
+  const int mode = sp > 1 ? GEMM_ATOMIC : (accumulate ? GEMM_ACCUMULATE : GEMM_STORE);
+  if (batch > 1 && c_batch_stride < M * N)
+    return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32: batch stride of C overlaps its batches");
+  if (mode == GEMM_ATOMIC && !accumulate) {
+    const size_t elems = (size_t)((batch - 1) * c_batch_stride + M * N);
+    cudaError_t e = cudaMemsetAsync(C, 0, elems * sizeof(float), st);
+    if (e != cudaSuccess) return set_error(EMMY_ERR_CUDA, "emmy_gemm_f32: %s", cudaGetErrorString(e));
+  }
+  if ((int64_t)batch * sp > 65535)
+    return set_error(EMMY_ERR_UNSUPPORTED, "emmy_gemm_f32: batch x splits beyond the grid limit");
+
+  const bool tma_ok = K % 4 == 0 && N % 4 == 0 && aligned16(A) && aligned16(B) && aligned16(C) &&
+                      (a_batch_stride * 4) % 16 == 0 && (b_batch_stride * 4) % 16 == 0 &&
+                      (c_batch_stride % 4) == 0 && K > 0;
+  if (tma_ok) {
+    CUtensorMap ta, tb;
+    const uint64_t adims[3] = {(uint64_t)K, (uint64_t)M, (uint64_t)batch};
+    const uint64_t astr[2] = {(uint64_t)K * 4, (uint64_t)(batch > 1 ? a_batch_stride : M * K) * 4};
+    const uint32_t abox[3] = {BK, BM, 1};
+    const uint64_t bdims[3] = {(uint64_t)N, (uint64_t)K, (uint64_t)batch};
+    const uint64_t bstr[2] = {(uint64_t)N * 4, (uint64_t)(batch > 1 ? b_batch_stride : K * N) * 4};
+    const uint32_t bbox[3] = {BN, BK, 1};
+    int rc = make_tensor_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, A, adims, astr, abox,
+                             CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    rc = make_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, B, bdims, bstr, bbox,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+      cudaFuncSetAttribute(gemm_f32_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           SMEM_BYTES);
+      attr_set[dev] = true;
+    }
+    dim3 grid((unsigned)mt, (unsigned)nt, (unsigned)(batch * sp));
+    gemm_f32_tma_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(
+        ta, tb, bias, C, (int)M, (int)N, (int)K, c_batch_stride, sp, (int)kps, epilogue, mode,
+        device_status_ptr());
+    return check_launch("emmy_gemm_f32 (tma)");
+  }
+  dim3 grid((unsigned)((M + 63) / 64), (unsigned)((N + 63) / 64), (unsigned)(batch * sp));
+  gemm_f32_plain_kernel<<<grid, 256, 0, st>>>(A, B, bias, C, (int)M, (int)N, (int)K, a_batch_stride,
+                                              b_batch_stride, c_batch_stride, sp, (int)kps,
+                                              epilogue, mode);
+  return check_launch("emmy_gemm_f32 (plain)");
+}

@@ -27,8 +27,9 @@ import math
 import numpy as np
 
 from .nodes import (
-    Accum, Assign, Axis, BinaryExpr, Cond, DataType, Dim, ElementwiseImpl, KernelOp, Let,
-    Literal, Load, NpDType, Smem, StridedLoop, Sync, Tile, TreeHalve, Var, WarpShuffle, Write,
+    Accum, Assign, Axis, BinaryExpr, Cond, CpAsyncCommit, CpAsyncCopy, CpAsyncWait, DataType, Dim,
+    ElementwiseImpl, Init, KernelOp, Let, Literal, Load, Loop, NpDType, Smem, StridedLoop, Sync,
+    Tile, TreeHalve, Var, WarpShuffle, Write,
 )
 
 DT = {
@@ -390,3 +391,111 @@ def make_inputs(meta: dict, seed_offset: int = 0, only=None) -> dict:
                 raise ValueError(f"unknown init {init!r}")
             out[a["name"]] = v.astype(dt)
     return out
+
+
+# ---------------------------------------------------------------------------
+# tiled matmul (w_m_batch / v_m_rect_small shape)
+
+
+def _B(op, left, right):
+    return BinaryExpr(op=op, left=left, right=right)
+
+
+def matmul(M, N, K, batch=1, splits=1, dtype="f32", out_dtype=None, bias=False, relu=False,
+           tm=64, tn=64, rm=4, rn=4, bk=None, entry="k_matmul", a_init=None, b_init=None,
+           bias_init=None):
+    """``C = A @ B`` (+ bias, relu) in the reference's cp.async tiled-matmul shape.
+
+    Tile axes ``(_aS_ks?, a0? (batch), a1_b, a2_b, a1_u, a2_u)``: per split and
+    batch, a (tm x tn) output block computed by (tm/rm) x (tn/rn) threads, each
+    holding an rm x rn accumulator micro-tile (``Init`` seeds); per K step
+    ``bk`` the block stages A[tm, bk] and B[bk, tn] through ``CpAsyncCopy`` of
+    16 bytes into ``_a_smem`` / ``_b_smem``, then an unrolled ``Loop _ki``
+    folds smem products into the accumulators; writes are atomic when K is
+    split (``zero_outputs`` names C), as in ``tests/variants/w_m_batch``.
+    """
+    out_dtype = out_dtype or dtype
+    esz = {"f32": 4, "f16": 2, "f64": 8}[dtype]
+    vec = 16 // esz                                # elements per 16-byte copy
+    bk = bk or (16 if dtype == "f32" else 32)
+    assert M % tm == 0 and N % tn == 0 and tm % rm == 0 and tn % rn == 0
+    assert K % splits == 0 and (K // splits) % bk == 0 and bk % vec == 0 and tn % vec == 0
+    ksplit = K // splits
+    mu, nu = tm // rm, tn // rn
+    threads = mu * nu
+    axes = []
+    if splits > 1:
+        axes.append(ax("_a3_ks", splits))
+    if batch > 1:
+        axes.append(ax("a0", batch))
+    axes += [Axis(name="a1_b", extent=Dim(M // tm), window=None),
+             Axis(name="a2_b", extent=Dim(N // tn), window=None),
+             ax("a1_u", mu), ax("a2_u", nu)]
+    tid = _B("+", _B("*", V("a1_u"), L(nu)), V("a2_u"))
+    kbase = _B("*", V("_a3_ks"), L(ksplit)) if splits > 1 else L(0)
+    bidx = (V("a0"),) if batch > 1 else ()
+    body = []
+    for i in range(rm):
+        for j in range(rn):
+            body.append(Init(name=f"acc0__c{i}_{j}", identity=0.0, dtype=DT["f32"]))
+    body += [Smem(name="_a_smem", extents=(tm, bk), dtype=C_NAME[dtype], align=16),
+             Smem(name="_b_smem", extents=(bk, tn), dtype=C_NAME[dtype], align=16)]
+    a_chunks = tm * bk // vec
+    b_chunks = bk * tn // vec
+    fa = _B("*", V("_fa"), L(vec))
+    fb = _B("*", V("_fb"), L(vec))
+    copy_a = StridedLoop(axis=ax("_fa", a_chunks), start=tid, step=L(threads), body=(
+        CpAsyncCopy(
+            smem="_a_smem", smem_index=(_B("/", fa, L(bk)), _B("%", fa, L(bk))), src="A",
+            src_index=bidx + (_B("+", _B("*", V("a1_b"), L(tm)), _B("/", fa, L(bk))),
+                              _B("+", kbase, _B("+", V("_ks"), _B("%", fa, L(bk))))),
+            nbytes=16, swizzle="NONE", lane_index=None, lane_rows=0),), unroll=False, end=None, seed=True)
+    copy_b = StridedLoop(axis=ax("_fb", b_chunks), start=tid, step=L(threads), body=(
+        CpAsyncCopy(
+            smem="_b_smem", smem_index=(_B("/", fb, L(tn)), _B("%", fb, L(tn))), src="B",
+            src_index=bidx + (_B("+", kbase, _B("+", V("_ks"), _B("/", fb, L(tn)))),
+                              _B("+", _B("*", V("a2_b"), L(tn)), _B("%", fb, L(tn)))),
+            nbytes=16, swizzle="NONE", lane_index=None, lane_rows=0),), unroll=False, end=None, seed=True)
+    inner = []
+    for i in range(rm):
+        row_l = _B("-", _B("+", _B("+", _B("*", V("a1_b"), L(tm)), _B("*", V("a1_u"), L(rm))), L(i)),
+                   _B("*", V("a1_b"), L(tm)))
+        inner.append(Load(names=(f"in0__c{i}_0",), input="_a_smem", index=(row_l, V("_ki")), dtype=None))
+        for j in range(rn):
+            if i == 0:
+                col_l = _B("-", _B("+", _B("+", _B("*", V("a2_b"), L(tn)), _B("*", V("a2_u"), L(rn))), L(j)),
+                           _B("*", V("a2_b"), L(tn)))
+                inner.append(Load(names=(f"in1__c0_{j}",), input="_b_smem", index=(V("_ki"), col_l), dtype=None))
+            inner.append(A(f"acc0__v__c{i}_{j}", "multiply", (f"in1__c0_{j}", f"in0__c{i}_0")))
+            inner.append(Accum(name=f"acc0__c{i}_{j}", value=f"acc0__v__c{i}_{j}", op=E("add"),
+                               dtype=DT["f32"], axes=("_ki",), base=None))
+    body.append(StridedLoop(axis=ax("_ks", ksplit), start=L(0), step=L(bk), body=(
+        copy_a, copy_b, CpAsyncCommit(), CpAsyncWait(group=0), Sync(barrier_id=0, count=None, warp=False),
+        Loop(axis=ax("_ki", bk), body=tuple(inner), unroll=True, seed=False),
+        Sync(barrier_id=0, count=None, warp=False)), unroll=False, end=None, seed=True))
+    for i in range(rm):
+        row = _B("+", _B("+", _B("*", V("a1_b"), L(tm)), _B("*", V("a1_u"), L(rm))), L(i))
+        for j in range(rn):
+            col = _B("+", _B("+", _B("*", V("a2_b"), L(tn)), _B("*", V("a2_u"), L(rn))), L(j))
+            val = f"acc0__c{i}_{j}"
+            if bias:
+                body.append(Load(names=(f"bias__c{i}_{j}",), input="bias", index=(col,), dtype=DT["f32"]))
+                body.append(A(f"v0__c{i}_{j}", "add", (val, f"bias__c{i}_{j}")))
+                val = f"v0__c{i}_{j}"
+            if relu:
+                body.append(Let(name=f"zero__c{i}_{j}", value=L(0.0), dtype=DT["f32"]))
+                body.append(A(f"v1__c{i}_{j}", "maximum", (val, f"zero__c{i}_{j}")))
+                val = f"v1__c{i}_{j}"
+            body.append(Write(output="C", index=bidx + (row, col), values=(val,), value_dtype=DT[out_dtype],
+                              atomic=splits > 1, swizzle="NONE"))
+    tile = Tile(axes=tuple(axes), body=tuple(body), block_threads=threads, aux_threads=0,
+                raster_axes=("a1_b", "a2_b"), raster_group=None, raster_orient="m")
+    kop = KernelOp(name=entry, body=(tile,))
+    lead = [batch] if batch > 1 else []
+    args = [_arg("B", dtype, lead + [K, N], seed=1, **({"init": b_init} if b_init else {})),
+            _arg("A", dtype, lead + [M, K], seed=0, **({"init": a_init} if a_init else {}))]
+    if bias:
+        args.append(_arg("bias", "f32", [N], seed=2, **({"init": bias_init} if bias_init else {})))
+    args.append(_arg("C", out_dtype, lead + [M, N], output=True))
+    nblocks = splits * batch * (M // tm) * (N // tn)
+    return kop, _meta(entry, args, nblocks, threads, zero=["C"] if splits > 1 else [])

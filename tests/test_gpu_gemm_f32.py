@@ -1,0 +1,97 @@
+"""GPU parity of the f32 CUDA-core GEMM family (plain, batched, split-K, epilogue).
+
+IR cases are the reference fixture shapes (``v_m_*``, ``w_m_*``), the K4a
+benchmark (split-K 256x65536x256 in 64 partitions, U(-1,1) inputs) and an
+epilogue case, compiled to plans and run through the C-ABI; direct C-ABI
+cases cover shapes the TMA path cannot take (K or N not a multiple of 4).
+
+Tolerance per output element: ``|got - ref| <= 1e-5 * (|A| @ |B|)`` (the
+dot product's own scale, f64 reference), plus ``|bias|`` when a bias is added.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from emmy_ir import synth
+from gpu_util import run_on_gpu, shaped
+from oracle import formulas as F
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-5
+
+IR_CASES = [
+    ("v_m_256", dict(M=256, N=256, K=256)),
+    ("v_m_rect_small_splitk16", dict(M=64, N=32, K=128, splits=16, tm=32, tn=32, rm=2, rn=2, bk=8)),
+    ("v_m_tall_split2", dict(M=512, N=64, K=128, splits=2)),
+    ("v_m_wide_split16", dict(M=128, N=512, K=64, splits=16, bk=4)),
+    ("w_m_1024_split4", dict(M=1024, N=128, K=128, splits=4)),
+    ("w_m_k96_split4", dict(M=128, N=64, K=96, splits=4, bk=8)),
+    ("w_m_batch_split16", dict(M=64, N=64, K=64, batch=4, splits=16, bk=4)),
+    ("K4a_splitk64", dict(M=256, N=256, K=65536, splits=64, tm=128, tn=128, rm=8, rn=8,
+                          a_init={"dist": "uniform", "low": -1.0, "high": 1.0},
+                          b_init={"dist": "uniform", "low": -1.0, "high": 1.0})),
+    ("bias_relu_192x320x200", dict(M=192, N=320, K=200, bias=True, relu=True, tm=64, tn=64, bk=8)),
+    ("batch3_bias", dict(M=128, N=64, K=48, batch=3, bias=True, bk=16)),
+]
+
+
+@pytest.mark.parametrize("name,kw", IR_CASES, ids=[c[0] for c in IR_CASES])
+def test_gemm_f32_ir(name, kw):
+    kop, meta = synth.matmul(**kw)
+    plan, host, out = run_on_gpu(kop, meta)
+    assert plan["family"] == "gemm_f32"
+    x = shaped(meta, host)
+    ref = F.matmul(x["A"], x["B"], x.get("bias"), kw.get("relu", False), out_dtype=np.float64)
+    scale = F.matmul_abs_bound(x["A"], x["B"], x.get("bias"))
+    got = out["C"].reshape(ref.shape).astype(np.float64)
+    assert np.all(np.abs(got - ref) <= RTOL * scale + 1e-30), name
+
+
+@pytest.mark.parametrize("M,N,K,batch", [(33, 30, 17, 1), (5, 7, 9, 2), (130, 4, 1024, 1),
+                                         (1, 1, 1, 1), (129, 257, 64, 1)])
+def test_gemm_f32_cabi_odd_shapes(M, N, K, batch):
+    import torch
+    from ptxc.launch import load_library
+    lib = load_library()
+    g = torch.Generator(device="cuda").manual_seed(M * 1000 + N)
+    A = torch.randn(batch, M, K, device="cuda", generator=g)
+    B = torch.randn(batch, K, N, device="cuda", generator=g)
+    C = torch.full((batch, M, N), float("nan"), device="cuda")
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    rc = lib.emmy_gemm_f32(P(A), P(B), None, P(C), batch, M, N, K, M * K, K * N, M * N, 0, 0, 0, None)
+    assert rc == 0, lib.emmy_last_error()
+    torch.cuda.synchronize()
+    ref = torch.bmm(A.double(), B.double())
+    scale = torch.bmm(A.abs().double(), B.abs().double())
+    assert torch.all((C.double() - ref).abs() <= RTOL * scale + 1e-30)
+
+
+def test_gemm_f32_accumulate_adds_into_c():
+    import torch
+    from ptxc.launch import load_library
+    lib = load_library()
+    A = torch.randn(96, 64, device="cuda")
+    B = torch.randn(64, 80, device="cuda")
+    C0 = torch.randn(96, 80, device="cuda")
+    C = C0.clone()
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    for splits in (1, 4):
+        C.copy_(C0)
+        assert lib.emmy_gemm_f32(P(A), P(B), None, P(C), 1, 96, 80, 64, 0, 0, 0, splits, 1, 0, None) == 0
+        torch.cuda.synchronize()
+        ref = C0.double() + A.double() @ B.double()
+        scale = C0.double().abs() + A.abs().double() @ B.abs().double()
+        assert torch.all((C.double() - ref).abs() <= RTOL * scale)
+
+
+def test_gemm_f32_rejects_relu_on_partial_sums():
+    from ptxc.launch import load_library
+    lib = load_library()
+    rc = lib.emmy_gemm_f32(ctypes.c_void_p(16), ctypes.c_void_p(16), None, ctypes.c_void_p(16),
+                           1, 8, 8, 8, 0, 0, 0, 4, 0, 2, None)
+    assert rc == 1
