@@ -60,6 +60,16 @@ def hbm_peak():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def tensor_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except (ValueError, KeyError):
+            pass
+    return 1590.0, "fallback"
+
+
 def profile_traffic(name):
     """dram bytes per launch recorded from an ncu capture in profiles/<name>."""
     p = ROOT / "profiles" / name
@@ -275,6 +285,12 @@ def family_extras(device, peak):
         "K4b_matvec_f64_16384": synth.matvec(16384, 16384),
         "K4a_splitk_f32_256x65536x256": synth.matmul(256, 256, 65536, splits=64, tm=128, tn=128,
                                                      rm=8, rn=8),
+        "K3a_gemm_f16_4096x2048x8192_bias_relu": synth.matmul(
+            4096, 8192, 2048, dtype="f16", out_dtype="f16", bias=True, relu=True, tm=128, tn=128,
+            rm=8, rn=8),
+        "K3b_bmm_f16_64x512": synth.matmul(512, 512, 512, batch=64, dtype="f16", out_dtype="f16",
+                                           tm=128, tn=128, rm=8, rn=8),
+        "K5_attention_f16_8x32x512x128": synth.attention(8, 32, 512, 128, dtype="f16"),
     }
     for name, (kop, meta) in cases.items():
         plan = Lowerer(kop, meta).plan()
@@ -301,13 +317,19 @@ def family_extras(device, peak):
         gbs = plan_bytes(plan) / (ms * 1e-3) / 1e9
         out[name] = {"us": round(ms * 1000, 2), "gbs": round(gbs, 1), "frac_hbm": round(gbs / peak, 3),
                      "bytes": plan_bytes(plan)}
-        if "gemm" in plan:
-            g = plan["gemm"]
-            flops = 2.0 * g["batch"] * g["m"] * g["n"] * g["k"]
+        if "gemm" in plan or "attention" in plan:
+            if "gemm" in plan:
+                g = plan["gemm"]
+                flops = 2.0 * g["batch"] * g["m"] * g["n"] * g["k"]
+            else:
+                a = plan["attention"]
+                flops = 2.0 * a["batch"] * a["sq"] * a["sk"] * (a["d"] + a["dv"])
             tf = flops / (ms * 1e-3) / 1e12
             out[name]["tflops"] = round(tf, 2)
             if plan["family"] == "gemm_f32":
                 out[name]["frac_fp32_nominal"] = round(tf / FP32_NOMINAL_TFLOPS, 3)
+            else:
+                out[name]["frac_tensor"] = round(tf / tensor_peak()[0], 3)
         del ex
     del flush
     torch.cuda.empty_cache()
@@ -487,6 +509,12 @@ PROFILE_CASES = {
     "layernorm_16384x1024": lambda s: s.layernorm(16384, 1024),
     "rmsnorm_65536x512": lambda s: s.rmsnorm(65536, 512, eps=1e-6),
     "matvec_f64_8192x4096": lambda s: s.matvec(8192, 4096),
+    "gemm_f16_K3a": lambda s: s.matmul(4096, 8192, 2048, dtype="f16", out_dtype="f16", bias=True,
+                                       relu=True, tm=128, tn=128, rm=8, rn=8),
+    "gemm_f16_2048": lambda s: s.matmul(2048, 2048, 2048, dtype="f16", out_dtype="f16",
+                                        tm=128, tn=128, rm=8, rn=8),
+    "attention_f16_K5": lambda s: s.attention(8, 32, 512, 128, dtype="f16"),
+    "gemm_f32_splitk_K4a": lambda s: s.matmul(256, 256, 65536, splits=64, tm=128, tn=128, rm=8, rn=8),
 }
 
 

@@ -1,0 +1,338 @@
+// f16 GEMM / batched GEMM with f32 accumulation on the sm_100a tensor cores
+// (tcgen05.mma, accumulator in tensor memory), with a fused bias + ReLU
+// epilogue and f16 or f32 output.
+//
+// Replaces the entry the reference would emit for its tiled-matmul IR shape
+// with f16 operands: the same cp.async staging and register micro-tile walk as
+// the f32 fixtures, each f16 load widened to f32 for an fma.rn chain
+// (reference ptxc/expr.py:168-180, ptxc/stmts.py:614-632, 663-725), followed by
+// the epilogue Assigns and the converting Write (ptxc/stmts.py:434-487).
+//
+// Here: a persistent kernel, one CTA per SM, walking 128 x 256 output tiles.
+//   warp 0      TMA producer: A [128 x 64] K-major and B [64 x 256] N-major
+//               (row-major B as stored) into a 4-stage ring of 128-byte
+//               swizzled shared memory (no multicast)
+//   warp 1      one thread issues tcgen05.mma (M128 N256 K16), four per stage,
+//               into one of two 256-column f32 TMEM accumulators, and commits
+//               each stage back to the producer and each finished tile to the
+//               epilogue
+//   warps 2-5   epilogue: each warp drains its 32 TMEM lanes (one output row
+//               per thread), adds the bias, applies ReLU, converts and stores,
+//               then hands the accumulator back -- while the MMA warp already
+//               fills the other accumulator with the next tile.
+// Tiles are visited M-fastest within groups of 16 N-tiles, so concurrently
+// running CTAs share B column panels in L2.  All mbarrier waits are bounded.
+
+#include "common.cuh"
+#include "tcgen05.cuh"
+
+namespace emmy {
+
+namespace gemm16 {
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, THREADS = 192;
+constexpr int A_BYTES = BM * BK * 2;                 // 16 KB
+constexpr int B_BOX_BYTES = BK * 64 * 2;             // 8 KB: 64 k-rows x 64 n (128 B)
+constexpr int B_BYTES = BK * BN * 2;                 // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+constexpr uint32_t TMEM_COLS = 512;                  // two 256-column accumulators
+constexpr int GROUP_N = 16;                          // raster group width in N tiles
+constexpr int kStatusGemmTimeout = 0x1101;
+}  // namespace gemm16
+
+struct TileCoord {
+  int m0, n0, b;
+};
+
+// Tile t of (batch, mt, nt) tiles: batches outermost, then groups of GROUP_N
+// N-tiles; inside a group M varies fastest.
+__device__ __forceinline__ TileCoord gemm16_tile(int t, int mt, int nt) {
+  using namespace gemm16;
+  const int per_batch = mt * nt;
+  const int b = t / per_batch;
+  int r = t - b * per_batch;
+  const int group = r / (mt * GROUP_N);
+  const int first_n = group * GROUP_N;
+  r -= group * mt * GROUP_N;
+  const int m = r % mt;
+  const int n = first_n + r / mt;
+  return {m * BM, n * BN, b};
+}
+
+__global__ void __launch_bounds__(gemm16::THREADS, 1)
+gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const float *__restrict__ bias, void *__restrict__ C, int M, int N, int K,
+                   int batch, int64_t c_batch_stride, int out_f16, int epilogue, int *status) {
+  using namespace gemm16;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[STAGES];
+  __shared__ __align__(8) uint64_t empty[STAGES];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ uint32_t tmem_holder;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
+  const int tiles = mt * nt * batch;
+  const int ktiles = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);      // one arrival per epilogue warp
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_holder, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // TMA producer: one continuous stage sequence across all of this CTA's tiles
+      int g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+        const TileCoord tc = gemm16_tile(t, mt, nt);
+        for (int kt = 0; kt < ktiles; ++kt, ++g) {
+          const int s = g % STAGES;
+          if (g >= STAGES &&
+              !mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, status, kStatusGemmTimeout)) {
+            ok = false;
+            break;
+          }
+          unsigned char *sa = smem + s * STAGE_BYTES;
+          unsigned char *sb = sa + A_BYTES;
+          mbar_expect_tx(&full[s], STAGE_BYTES);
+          tma_load_3d(sa, &tmA, &full[s], kt * BK, tc.m0, tc.b);
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j)
+            tma_load_3d(sb + j * B_BOX_BYTES, &tmB, &full[s], tc.n0 + 64 * j, kt * BK, tc.b);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // MMA issuer
+      constexpr uint32_t idesc = f16_idesc(BM, BN, false, true);
+      int g = 0, i = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++i) {
+        const int a = i & 1;
+        if (i >= 2 && !mbar_wait(&acc_empty[a], ((i >> 1) - 1) & 1, status, kStatusGemmTimeout))
+          break;
+        tc_fence_after();
+        const uint32_t acc = tmem + a * BN;
+        for (int kt = 0; kt < ktiles; ++kt, ++g) {
+          const int s = g % STAGES;
+          if (!mbar_wait(&full[s], (g / STAGES) & 1, status, kStatusGemmTimeout)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // A: K-major, 128-byte rows, 8-row atoms 1024 B apart; a K16 step is 32 B
+            const uint64_t da = sw128_desc(sa + kk * 32, 16, 1024);
+            // B: N-major, 64-wide n atoms 8 KB apart, 8-row k atoms 1024 B apart; K16 = 2048 B
+            const uint64_t db = sw128_desc(sb + kk * 2048, B_BOX_BYTES, 1024);
+            mma_f16(acc, da, db, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[s]);
+        }
+        mma_commit(&acc_full[a]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // epilogue warps 2..5: warp w reads TMEM lanes [32*(w%4), +32)
+    const int q = warp & 3;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const bool relu = epilogue & EMMY_EPI_RELU;
+    const bool add_bias = (epilogue & EMMY_EPI_BIAS) && bias != nullptr;
+    int i = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      const int a = i & 1;
+      const TileCoord tc = gemm16_tile(t, mt, nt);
+      if (!mbar_wait(&acc_full[a], (i >> 1) & 1, status, kStatusGemmTimeout)) break;
+      __syncwarp();
+      tc_fence_after();
+      const int row = tc.m0 + q * 32 + lane;
+      const uint32_t base = tmem + lane_off + a * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        __syncwarp();   // tcgen05.ld is warp-collective: reconverge after the masked stores
+        tmem_ld32(base + c * 32, v);
+        const int n = tc.n0 + c * 32;
+        if (row >= M || n >= N) continue;
+        if (ktiles == 0) {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) v[k] = 0.f;
+        }
+        if (add_bias) {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) v[k] += (n + k < N) ? __ldg(bias + n + k) : 0.f;
+        }
+        if (relu) {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) v[k] = fmaxf(v[k], 0.f);
+        }
+        const int64_t off = (int64_t)tc.b * c_batch_stride + (int64_t)row * N + n;
+        if (out_f16) {
+          __half *dst = reinterpret_cast<__half *>(C) + off;
+          if (n + 32 <= N) {
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+              uint32_t w[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                __half2 hh = __floats2half2_rn(v[8 * p + 2 * k], v[8 * p + 2 * k + 1]);
+                w[k] = *reinterpret_cast<uint32_t *>(&hh);
+              }
+              *reinterpret_cast<uint4 *>(dst + 8 * p) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          } else {
+            for (int k = 0; k < 32 && n + k < N; ++k) dst[k] = __float2half_rn(v[k]);
+          }
+        } else {
+          float *dst = reinterpret_cast<float *>(C) + off;
+          if (n + 32 <= N) {
+#pragma unroll
+            for (int p = 0; p < 8; ++p)
+              *reinterpret_cast<float4 *>(dst + 4 * p) =
+                  make_float4(v[4 * p], v[4 * p + 1], v[4 * p + 2], v[4 * p + 3]);
+          } else {
+            for (int k = 0; k < 32 && n + k < N; ++k) dst[k] = v[k];
+          }
+        }
+      }
+      // the accumulator's TMEM reads are complete (tcgen05.wait::ld in tmem_ld32)
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// CUDA-core fallback for shapes the TMA descriptors cannot take (K or N not a
+// multiple of 8, unaligned bases): f16 loads widened to f32, fma accumulate.
+__global__ void __launch_bounds__(256)
+gemm_f16_plain_kernel(const __half *__restrict__ A, const __half *__restrict__ B,
+                      const float *__restrict__ bias, void *__restrict__ C, int M, int N, int K,
+                      int64_t sa, int64_t sb, int64_t sc, int out_f16, int epilogue) {
+  __shared__ float As[16][64 + 1];
+  __shared__ float Bs[16][64 + 1];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int m0 = blockIdx.x * 64, n0 = blockIdx.y * 64, b = blockIdx.z;
+  const __half *Ab = A + (int64_t)b * sa;
+  const __half *Bb = B + (int64_t)b * sb;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int i = tid; i < 16 * 64; i += 256) {
+      const int r = i / 16, c = i % 16;
+      As[c][r] = (m0 + r < M && k0 + c < K) ? __half2float(Ab[(int64_t)(m0 + r) * K + k0 + c]) : 0.f;
+      const int kr = i / 64, nc = i % 64;
+      Bs[kr][nc] = (k0 + kr < K && n0 + nc < N) ? __half2float(Bb[(int64_t)(k0 + kr) * N + n0 + nc]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(As[k][ty + 16 * i], Bs[k][tx + 16 * j], acc[i][j]);
+    __syncthreads();
+  }
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty + 16 * i;
+    if (m >= M) continue;
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tx + 16 * j;
+      if (n >= N) continue;
+      float v = acc[i][j];
+      if ((epilogue & EMMY_EPI_BIAS) && bias) v += bias[n];
+      if (epilogue & EMMY_EPI_RELU) v = fmaxf(v, 0.f);
+      const int64_t off = (int64_t)b * sc + (int64_t)m * N + n;
+      if (out_f16) reinterpret_cast<__half *>(C)[off] = __float2half_rn(v);
+      else reinterpret_cast<float *>(C)[off] = v;
+    }
+  }
+}
+
+}  // namespace emmy
+
+using namespace emmy;
+
+extern "C" int emmy_gemm_f16(const void *A, const void *B, const float *bias, void *C,
+                             int64_t batch, int64_t M, int64_t N, int64_t K, int out_dtype,
+                             int epilogue, int accumulate, void *stream) {
+  using namespace gemm16;
+  clear_error();
+  if (batch < 0 || M < 0 || N < 0 || K < 0)
+    return set_error(EMMY_ERR_INVALID, "emmy_gemm_f16: negative size");
+  if (batch == 0 || M == 0 || N == 0) return EMMY_OK;
+  if (!A || !B || !C) return set_error(EMMY_ERR_INVALID, "emmy_gemm_f16: null operand");
+  if (out_dtype != EMMY_DT_F32 && out_dtype != EMMY_DT_F16)
+    return set_error(EMMY_ERR_INVALID, "emmy_gemm_f16: bad output dtype %d", out_dtype);
+  if (accumulate)
+    return set_error(EMMY_ERR_UNSUPPORTED, "emmy_gemm_f16: accumulating into C is not supported");
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || batch > 65535)
+    return set_error(EMMY_ERR_UNSUPPORTED, "emmy_gemm_f16: size beyond 32-bit tile indexing");
+  cudaStream_t st = as_stream(stream);
+  const int out_f16 = out_dtype == EMMY_DT_F16;
+  const bool tma_ok = K % 8 == 0 && N % 8 == 0 && K > 0 && aligned16(A) && aligned16(B) &&
+                      aligned16(C);
+  if (tma_ok) {
+    const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
+    if (tiles > INT32_MAX) return set_error(EMMY_ERR_UNSUPPORTED, "emmy_gemm_f16: too many tiles");
+    CUtensorMap ta, tb;
+    const uint64_t adims[3] = {(uint64_t)K, (uint64_t)M, (uint64_t)batch};
+    const uint64_t astr[2] = {(uint64_t)K * 2, (uint64_t)M * K * 2};
+    const uint32_t abox[3] = {BK, BM, 1};
+    const uint64_t bdims[3] = {(uint64_t)N, (uint64_t)K, (uint64_t)batch};
+    const uint64_t bstr[2] = {(uint64_t)N * 2, (uint64_t)K * N * 2};
+    const uint32_t bbox[3] = {64, BK, 1};
+    int rc = make_tensor_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, A, adims, astr, abox,
+                             CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = make_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, B, bdims, bstr, bbox,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+      cudaFuncSetAttribute(gemm_f16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           SMEM_BYTES);
+      attr_set[dev] = true;
+    }
+    const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
+    gemm_f16_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, bias, C, (int)M, (int)N, (int)K,
+                                                          (int)batch, M * N, out_f16, epilogue,
+                                                          device_status_ptr());
+    return check_launch("emmy_gemm_f16 (tcgen05)");
+  }
+  dim3 grid((unsigned)((M + 63) / 64), (unsigned)((N + 63) / 64), (unsigned)batch);
+  gemm_f16_plain_kernel<<<grid, 256, 0, st>>>(static_cast<const __half *>(A),
+                                              static_cast<const __half *>(B), bias, C, (int)M,
+                                              (int)N, (int)K, M * K, K * N, M * N, out_f16,
+                                              epilogue);
+  return check_launch("emmy_gemm_f16 (plain)");
+}

@@ -2,10 +2,10 @@
 // inline PTX.  No multicast anywhere: every CTA loads its own tiles, so the
 // same kernels are safe in multi-GPU jobs.
 //
-// Every wait on an mbarrier is bounded: after kSpinLimit polls the waiting
-// thread records an error code in the library's device status word and gives
-// up, so a lost transaction turns into EMMY_ERR_DEVICE on the host instead of
-// a hung GPU.
+// Every wait on an mbarrier is bounded in wall-clock time: after kWaitLimitNs
+// the waiting thread records an error code in the library's device status word
+// and gives up, so a lost transaction turns into an error the host can read
+// instead of a hung GPU.
 #pragma once
 
 #include <cuda.h>
@@ -17,8 +17,20 @@
 
 namespace emmy {
 
-constexpr uint32_t kSpinLimit = 1u << 26;   // ~67M polls: seconds, far above any real wait
+// Wall-clock bound of one mbarrier wait, read from %globaltimer (nanoseconds).
+// mbarrier.try_wait may itself suspend for an implementation-defined time, so
+// the bound is on elapsed time, not on the number of polls.
+#ifndef EMMY_WAIT_LIMIT_NS
+#define EMMY_WAIT_LIMIT_NS 2000000000ull
+#endif
+constexpr unsigned long long kWaitLimitNs = EMMY_WAIT_LIMIT_NS;
 constexpr int kStatusMbarTimeout = 0x1001;
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -59,12 +71,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: returns false (and records `code` in *status) when the limit is hit.
+// Bounded wait: returns false (and records `code` in *status) once kWaitLimitNs
+// of wall-clock time has passed without the phase completing.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status, int code) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  if (status) atomicExch(status, code);
-  return false;
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - t0 > kWaitLimitNs) {
+      if (status) atomicCAS(status, 0, code);   // the first wait to give up names itself
+      return false;
+    }
+  }
+  return true;
 }
 
 // 2-D / 3-D tiled TMA loads into shared memory, completing on `bar`.

@@ -499,3 +499,79 @@ def matmul(M, N, K, batch=1, splits=1, dtype="f32", out_dtype=None, bias=False, 
     args.append(_arg("C", out_dtype, lead + [M, N], output=True))
     nblocks = splits * batch * (M // tm) * (N // tn)
     return kop, _meta(entry, args, nblocks, threads, zero=["C"] if splits > 1 else [])
+
+
+# ---------------------------------------------------------------------------
+# attention-like chain (w_a_head64 shape, with batch and head Tile axes)
+
+
+def attention(B, H, S, D, dtype="f16", out_dtype=None, scale_div=None, entry="k_attention",
+              q_init=None, k_init=None, v_init=None, k_transposed=False, Dv=None):
+    """``softmax(q @ k^T * recip(div)) @ v`` per (batch, head), in the shape of
+    ``tests/variants/w_a_head64``: one thread per output element (query row,
+    value column) walks the keys in a ``Loop``, each key's score is an inner
+    ``Loop`` dot product over the head dim, followed by the online max/sum
+    update and the rescaled accumulation of ``v``; the write divides by the
+    sum.  ``q, k, v, out`` are ``[B, H, S, D]`` (k not pre-transposed).
+    """
+    out_dtype = out_dtype or dtype
+    Dv = Dv or D
+    div = float(scale_div if scale_div is not None else math.sqrt(D))
+    rows_u, cols_u = 1, min(Dv, 64)
+    threads = rows_u * cols_u
+    axes = [ax("a6", B), ax("a7", H),
+            Axis(name="a0_b", extent=Dim(S // rows_u), window=None),
+            Axis(name="a5_b", extent=Dim(Dv // cols_u), window=None),
+            ax("a0_u", rows_u), ax("a5_u", cols_u)]
+    row = _B("+", _B("+", _B("*", V("a0_b"), L(rows_u)), _B("*", V("a0_u"), L(1))), L(0))
+    col = _B("+", _B("+", _B("*", V("a5_b"), L(cols_u)), _B("*", V("a5_u"), L(1))), L(0))
+    bh = (V("a6"), V("a7"))
+    f = "f32"
+    dot = Loop(axis=ax("a2", D), body=(
+        Load(names=("in2__ar0",), input="q", index=bh + (row, V("a2")), dtype=DT[dtype]),
+        Load(names=("in1__ar0",), input="k",
+             index=bh + ((V("a2"), V("a1")) if k_transposed else (V("a1"), V("a2"))), dtype=DT[dtype]),
+        A("v3__ar0", "multiply", ("in1__ar0", "in2__ar0")),
+        Accum(name="acc0__ar0", value="v3__ar0", op=E("add"), dtype=DT[f], axes=("a2",), base=None),
+    ), unroll=False, seed=True)
+    x = "v4__c0_0"
+    keys = Loop(axis=ax("a1", S), body=(
+        dot,
+        A(x, "multiply", ("acc0__ar0", "v1")),
+        Let(name="one__c0_0", value=L(1.0), dtype=DT[f]),
+        A(x + "__gn", "maximum", ("acc1__c0_0", x)),
+        A(x + "__dg", "subtract", ("acc1__c0_0", x + "__gn")),
+        A(x + "__alpha", "exp", (x + "__dg",)),
+        A(x + "__dg_o", "subtract", (x, x + "__gn")),
+        A(x + "__beta", "exp", (x + "__dg_o",)),
+        A(x + "__acc3_sa", "multiply", ("acc3__c0_0", x + "__alpha")),
+        A(x + "__acc3_sb", "multiply", ("one__c0_0", x + "__beta")),
+        Accum(name="acc3__c0_0", value=x + "__acc3_sb", op=E("add"), dtype=DT[f], axes=("a1",),
+              base=x + "__acc3_sa"),
+        A(x + "__acc5__sum_sa", "multiply", ("acc5__sum__c0_0", x + "__alpha")),
+        Load(names=("in7__bc0",), input="v", index=bh + (V("a1"), col), dtype=DT[dtype]),
+        A(x + "__acc5__sum_sb", "multiply", ("in7__bc0", x + "__beta")),
+        Accum(name="acc5__sum__c0_0", value=x + "__acc5__sum_sb", op=E("add"), dtype=DT[f],
+              axes=("a1",), base=x + "__acc5__sum_sa"),
+        Accum(name="acc1__c0_0", value=x, op=E("maximum"), dtype=DT[f], axes=("a1",), base=None),
+    ), unroll=False, seed=True)
+    body = [
+        Load(names=("in0",), input="div_c1", index=(L(0),), dtype=DT[f]),
+        A("v1", "reciprocal", ("in0",)),
+        keys,
+        A("v9__c0_0", "reciprocal", ("acc3__c0_0",)),
+        A("acc5__c0_0", "multiply", ("acc5__sum__c0_0", "v9__c0_0")),
+        Write(output="o", index=bh + (row, col), values=("acc5__c0_0",), value_dtype=DT[out_dtype],
+              atomic=False, swizzle="NONE"),
+    ]
+    tile = Tile(axes=tuple(axes), body=tuple(body), block_threads=threads, aux_threads=0,
+                raster_axes=("a0_b", "a5_b"), raster_group=None, raster_orient="m")
+    kop = KernelOp(name=entry, body=(tile,))
+    shp = [B, H, S, D]
+    args = [_arg("div_c1", "f32", [1], data=[div]),
+            _arg("q", dtype, shp, seed=0, **({"init": q_init} if q_init else {})),
+            _arg("k", dtype, [B, H, D, S] if k_transposed else shp, seed=1,
+                 **({"init": k_init} if k_init else {})),
+            _arg("v", dtype, [B, H, S, Dv], seed=2, **({"init": v_init} if v_init else {})),
+            _arg("o", out_dtype, [B, H, S, Dv], output=True)]
+    return kop, _meta(entry, args, B * H * S * Dv // threads, threads)

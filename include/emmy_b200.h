@@ -127,6 +127,59 @@ int emmy_softmax_f32(const float *x, float *y, int64_t outer, int64_t n, int64_t
 int emmy_matvec_f64(const double *A, const double *v, double *y, int64_t rows, int64_t cols,
                     void *stream);
 
+/*
+ * f32 GEMM on CUDA cores: C[b] (+)= A[b] @ B[b] (+ bias[n]) (ReLU), A [M,K],
+ * B [K,N], C [M,N] row-major, batch strides in elements.  `splits` K
+ * partitions (0 = choose) are combined with atomic adds, the reference's
+ * atomic Write of a split-K Tile axis; `accumulate` adds into C instead of
+ * overwriting it.  Replaces the entry the reference emits for the tiled
+ * matmul shape (reference ptxc/stmts.py:663-725, 614-632, 1590-1623,
+ * 434-487; fixtures v_m_*, w_m_*).
+ */
+int emmy_gemm_f32(const float *A, const float *B, const float *bias, float *C, int64_t batch,
+                  int64_t M, int64_t N, int64_t K, int64_t a_batch_stride,
+                  int64_t b_batch_stride, int64_t c_batch_stride, int splits, int accumulate,
+                  int epilogue, void *stream);
+
+/*
+ * f16 GEMM with f32 accumulation on the tcgen05 tensor cores:
+ * C[b] = A[b] @ B[b] (+ bias[n]) (ReLU), A [M,K] f16, B [K,N] f16 row-major,
+ * C [M,N] f32 or f16 (out_dtype), bias f32 (nullable), dense batches.
+ * Replaces the entry the reference emits for the tiled matmul shape with f16
+ * operands (f16 loads widened to f32, reference ptxc/expr.py:168-180, then
+ * ptxc/stmts.py:614-632 and the converting Write, ptxc/stmts.py:434-487).
+ * `accumulate` must be 0.
+ */
+int emmy_gemm_f16(const void *A, const void *B, const float *bias, void *C, int64_t batch,
+                  int64_t M, int64_t N, int64_t K, int out_dtype, int epilogue, int accumulate,
+                  void *stream);
+
+/*
+ * Attention-like chain, f32 on CUDA cores, per batch-head b:
+ *   o[b] = softmax(q[b] @ k[b]^T * recip(*scale_div)) @ v[b]
+ * q [B, Sq, D], k [B, Sk, D] (or, with k_transposed, kt [B, D, Sk]),
+ * v [B, Sk, Dv], o [B, Sq, Dv]; scale_div (nullable: 1) is the one-element
+ * divisor constant.  Replaces the entry the reference emits for the
+ * matmul -> softmax -> reduce fixtures v_a_*, w_a_* (reference
+ * ptxc/stmts.py:663-725, 564-611, 1311-1392).
+ */
+int emmy_attention_f32(const float *q, const float *k, const float *v, float *o,
+                       const float *scale_div, int64_t batch, int64_t sq, int64_t sk, int64_t d,
+                       int64_t dv, int k_transposed, void *stream);
+
+/*
+ * Attention-like chain, f16 in, f32 softmax and accumulation, per batch-head b:
+ *   o[b] = softmax(q[b] @ k[b]^T * recip(*scale_div)) @ v[b]
+ * q, k, v, o [B, S, D] (sq == sk and D in {64, 128, 256} run on the tcgen05
+ * tensor cores: S = Q K^T and O += P V accumulate in tensor memory; other
+ * shapes, or k pre-transposed [B, D, Sk], run on CUDA cores), o f16 or f32.
+ * Replaces the entry the reference emits for the attention IR shape
+ * (reference ptxc/stmts.py:663-725, 564-611, 1311-1392) with f16 operands.
+ */
+int emmy_attention_f16(const void *q, const void *k, const void *v, void *o,
+                       const float *scale_div, int64_t batch, int64_t sq, int64_t sk, int64_t d,
+                       int out_dtype, int k_transposed, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

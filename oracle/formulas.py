@@ -107,6 +107,6 @@ def attention(q, kt, v, scale_div, out_dtype=np.float32):
 
 def attention_bhsd(q, k, v, scale, out_dtype=np.float32):
     """Batched form: ``q, k, v [B,H,S,D]``; scores ``q @ k^T * scale``."""
-    s = np.einsum("bhsd,bhtd->bhst", _f64(q), _f64(k)) * float(scale)
+    s = np.matmul(_f64(q), np.swapaxes(_f64(k), -1, -2)) * float(scale)
     p = softmax(s, axis=-1, out_dtype=np.float64)
-    return np.einsum("bhst,bhtd->bhsd", p, _f64(v)).astype(out_dtype)
+    return np.matmul(p, _f64(v)).astype(out_dtype)

@@ -1,0 +1,79 @@
+"""GPU parity of the attention family.
+
+IR cases are synthesised in the ``w_a_head64`` statement shape: the f32
+fixture shapes (q [S,D], kt [D,S] pre-transposed, v [S,Dv]) on CUDA cores,
+and the f16 benchmark shapes (q, k, v [B,H,S,D]) on the tcgen05 kernel.
+
+Tolerance per output element, against the float64 oracle
+``oracle.formulas.attention_bhsd``: f32 ``|d| <= 1e-5 * max|v|`` (outputs are
+convex combinations of rows of v); f16 (f32 softmax and accumulation)
+``|d| <= 1e-3 * max|v| + u * |ref|`` with ``u = 2^-11`` for f16 output.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from emmy_ir import synth
+from gpu_util import run_on_gpu, shaped
+from oracle import formulas as F
+from oracle.interp import run_ir
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(meta, host, kt):
+    x = shaped(meta, host)
+    k = np.swapaxes(x["k"], -1, -2) if kt else x["k"]
+    div = [a["data"][0] for a in meta["args"] if a["name"] == "div_c1"][0]
+    return x, F.attention_bhsd(x["q"], k, x["v"], 1.0 / div, out_dtype=np.float64)
+
+
+F32_CASES = [
+    ("v_a_128", dict(B=1, H=1, S=128, D=128, k_transposed=True, scale_div=11.313708)),
+    ("v_a_32x256", dict(B=1, H=1, S=32, D=256, Dv=32, k_transposed=True, scale_div=16.0)),
+    ("v_a_64x128", dict(B=1, H=1, S=64, D=128, Dv=64, k_transposed=True, scale_div=8.0)),
+    ("w_a_256", dict(B=1, H=1, S=256, D=64, k_transposed=True, scale_div=8.0)),
+    ("w_a_head64", dict(B=1, H=1, S=128, D=64, k_transposed=True, scale_div=8.0)),
+    ("bhsd_2x3x100x48", dict(B=2, H=3, S=100, D=48, Dv=16)),
+]
+
+
+@pytest.mark.parametrize("name,kw", F32_CASES, ids=[c[0] for c in F32_CASES])
+def test_attention_f32(name, kw):
+    kop, meta = synth.attention(dtype="f32", **kw)
+    plan, host, out = run_on_gpu(kop, meta)
+    assert plan["family"] == "attention_f32"
+    x, ref = _ref(meta, host, kw.get("k_transposed", False))
+    got = out["o"].reshape(ref.shape).astype(np.float64)
+    assert np.all(np.abs(got - ref) <= 1e-5 * np.abs(x["v"]).max()), name
+    if kw["S"] * kw["D"] <= 64 * 128:
+        interp = run_ir(kop, meta, host)["o"].reshape(ref.shape).astype(np.float64)
+        assert np.all(np.abs(got - interp) <= 2e-5 * np.abs(x["v"]).max())
+
+
+F16_CASES = [
+    ("K5_8x32x512x128_f16out", dict(B=8, H=32, S=512, D=128, out_dtype="f16")),
+    ("K5_2x4x512x128_f32out", dict(B=2, H=4, S=512, D=128, out_dtype="f32")),
+] + [
+    (f"sweep_S{S}_D{D}", dict(B=2, H=4, S=S, D=D, out_dtype="f16"))
+    for D in (16, 64, 256) for S in (16, 128, 512)
+] + [
+    ("ragged_S200_D64", dict(B=1, H=3, S=200, D=64, out_dtype="f32")),
+    ("kt_f16_fallback", dict(B=1, H=2, S=64, D=32, out_dtype="f32", k_transposed=True)),
+]
+
+
+@pytest.mark.parametrize("name,kw", F16_CASES, ids=[c[0] for c in F16_CASES])
+def test_attention_f16(name, kw):
+    kop, meta = synth.attention(dtype="f16", **kw)
+    plan, host, out = run_on_gpu(kop, meta)
+    assert plan["family"] == "attention_f16"
+    x, ref = _ref(meta, host, kw.get("k_transposed", False))
+    got = out["o"].reshape(ref.shape).astype(np.float64)
+    u = 2.0 ** -11 if kw["out_dtype"] == "f16" else 0.0
+    vmax = np.abs(x["v"].astype(np.float64)).max()
+    err = np.abs(got - ref)
+    bound = 1e-3 * vmax + u * np.abs(ref)
+    assert np.all(err <= bound), f"{name}: max excess {np.max(err - bound)}"
