@@ -621,3 +621,91 @@ extern "C" int emmy_softmax_f32(const float *x, float *y, int64_t outer, int64_t
   softmax_cols_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, y, outer, n, inner);
   return check_launch("column softmax");
 }
+
+// ---------------------------------------------------------------------------
+// Long-row reduction with no allocation at all.
+//
+// emmy_reduce_f32 splits one long row over many CTAs only when the caller
+// hands it a device workspace for the per-CTA partials.  Some callers cannot
+// allocate device memory at the point of the call: code recorded into a CUDA
+// graph (cudaMalloc is not allowed while a stream is being captured), hosts
+// whose device memory is owned by a pool or budget fixed at start-up, and
+// latency-critical loops where an allocation's implicit device
+// synchronisation is not acceptable.  emmy_reduce_f32_noalloc serves them by
+// keeping the partials in a fixed array in the library's own device memory.
+
+namespace emmy {
+
+// Capacity of the partials array: one float per CTA, 4096 CTAs (16 KB held on
+// every device that loads the library, for the life of the process).
+constexpr int kNoallocParts = 4096;
+// Each CTA of the split reduces a fixed 16384-element chunk, so the longest
+// row this entry point accepts is kNoallocParts * kNoallocChunk elements.
+constexpr int64_t kNoallocChunk = 16384;
+
+static __device__ __align__(256) float g_noalloc_partials[kNoallocParts];
+
+// Device address of g_noalloc_partials for the current device.  Host code may
+// not pass the symbol itself to a kernel (on the host it names a stand-in, not
+// device memory), so the address is looked up once per device, with that
+// device current, and cached.
+static float *noalloc_partials_ptr(int *rc) {
+  static float *cached[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    *rc = set_error(EMMY_ERR_CUDA, "emmy_reduce_f32_noalloc: no current device");
+    return nullptr;
+  }
+  if (!cached[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+    if (e != cudaSuccess || p == nullptr) {
+      *rc = set_error(EMMY_ERR_CUDA, "emmy_reduce_f32_noalloc: cudaGetSymbolAddress: %s",
+                      cudaGetErrorString(e));
+      return nullptr;
+    }
+    cached[dev] = static_cast<float *>(p);
+  }
+  *rc = EMMY_OK;
+  return cached[dev];
+}
+
+template <int OP, int PRE>
+int noalloc_long(const float *x, float *y, int64_t n, const float *count, float *part,
+                 cudaStream_t st) {
+  const int64_t parts = (n + kNoallocChunk - 1) / kNoallocChunk;
+  reduce_long_partial_kernel<OP, PRE><<<(unsigned)parts, 1024, 0, st>>>(x, n, kNoallocChunk, part);
+  int rc = check_launch("emmy_reduce_f32_noalloc (partials)");
+  if (rc) return rc;
+  reduce_long_finish_kernel<OP><<<1, 1024, 0, st>>>(part, (int)parts, y, count);
+  return check_launch("emmy_reduce_f32_noalloc (finish)");
+}
+
+}  // namespace emmy
+
+extern "C" int emmy_reduce_f32_noalloc(const float *x, float *y, int64_t n, int op, int pre,
+                                       const float *count, void *stream) {
+  clear_error();
+  if (n <= 0) return set_error(EMMY_ERR_INVALID, "emmy_reduce_f32_noalloc: row length %lld",
+                               (long long)n);
+  if (n > (int64_t)kNoallocParts * kNoallocChunk)
+    return set_error(EMMY_ERR_INVALID,
+                     "emmy_reduce_f32_noalloc: row of %lld elements exceeds the %lld-element "
+                     "limit of the built-in scratch (use emmy_reduce_f32 with a workspace)",
+                     (long long)n, (long long)kNoallocParts * kNoallocChunk);
+  if (!x || !y) return set_error(EMMY_ERR_INVALID, "emmy_reduce_f32_noalloc: null tensor pointer");
+  if (op < 0 || op > 2 || pre < 0 || pre > 2)
+    return set_error(EMMY_ERR_INVALID, "emmy_reduce_f32_noalloc: bad op %d / pre %d", op, pre);
+  int rc = EMMY_OK;
+  float *part = noalloc_partials_ptr(&rc);
+  if (!part) return rc;
+  cudaStream_t st = as_stream(stream);
+#define EMMY_NA(O, P) \
+  if (op == O && pre == P) return noalloc_long<O, P>(x, y, n, count, part, st);
+  EMMY_NA(0, 0) EMMY_NA(0, 1) EMMY_NA(0, 2)
+  EMMY_NA(1, 0) EMMY_NA(1, 1) EMMY_NA(1, 2)
+  EMMY_NA(2, 0) EMMY_NA(2, 1) EMMY_NA(2, 2)
+#undef EMMY_NA
+  return set_error(EMMY_ERR_INVALID, "emmy_reduce_f32_noalloc: unreachable op");
+}

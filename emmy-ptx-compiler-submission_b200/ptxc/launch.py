@@ -32,6 +32,7 @@ SIGNATURES = {
     "emmy_zero": [_vp, _sz, _vp],
     "emmy_reduce_f32": [_vp, _vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _sz, _vp],
     "emmy_reduce_workspace_bytes": [_i64, _i64, _i64],
+    "emmy_reduce_f32_noalloc": [_vp, _vp, _i64, _int, _int, _vp, _vp],
     "emmy_rownorm_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _int, _vp],
     "emmy_softmax_f32": [_vp, _vp, _i64, _i64, _i64, _vp],
     "emmy_matvec_f64": [_vp, _vp, _vp, _i64, _i64, _vp],

@@ -180,6 +180,24 @@ int emmy_attention_f16(const void *q, const void *k, const void *v, void *o,
                        const float *scale_div, int64_t batch, int64_t sq, int64_t sk, int64_t d,
                        int out_dtype, int k_transposed, void *stream);
 
+/*
+ * Long-row reduction that allocates nothing: y[0] = fold_op(pre(x[0..n))) [* 1/count].
+ * No counterpart in the reference: it exists for callers that cannot allocate
+ * device memory when they call -- work recorded into a CUDA graph (no
+ * cudaMalloc while a stream is being captured), hosts whose device memory is
+ * a pool fixed at start-up, and loops that cannot afford an allocation's
+ * implicit synchronisation.  The per-CTA partials live in a 4096-float array
+ * inside the library (16 KB on every device that loads it, kept until exit).
+ * Limit: n <= 4096 * 16384 = 67,108,864 elements; longer rows are rejected
+ * with EMMY_ERR_INVALID (use emmy_reduce_f32 with a workspace instead).
+ * The first call on a device looks up the array's device address; make that
+ * first call before any stream capture.  Calls share the array, so calls
+ * that overlap on the GPU (different streams, no ordering) race; every call
+ * overwrites the partials it reads, so nothing needs clearing between calls.
+ */
+int emmy_reduce_f32_noalloc(const float *x, float *y, int64_t n, int op, int pre,
+                            const float *count, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
