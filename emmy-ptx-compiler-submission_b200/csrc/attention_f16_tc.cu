@@ -366,11 +366,8 @@ extern "C" int emmy_attention_f16(const void *q, const void *k, const void *v, v
     return set_error(EMMY_ERR_UNSUPPORTED, "emmy_attention_f16: grid too large");
   cudaStream_t st = as_stream(stream);
   const int out_f16 = out_dtype == EMMY_DT_F16;
-  // The tensor-core kernel is held back from dispatch until its barrier
-  // protocol has passed on the GPU; every shape runs the CUDA-core kernel.
-  constexpr bool kTensorCorePath = false;
-  const bool tc = kTensorCorePath && !k_transposed && sq == sk && aligned16(q) && aligned16(k) &&
-                  aligned16(v) && aligned16(o) && (d == 64 || d == 128 || d == 256);
+  const bool tc = !k_transposed && sq == sk && aligned16(q) && aligned16(k) && aligned16(v) &&
+                  aligned16(o) && (d == 64 || d == 128 || d == 256);
   if (tc) {
     if (d == 64) return launch_attention_tc<64, 128>(q, k, v, o, scale_div, batch, sq, out_f16, st);
     if (d == 128) return launch_attention_tc<128, 128>(q, k, v, o, scale_div, batch, sq, out_f16, st);
