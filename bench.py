@@ -291,6 +291,9 @@ def family_extras(device, peak):
         "K3b_bmm_f16_64x512": synth.matmul(512, 512, 512, batch=64, dtype="f16", out_dtype="f16",
                                            tm=128, tn=128, rm=8, rn=8),
         "K5_attention_f16_8x32x512x128": synth.attention(8, 32, 512, 128, dtype="f16"),
+        "F8a_pointwise_add_f32_2^26": synth.pointwise(1 << 26, ("add", "x0", "x1"), "f32"),
+        "F8b_pointwise_gelu_tanh_f16_16384x4096": synth.pointwise(
+            16384 * 4096, ("gelu_tanh", "x0"), "f16", shape=[16384, 4096]),
     }
     for name, (kop, meta) in cases.items():
         plan = Lowerer(kop, meta).plan()
@@ -515,6 +518,8 @@ PROFILE_CASES = {
                                         tm=128, tn=128, rm=8, rn=8),
     "attention_f16_K5": lambda s: s.attention(8, 32, 512, 128, dtype="f16"),
     "gemm_f32_splitk_K4a": lambda s: s.matmul(256, 256, 65536, splits=64, tm=128, tn=128, rm=8, rn=8),
+    "pointwise_add_2^26": lambda s: s.pointwise(1 << 26, ("add", "x0", "x1"), "f32"),
+    "pointwise_gelu_f16_2^26": lambda s: s.pointwise(1 << 26, ("gelu_tanh", "x0"), "f16"),
 }
 
 

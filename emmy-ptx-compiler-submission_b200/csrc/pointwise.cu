@@ -1,0 +1,294 @@
+// Pointwise (elementwise) family on sm_100a: out[i] = f(in_0[i], ..., scalars, immediates).
+//
+// Replaces the entry the reference emits for its pointwise IR shape: one
+// thread per 1-4 elements, each element a chain of Loads, Assigns and a
+// converting Write (reference ptxc/stmts.py:73-145 Load, :510-560 Assign,
+// :434-487 Write; op spellings ptxc/expr.py:880-1089 and ptxc/ops.py:81-96).
+// add/sub/mul/div/sqrt are rounded per op with no contraction, so chains the
+// reference checks with rtol = atol = 0 stay bit-exact.  An f16-typed Assign
+// computes in f32 and rounds to f16 (the matcher adds a round_f16 step).
+//
+// The matcher hands over the element's expression as a register program; one
+// kernel evaluates it for every element.  The register file lives in shared
+// memory (lane j of register r of thread t at [(r*VEC + j)*THREADS + t], no
+// bank conflicts), scalar constants and immediates are written once per
+// thread, and each instruction is decoded once per VEC elements.  Inputs and
+// the output move as 16-byte (f32, f64) or 8-byte (f16) vectors when every
+// pointer allows it; HBM traffic is then the algorithmic minimum.
+
+#include "common.cuh"
+
+namespace emmy {
+
+constexpr int kPwMaxRegs = 32, kPwMaxInstr = 48, kPwMaxIn = 8, kPwThreads = 256;
+
+enum PwOp {
+  PW_COPY = 0, PW_ADD, PW_SUB, PW_MUL, PW_DIV, PW_MAX, PW_MIN, PW_NEG, PW_ABS, PW_EXP, PW_LOG,
+  PW_SQRT, PW_RSQRT, PW_RECIP, PW_TANH, PW_SIGMOID, PW_RELU, PW_GT, PW_LT, PW_GE, PW_LE, PW_EQ,
+  PW_WHERE, PW_ROUND_F16, PW_FMA, PW_LOG2, PW_LOG10, PW_COS, PW_SIN, PW_TAN, PW_ERF, PW_GELU,
+  PW_GELU_TANH, PW_SOFTPLUS, PW_EXP2, PW_SILU, PW_POW, PW_FLOOR, PW_CEIL, PW_SIGN, PW_NOPS
+};
+
+struct PwProgram {
+  const void *inputs[kPwMaxIn];
+  const void *scalars[kPwMaxIn];
+  int in_dtype[kPwMaxIn];
+  int sc_dtype[kPwMaxIn];
+  double imm[kPwMaxIn];
+  int n_in, n_sc, n_imm, n_instr, result_reg;
+  signed char code[kPwMaxInstr][5];
+};
+
+// Correctly rounded arithmetic in both compute precisions (no FMA contraction).
+__device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ double add_rn(double a, double b) { return __dadd_rn(a, b); }
+__device__ __forceinline__ float sub_rn(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ double sub_rn(double a, double b) { return __dsub_rn(a, b); }
+__device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ double mul_rn(double a, double b) { return __dmul_rn(a, b); }
+__device__ __forceinline__ float div_rn(float a, float b) { return __fdiv_rn(a, b); }
+__device__ __forceinline__ double div_rn(double a, double b) { return __ddiv_rn(a, b); }
+__device__ __forceinline__ float fma_rn(float a, float b, float c) { return __fmaf_rn(a, b, c); }
+__device__ __forceinline__ double fma_rn(double a, double b, double c) { return __fma_rn(a, b, c); }
+__device__ __forceinline__ float sqrt_rn(float a) { return __fsqrt_rn(a); }
+__device__ __forceinline__ double sqrt_rn(double a) { return __dsqrt_rn(a); }
+
+template <typename T> __device__ __forceinline__ T pw_eval(int op, T a, T b, T c) {
+  const T zero = T(0), one = T(1), half = T(0.5);
+  switch (op) {
+    case PW_COPY: return a;
+    case PW_ADD: return add_rn(a, b);
+    case PW_SUB: return sub_rn(a, b);
+    case PW_MUL: return mul_rn(a, b);
+    case PW_DIV: return div_rn(a, b);
+    case PW_MAX: return fmax(a, b);       // maxNum, as max.f32 in the reference
+    case PW_MIN: return fmin(a, b);
+    case PW_NEG: return -a;
+    case PW_ABS: return fabs(a);
+    case PW_EXP: return exp(a);
+    case PW_LOG: return log(a);
+    case PW_SQRT: return sqrt_rn(a);
+    case PW_RSQRT: return rsqrt(a);
+    case PW_RECIP: return div_rn(one, a);
+    case PW_TANH: return tanh(a);
+    case PW_SIGMOID: return div_rn(one, add_rn(one, exp(-a)));
+    case PW_RELU: return fmax(a, zero);
+    case PW_GT: return a > b ? one : zero;
+    case PW_LT: return a < b ? one : zero;
+    case PW_GE: return a >= b ? one : zero;
+    case PW_LE: return a <= b ? one : zero;
+    case PW_EQ: return a == b ? one : zero;
+    case PW_WHERE: return a != zero ? b : c;
+    case PW_ROUND_F16: return T(__half2float(__float2half_rn(float(a))));
+    case PW_FMA: return fma_rn(a, b, c);
+    case PW_LOG2: return log2(a);
+    case PW_LOG10: return log10(a);
+    case PW_COS: return cos(a);
+    case PW_SIN: return sin(a);
+    case PW_TAN: return tan(a);
+    case PW_ERF: return erf(a);
+    case PW_GELU:        // x/2 * (1 + erf(x / sqrt 2))
+      return mul_rn(mul_rn(half, a), add_rn(one, erf(mul_rn(a, T(0.7071067811865476)))));
+    case PW_GELU_TANH: { // x/2 * (1 + tanh(sqrt(2/pi) * (x + 0.044715 x^3)))
+      const T x3 = mul_rn(mul_rn(a, a), a);
+      const T t = mul_rn(fma_rn(T(0.044715), x3, a), T(0.7978845608028654));
+      return mul_rn(mul_rn(half, a), add_rn(one, tanh(t)));
+    }
+    case PW_SOFTPLUS: return add_rn(fmax(a, zero), log1p(exp(-fabs(a))));
+    case PW_EXP2: return exp2(a);
+    case PW_SILU: return div_rn(a, add_rn(one, exp(-a)));
+    case PW_POW: return pow(a, b);
+    case PW_FLOOR: return floor(a);
+    case PW_CEIL: return ceil(a);
+    case PW_SIGN: return a > zero ? one : (a < zero ? -one : a);   // keeps +-0 and NaN
+    default: return zero;
+  }
+}
+
+template <typename T> __device__ __forceinline__ T pw_load1(const void *p, int dt, int64_t i) {
+  if (dt == EMMY_DT_F16) return T(__half2float(static_cast<const __half *>(p)[i]));
+  if (dt == EMMY_DT_F64) return T(static_cast<const double *>(p)[i]);
+  return T(static_cast<const float *>(p)[i]);
+}
+
+// VEC = 4 consecutive elements from an aligned base (checked on the host).
+template <typename T> __device__ __forceinline__ void pw_load4(const void *p, int dt, int64_t i, T v[4]) {
+  if (dt == EMMY_DT_F16) {
+    const uint2 u = __ldcs(reinterpret_cast<const uint2 *>(static_cast<const __half *>(p) + i));
+    const __half2 h0 = *reinterpret_cast<const __half2 *>(&u.x);
+    const __half2 h1 = *reinterpret_cast<const __half2 *>(&u.y);
+    v[0] = T(__low2float(h0)); v[1] = T(__high2float(h0));
+    v[2] = T(__low2float(h1)); v[3] = T(__high2float(h1));
+  } else if (dt == EMMY_DT_F64) {
+    const double2 *q = reinterpret_cast<const double2 *>(static_cast<const double *>(p) + i);
+    const double2 a = __ldcs(q), b = __ldcs(q + 1);
+    v[0] = T(a.x); v[1] = T(a.y); v[2] = T(b.x); v[3] = T(b.y);
+  } else {
+    const float4 a = __ldcs(reinterpret_cast<const float4 *>(static_cast<const float *>(p) + i));
+    v[0] = T(a.x); v[1] = T(a.y); v[2] = T(a.z); v[3] = T(a.w);
+  }
+}
+
+template <typename T> __device__ __forceinline__ void pw_store1(void *p, int dt, int64_t i, T v) {
+  if (dt == EMMY_DT_F16) static_cast<__half *>(p)[i] = __float2half_rn(float(v));
+  else if (dt == EMMY_DT_F64) static_cast<double *>(p)[i] = double(v);
+  else static_cast<float *>(p)[i] = float(v);
+}
+
+template <typename T> __device__ __forceinline__ void pw_store4(void *p, int dt, int64_t i, const T v[4]) {
+  if (dt == EMMY_DT_F16) {
+    __half2 h0 = __floats2half2_rn(float(v[0]), float(v[1]));
+    __half2 h1 = __floats2half2_rn(float(v[2]), float(v[3]));
+    uint2 u;
+    u.x = *reinterpret_cast<unsigned *>(&h0);
+    u.y = *reinterpret_cast<unsigned *>(&h1);
+    __stcs(reinterpret_cast<uint2 *>(static_cast<__half *>(p) + i), u);
+  } else if (dt == EMMY_DT_F64) {
+    double2 *q = reinterpret_cast<double2 *>(static_cast<double *>(p) + i);
+    __stcs(q, make_double2(double(v[0]), double(v[1])));
+    __stcs(q + 1, make_double2(double(v[2]), double(v[3])));
+  } else {
+    __stcs(reinterpret_cast<float4 *>(static_cast<float *>(p) + i),
+           make_float4(float(v[0]), float(v[1]), float(v[2]), float(v[3])));
+  }
+}
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(kPwThreads)
+pointwise_kernel(const PwProgram p, void *out, int out_dtype, int64_t n) {
+  extern __shared__ __align__(16) unsigned char pw_smem[];
+  T *R = reinterpret_cast<T *>(pw_smem);
+  const int tid = threadIdx.x;
+  auto reg = [&](int r, int j) -> T & { return R[(r * VEC + j) * kPwThreads + tid]; };
+  for (int s = 0; s < p.n_sc; ++s) {
+    const T v = pw_load1<T>(p.scalars[s], p.sc_dtype[s], 0);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) reg(p.n_in + s, j) = v;
+  }
+  for (int s = 0; s < p.n_imm; ++s) {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) reg(p.n_in + p.n_sc + s, j) = T(p.imm[s]);
+  }
+  const int64_t groups = (n + VEC - 1) / VEC;
+  for (int64_t g = (int64_t)blockIdx.x * kPwThreads + tid; g < groups;
+       g += (int64_t)gridDim.x * kPwThreads) {
+    const int64_t base = g * VEC;
+    const bool full = base + VEC <= n;
+    for (int k = 0; k < p.n_in; ++k) {
+      if (VEC == 4 && full) {
+        T v[4];
+        pw_load4<T>(p.inputs[k], p.in_dtype[k], base, v);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) reg(k, j) = v[j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j)
+          reg(k, j) = base + j < n ? pw_load1<T>(p.inputs[k], p.in_dtype[k], base + j) : T(0);
+      }
+    }
+    for (int k = 0; k < p.n_instr; ++k) {
+      const int op = p.code[k][0], d = p.code[k][1], a = p.code[k][2], b = p.code[k][3],
+                c = p.code[k][4];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) reg(d, j) = pw_eval<T>(op, reg(a, j), reg(b, j), reg(c, j));
+    }
+    T v[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) v[j] = reg(p.result_reg, j);
+    if (VEC == 4 && full) {
+      pw_store4<T>(out, out_dtype, base, v);
+    } else {
+#pragma unroll
+      for (int j = 0; j < VEC; ++j)
+        if (base + j < n) pw_store1<T>(out, out_dtype, base + j, v[j]);
+    }
+  }
+}
+
+template <typename T, int VEC>
+void launch_pointwise(const PwProgram &p, int nregs, void *out, int out_dtype, int64_t n,
+                      cudaStream_t st) {
+  const int64_t groups = (n + VEC - 1) / VEC;
+  int64_t blocks = (groups + kPwThreads - 1) / kPwThreads;
+  // enough resident blocks to cover HBM latency; the grid-stride loop does the rest
+  const int64_t cap = (int64_t)sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  const size_t smem = (size_t)nregs * VEC * kPwThreads * sizeof(T);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(pointwise_kernel<T, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+  pointwise_kernel<T, VEC><<<(unsigned)blocks, kPwThreads, smem, st>>>(p, out, out_dtype, n);
+}
+
+}  // namespace emmy
+
+using namespace emmy;
+
+extern "C" int emmy_pointwise(const void *const *inputs, const int *input_dtypes, int n_inputs,
+                              const void *const *scalars, const int *scalar_dtypes, int n_scalars,
+                              const double *immediates, int n_imm, const int *program, int n_instr,
+                              int result_reg, int compute_f64, void *out, int out_dtype, int64_t n,
+                              void *stream) {
+  clear_error();
+  if (n < 0) return set_error(EMMY_ERR_INVALID, "emmy_pointwise: negative size");
+  if (n == 0) return EMMY_OK;
+  if (!out) return set_error(EMMY_ERR_INVALID, "emmy_pointwise: null output");
+  if (n_inputs < 0 || n_inputs > kPwMaxIn || n_scalars < 0 || n_scalars > kPwMaxIn || n_imm < 0 ||
+      n_imm > kPwMaxIn || n_instr < 1 || n_instr > kPwMaxInstr)
+    return set_error(EMMY_ERR_INVALID, "emmy_pointwise: program has too many inputs or steps");
+  if ((n_inputs && (!inputs || !input_dtypes)) || (n_scalars && (!scalars || !scalar_dtypes)) ||
+      (n_imm && !immediates) || !program)
+    return set_error(EMMY_ERR_INVALID, "emmy_pointwise: null argument array");
+  const int nregs = n_inputs + n_scalars + n_imm + n_instr;
+  if (nregs > kPwMaxRegs) return set_error(EMMY_ERR_INVALID, "emmy_pointwise: too many registers");
+  if (result_reg < 0 || result_reg >= nregs)
+    return set_error(EMMY_ERR_INVALID, "emmy_pointwise: bad result register");
+  auto dt_ok = [](int dt) { return dt == EMMY_DT_F32 || dt == EMMY_DT_F16 || dt == EMMY_DT_F64; };
+  if (!dt_ok(out_dtype)) return set_error(EMMY_ERR_INVALID, "emmy_pointwise: bad output dtype");
+  PwProgram p{};
+  p.n_in = n_inputs;
+  p.n_sc = n_scalars;
+  p.n_imm = n_imm;
+  p.n_instr = n_instr;
+  p.result_reg = result_reg;
+  bool vec_ok = aligned16(out) || (out_dtype == EMMY_DT_F16 && ((uintptr_t)out & 7) == 0);
+  for (int i = 0; i < n_inputs; ++i) {
+    if (!inputs[i]) return set_error(EMMY_ERR_INVALID, "emmy_pointwise: null input %d", i);
+    if (!dt_ok(input_dtypes[i])) return set_error(EMMY_ERR_INVALID, "emmy_pointwise: bad input dtype");
+    p.inputs[i] = inputs[i];
+    p.in_dtype[i] = input_dtypes[i];
+    const uintptr_t need = input_dtypes[i] == EMMY_DT_F16 ? 8 : 16;
+    vec_ok = vec_ok && ((uintptr_t)inputs[i] % need) == 0;
+  }
+  for (int i = 0; i < n_scalars; ++i) {
+    if (!scalars[i]) return set_error(EMMY_ERR_INVALID, "emmy_pointwise: null scalar %d", i);
+    if (!dt_ok(scalar_dtypes[i])) return set_error(EMMY_ERR_INVALID, "emmy_pointwise: bad scalar dtype");
+    p.scalars[i] = scalars[i];
+    p.sc_dtype[i] = scalar_dtypes[i];
+  }
+  for (int i = 0; i < n_imm; ++i) p.imm[i] = immediates[i];
+  for (int k = 0; k < n_instr; ++k) {
+    const int *c = program + 5 * k;
+    if (c[0] < 0 || c[0] >= PW_NOPS)
+      return set_error(EMMY_ERR_INVALID, "emmy_pointwise: unknown opcode %d", c[0]);
+    // destinations are the temporaries (never an input, scalar or immediate)
+    if (c[1] < n_inputs + n_scalars + n_imm || c[1] >= nregs)
+      return set_error(EMMY_ERR_INVALID, "emmy_pointwise: step %d writes register %d", k, c[1]);
+    for (int j = 2; j < 5; ++j)
+      if (c[j] < 0 || c[j] >= nregs)
+        return set_error(EMMY_ERR_INVALID, "emmy_pointwise: register %d out of range", c[j]);
+    for (int j = 0; j < 5; ++j) p.code[k][j] = (signed char)c[j];
+  }
+  // the shared register file of a 4-wide double program with many registers
+  // would not fit; such programs run one element per thread
+  if ((size_t)nregs * 4 * kPwThreads * (compute_f64 ? 8 : 4) > 160 * 1024) vec_ok = false;
+  cudaStream_t st = as_stream(stream);
+  if (compute_f64) {
+    if (vec_ok) launch_pointwise<double, 4>(p, nregs, out, out_dtype, n, st);
+    else launch_pointwise<double, 1>(p, nregs, out, out_dtype, n, st);
+  } else {
+    if (vec_ok) launch_pointwise<float, 4>(p, nregs, out, out_dtype, n, st);
+    else launch_pointwise<float, 1>(p, nregs, out, out_dtype, n, st);
+  }
+  return check_launch("emmy_pointwise");
+}

@@ -575,3 +575,107 @@ def attention(B, H, S, D, dtype="f16", out_dtype=None, scale_div=None, entry="k_
             _arg("v", dtype, [B, H, S, Dv], seed=2, **({"init": v_init} if v_init else {})),
             _arg("o", out_dtype, [B, H, S, Dv], output=True)]
     return kop, _meta(entry, args, B * H * S * Dv // threads, threads)
+
+
+# ---------------------------------------------------------------------------
+# pointwise (v_p_* / w_p_* shape)
+
+BOOL = DataType(name="bool", np=NpDType("bool"), nbytes=1)
+_COMPARE = {"greater", "less", "greater_equal", "less_equal", "equal"}
+
+
+def pointwise(n, expr, dtype="f32", shape=None, block=256, unroll=None, entry="k_pointwise",
+              vector_write=True, inits=None, out="out", seeds=None):
+    """The reference pointwise shape: ``Tile(a0 : n/U)`` with U unrolled copies.
+
+    Each copy u loads its element ``a0*U + u`` of every input, loads the
+    one-element constant tensors at index 0, evaluates ``expr`` with one Assign
+    per op (typed ``dtype``; comparisons typed bool) and the copies' results
+    are written by one vector Write (``vector_write``) or U scalar Writes --
+    ``v_p_big`` / ``w_p_f64`` respectively.  ``expr`` is a nested tuple:
+    ``"x0"`` names an input tensor of ``shape`` (default ``[n]``),
+    ``("const", name, value)`` a one-element constant tensor, ``("imm", value)``
+    an immediate (Let), and ``(op, arg, ...)`` an elementwise op.  Inputs get
+    seeds 0, 1, ... in order of first use unless ``seeds`` names them.
+    """
+    shape = list(shape) if shape else [int(n)]
+    if math.prod(shape) != n:
+        raise ValueError("shape does not hold n elements")
+    if unroll is None:
+        unroll = next(u for u in (4, 3, 2, 1) if n % u == 0)
+    if n % unroll:
+        raise ValueError("unroll must divide n")
+    T = n // unroll
+    inputs, consts = [], {}
+
+    def walk(e):
+        if isinstance(e, str):
+            if e not in inputs:
+                inputs.append(e)
+        elif e[0] == "const":
+            consts[e[1]] = float(e[2])
+        elif e[0] != "imm":
+            for a in e[1:]:
+                walk(a)
+    walk(expr)
+
+    def flat_index(u):
+        lin = _B("+", _B("*", V("a0"), L(unroll)), L(u)) if T > 1 else L(u)
+        if len(shape) == 1:
+            return (lin,)
+        idx = []
+        for i in range(len(shape)):
+            stride = math.prod(shape[i + 1:])
+            c = _B("//", lin, L(stride)) if i < len(shape) - 1 else lin
+            idx.append(_B("%", c, L(shape[i])) if i > 0 else c)
+        return tuple(idx)
+
+    body = []
+    results = []
+    for u in range(unroll):
+        counter = [0]
+        loaded = {}
+
+        def emit(e):
+            if isinstance(e, str):
+                if e not in loaded:
+                    nm = f"in{inputs.index(e)}__u{u}"
+                    body.append(Load(names=(nm,), input=e, index=flat_index(u), dtype=DT[dtype]))
+                    loaded[e] = nm
+                return loaded[e]
+            if e[0] == "const":
+                nm = f"c_{e[1]}__u{u}"
+                if nm not in loaded:
+                    body.append(Load(names=(nm,), input=e[1], index=(L(0),), dtype=DT[dtype]))
+                    loaded[nm] = nm
+                return nm
+            if e[0] == "imm":
+                nm = f"k{counter[0]}__u{u}"
+                counter[0] += 1
+                body.append(Let(name=nm, value=L(float(e[1])), dtype=DT[dtype]))
+                return nm
+            args = [emit(a) for a in e[1:]]
+            nm = f"v{counter[0]}__u{u}"
+            counter[0] += 1
+            dt = BOOL if e[0] in _COMPARE else DT[dtype]
+            body.append(Assign(name=nm, op=E(e[0]), args=tuple(args), dtype=dt))
+            return nm
+        results.append(emit(expr))
+    base = _B("*", V("a0"), L(unroll)) if T > 1 else L(0)
+    if vector_write:
+        body.append(Write(output=out, index=(_B("+", base, L(0)) if T > 1 else L(0),),
+                          values=tuple(results), value_dtype=DT[dtype], atomic=False,
+                          swizzle="NONE"))
+    else:
+        for u, r in enumerate(results):
+            body.append(Write(output=out, index=(_B("+", base, L(u)) if T > 1 else L(u),),
+                              values=(r,), value_dtype=DT[dtype], atomic=False, swizzle="NONE"))
+    axes = [ax("a0", T)]
+    kop = KernelOp(name=entry, body=(_tile(axes, body, block),))
+    args = [_arg(c, dtype, [1], data=[v]) for c, v in consts.items()]
+    for i, name in enumerate(inputs):
+        kw = {"init": inits[name]} if inits and name in inits else {}
+        seed = seeds[name] if seeds and name in seeds else i
+        args.append(_arg(name, dtype, shape, seed=seed, **kw))
+    args.append(_arg(out, dtype, shape, output=True))
+    return kop, _meta(entry, args, (T + block - 1) // block, block)

@@ -76,18 +76,19 @@ def affine_of(e, rename=None):
                 return _scale(left, right.const())
             return None
         if e.op in ("/", "//", "divide", "floor_divide", "%", "mod", "remainder"):
-            # (v // c) and (v % c) of a lone variable stay symbolic atoms; a flat
-            # index that holds c*k*(v//c) + k*(v%c) recombines to k*v below.
+            # (E // c) and (E % c) of an affine E stay symbolic atoms; a flat
+            # index that holds c*k*(E//c) + k*(E%c) recombines to k*E below.
             c = right.const() if not right.vars() else None
-            if c is None or c <= 0 or len(left.vars()) != 1 or left.const() != 0:
-                return None
-            (v,) = left.vars()
-            if left.coef(v) != 1 or not isinstance(v, str):
+            if c is None or c <= 0 or not left.atoms_ok():
                 return None
             kind = "div" if e.op in ("/", "//", "divide", "floor_divide") else "mod"
-            return Affine({(kind, v, c): 1})
+            return Affine({(kind, _frozen(left), c): 1})
         return None
     return None
+
+
+def _frozen(a: Affine) -> tuple:
+    return tuple(sorted(((k, v) for k, v in a.items() if v), key=repr))
 
 
 def _recombine(a: Affine):
@@ -99,7 +100,7 @@ def _recombine(a: Affine):
             if k2 and out[key] == key[2] * k2:
                 del out[key]
                 del out[mod]
-                out[key[1]] = out.get(key[1], 0) + k2
+                out = _add(out, _scale(Affine(dict(key[1])), k2))
     if not out.atoms_ok():
         return None
     return out

@@ -8,7 +8,9 @@ the data path:
   (x and y sliced by rows; weights, bias and scalar constants replicated);
 * matmul (f32 and f16): batches when there are at least as many as ranks,
   otherwise rows of A and C (B and the bias replicated);
-* attention: (batch, head) slices of q, k, v and o.
+* attention: (batch, head) slices of q, k, v and o;
+* pointwise: contiguous element ranges of every input and the output (the
+  one-element constant tensors replicated).
 
 The one family with an exchange step is split-K matmul spread over ranks:
 each rank multiplies its K slice into a full-size partial C, and the partials
@@ -101,6 +103,13 @@ def shard_plan(plan: dict, rank: int, world: int):
         set_shape(a["k"], [hi - lo, g["d"], g["sk"]] if g["k_transposed"] else [hi - lo, g["sk"], g["d"]])
         set_shape(a["v"], [hi - lo, g["sk"], g["dv"]])
         set_shape(a["o"], [hi - lo, g["sq"], g["dv"]])
+    elif fam == "pointwise":
+        g = plan["pointwise"]
+        lo, hi = shard_ranges(g["n"], world)[rank]
+        sub["pointwise"]["n"] = hi - lo
+        for name in list(g["inputs"]) + [a["out"]]:
+            slices[name] = (lo, hi - lo)
+            set_shape(name, [hi - lo])
     else:
         raise ValueError(f"family {fam!r} has no sharding rule")
     sub["shard"] = {"rank": rank, "world": world}

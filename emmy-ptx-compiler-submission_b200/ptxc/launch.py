@@ -40,12 +40,15 @@ SIGNATURES = {
     "emmy_gemm_f16": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _int, _vp],
     "emmy_attention_f32": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _int, _vp],
     "emmy_attention_f16": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _vp],
+    "emmy_pointwise": [_vp, _vp, _int, _vp, _vp, _int, _vp, _int, _vp, _int, _int, _int, _vp, _int,
+                       _i64, _vp],
 }
 RESTYPES = {"emmy_reduce_workspace_bytes": _sz}
 
 REDUCE_OP = {"sum": 0, "max": 1, "min": 2}
 REDUCE_PRE = {"identity": 0, "square": 1, "abs": 2}
 NORM_MODE = {"rms": 0, "l2": 1, "layer": 2}
+DT_CODE = {"f32": 0, "f16": 1, "f64": 2}
 
 
 class LibraryError(RuntimeError):
@@ -201,6 +204,21 @@ def run(plan: dict, tensors: dict, stream=None, workspace=None, check: bool = Tr
                                       _ptr(T("scale")), g["batch"], g["sq"], g["sk"], g["d"],
                                       g["out_dtype"], int(g["k_transposed"]), st),
                "emmy_attention_f16")
+        launches += 1
+    elif fam == "pointwise":
+        g = plan["pointwise"]
+        ins, scs, imms = g["inputs"], g["scalars"], g["immediates"]
+        in_ptrs = (_vp * max(1, len(ins)))(*[_ptr(tensors[n]) for n in ins])
+        in_dts = (_int * max(1, len(ins)))(*[DT_CODE[plan["tensors"][n]["dtype"]] for n in ins])
+        sc_ptrs = (_vp * max(1, len(scs)))(*[_ptr(tensors[n]) for n in scs])
+        sc_dts = (_int * max(1, len(scs)))(*[DT_CODE[plan["tensors"][n]["dtype"]] for n in scs])
+        imm = (ctypes.c_double * max(1, len(imms)))(*[float(v) for v in imms])
+        flat = [int(x) for row in g["program"] for x in row]
+        prog = (_int * len(flat))(*flat)
+        _check(lib.emmy_pointwise(in_ptrs, in_dts, len(ins), sc_ptrs, sc_dts, len(scs), imm,
+                                  len(imms), prog, len(g["program"]), g["result_reg"],
+                                  int(g["compute"] == "f64"), _ptr(T("out")),
+                                  DT_CODE[g["out_dtype"]], g["n"], st), "emmy_pointwise")
         launches += 1
     else:
         raise ValueError(f"plan family {fam!r} has no launcher")

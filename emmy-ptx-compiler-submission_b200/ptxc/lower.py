@@ -43,7 +43,9 @@ def _has(stmts, names) -> bool:
 def _matchers():
     from .match_gemm import match_gemm
     from .match_attention import match_attention
-    return [("reduction", match_reduction), ("matmul", match_gemm), ("attention", match_attention)]
+    from .match_pointwise import match_pointwise
+    return [("pointwise", match_pointwise), ("reduction", match_reduction),
+            ("matmul", match_gemm), ("attention", match_attention)]
 
 
 class Lowerer:

@@ -51,9 +51,10 @@ extern "C" {
 #define EMMY_NORM_L2 1
 #define EMMY_NORM_LAYER 2
 
-/* output dtypes */
+/* element dtypes */
 #define EMMY_DT_F32 0
 #define EMMY_DT_F16 1
+#define EMMY_DT_F64 2
 
 /* GEMM epilogue bits */
 #define EMMY_EPI_BIAS 1
@@ -179,6 +180,31 @@ int emmy_attention_f32(const float *q, const float *k, const float *v, float *o,
 int emmy_attention_f16(const void *q, const void *k, const void *v, void *o,
                        const float *scale_div, int64_t batch, int64_t sq, int64_t sk, int64_t d,
                        int out_dtype, int k_transposed, void *stream);
+
+/*
+ * Elementwise chain: out[i] = program(inputs[0][i], ..., *scalars[0], ..., immediates)
+ * for i in [0, n).  Replaces the entry the reference emits for its pointwise
+ * IR shape (reference ptxc/stmts.py:73-145, 434-487, 510-560; float ops
+ * ptxc/expr.py:880-1089, ptxc/ops.py:81-96).
+ * Registers: 0..n_inputs-1 hold the element of each input (EMMY_DT_*), then one
+ * per one-element scalar tensor, then one per immediate, then one per program
+ * step.  program holds n_instr rows {opcode, dst, a, b, c}; opcodes are the
+ * table in ptxc/match_pointwise.py (OPCODES): 0 copy, 1 add, 2 subtract,
+ * 3 multiply, 4 divide, 5 maximum, 6 minimum, 7 negative, 8 abs, 9 exp, 10 log,
+ * 11 sqrt, 12 rsqrt, 13 reciprocal, 14 tanh, 15 sigmoid, 16 relu, 17 greater,
+ * 18 less, 19 greater_equal, 20 less_equal, 21 equal, 22 where(a, b, c),
+ * 23 round to f16, 24 fma, 25 log2, 26 log10, 27 cos, 28 sin, 29 tan, 30 erf,
+ * 31 gelu, 32 gelu_tanh, 33 softplus, 34 exp2, 35 silu, 36 pow, 37 floor,
+ * 38 ceil, 39 sign.  Comparisons give 1 or 0.  compute_f64 selects double
+ * arithmetic, else f32; add/subtract/multiply/divide/sqrt/fma are correctly
+ * rounded and never contracted.  Limits: 8 inputs, 8 scalars, 8 immediates,
+ * 48 steps, 32 registers in all.
+ */
+int emmy_pointwise(const void *const *inputs, const int *input_dtypes, int n_inputs,
+                   const void *const *scalars, const int *scalar_dtypes, int n_scalars,
+                   const double *immediates, int n_imm, const int *program, int n_instr,
+                   int result_reg, int compute_f64, void *out, int out_dtype, int64_t n,
+                   void *stream);
 
 /*
  * Long-row reduction that allocates nothing: y[0] = fold_op(pre(x[0..n))) [* 1/count].

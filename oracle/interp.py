@@ -678,6 +678,33 @@ def _elementwise(opname, args, kinds, kind):
         return torch.sigmoid(a)
     if opname == "pow":
         return torch.pow(a, b)
+    # the rest of the reference's float op table (ptxc/expr.py:899-1075)
+    if opname == "log2":
+        return torch.log2(a)
+    if opname == "log10":
+        return torch.log10(a)
+    if opname == "cos":
+        return torch.cos(a)
+    if opname == "sin":
+        return torch.sin(a)
+    if opname == "tan":
+        return torch.tan(a)
+    if opname == "erf":
+        return torch.erf(a)
+    if opname == "gelu":
+        return 0.5 * a * (1.0 + torch.erf(a * 0.7071067811865476))
+    if opname == "gelu_tanh":
+        return 0.5 * a * (1.0 + torch.tanh(0.7978845608028654 * (a + 0.044715 * a * a * a)))
+    if opname == "softplus":
+        return torch.clamp_min(a, 0) + torch.log1p(torch.exp(-torch.abs(a)))
+    if opname == "silu":
+        return a * torch.sigmoid(a)
+    if opname == "floor":
+        return torch.floor(a)
+    if opname == "ceil":
+        return torch.ceil(a)
+    if opname == "sign":
+        return torch.sign(a)
     if opname in ("greater", "gt"):
         return (a > b), "pred"
     if opname in ("less", "lt"):

@@ -61,6 +61,30 @@ def test_host_side_argument_checks_run_before_any_cuda_call(lib):
     assert lib.emmy_rownorm_f32(None, None, None, None, 0, 4, None, None, 0, None) == 0
 
 
+def test_pointwise_program_checks_need_no_gpu(lib):
+    vp, i32, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+    lib.emmy_pointwise.argtypes = [vp, vp, i32, vp, vp, i32, vp, i32, vp, i32, i32, i32, vp, i32,
+                                   i64, vp]
+    lib.emmy_last_error.restype = ctypes.c_char_p
+    ins = (vp * 1)(vp(16))
+    dts = (i32 * 1)(0)
+    # empty output: nothing to do, success without touching a device
+    prog = (i32 * 5)(1, 1, 0, 0, 0)
+    assert lib.emmy_pointwise(ins, dts, 1, None, None, 0, None, 0, prog, 1, 1, 0, vp(16), 0, 0,
+                              None) == 0
+    # unknown opcode, a step that overwrites an input register, a bad result register
+    bad = (i32 * 5)(99, 1, 0, 0, 0)
+    assert lib.emmy_pointwise(ins, dts, 1, None, None, 0, None, 0, bad, 1, 1, 0, vp(16), 0, 8,
+                              None) == 1
+    assert b"unknown opcode" in lib.emmy_last_error()
+    clobber = (i32 * 5)(1, 0, 0, 0, 0)
+    assert lib.emmy_pointwise(ins, dts, 1, None, None, 0, None, 0, clobber, 1, 1, 0, vp(16), 0, 8,
+                              None) == 1
+    assert lib.emmy_pointwise(ins, dts, 1, None, None, 0, None, 0, prog, 1, 7, 0, vp(16), 0, 8,
+                              None) == 1
+    assert b"result register" in lib.emmy_last_error()
+
+
 def test_launcher_refuses_to_run_without_the_library(tmp_path, monkeypatch):
     import ptxc.launch as L
     monkeypatch.setattr(L, "_LIB", None)

@@ -72,6 +72,15 @@ def _family_result(plan, meta, full):
         vv = full[a["v"]].reshape(1, g["batch"], g["sk"], g["dv"])
         div = [m["data"][0] for m in meta["args"] if m["name"] == a["scale"]][0]
         return F.attention_bhsd(q, k, vv, 1.0 / div, out_dtype=np.float64).reshape(-1)
+    if fam == "pointwise":
+        # float64 walk of the plan's register program (add / multiply only here)
+        g = plan["pointwise"]
+        regs = [full[n] for n in g["inputs"]] + [full[n] for n in g["scalars"]] + \
+            [np.float64(v) for v in g["immediates"]]
+        for op, _dst, ra, rb, _rc in g["program"]:
+            x, y = regs[ra], regs[rb]
+            regs.append({1: lambda: x + y, 3: lambda: x * y}[op]())
+        return np.asarray(regs[g["result_reg"]], dtype=np.float64).reshape(-1)
     raise ValueError(fam)
 
 
@@ -84,6 +93,8 @@ CASES = {
     "gemm_rows": lambda: synth.matmul(96, 64, 32, bias=True, relu=True, tm=32, tn=32),
     "bmm_batches": lambda: synth.matmul(32, 32, 16, batch=5, tm=32, tn=32),
     "attention_heads": lambda: synth.attention(2, 3, 16, 16, dtype="f32"),
+    "pointwise_elements": lambda: synth.pointwise(
+        1001, ("add", ("multiply", ("const", "c", 1.5), "x0"), "x1"), "f32"),
 }
 
 
@@ -99,6 +110,8 @@ def _worker(rank, world, port, case, q):
         local = {}
         for name, (off, cnt) in slices.items():
             local[name] = host[name][off:off + cnt]
+        for name in sub.get("pointwise", {}).get("scalars", []):
+            local[name] = host[name]
         out_name = plan["outputs"][0]
         mine = _family_result(sub, meta, local)
         pieces = [None] * world
