@@ -53,34 +53,11 @@ __device__ __forceinline__ double fma_rn(double a, double b, double c) { return 
 __device__ __forceinline__ float sqrt_rn(float a) { return __fsqrt_rn(a); }
 __device__ __forceinline__ double sqrt_rn(double a) { return __dsqrt_rn(a); }
 
-template <typename T> __device__ __forceinline__ T pw_eval(int op, T a, T b, T c) {
-  const T zero = T(0), one = T(1), half = T(0.5);
+// Ops whose library code is long stay out of line, so the dispatch below
+// keeps a small instruction footprint.
+template <typename T> __device__ __noinline__ T pw_slow(int op, T a, T b) {
+  const T one = T(1), half = T(0.5);
   switch (op) {
-    case PW_COPY: return a;
-    case PW_ADD: return add_rn(a, b);
-    case PW_SUB: return sub_rn(a, b);
-    case PW_MUL: return mul_rn(a, b);
-    case PW_DIV: return div_rn(a, b);
-    case PW_MAX: return fmax(a, b);       // maxNum, as max.f32 in the reference
-    case PW_MIN: return fmin(a, b);
-    case PW_NEG: return -a;
-    case PW_ABS: return fabs(a);
-    case PW_EXP: return exp(a);
-    case PW_LOG: return log(a);
-    case PW_SQRT: return sqrt_rn(a);
-    case PW_RSQRT: return rsqrt(a);
-    case PW_RECIP: return div_rn(one, a);
-    case PW_TANH: return tanh(a);
-    case PW_SIGMOID: return div_rn(one, add_rn(one, exp(-a)));
-    case PW_RELU: return fmax(a, zero);
-    case PW_GT: return a > b ? one : zero;
-    case PW_LT: return a < b ? one : zero;
-    case PW_GE: return a >= b ? one : zero;
-    case PW_LE: return a <= b ? one : zero;
-    case PW_EQ: return a == b ? one : zero;
-    case PW_WHERE: return a != zero ? b : c;
-    case PW_ROUND_F16: return T(__half2float(__float2half_rn(float(a))));
-    case PW_FMA: return fma_rn(a, b, c);
     case PW_LOG2: return log2(a);
     case PW_LOG10: return log10(a);
     case PW_COS: return cos(a);
@@ -89,20 +66,62 @@ template <typename T> __device__ __forceinline__ T pw_eval(int op, T a, T b, T c
     case PW_ERF: return erf(a);
     case PW_GELU:        // x/2 * (1 + erf(x / sqrt 2))
       return mul_rn(mul_rn(half, a), add_rn(one, erf(mul_rn(a, T(0.7071067811865476)))));
-    case PW_GELU_TANH: { // x/2 * (1 + tanh(sqrt(2/pi) * (x + 0.044715 x^3)))
-      const T x3 = mul_rn(mul_rn(a, a), a);
-      const T t = mul_rn(fma_rn(T(0.044715), x3, a), T(0.7978845608028654));
-      return mul_rn(mul_rn(half, a), add_rn(one, tanh(t)));
-    }
-    case PW_SOFTPLUS: return add_rn(fmax(a, zero), log1p(exp(-fabs(a))));
-    case PW_EXP2: return exp2(a);
-    case PW_SILU: return div_rn(a, add_rn(one, exp(-a)));
     case PW_POW: return pow(a, b);
-    case PW_FLOOR: return floor(a);
-    case PW_CEIL: return ceil(a);
-    case PW_SIGN: return a > zero ? one : (a < zero ? -one : a);   // keeps +-0 and NaN
-    default: return zero;
+    case PW_SOFTPLUS: return add_rn(fmax(a, T(0)), log1p(exp(-fabs(a))));
+    default: return T(0);
   }
+}
+
+// One program step over the VEC lanes of this thread: RD[j] = op(RA[j], RB[j], RC[j]).
+template <typename T, int VEC>
+__device__ __forceinline__ void pw_step(int op, T *RD, const T *RA, const T *RB, const T *RC) {
+  constexpr int S = kPwThreads;
+  const T zero = T(0), one = T(1), half = T(0.5);
+#define PW_LANES(EXPR)                                                              \
+  _Pragma("unroll") for (int j = 0; j < VEC; ++j) {                                 \
+    const T a = RA[j * S], b = RB[j * S], c = RC[j * S];                            \
+    (void)b; (void)c;                                                               \
+    RD[j * S] = (EXPR);                                                             \
+  }                                                                                 \
+  break;
+  switch (op) {
+    case PW_COPY: PW_LANES(a)
+    case PW_ADD: PW_LANES(add_rn(a, b))
+    case PW_SUB: PW_LANES(sub_rn(a, b))
+    case PW_MUL: PW_LANES(mul_rn(a, b))
+    case PW_DIV: PW_LANES(div_rn(a, b))
+    case PW_MAX: PW_LANES(fmax(a, b))       // maxNum, as max.f32 in the reference
+    case PW_MIN: PW_LANES(fmin(a, b))
+    case PW_NEG: PW_LANES(-a)
+    case PW_ABS: PW_LANES(fabs(a))
+    case PW_EXP: PW_LANES(exp(a))
+    case PW_LOG: PW_LANES(log(a))
+    case PW_SQRT: PW_LANES(sqrt_rn(a))
+    case PW_RSQRT: PW_LANES(rsqrt(a))
+    case PW_RECIP: PW_LANES(div_rn(one, a))
+    case PW_TANH: PW_LANES(tanh(a))
+    case PW_SIGMOID: PW_LANES(div_rn(one, add_rn(one, exp(-a))))
+    case PW_RELU: PW_LANES(fmax(a, zero))
+    case PW_GT: PW_LANES(a > b ? one : zero)
+    case PW_LT: PW_LANES(a < b ? one : zero)
+    case PW_GE: PW_LANES(a >= b ? one : zero)
+    case PW_LE: PW_LANES(a <= b ? one : zero)
+    case PW_EQ: PW_LANES(a == b ? one : zero)
+    case PW_WHERE: PW_LANES(a != zero ? b : c)
+    case PW_ROUND_F16: PW_LANES(T(__half2float(__float2half_rn(float(a)))))
+    case PW_FMA: PW_LANES(fma_rn(a, b, c))
+    case PW_GELU_TANH:   // x/2 * (1 + tanh(sqrt(2/pi) * (x + 0.044715 x^3)))
+      PW_LANES(mul_rn(mul_rn(half, a),
+                      add_rn(one, tanh(mul_rn(fma_rn(T(0.044715), mul_rn(mul_rn(a, a), a), a),
+                                              T(0.7978845608028654))))))
+    case PW_EXP2: PW_LANES(exp2(a))
+    case PW_SILU: PW_LANES(div_rn(a, add_rn(one, exp(-a))))
+    case PW_FLOOR: PW_LANES(floor(a))
+    case PW_CEIL: PW_LANES(ceil(a))
+    case PW_SIGN: PW_LANES(a > zero ? one : (a < zero ? -one : a))   // keeps +-0 and NaN
+    default: PW_LANES(pw_slow<T>(op, a, b))
+  }
+#undef PW_LANES
 }
 
 template <typename T> __device__ __forceinline__ T pw_load1(const void *p, int dt, int64_t i) {
@@ -153,59 +172,95 @@ template <typename T> __device__ __forceinline__ void pw_store4(void *p, int dt,
   }
 }
 
-template <typename T, int VEC>
+// NIN >= 0: the input count is a compile-time constant and each thread loads
+// all inputs of G groups before evaluating any of them (G * NIN vector loads
+// in flight per thread).  NIN < 0: any input count, one group at a time.
+template <typename T, int VEC, int NIN, int G>
 __global__ void __launch_bounds__(kPwThreads)
 pointwise_kernel(const PwProgram p, void *out, int out_dtype, int64_t n) {
+  constexpr int S = kPwThreads;
+  constexpr int NI = NIN < 0 ? 1 : (NIN == 0 ? 1 : NIN);
   extern __shared__ __align__(16) unsigned char pw_smem[];
-  T *R = reinterpret_cast<T *>(pw_smem);
-  const int tid = threadIdx.x;
-  auto reg = [&](int r, int j) -> T & { return R[(r * VEC + j) * kPwThreads + tid]; };
+  T *R = reinterpret_cast<T *>(pw_smem) + threadIdx.x;   // register r, lane j at R[(r*VEC+j)*S]
   for (int s = 0; s < p.n_sc; ++s) {
     const T v = pw_load1<T>(p.scalars[s], p.sc_dtype[s], 0);
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) reg(p.n_in + s, j) = v;
+    for (int j = 0; j < VEC; ++j) R[((p.n_in + s) * VEC + j) * S] = v;
   }
   for (int s = 0; s < p.n_imm; ++s) {
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) reg(p.n_in + p.n_sc + s, j) = T(p.imm[s]);
+    for (int j = 0; j < VEC; ++j) R[((p.n_in + p.n_sc + s) * VEC + j) * S] = T(p.imm[s]);
   }
+  const int n_in = NIN < 0 ? p.n_in : NIN;
   const int64_t groups = (n + VEC - 1) / VEC;
-  for (int64_t g = (int64_t)blockIdx.x * kPwThreads + tid; g < groups;
-       g += (int64_t)gridDim.x * kPwThreads) {
-    const int64_t base = g * VEC;
-    const bool full = base + VEC <= n;
-    for (int k = 0; k < p.n_in; ++k) {
-      if (VEC == 4 && full) {
-        T v[4];
-        pw_load4<T>(p.inputs[k], p.in_dtype[k], base, v);
+  const int64_t stride = (int64_t)gridDim.x * S;
+  for (int64_t g0 = (int64_t)blockIdx.x * S + threadIdx.x; g0 < groups; g0 += stride * G) {
+    T v[G][NI][VEC];
+    if (NIN >= 0) {
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) reg(k, j) = v[j];
+      for (int q = 0; q < G; ++q) {
+        const int64_t base = (g0 + q * stride) * VEC;
+#pragma unroll
+        for (int k = 0; k < NI; ++k) {
+          if (k >= NIN) break;
+          if (VEC == 4 && base + VEC <= n) {
+            pw_load4<T>(p.inputs[k], p.in_dtype[k], base, v[q][k]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < VEC; ++j)
+              v[q][k][j] = base + j < n ? pw_load1<T>(p.inputs[k], p.in_dtype[k], base + j) : T(0);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < G; ++q) {
+      const int64_t g = g0 + q * stride;
+      if (g >= groups) break;
+      const int64_t base = g * VEC;
+      const bool full = base + VEC <= n;
+      if (NIN >= 0) {
+#pragma unroll
+        for (int k = 0; k < NI; ++k) {
+          if (k >= NIN) break;
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) R[(k * VEC + j) * S] = v[q][k][j];
+        }
+      } else {
+        for (int k = 0; k < n_in; ++k) {
+          if (VEC == 4 && full) {
+            T w[4];
+            pw_load4<T>(p.inputs[k], p.in_dtype[k], base, w);
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) R[(k * VEC + j) * S] = w[j];
+          } else {
+#pragma unroll
+            for (int j = 0; j < VEC; ++j)
+              R[(k * VEC + j) * S] =
+                  base + j < n ? pw_load1<T>(p.inputs[k], p.in_dtype[k], base + j) : T(0);
+          }
+        }
+      }
+      for (int k = 0; k < p.n_instr; ++k) {
+        const signed char *c = p.code[k];
+        pw_step<T, VEC>(c[0], R + c[1] * VEC * S, R + c[2] * VEC * S, R + c[3] * VEC * S,
+                        R + c[4] * VEC * S);
+      }
+      T o[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) o[j] = R[(p.result_reg * VEC + j) * S];
+      if (VEC == 4 && full) {
+        pw_store4<T>(out, out_dtype, base, o);
       } else {
 #pragma unroll
         for (int j = 0; j < VEC; ++j)
-          reg(k, j) = base + j < n ? pw_load1<T>(p.inputs[k], p.in_dtype[k], base + j) : T(0);
+          if (base + j < n) pw_store1<T>(out, out_dtype, base + j, o[j]);
       }
-    }
-    for (int k = 0; k < p.n_instr; ++k) {
-      const int op = p.code[k][0], d = p.code[k][1], a = p.code[k][2], b = p.code[k][3],
-                c = p.code[k][4];
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) reg(d, j) = pw_eval<T>(op, reg(a, j), reg(b, j), reg(c, j));
-    }
-    T v[VEC];
-#pragma unroll
-    for (int j = 0; j < VEC; ++j) v[j] = reg(p.result_reg, j);
-    if (VEC == 4 && full) {
-      pw_store4<T>(out, out_dtype, base, v);
-    } else {
-#pragma unroll
-      for (int j = 0; j < VEC; ++j)
-        if (base + j < n) pw_store1<T>(out, out_dtype, base + j, v[j]);
     }
   }
 }
 
-template <typename T, int VEC>
+template <typename T, int VEC, int NIN, int G>
 void launch_pointwise(const PwProgram &p, int nregs, void *out, int out_dtype, int64_t n,
                       cudaStream_t st) {
   const int64_t groups = (n + VEC - 1) / VEC;
@@ -215,9 +270,22 @@ void launch_pointwise(const PwProgram &p, int nregs, void *out, int out_dtype, i
   if (blocks > cap) blocks = cap;
   const size_t smem = (size_t)nregs * VEC * kPwThreads * sizeof(T);
   if (smem > 48 * 1024)
-    cudaFuncSetAttribute(pointwise_kernel<T, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-  pointwise_kernel<T, VEC><<<(unsigned)blocks, kPwThreads, smem, st>>>(p, out, out_dtype, n);
+    cudaFuncSetAttribute(pointwise_kernel<T, VEC, NIN, G>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  pointwise_kernel<T, VEC, NIN, G><<<(unsigned)blocks, kPwThreads, smem, st>>>(p, out, out_dtype, n);
+}
+
+template <typename T, int VEC>
+void dispatch_inputs(const PwProgram &p, int nregs, void *out, int out_dtype, int64_t n,
+                     cudaStream_t st) {
+  switch (p.n_in) {
+    case 0: launch_pointwise<T, VEC, 0, 1>(p, nregs, out, out_dtype, n, st); break;
+    case 1: launch_pointwise<T, VEC, 1, 2>(p, nregs, out, out_dtype, n, st); break;
+    case 2: launch_pointwise<T, VEC, 2, 2>(p, nregs, out, out_dtype, n, st); break;
+    case 3: launch_pointwise<T, VEC, 3, 2>(p, nregs, out, out_dtype, n, st); break;
+    case 4: launch_pointwise<T, VEC, 4, 1>(p, nregs, out, out_dtype, n, st); break;
+    default: launch_pointwise<T, VEC, -1, 1>(p, nregs, out, out_dtype, n, st); break;
+  }
 }
 
 }  // namespace emmy
@@ -284,11 +352,11 @@ extern "C" int emmy_pointwise(const void *const *inputs, const int *input_dtypes
   if ((size_t)nregs * 4 * kPwThreads * (compute_f64 ? 8 : 4) > 160 * 1024) vec_ok = false;
   cudaStream_t st = as_stream(stream);
   if (compute_f64) {
-    if (vec_ok) launch_pointwise<double, 4>(p, nregs, out, out_dtype, n, st);
-    else launch_pointwise<double, 1>(p, nregs, out, out_dtype, n, st);
+    if (vec_ok) dispatch_inputs<double, 4>(p, nregs, out, out_dtype, n, st);
+    else dispatch_inputs<double, 1>(p, nregs, out, out_dtype, n, st);
   } else {
-    if (vec_ok) launch_pointwise<float, 4>(p, nregs, out, out_dtype, n, st);
-    else launch_pointwise<float, 1>(p, nregs, out, out_dtype, n, st);
+    if (vec_ok) dispatch_inputs<float, 4>(p, nregs, out, out_dtype, n, st);
+    else dispatch_inputs<float, 1>(p, nregs, out, out_dtype, n, st);
   }
   return check_launch("emmy_pointwise");
 }

@@ -628,6 +628,12 @@ def _f(v, kind):
     return v
 
 
+def _rn32(x64):
+    """Round a float64 result to float32 (one rounding of the exact value when
+    float64 holds it to 2*24+2 bits, as for +, -, *, /, sqrt)."""
+    return x64.to(torch.float32)
+
+
 def _elementwise(opname, args, kinds, kind):
     """One elementwise op in the compute kind (f32 or f64 tensors, int64 or bool)."""
     fl = kind in ("f32", "f64")
@@ -643,6 +649,8 @@ def _elementwise(opname, args, kinds, kind):
     if opname in ("multiply", "prod"):
         return a * b
     if opname in ("divide", "true_divide", "divide_rn_f32"):
+        if kind == "f32":
+            return _rn32(a.double() / b.double())
         return a / b if fl else torch.div(a, b, rounding_mode="trunc")
     if opname in ("maximum", "amax", "max"):
         return torch.maximum(a, b)
@@ -659,11 +667,13 @@ def _elementwise(opname, args, kinds, kind):
     if opname == "log":
         return torch.log(a)
     if opname == "sqrt":
-        return torch.sqrt(a)
+        # sqrt.rn.f32 is correctly rounded; torch's vectorised CPU float32 sqrt
+        # is not always, so round the float64 root (exact for sqrt and divide)
+        return _rn32(torch.sqrt(a.double())) if kind == "f32" else torch.sqrt(a)
     if opname == "rsqrt":
         return torch.rsqrt(a)
     if opname == "reciprocal":
-        return torch.reciprocal(a)
+        return _rn32(1.0 / a.double()) if kind == "f32" else torch.reciprocal(a)
     if opname == "relu":
         return torch.clamp_min(a, 0)
     if opname in ("copy", "pad", "bitcast"):
