@@ -634,6 +634,30 @@ def _rn32(x64):
     return x64.to(torch.float32)
 
 
+def _fma_rn(a, b, c, tdt):
+    """a*b + c rounded once (fma.rn): exact rational sum, then one rounding.
+
+    float64: ``Fraction.__float__`` rounds correctly.  float32: the float64
+    nearest is moved to its odd neighbour when inexact (round-to-odd at 53
+    bits), after which rounding to 24 bits is correct.
+    """
+    from fractions import Fraction
+    a, b, c = torch.broadcast_tensors(a.to(tdt), b.to(tdt), c.to(tdt))
+    av, bv, cv = (t.contiguous().reshape(-1).double().tolist() for t in (a, b, c))
+    out = []
+    for x, y, z in zip(av, bv, cv):
+        if not (math.isfinite(x) and math.isfinite(y) and math.isfinite(z)):
+            out.append(x * y + z)
+            continue
+        exact = Fraction(x) * Fraction(y) + Fraction(z)
+        d = float(exact)
+        if tdt == torch.float32 and Fraction(d) != exact and math.isfinite(d):
+            if np.frombuffer(np.float64(d).tobytes(), np.int64)[0] & 1 == 0:
+                d = float(np.nextafter(d, math.inf if exact > Fraction(d) else -math.inf))
+        out.append(d)
+    return torch.tensor(out, dtype=torch.float64).reshape(a.shape).to(tdt)
+
+
 def _elementwise(opname, args, kinds, kind):
     """One elementwise op in the compute kind (f32 or f64 tensors, int64 or bool)."""
     fl = kind in ("f32", "f64")
@@ -657,7 +681,7 @@ def _elementwise(opname, args, kinds, kind):
     if opname in ("minimum", "min"):
         return torch.minimum(a, b)
     if opname == "fma":
-        return (a.double() * b.double() + args[2].double()).to(tdt)
+        return _fma_rn(a, b, args[2], tdt)
     if opname in ("exp", "exp_fast"):
         if kind == "f64":
             return torch.exp(a)
@@ -667,9 +691,9 @@ def _elementwise(opname, args, kinds, kind):
     if opname == "log":
         return torch.log(a)
     if opname == "sqrt":
-        # sqrt.rn.f32 is correctly rounded; torch's vectorised CPU float32 sqrt
-        # is not always, so round the float64 root (exact for sqrt and divide)
-        return _rn32(torch.sqrt(a.double())) if kind == "f32" else torch.sqrt(a)
+        # sqrt.rn is correctly rounded; torch's vectorised CPU sqrt is not
+        # always (float32 and float64), numpy's is
+        return torch.from_numpy(np.sqrt(a.contiguous().numpy()))
     if opname == "rsqrt":
         return torch.rsqrt(a)
     if opname == "reciprocal":
