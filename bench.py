@@ -519,6 +519,9 @@ PROFILE_CASES = {
     "attention_f16_K5": lambda s: s.attention(8, 32, 512, 128, dtype="f16"),
     "gemm_f32_splitk_K4a": lambda s: s.matmul(256, 256, 65536, splits=64, tm=128, tn=128, rm=8, rn=8),
     "pointwise_add_2^26": lambda s: s.pointwise(1 << 26, ("add", "x0", "x1"), "f32"),
+    "bmm_f16_K3b": lambda s: s.matmul(512, 512, 512, batch=64, dtype="f16", out_dtype="f16",
+                                      tm=128, tn=128, rm=8, rn=8),
+    "rmsnorm_K1": lambda s: s.rmsnorm(4096, 512, eps=1e-6),
     "pointwise_gelu_f16_2^26": lambda s: s.pointwise(1 << 26, ("gelu_tanh", "x0"), "f16"),
 }
 

@@ -8,18 +8,24 @@
 // benchmark configuration asks.
 //
 // One CTA owns 128 query rows of one (batch, head) and walks the keys in
-// blocks of 64; up to D = 128 two CTAs share an SM, so one CTA's softmax runs
-// while the other's tensor-core work does.  Warp roles:
-//   warp 4      TMA producer: Q once, K blocks through a 2-stage ring (one
-//               block ahead), V blocks through one buffer (no multicast;
-//               128-byte swizzled boxes)
-//   warp 5      one thread issues tcgen05.mma: S = Q K^T into TMEM (M128 x 64
-//               keys), then, once P is ready, O += P V into TMEM (M128 x D)
-//   warps 0-3   one query row per thread (TMEM lane): read the 64 scores once,
-//               keep the running max m and sum l (base-2, scale folded in),
-//               rescale the O row in TMEM when the max moves, write P as f16
-//               into swizzled shared memory, and finally store O / l.
-// Every mbarrier wait is bounded and reports through the device status word.
+// blocks of 64; up to D = 128 two CTAs share an SM.  Warp roles:
+//   warp 4      TMA producer: Q once, then K and V blocks through one 3-slot
+//               ring in the order the MMA thread consumes them
+//               (K0, K1, V0, K2, V1, ...; no multicast, 128-byte swizzle)
+//   warp 5      one thread issues tcgen05.mma.  S = Q K^T goes to one of two
+//               TMEM score buffers, one block ahead: S[j+1] is computed while
+//               the softmax warps work on S[j].  O += P V (into TMEM) follows
+//               once P[j] is written.
+//   warps 0-3   one query row per thread (TMEM lane): read the 64 scores,
+//               exponentiate against the running max, write P as f16 into
+//               swizzled shared memory, keep the running sum; finally O / l.
+// The running max is moved lazily: a row keeps its max until a block's max
+// exceeds it by more than 2^8 (so P <= 256, well inside f16), and only then
+// is its O row rescaled in TMEM.  The result is the same softmax; only the
+// rounding differs from rescaling every block.
+// Every mbarrier wait is bounded and reports through the device status word;
+// on a timeout each role stops, in-flight TMA copies and MMAs are waited for
+// (bounded), and TMEM is freed before the CTA exits.
 
 #include "common.cuh"
 #include "tcgen05.cuh"
@@ -30,28 +36,33 @@ template <int D>
 struct AttnCfg {
   static constexpr int BN = 64;                      // keys per block
   static constexpr int NKB = D / 64;                 // 64-wide head-dim blocks of Q and K
-  static constexpr int NVB = D / 64;                 // 64-wide column blocks of V
   static constexpr int Q_BOX = 128 * 128;            // [128 rows][128 B]
   static constexpr int K_BOX = BN * 128;             // [BN keys][128 B]
   static constexpr int Q_BYTES = NKB * Q_BOX;
-  static constexpr int K_BYTES = NKB * K_BOX;
-  static constexpr int V_BYTES = NVB * K_BOX;
+  static constexpr int SLOT_BYTES = NKB * K_BOX;     // one K or V block
+  static constexpr int SLOTS = 3;
   static constexpr int P_BYTES = Q_BOX;              // [128 rows][64 keys] f16
-  static constexpr int K_STAGES = 2;
-  // Q | K stage 0 | K stage 1 | V | P, then the mbarriers
-  static constexpr int BAR_OFF = Q_BYTES + K_STAGES * K_BYTES + V_BYTES + P_BYTES;
+  // Q | ring slots | P, then the mbarriers
+  static constexpr int BAR_OFF = Q_BYTES + SLOTS * SLOT_BYTES + P_BYTES;
   static constexpr int SMEM = BAR_OFF + 128 + 1024;
-  static constexpr uint32_t S_COL = 0;
-  static constexpr uint32_t O_COL = 64;
-  static constexpr uint32_t TMEM_COLS = O_COL + D <= 128 ? 128 : (O_COL + D <= 256 ? 256 : 512);
+  static constexpr uint32_t S_COL0 = 0;              // score buffers at columns 0 and 64
+  static constexpr uint32_t O_COL = 2 * BN;
+  static constexpr uint32_t TMEM_COLS = O_COL + D <= 256 ? 256 : 512;
   static constexpr int THREADS = 192;
-  static constexpr int MIN_BLOCKS = D <= 128 ? 2 : 1;   // two CTAs per SM overlap softmax and MMA
+  static constexpr int MIN_BLOCKS = D <= 128 ? 2 : 1;   // two CTAs per SM
+  static constexpr float RESCALE_LOG2 = 8.0f;        // lazy max threshold (P <= 2^8)
 };
 
 // status codes of the waits that can give up (first one recorded wins)
-constexpr int kAttnWaitQ = 0x1201, kAttnWaitK = 0x1202, kAttnWaitP = 0x1203,
-              kAttnWaitKEmpty = 0x1204, kAttnWaitS = 0x1205, kAttnWaitO = 0x1206,
-              kAttnWaitOFinal = 0x1207, kAttnWaitV = 0x1208, kAttnWaitVEmpty = 0x1209;
+constexpr int kAttnWaitQ = 0x1201, kAttnWaitSlot = 0x1202, kAttnWaitP = 0x1203,
+              kAttnWaitEmpty = 0x1204, kAttnWaitS = 0x1205, kAttnWaitO = 0x1206,
+              kAttnWaitOFinal = 0x1207, kAttnWaitDrain = 0x1208, kAttnWaitMma = 0x1209;
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 template <int D>
 __global__ void __launch_bounds__(192, AttnCfg<D>::MIN_BLOCKS)
@@ -65,13 +76,13 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char *sQ = smem;
-  unsigned char *sK = sQ + C::Q_BYTES;                          // 2 stages
-  unsigned char *sV = sK + C::K_STAGES * C::K_BYTES;
-  unsigned char *sP = sV + C::V_BYTES;
+  unsigned char *sRing = sQ + C::Q_BYTES;
+  unsigned char *sP = sRing + C::SLOTS * C::SLOT_BYTES;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
-  uint64_t *q_full = bars + 0, *s_full = bars + 1, *p_full = bars + 2, *o_full = bars + 3;
-  uint64_t *v_full = bars + 4, *v_empty = bars + 5, *k_full = bars + 6, *k_empty = bars + 8;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 10);
+  uint64_t *q_full = bars + 0, *p_full = bars + 1, *o_full = bars + 2, *mma_done = bars + 3;
+  uint64_t *s_full = bars + 4;                       // [2]
+  uint64_t *full = bars + 6, *empty = bars + 9;      // [SLOTS] each
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 12);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * 128, bh = blockIdx.y;
@@ -82,14 +93,14 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     prefetch_tensormap(&tmK);
     prefetch_tensormap(&tmV);
     mbar_init(q_full, 1);
-    mbar_init(s_full, 1);
     mbar_init(p_full, 128);
     mbar_init(o_full, 1);
-    mbar_init(v_full, 1);
-    mbar_init(v_empty, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
+    mbar_init(mma_done, 1);
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
+    for (int s = 0; s < C::SLOTS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
     }
     fence_barrier_init();
   }
@@ -101,55 +112,79 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
 
   if (warp == 4) {
     if (lane == 0) {
-      // TMA producer.  K runs one block ahead of V: K[j+1] is issued before
-      // V[j] waits for the previous P V product to release the V buffer.
-      auto load_k = [&](int j) -> bool {
-        const int s = j & 1;
-        if (j >= 2 && !mbar_wait(&k_empty[s], ((j >> 1) - 1) & 1, status, kAttnWaitKEmpty))
-          return false;
-        mbar_expect_tx(&k_full[s], C::K_BYTES);
-        for (int kb = 0; kb < C::NKB; ++kb)
-          tma_load_3d(sK + s * C::K_BYTES + kb * C::K_BOX, &tmK, &k_full[s], kb * 64, j * BN, bh);
-        return true;
-      };
+      // TMA producer: ring item i goes to slot i % SLOTS once item i - SLOTS
+      // has been consumed.  Order: K0, then per block j: K[j+1] (if any), V[j].
       mbar_expect_tx(q_full, C::Q_BYTES);
       for (int kb = 0; kb < C::NKB; ++kb)
         tma_load_3d(sQ + kb * C::Q_BOX, &tmQ, q_full, kb * 64, m0, bh);
-      bool ok = load_k(0);
+      int issued = 0;
+      auto load = [&](const CUtensorMap *map, int key_block) -> bool {
+        const int slot = issued % C::SLOTS;
+        if (issued >= C::SLOTS &&
+            !mbar_wait(&empty[slot], ((issued / C::SLOTS) - 1) & 1, status, kAttnWaitEmpty))
+          return false;
+        mbar_expect_tx(&full[slot], C::SLOT_BYTES);
+        for (int kb = 0; kb < C::NKB; ++kb)
+          tma_load_3d(sRing + slot * C::SLOT_BYTES + kb * C::K_BOX, map, &full[slot], kb * 64,
+                      key_block * BN, bh);
+        ++issued;
+        return true;
+      };
+      bool ok = load(&tmK, 0);
       for (int j = 0; ok && j < nblk; ++j) {
-        if (j + 1 < nblk && !load_k(j + 1)) break;
-        if (j >= 1 && !mbar_wait(v_empty, (j - 1) & 1, status, kAttnWaitVEmpty)) break;
-        mbar_expect_tx(v_full, C::V_BYTES);
-        for (int vb = 0; vb < C::NVB; ++vb)
-          tma_load_3d(sV + vb * C::K_BOX, &tmV, v_full, vb * 64, j * BN, bh);
+        if (j + 1 < nblk) ok = load(&tmK, j + 1);
+        if (ok) ok = load(&tmV, j);
       }
+      // drain: every issued copy has landed before the CTA may exit
+      mbar_wait(q_full, 0, status, kAttnWaitDrain);
+      for (int i = issued - C::SLOTS > 0 ? issued - C::SLOTS : 0; i < issued; ++i)
+        mbar_wait(&full[i % C::SLOTS], (i / C::SLOTS) & 1, status, kAttnWaitDrain);
     }
     __syncwarp();
   } else if (warp == 5) {
     if (lane == 0) {
       constexpr uint32_t idesc_s = f16_idesc(128, BN, false, false);
       constexpr uint32_t idesc_o = f16_idesc(128, D, false, true);
-      bool ok = mbar_wait(q_full, 0, status, kAttnWaitQ);
       const uint32_t qa = smem_u32(sQ);
       const uint32_t pa = smem_u32(sP);
-      const uint32_t va = smem_u32(sV);
-      for (int j = 0; ok && j < nblk; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&k_full[s], (j >> 1) & 1, status, kAttnWaitK)) break;
-        tc_fence_after();
-        const uint32_t ka = smem_u32(sK + s * C::K_BYTES);
-        // S = Q K^T: both operands K-major (head dim contiguous)
+      int taken = 0;
+      // next ring item: wait until it has landed, return its shared address
+      auto take = [&](uint32_t &addr) -> bool {
+        const int slot = taken % C::SLOTS;
+        if (!mbar_wait(&full[slot], (taken / C::SLOTS) & 1, status, kAttnWaitSlot)) return false;
+        addr = smem_u32(sRing + slot * C::SLOT_BYTES);
+        return true;
+      };
+      auto release = [&]() { mma_commit(&empty[taken % C::SLOTS]); ++taken; };
+      auto issue_s = [&](int j, uint32_t ka) {
+        // S[j & 1] = Q K^T: both operands K-major (head dim contiguous)
 #pragma unroll
         for (int kb = 0; kb < C::NKB; ++kb)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_f16(tmem + C::S_COL, sw128_desc(qa + kb * C::Q_BOX + kk * 32, 16, 1024),
+            mma_f16(tmem + C::S_COL0 + (j & 1) * BN,
+                    sw128_desc(qa + kb * C::Q_BOX + kk * 32, 16, 1024),
                     sw128_desc(ka + kb * C::K_BOX + kk * 32, 16, 1024), idesc_s,
                     (kb | kk) != 0 ? 1u : 0u);
-        mma_commit(s_full);
-        mma_commit(&k_empty[s]);
-        if (!mbar_wait(p_full, j & 1, status, kAttnWaitP)) break;
-        if (!mbar_wait(v_full, j & 1, status, kAttnWaitV)) break;
+        mma_commit(&s_full[j & 1]);
+      };
+      uint32_t ka = 0, va = 0;
+      bool ok = mbar_wait(q_full, 0, status, kAttnWaitQ) && take(ka);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, ka);
+        release();
+      }
+      for (int j = 0; ok && j < nblk; ++j) {
+        if (j + 1 < nblk) {
+          // S[j+1] into the other buffer: its previous contents (S[j-1]) were
+          // read before P[j-1] was published, which was waited for below
+          if (!take(ka)) break;
+          tc_fence_after();
+          issue_s(j + 1, ka);
+          release();
+        }
+        if (!mbar_wait(p_full, j & 1, status, kAttnWaitP) || !take(va)) break;
         tc_fence_after();
         // O += P V: P K-major over the 64 keys, V N-major (value columns contiguous)
 #pragma unroll
@@ -158,46 +193,67 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                   sw128_desc(va + kk * 16 * 128, C::K_BOX, 1024), idesc_o,
                   (j | kk) != 0 ? 1u : 0u);
         mma_commit(o_full);
-        mma_commit(v_empty);
+        release();
       }
+      // every MMA this thread issued has finished before TMEM is freed
+      mma_commit(mma_done);
+      mbar_wait(mma_done, 0, status, kAttnWaitMma);
     }
     __syncwarp();
   } else {
-    // softmax / correction / epilogue: thread r owns query row m0 + r (TMEM lane r).
+    // softmax / epilogue: thread r owns query row m0 + r (TMEM lane r).
     // Scores are kept as t = s * scale * log2(e), so p = 2^(t - m).
     const int r = threadIdx.x;
     const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
     const float c = (scale_div ? 1.0f / __ldg(scale_div) : 1.0f) * 1.4426950408889634f;
     float m = -INFINITY, l = 0.f;
+    bool ok = true;
     for (int j = 0; j < nblk; ++j) {
-      mbar_wait(s_full, j & 1, status, kAttnWaitS);
-      __syncwarp();
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, status, kAttnWaitS));
+      if (!ok) break;
       tc_fence_after();
       const int key0 = j * BN;
       float t[64];
       {
         float v0[32], v1[32];
-        tmem_ld32(lane_base + C::S_COL, v0);
-        tmem_ld32(lane_base + C::S_COL + 32, v1);
+        tmem_ld32(lane_base + C::S_COL0 + (j & 1) * BN, v0);
+        tmem_ld32(lane_base + C::S_COL0 + (j & 1) * BN + 32, v1);
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          t[i] = key0 + i < S ? v0[i] * c : -INFINITY;
-          t[32 + i] = key0 + 32 + i < S ? v1[i] * c : -INFINITY;
+          t[i] = v0[i] * c;
+          t[32 + i] = v1[i] * c;
+        }
+        if (key0 + BN > S) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (key0 + i >= S) t[i] = -INFINITY;
         }
       }
       float mb = t[0];
 #pragma unroll
       for (int i = 1; i < 64; ++i) mb = fmaxf(mb, t[i]);
-      const float m_new = fmaxf(m, mb);
-      const float alpha = exp2f(m - m_new);
+      // lazy max: move only when the block's max is more than 2^8 above it
+      const bool move = mb > m + C::RESCALE_LOG2;
+      const float m_use = move ? mb : m;
+      const float alpha = move ? ex2_approx(m - mb) : 1.0f;
+      float ps = 0.f;
+      uint32_t h[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float p0 = ex2_approx(t[2 * i] - m_use);
+        const float p1 = ex2_approx(t[2 * i + 1] - m_use);
+        ps += p0 + p1;
+        __half2 hh = __floats2half2_rn(p0, p1);
+        h[i] = *reinterpret_cast<uint32_t *>(&hh);
+      }
       if (j > 0) {
         // P and O are still in use by the previous block's P V product
-        mbar_wait(o_full, (j - 1) & 1, status, kAttnWaitO);
-        __syncwarp();
+        ok = __all_sync(0xffffffffu, mbar_wait(o_full, (j - 1) & 1, status, kAttnWaitO));
+        if (!ok) break;
         tc_fence_after();
         // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp
-        // rescales when any of its rows' max moved (alpha is 1 for the others)
-        if (__any_sync(0xffffffffu, m_new > m)) {
+        // rescales when any of its rows moved its max (alpha is 1 for the others)
+        if (__any_sync(0xffffffffu, move)) {
 #pragma unroll 1
           for (int cc = 0; cc < D / 32; ++cc) {
             float v[32];
@@ -209,16 +265,6 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
           }
         }
       }
-      float ps = 0.f;
-      uint32_t h[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float p0 = exp2f(t[2 * i] - m_new);
-        const float p1 = exp2f(t[2 * i + 1] - m_new);
-        ps += p0 + p1;
-        __half2 hh = __floats2half2_rn(p0, p1);
-        h[i] = *reinterpret_cast<uint32_t *>(&hh);
-      }
       // 64 keys = eight 16-byte chunks of this row's 128-byte line; chunk
       // index XOR (row % 8) is the 128-byte swizzle
       unsigned char *rowp = sP + r * 128;
@@ -227,42 +273,43 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         *reinterpret_cast<uint4 *>(rowp + ((q ^ (r & 7)) * 16)) =
             make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
       l = l * alpha + ps;
-      m = m_new;
+      m = m_use;
       fence_proxy_async();      // P (generic-proxy writes) visible to the tensor core
       tc_fence_before();
       mbar_arrive(p_full);
     }
     // epilogue: O / l
-    mbar_wait(o_full, (nblk - 1) & 1, status, kAttnWaitOFinal);
-    __syncwarp();
-    tc_fence_after();
-    const float rl = 1.0f / l;
-    const int row = m0 + r;
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_full, (nblk - 1) & 1, status, kAttnWaitOFinal));
+    if (ok) {
+      tc_fence_after();
+      const float rl = 1.0f / l;
+      const int row = m0 + r;
 #pragma unroll 1
-    for (int cc = 0; cc < D / 32; ++cc) {
-      float v[32];
-      __syncwarp();   // reconverge after the masked stores of the previous chunk
-      tmem_ld32(lane_base + C::O_COL + cc * 32, v);
-      if (row < S) {
-        const int64_t off = ((int64_t)bh * S + row) * D + cc * 32;
-        if (out_f16) {
-          __half *dst = reinterpret_cast<__half *>(O) + off;
+      for (int cc = 0; cc < D / 32; ++cc) {
+        float v[32];
+        __syncwarp();   // reconverge after the masked stores of the previous chunk
+        tmem_ld32(lane_base + C::O_COL + cc * 32, v);
+        if (row < S) {
+          const int64_t off = ((int64_t)bh * S + row) * D + cc * 32;
+          if (out_f16) {
+            __half *dst = reinterpret_cast<__half *>(O) + off;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint32_t w[4];
+            for (int q = 0; q < 4; ++q) {
+              uint32_t w[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              __half2 hh = __floats2half2_rn(v[8 * q + 2 * i] * rl, v[8 * q + 2 * i + 1] * rl);
-              w[i] = *reinterpret_cast<uint32_t *>(&hh);
+              for (int i = 0; i < 4; ++i) {
+                __half2 hh = __floats2half2_rn(v[8 * q + 2 * i] * rl, v[8 * q + 2 * i + 1] * rl);
+                w[i] = *reinterpret_cast<uint32_t *>(&hh);
+              }
+              *reinterpret_cast<uint4 *>(dst + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
             }
-            *reinterpret_cast<uint4 *>(dst + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
-          }
-        } else {
-          float *dst = reinterpret_cast<float *>(O) + off;
+          } else {
+            float *dst = reinterpret_cast<float *>(O) + off;
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            *reinterpret_cast<float4 *>(dst + 4 * q) =
-                make_float4(v[4 * q] * rl, v[4 * q + 1] * rl, v[4 * q + 2] * rl, v[4 * q + 3] * rl);
+            for (int q = 0; q < 8; ++q)
+              *reinterpret_cast<float4 *>(dst + 4 * q) = make_float4(
+                  v[4 * q] * rl, v[4 * q + 1] * rl, v[4 * q + 2] * rl, v[4 * q + 3] * rl);
+          }
         }
       }
     }

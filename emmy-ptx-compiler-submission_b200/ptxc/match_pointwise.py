@@ -164,6 +164,11 @@ def match_pointwise(kop, tile, meta) -> dict:
         return ref
 
     result = emit(form)
+    if (prog and prog[-1][0] == "round_f16" and dtypes[out] == "f16"
+            and result == ("tmp", len(prog) - 1)):
+        # the f16 store rounds once; rounding to f16 twice gives the same value
+        src = prog.pop()[1][0]
+        result = src
     if result[0] != "tmp":
         prog.append(["copy", [result]])
         result = ("tmp", len(prog) - 1)
