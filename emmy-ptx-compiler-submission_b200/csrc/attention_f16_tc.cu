@@ -213,39 +213,51 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       if (!ok) break;
       tc_fence_after();
       const int key0 = j * BN;
-      float t[64];
-      {
-        float v0[32], v1[32];
-        tmem_ld32(lane_base + C::S_COL0 + (j & 1) * BN, v0);
-        tmem_ld32(lane_base + C::S_COL0 + (j & 1) * BN + 32, v1);
+      // raw scores v; t = v * c is folded into one FFMA below.  With c > 0 the
+      // row max of t is c * max(v), with c < 0 it is c * min(v); masked keys
+      // get the value whose t is -inf.
+      float v[64];
+      tmem_ld64(lane_base + C::S_COL0 + (j & 1) * BN, v);
+      if (key0 + BN > S) {
+        const float far = c > 0.f ? -INFINITY : INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          t[i] = v0[i] * c;
-          t[32 + i] = v1[i] * c;
-        }
-        if (key0 + BN > S) {
-#pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (key0 + i >= S) t[i] = -INFINITY;
-        }
+        for (int i = 0; i < 64; ++i)
+          if (key0 + i >= S) v[i] = far;
       }
-      float mb = t[0];
+      float ext[8];
 #pragma unroll
-      for (int i = 1; i < 64; ++i) mb = fmaxf(mb, t[i]);
+      for (int q = 0; q < 8; ++q) ext[q] = v[q];
+      if (c > 0.f) {
+#pragma unroll
+        for (int i = 8; i < 64; ++i) ext[i & 7] = fmaxf(ext[i & 7], v[i]);
+#pragma unroll
+        for (int w = 4; w >= 1; w >>= 1)
+#pragma unroll
+          for (int q = 0; q < w; ++q) ext[q] = fmaxf(ext[q], ext[q + w]);
+      } else {
+#pragma unroll
+        for (int i = 8; i < 64; ++i) ext[i & 7] = fminf(ext[i & 7], v[i]);
+#pragma unroll
+        for (int w = 4; w >= 1; w >>= 1)
+#pragma unroll
+          for (int q = 0; q < w; ++q) ext[q] = fminf(ext[q], ext[q + w]);
+      }
+      const float mb = ext[0] * c;
       // lazy max: move only when the block's max is more than 2^8 above it
       const bool move = mb > m + C::RESCALE_LOG2;
       const float m_use = move ? mb : m;
       const float alpha = move ? ex2_approx(m - mb) : 1.0f;
-      float ps = 0.f;
+      float psum[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t h[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float p0 = ex2_approx(t[2 * i] - m_use);
-        const float p1 = ex2_approx(t[2 * i + 1] - m_use);
-        ps += p0 + p1;
+        const float p0 = ex2_approx(fmaf(v[2 * i], c, -m_use));
+        const float p1 = ex2_approx(fmaf(v[2 * i + 1], c, -m_use));
+        psum[i & 3] += p0 + p1;
         __half2 hh = __floats2half2_rn(p0, p1);
         h[i] = *reinterpret_cast<uint32_t *>(&hh);
       }
+      const float ps = (psum[0] + psum[1]) + (psum[2] + psum[3]);
       if (j > 0) {
         // P and O are still in use by the previous block's P V product
         ok = __all_sync(0xffffffffu, mbar_wait(o_full, (j - 1) & 1, status, kAttnWaitO));
@@ -256,12 +268,12 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         if (__any_sync(0xffffffffu, move)) {
 #pragma unroll 1
           for (int cc = 0; cc < D / 32; ++cc) {
-            float v[32];
+            float ov[32];
             __syncwarp();
-            tmem_ld32(lane_base + C::O_COL + cc * 32, v);
+            tmem_ld32(lane_base + C::O_COL + cc * 32, ov);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] *= alpha;
-            tmem_st32(lane_base + C::O_COL + cc * 32, v);
+            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+            tmem_st32(lane_base + C::O_COL + cc * 32, ov);
           }
         }
       }
