@@ -156,22 +156,25 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         return true;
       };
       auto release = [&]() { mma_commit(&empty[taken % C::SLOTS]); ++taken; };
+      // descriptors built once; a byte offset d inside a 1024-byte-aligned tile
+      // adds d >> 4 to the start-address field
+      const uint64_t dq = sw128_desc(qa, 16, 1024);
       auto issue_s = [&](int j, uint32_t ka) {
         // S[j & 1] = Q K^T: both operands K-major (head dim contiguous)
+        const uint64_t dk = sw128_desc(ka, 16, 1024);
 #pragma unroll
         for (int kb = 0; kb < C::NKB; ++kb)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_f16(tmem + C::S_COL0 + (j & 1) * BN,
-                    sw128_desc(qa + kb * C::Q_BOX + kk * 32, 16, 1024),
-                    sw128_desc(ka + kb * C::K_BOX + kk * 32, 16, 1024), idesc_s,
-                    (kb | kk) != 0 ? 1u : 0u);
+            mma_f16(tmem + C::S_COL0 + (j & 1) * BN, dq + ((kb * C::Q_BOX + kk * 32) >> 4),
+                    dk + ((kb * C::K_BOX + kk * 32) >> 4), idesc_s, (kb | kk) != 0 ? 1u : 0u);
         mma_commit(&s_full[j & 1]);
       };
       uint32_t ka = 0, va = 0;
+      // Q, K and V come from TMA: their barriers need no tcgen05 fence; P and
+      // the rescaled O come from the softmax threads and do
       bool ok = mbar_wait(q_full, 0, status, kAttnWaitQ) && take(ka);
       if (ok) {
-        tc_fence_after();
         issue_s(0, ka);
         release();
       }
@@ -180,7 +183,6 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
           // S[j+1] into the other buffer: its previous contents (S[j-1]) were
           // read before P[j-1] was published, which was waited for below
           if (!take(ka)) break;
-          tc_fence_after();
           issue_s(j + 1, ka);
           release();
         }

@@ -134,25 +134,37 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
           break;
         tc_fence_after();
         const uint32_t acc = tmem + a * BN;
-        for (int kt = 0; kt < ktiles; ++kt, ++g) {
-          const int s = g % STAGES;
-          if (!mbar_wait(&full[s], (g / STAGES) & 1, status, kStatusGemmTimeout)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
-          const uint32_t sb = sa + A_BYTES;
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
+        // This thread runs only about one MMA ahead of the tensor core, and a
+        // barrier wait between MMAs leaves the pipe empty for ~200 cycles, so
+        // stages are taken two at a time: both waits, then eight MMAs back to
+        // back (each stage is still released as soon as its own four are done).
+        // Shared-memory operands written by TMA need no tcgen05 fence after
+        // their barrier.
+        for (int kt = 0; kt < ktiles; kt += 2) {
+          const int n2 = kt + 1 < ktiles ? 2 : 1;
+          for (int h = 0; h < n2; ++h)
+            if (!mbar_wait(&full[(g + h) % STAGES], ((g + h) / STAGES) & 1, status,
+                           kStatusGemmTimeout)) {
+              ok = false;
+              break;
+            }
+          if (!ok) break;
+          for (int h = 0; h < n2; ++h, ++g) {
+            const int s = g % STAGES;
+            const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+            const uint32_t sb = sa + A_BYTES;
             // A: K-major, 128-byte rows, 8-row atoms 1024 B apart; a K16 step is 32 B
-            const uint64_t da = sw128_desc(sa + kk * 32, 16, 1024);
+            const uint64_t da = sw128_desc(sa, 16, 1024);
             // B: N-major, 64-wide n atoms 8 KB apart, 8-row k atoms 1024 B apart; K16 = 2048 B
-            const uint64_t db = sw128_desc(sb + kk * 2048, B_BOX_BYTES, 1024);
-            mma_f16(acc, da, db, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+            const uint64_t db = sw128_desc(sb, B_BOX_BYTES, 1024);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              mma_f16(acc, da + ((kk * 32) >> 4), db + ((kk * 2048) >> 4), idesc,
+                      (kt + h > 0 || kk > 0) ? 1u : 0u);
+            mma_commit(&empty[s]);
           }
-          mma_commit(&empty[s]);
         }
+        if (!ok) break;
         mma_commit(&acc_full[a]);
       }
     }
