@@ -46,26 +46,44 @@ def test_table_matches_reference_files():
 
 @pytest.mark.parametrize("fid", replicas.replica_ids())
 def test_replica_declares_fixture_inputs(fid):
-    _, meta = replicas.build(fid)
-    assert replicas.same_inputs(fid, meta)
+    _, meta, names = replicas.build(fid)
+    assert replicas.same_inputs(fid, meta, names)
+
+
+def test_every_fixture_has_a_replica():
+    assert replicas.replica_ids() == sorted(replicas.table())
 
 
 @pytest.mark.parametrize("fid", replicas.replica_ids())
 def test_oracle_on_replica_reproduces_golden(fid):
-    kop, meta = replicas.build(fid)
-    out = run_ir(kop, meta, make_inputs(meta))[replicas.table()[fid]["output"]]
+    kop, meta, names = replicas.build(fid)
+    host = replicas.fixture_inputs(fid, meta, names)
+    out_name = next(a["name"] for a in meta["args"] if a.get("output"))
+    out = run_ir(kop, meta, host)[out_name]
     worst, msg = replicas.compare(fid, out)
     assert worst <= 0, msg
+
+
+def _plan_key(plan):
+    fam = plan["family"]
+    if fam == "pointwise":
+        return plan["pointwise"]
+    if fam in ("reduce", "rownorm", "softmax", "matvec"):
+        return plan["view"], plan.get("params")
+    if fam.startswith("gemm"):
+        g = plan["gemm"]
+        return {k: g[k] for k in ("batch", "m", "n", "k", "epilogue")}
+    if fam.startswith("attention"):
+        return plan["attention"]
+    return None
 
 
 @needs_reference
 @pytest.mark.parametrize("fid", replicas.replica_ids())
 def test_replica_plans_like_the_fixture(fid):
-    kop, meta = replicas.build(fid)
+    kop, meta, _ = replicas.build(fid)
     mine = Lowerer(kop, meta).plan()
     fkop, fmeta, _ = load_variant(REFERENCE_VARIANTS / fid)
     theirs = Lowerer(fkop, fmeta["kernels"][-1]).plan()
     assert mine["family"] == theirs["family"]
-    key = {"pointwise": "pointwise"}.get(mine["family"])
-    if key:
-        assert mine[key] == theirs[key]
+    assert _plan_key(mine) == _plan_key(theirs)
