@@ -59,6 +59,63 @@ __device__ __forceinline__ TileCoord gemm16_tile(int t, int mt, int nt) {
   return {m * BM, n * BN, b};
 }
 
+// One thread's accumulator row (its TMEM lane, 256 columns from `base`):
+// bias, ReLU, convert, store.  tcgen05.ld is warp-collective, so every lane
+// runs every chunk and only the stores are masked.
+__device__ __forceinline__ void gemm16_drain_row(uint32_t base, int row, TileCoord tc, int M,
+                                                 int N, int ktiles, const float *__restrict__ bias,
+                                                 bool add_bias, bool relu, int out_f16,
+                                                 void *__restrict__ C, int64_t c_batch_stride) {
+#pragma unroll 1
+  for (int c = 0; c < 256 / 32; ++c) {
+    float v[32];
+    __syncwarp();   // reconverge after the masked stores of the previous chunk
+    tmem_ld32(base + c * 32, v);
+    const int n = tc.n0 + c * 32;
+    if (row >= M || n >= N) continue;
+    if (ktiles == 0) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] = 0.f;
+    }
+    if (add_bias) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] += (n + k < N) ? __ldg(bias + n + k) : 0.f;
+    }
+    if (relu) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] = fmaxf(v[k], 0.f);
+    }
+    const int64_t off = (int64_t)tc.b * c_batch_stride + (int64_t)row * N + n;
+    if (out_f16) {
+      __half *dst = reinterpret_cast<__half *>(C) + off;
+      if (n + 32 <= N) {
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          uint32_t w[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            __half2 hh = __floats2half2_rn(v[8 * p + 2 * k], v[8 * p + 2 * k + 1]);
+            w[k] = *reinterpret_cast<uint32_t *>(&hh);
+          }
+          *reinterpret_cast<uint4 *>(dst + 8 * p) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      } else {
+        for (int k = 0; k < 32 && n + k < N; ++k) dst[k] = __float2half_rn(v[k]);
+      }
+    } else {
+      float *dst = reinterpret_cast<float *>(C) + off;
+      if (n + 32 <= N) {
+#pragma unroll
+        for (int p = 0; p < 8; ++p)
+          *reinterpret_cast<float4 *>(dst + 4 * p) =
+              make_float4(v[4 * p], v[4 * p + 1], v[4 * p + 2], v[4 * p + 3]);
+      } else {
+        for (int k = 0; k < 32 && n + k < N; ++k) dst[k] = v[k];
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(gemm16::THREADS, 1)
 gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const float *__restrict__ bias, void *__restrict__ C, int M, int N, int K,
@@ -182,56 +239,8 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
       if (!mbar_wait(&acc_full[a], (i >> 1) & 1, status, kStatusGemmTimeout)) break;
       __syncwarp();
       tc_fence_after();
-      const int row = tc.m0 + q * 32 + lane;
-      const uint32_t base = tmem + lane_off + a * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        __syncwarp();   // tcgen05.ld is warp-collective: reconverge after the masked stores
-        tmem_ld32(base + c * 32, v);
-        const int n = tc.n0 + c * 32;
-        if (row >= M || n >= N) continue;
-        if (ktiles == 0) {
-#pragma unroll
-          for (int k = 0; k < 32; ++k) v[k] = 0.f;
-        }
-        if (add_bias) {
-#pragma unroll
-          for (int k = 0; k < 32; ++k) v[k] += (n + k < N) ? __ldg(bias + n + k) : 0.f;
-        }
-        if (relu) {
-#pragma unroll
-          for (int k = 0; k < 32; ++k) v[k] = fmaxf(v[k], 0.f);
-        }
-        const int64_t off = (int64_t)tc.b * c_batch_stride + (int64_t)row * N + n;
-        if (out_f16) {
-          __half *dst = reinterpret_cast<__half *>(C) + off;
-          if (n + 32 <= N) {
-#pragma unroll
-            for (int p = 0; p < 4; ++p) {
-              uint32_t w[4];
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                __half2 hh = __floats2half2_rn(v[8 * p + 2 * k], v[8 * p + 2 * k + 1]);
-                w[k] = *reinterpret_cast<uint32_t *>(&hh);
-              }
-              *reinterpret_cast<uint4 *>(dst + 8 * p) = make_uint4(w[0], w[1], w[2], w[3]);
-            }
-          } else {
-            for (int k = 0; k < 32 && n + k < N; ++k) dst[k] = __float2half_rn(v[k]);
-          }
-        } else {
-          float *dst = reinterpret_cast<float *>(C) + off;
-          if (n + 32 <= N) {
-#pragma unroll
-            for (int p = 0; p < 8; ++p)
-              *reinterpret_cast<float4 *>(dst + 4 * p) =
-                  make_float4(v[4 * p], v[4 * p + 1], v[4 * p + 2], v[4 * p + 3]);
-          } else {
-            for (int k = 0; k < 32 && n + k < N; ++k) dst[k] = v[k];
-          }
-        }
-      }
+      gemm16_drain_row(tmem + lane_off + a * BN, tc.m0 + q * 32 + lane, tc, M, N, ktiles,
+                       bias, add_bias, relu, out_f16, C, c_batch_stride);
       // the accumulator's TMEM reads are complete (tcgen05.wait::ld in tmem_ld32)
       tc_fence_before();
       __syncwarp();
@@ -241,6 +250,188 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant (tcgen05.mma.cta_group::2): the two CTAs of a cluster own a
+// 256 x 256 output tile.  Each CTA stages its own 128 rows of A and its own
+// 128 columns of B; one thread of CTA 0 issues M256 N256 K16 MMAs that read
+// both CTAs' operands, and each CTA's tensor memory receives its 128 rows of
+// the accumulator.  Per SM this halves the shared-memory operand traffic of
+// the 128 x 256 single-CTA tile (which is shared-memory-bandwidth bound), and
+// each CTA loads half of B.
+//   warp 0 (both CTAs)   TMA producer for its own halves; transaction bytes
+//                        are counted on CTA 0's stage barrier (no multicast)
+//   warp 1 (CTA 0)       MMA issuer; stage and accumulator releases are
+//                        committed to the barrier in each CTA
+//   warps 2-5 (both)     epilogue of the CTA's 128 rows; the accumulator is
+//                        handed back on CTA 0's barrier (8 arrivals)
+
+namespace gemm16p {
+constexpr int BM = 256, BMH = 128, BN = 256, BNH = 128, BK = 64, STAGES = 6, THREADS = 192;
+constexpr int A_BYTES = BMH * BK * 2;                // 16 KB: this CTA's rows
+constexpr int B_BOX_BYTES = BK * 64 * 2;             // 8 KB
+constexpr int B_BYTES = BK * BNH * 2;                // 16 KB: this CTA's columns
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+constexpr uint32_t TMEM_COLS = 512;                  // two 256-column accumulators
+constexpr int GROUP_N = 8;
+constexpr int kStatusGemmTimeout = 0x1102;
+}  // namespace gemm16p
+
+__device__ __forceinline__ TileCoord gemm16p_tile(int t, int mt, int nt) {
+  using namespace gemm16p;
+  const int per_batch = mt * nt;
+  const int b = t / per_batch;
+  int r = t - b * per_batch;
+  const int group = r / (mt * GROUP_N);
+  const int first_n = group * GROUP_N;
+  r -= group * mt * GROUP_N;
+  const int m = r % mt;
+  const int n = first_n + r / mt;
+  return {m * BM, n * BN, b};
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm16p::THREADS, 1)
+gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB, const float *__restrict__ bias,
+                     void *__restrict__ C, int M, int N, int K, int batch, int64_t c_batch_stride,
+                     int out_f16, int epilogue, int *status) {
+  using namespace gemm16p;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[STAGES];
+  __shared__ __align__(8) uint64_t empty[STAGES];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ __align__(8) uint64_t mma_done;
+  __shared__ uint32_t tmem_holder;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const int mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
+  const int tiles = mt * nt * batch;
+  const int ktiles = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmB);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 8);      // four epilogue warps in each CTA
+    }
+    mbar_init(&mma_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc_pair(&tmem_holder, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();       // both CTAs' barriers exist before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem = tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int t = cluster; ok && t < tiles; t += nclusters) {
+        const TileCoord tc = gemm16p_tile(t, mt, nt);
+        for (int kt = 0; kt < ktiles; ++kt, ++g) {
+          const int s = g % STAGES;
+          if (g >= STAGES &&
+              !mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, status, kStatusGemmTimeout)) {
+            ok = false;
+            break;
+          }
+          unsigned char *sa = smem + s * STAGE_BYTES;
+          unsigned char *sb = sa + A_BYTES;
+          if (rank == 0) mbar_expect_tx(&full[s], 2 * STAGE_BYTES);
+          const uint32_t leader_full = mapa_shared(smem_u32(&full[s]), 0);
+          tma_load_3d_pair(sa, &tmA, leader_full, kt * BK, tc.m0 + BMH * (int)rank, tc.b);
+#pragma unroll
+          for (int j = 0; j < BNH / 64; ++j)
+            tma_load_3d_pair(sb + j * B_BOX_BYTES, &tmB, leader_full,
+                             tc.n0 + BNH * (int)rank + 64 * j, kt * BK, tc.b);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = f16_idesc(BM, BN, false, true);
+      int g = 0, i = 0;
+      bool ok = true;
+      for (int t = cluster; ok && t < tiles; t += nclusters, ++i) {
+        const int a = i & 1;
+        if (i >= 2 && !mbar_wait(&acc_empty[a], ((i >> 1) - 1) & 1, status, kStatusGemmTimeout))
+          break;
+        tc_fence_after();
+        const uint32_t acc = tmem + a * BN;
+        // two stages per barrier wait, then eight MMAs back to back; each stage
+        // is released to both CTAs' producers as soon as its own four are done
+        for (int kt = 0; kt < ktiles; kt += 2) {
+          const int n2 = kt + 1 < ktiles ? 2 : 1;
+          for (int h = 0; h < n2; ++h)
+            if (!mbar_wait(&full[(g + h) % STAGES], ((g + h) / STAGES) & 1, status,
+                           kStatusGemmTimeout)) {
+              ok = false;
+              break;
+            }
+          if (!ok) break;
+          for (int h = 0; h < n2; ++h, ++g) {
+            const int s = g % STAGES;
+            const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+            const uint64_t da = sw128_desc(sa, 16, 1024);
+            const uint64_t db = sw128_desc(sa + A_BYTES, B_BOX_BYTES, 1024);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              mma_f16_pair(acc, da + ((kk * 32) >> 4), db + ((kk * 2048) >> 4), idesc,
+                           (kt + h > 0 || kk > 0) ? 1u : 0u);
+            mma_commit_pair(smem_u32(&empty[s]));
+            mma_commit_pair(mapa_shared(smem_u32(&empty[s]), 1));
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair(smem_u32(&acc_full[a]));
+        mma_commit_pair(mapa_shared(smem_u32(&acc_full[a]), 1));
+      }
+      // every MMA issued has finished before the pair's tensor memory is freed
+      mma_commit_pair(smem_u32(&mma_done));
+      mbar_wait(&mma_done, 0, status, kStatusGemmTimeout);
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const bool relu = epilogue & EMMY_EPI_RELU;
+    const bool add_bias = (epilogue & EMMY_EPI_BIAS) && bias != nullptr;
+    int i = 0;
+    for (int t = cluster; t < tiles; t += nclusters, ++i) {
+      const int a = i & 1;
+      const TileCoord tc = gemm16p_tile(t, mt, nt);
+      if (!mbar_wait(&acc_full[a], (i >> 1) & 1, status, kStatusGemmTimeout)) break;
+      __syncwarp();
+      tc_fence_after();
+      gemm16_drain_row(tmem + lane_off + a * BN, tc.m0 + BMH * (int)rank + q * 32 + lane, tc, M,
+                       N, ktiles, bias, add_bias, relu, out_f16, C, c_batch_stride);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0) mbar_arrive(&acc_empty[a]);
+        else mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[a]), 0));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();       // the peer is done with the pair's TMEM and barriers
+  if (warp == 0) tmem_dealloc_pair(tmem, TMEM_COLS);
 }
 
 // CUDA-core fallback for shapes the TMA descriptors cannot take (K or N not a
@@ -333,7 +524,20 @@ extern "C" int emmy_gemm_f16(const void *A, const void *B, const float *bias, vo
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
       cudaFuncSetAttribute(gemm_f16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            SMEM_BYTES);
+      cudaFuncSetAttribute(gemm_f16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           gemm16p::SMEM_BYTES);
       attr_set[dev] = true;
+    }
+    if (M >= gemm16p::BM) {
+      // CTA pairs: 256 x 256 tiles, one cluster of two CTAs per two SMs
+      const int64_t ptiles = ((M + gemm16p::BM - 1) / gemm16p::BM) *
+                             ((N + gemm16p::BN - 1) / gemm16p::BN) * batch;
+      const int64_t pairs = sm_count() / 2;
+      const int clusters = (int)(ptiles < pairs ? ptiles : pairs);
+      gemm_f16_pair_kernel<<<2 * clusters, gemm16p::THREADS, gemm16p::SMEM_BYTES, st>>>(
+          ta, tb, bias, C, (int)M, (int)N, (int)K, (int)batch, M * N, out_f16, epilogue,
+          device_status_ptr());
+      return check_launch("emmy_gemm_f16 (tcgen05 pair)");
     }
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
     gemm_f16_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, bias, C, (int)M, (int)N, (int)K,
