@@ -273,7 +273,9 @@ constexpr int A_BYTES = BMH * BK * 2;                // 16 KB: this CTA's rows
 constexpr int B_BOX_BYTES = BK * 64 * 2;             // 8 KB
 constexpr int B_BYTES = BK * BNH * 2;                // 16 KB: this CTA's columns
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+constexpr int OUT_BOX_BYTES = 32 * 128;              // one warp's 32 rows x 128 B of C
+constexpr int OUT_BYTES = 4 * 2 * OUT_BOX_BYTES;     // 4 epilogue warps, double-buffered
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + 1024;
 constexpr uint32_t TMEM_COLS = 512;                  // two 256-column accumulators
 constexpr int GROUP_N = 8;
 constexpr int kStatusGemmTimeout = 0x1102;
@@ -292,9 +294,80 @@ __device__ __forceinline__ TileCoord gemm16p_tile(int t, int mt, int nt) {
   return {m * BM, n * BN, b};
 }
 
+// One epilogue warp's 32 accumulator rows (TMEM lanes), 256 columns: bias,
+// ReLU, convert, then stage 128-byte row pieces (64 f16 or 32 f32 columns) in
+// shared memory with the 128-byte swizzle and write each 32-row box with one
+// TMA store.  Coalesced writes, and TMA drops rows and columns outside C.
+// Two staging buffers per warp: a buffer is refilled once the store issued
+// from it two chunks earlier has finished reading it.
+__device__ __forceinline__ void gemm16_drain_warp_tma(uint32_t tbase, int lane, int row0,
+                                                      TileCoord tc, int N,
+                                                      const float *__restrict__ bias,
+                                                      bool add_bias, bool relu, int out_f16,
+                                                      const CUtensorMap *tmC,
+                                                      unsigned char *stage, int &seq) {
+  const int step = out_f16 ? 64 : 32;                // columns per 128-byte row piece
+#pragma unroll 1
+  for (int c0 = 0; c0 < 256; c0 += step, ++seq) {
+    unsigned char *buf = stage + (seq & 1) * gemm16p::OUT_BOX_BYTES;
+    if (seq >= 2 && lane == 0) bulk_wait_group_read<1>();
+    __syncwarp();
+    const int n = tc.n0 + c0;
+    uint4 w[8];
+    if (out_f16) {
+      float v[64];
+      tmem_ld64(tbase + c0, v);
+      if (add_bias) {
+#pragma unroll
+        for (int k = 0; k < 64; ++k) v[k] += (n + k < N) ? __ldg(bias + n + k) : 0.f;
+      }
+      if (relu) {
+#pragma unroll
+        for (int k = 0; k < 64; ++k) v[k] = fmaxf(v[k], 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t h[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          __half2 hh = __floats2half2_rn(v[8 * j + 2 * k], v[8 * j + 2 * k + 1]);
+          h[k] = *reinterpret_cast<uint32_t *>(&hh);
+        }
+        w[j] = make_uint4(h[0], h[1], h[2], h[3]);
+      }
+    } else {
+      float v[32];
+      tmem_ld32(tbase + c0, v);
+      if (add_bias) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) v[k] += (n + k < N) ? __ldg(bias + n + k) : 0.f;
+      }
+      if (relu) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) v[k] = fmaxf(v[k], 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        w[j] = make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
+                          __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
+    }
+    // row `lane` of the box: 16-byte piece j at (j ^ (lane % 8)) * 16
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<uint4 *>(buf + lane * 128 + ((j ^ (lane & 7)) * 16)) = w[j];
+    fence_proxy_async();                             // visible to the TMA (async proxy)
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(tmC, buf, n, row0, tc.b);
+      bulk_commit_group();
+    }
+  }
+}
+
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm16p::THREADS, 1)
 gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
-                     const __grid_constant__ CUtensorMap tmB, const float *__restrict__ bias,
+                     const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, const float *__restrict__ bias,
                      void *__restrict__ C, int M, int N, int K, int batch, int64_t c_batch_stride,
                      int out_f16, int epilogue, int *status) {
   using namespace gemm16p;
@@ -318,6 +391,7 @@ gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tmA);
     prefetch_tensormap(&tmB);
+    prefetch_tensormap(&tmC);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -411,15 +485,17 @@ gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     const bool relu = epilogue & EMMY_EPI_RELU;
     const bool add_bias = (epilogue & EMMY_EPI_BIAS) && bias != nullptr;
-    int i = 0;
+    unsigned char *stage = smem + STAGES * STAGE_BYTES + q * 2 * OUT_BOX_BYTES;
+    int i = 0, seq = 0;
     for (int t = cluster; t < tiles; t += nclusters, ++i) {
       const int a = i & 1;
       const TileCoord tc = gemm16p_tile(t, mt, nt);
       if (!mbar_wait(&acc_full[a], (i >> 1) & 1, status, kStatusGemmTimeout)) break;
       __syncwarp();
       tc_fence_after();
-      gemm16_drain_row(tmem + lane_off + a * BN, tc.m0 + BMH * (int)rank + q * 32 + lane, tc, M,
-                       N, ktiles, bias, add_bias, relu, out_f16, C, c_batch_stride);
+      gemm16_drain_warp_tma(tmem + lane_off + a * BN, lane, tc.m0 + BMH * (int)rank + q * 32, tc,
+                            N, bias, add_bias, relu, out_f16, &tmC, stage, seq);
+      // the accumulator's TMEM reads are complete (tcgen05.wait::ld)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -427,6 +503,8 @@ gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
         else mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[a]), 0));
       }
     }
+    if (lane == 0) bulk_wait_group<0>();             // this warp's stores have landed
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -529,13 +607,23 @@ extern "C" int emmy_gemm_f16(const void *A, const void *B, const float *bias, vo
       attr_set[dev] = true;
     }
     if (M >= gemm16p::BM) {
-      // CTA pairs: 256 x 256 tiles, one cluster of two CTAs per two SMs
+      // CTA pairs: 256 x 256 tiles, one cluster of two CTAs per two SMs; C is
+      // written by TMA stores of 32-row x 128-byte boxes
       const int64_t ptiles = ((M + gemm16p::BM - 1) / gemm16p::BM) *
                              ((N + gemm16p::BN - 1) / gemm16p::BN) * batch;
       const int64_t pairs = sm_count() / 2;
       const int clusters = (int)(ptiles < pairs ? ptiles : pairs);
+      const uint64_t esize = out_f16 ? 2 : 4;
+      CUtensorMap tc_map;
+      const uint64_t cdims[3] = {(uint64_t)N, (uint64_t)M, (uint64_t)batch};
+      const uint64_t cstr[2] = {(uint64_t)N * esize, (uint64_t)M * N * esize};
+      const uint32_t cbox[3] = {(uint32_t)(128 / esize), 32, 1};
+      rc = make_tensor_map(&tc_map, out_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                           3, C, cdims, cstr, cbox, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
       gemm_f16_pair_kernel<<<2 * clusters, gemm16p::THREADS, gemm16p::SMEM_BYTES, st>>>(
-          ta, tb, bias, C, (int)M, (int)N, (int)K, (int)batch, M * N, out_f16, epilogue,
+          ta, tb, tc_map, bias, C, (int)M, (int)N, (int)K, (int)batch, M * N, out_f16, epilogue,
           device_status_ptr());
       return check_launch("emmy_gemm_f16 (tcgen05 pair)");
     }
