@@ -68,7 +68,8 @@ template <int D>
 __global__ void __launch_bounds__(192, AttnCfg<D>::MIN_BLOCKS)
 attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
-                        const __grid_constant__ CUtensorMap tmV, void *__restrict__ O,
+                        const __grid_constant__ CUtensorMap tmV,
+                        const __grid_constant__ CUtensorMap tmO,
                         const float *__restrict__ scale_div, int S, int out_f16, int *status) {
   using C = AttnCfg<D>;
   constexpr int BN = C::BN;
@@ -292,40 +293,55 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    // epilogue: O / l
+    // epilogue: O / l, staged through shared memory (the Q and ring space,
+    // free once every MMA is done) in 32-row x 128-byte swizzled boxes and
+    // written by TMA stores; rows beyond S are dropped by the TMA
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_full, (nblk - 1) & 1, status, kAttnWaitOFinal));
     if (ok) {
       tc_fence_after();
       const float rl = 1.0f / l;
-      const int row = m0 + r;
+      unsigned char *stage = smem + warp * 2 * 4096;   // two 4 KB boxes per warp
+      const int step = out_f16 ? 64 : 32;               // columns per 128-byte row piece
+      int seq = 0;
 #pragma unroll 1
-      for (int cc = 0; cc < D / 32; ++cc) {
-        float v[32];
-        __syncwarp();   // reconverge after the masked stores of the previous chunk
-        tmem_ld32(lane_base + C::O_COL + cc * 32, v);
-        if (row < S) {
-          const int64_t off = ((int64_t)bh * S + row) * D + cc * 32;
-          if (out_f16) {
-            __half *dst = reinterpret_cast<__half *>(O) + off;
+      for (int c0 = 0; c0 < D; c0 += step, ++seq) {
+        unsigned char *buf = stage + (seq & 1) * 4096;
+        if (seq >= 2 && lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        uint4 w[8];
+        if (out_f16) {
+          float v[64];
+          tmem_ld64(lane_base + C::O_COL + c0, v);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint32_t w[4];
+          for (int j = 0; j < 8; ++j) {
+            uint32_t h[4];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                __half2 hh = __floats2half2_rn(v[8 * q + 2 * i] * rl, v[8 * q + 2 * i + 1] * rl);
-                w[i] = *reinterpret_cast<uint32_t *>(&hh);
-              }
-              *reinterpret_cast<uint4 *>(dst + 8 * q) = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int i = 0; i < 4; ++i) {
+              __half2 hh = __floats2half2_rn(v[8 * j + 2 * i] * rl, v[8 * j + 2 * i + 1] * rl);
+              h[i] = *reinterpret_cast<uint32_t *>(&hh);
             }
-          } else {
-            float *dst = reinterpret_cast<float *>(O) + off;
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-              *reinterpret_cast<float4 *>(dst + 4 * q) = make_float4(
-                  v[4 * q] * rl, v[4 * q + 1] * rl, v[4 * q + 2] * rl, v[4 * q + 3] * rl);
+            w[j] = make_uint4(h[0], h[1], h[2], h[3]);
           }
+        } else {
+          float v[32];
+          tmem_ld32(lane_base + C::O_COL + c0, v);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            w[j] = make_uint4(__float_as_uint(v[4 * j] * rl), __float_as_uint(v[4 * j + 1] * rl),
+                              __float_as_uint(v[4 * j + 2] * rl), __float_as_uint(v[4 * j + 3] * rl));
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          *reinterpret_cast<uint4 *>(buf + lane * 128 + ((j ^ (lane & 7)) * 16)) = w[j];
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&tmO, buf, c0, m0 + warp * 32, bh);
+          bulk_commit_group();
         }
       }
+      if (lane == 0) bulk_wait_group<0>();
+      __syncwarp();
     }
   }
   tc_fence_before();
@@ -406,6 +422,14 @@ int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   if (!rc) rc = make_tensor_map(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, v, dims, str, kbox,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
+  // O written by TMA stores of 32-row x 128-byte boxes
+  CUtensorMap to;
+  const uint64_t esize = out_f16 ? 2 : 4;
+  const uint64_t ostr[2] = {(uint64_t)D * esize, (uint64_t)S * D * esize};
+  const uint32_t obox[3] = {(uint32_t)(128 / esize), 32, 1};
+  if (!rc) rc = make_tensor_map(&to, out_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                                3, o, dims, ostr, obox, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -417,7 +441,7 @@ int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
   }
   dim3 grid((unsigned)((S + 127) / 128), (unsigned)batch);
   attention_f16_tc_kernel<D><<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(
-      tq, tk, tv, o, scale_div, (int)S, out_f16, device_status_ptr());
+      tq, tk, tv, to, scale_div, (int)S, out_f16, device_status_ptr());
   return check_launch("emmy_attention_f16 (tcgen05)");
 }
 
