@@ -234,17 +234,22 @@ extern "C" int emmy_gemm_f32(const float *A, const float *B, const float *bias, 
   cudaStream_t st = as_stream(stream);
   const int sms = sm_count();
   const int64_t mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
-  // split count: the caller's, or enough K partitions to give every SM two tiles
+  // split count: the caller's, or enough K partitions to give every SM two
+  // tiles.  A caller's split-K (> 1) whose grid would leave SMs short of two
+  // CTAs is widened to fill them: the partials meet in atomic adds either way,
+  // so only the (unordered) summation grouping changes.
   int sp = splits;
-  if (sp <= 0) {
+  const int64_t tiles_mn = mt * nt * batch;
+  if (sp <= 0 || (sp > 1 && tiles_mn * sp < 2 * sms)) {
+    const int want = sp;
     sp = 1;
-    const int64_t tiles = mt * nt * batch;
-    if (!accumulate && tiles < 2 * sms) {
-      sp = (int)((2 * sms + tiles - 1) / tiles);
+    if (!accumulate && tiles_mn < 2 * sms) {
+      sp = (int)((2 * sms + tiles_mn - 1) / tiles_mn);
       const int64_t kt = (K + BK - 1) / BK;
       if (sp > kt) sp = (int)(kt > 0 ? kt : 1);
       if (sp > 256) sp = 256;
     }
+    if (sp < want) sp = want;
   }
   int64_t kps = (K + sp - 1) / sp;
   kps = (kps + BK - 1) / BK * BK;
