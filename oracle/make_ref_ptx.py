@@ -1,0 +1,89 @@
+"""Emit the reference compiler's own PTX for every reference fixture and the
+benchmark configurations (test infrastructure; run where the reference
+checkout exists).
+
+The reference is a Python compiler whose only missing piece is the
+``emmy-ml`` package (``requirements.txt:1``); ``oracle/emmy_shim`` supplies the
+``emmy`` modules it imports on top of this repository's IR classes.  The
+reference's ``compile.py`` then runs **unmodified** as a subprocess, one
+kernel package per call (``compile.py:70-106``), and its PTX (``.target sm_89``
+by default, ``ptxc/lower.py:599``; the driver JIT-compiles it for sm_100) is
+written with the package's ``meta.json`` into ``oracle/_ref/<name>/``.  That
+directory is git-ignored and travels to the GPU box, where
+``oracle/ref_ptx.py`` loads and launches the PTX exactly as the reference
+harness does (``tools/localrun.py:102-142``).
+
+Usage: ``python oracle/make_ref_ptx.py [REFERENCE_DIR]``.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import shutil
+import subprocess
+import sys
+import tempfile
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parent
+PKG = ROOT / "emmy-ptx-compiler-submission_b200"
+OUT = HERE / "_ref"
+
+# benchmark configurations (the bench's family cases) as synthesised IR
+BENCH_CASES = {
+    "K1_rmsnorm": lambda s: s.rmsnorm(4096, 512, eps=1e-6),
+    "K2a_softmax": lambda s: s.softmax([32, 16, 512, 512]),
+    "K2b_layernorm": lambda s: s.layernorm(16384, 1024),
+    "K4b_matvec_f64": lambda s: s.matvec(16384, 16384),
+    "K4a_splitk_f32": lambda s: s.matmul(256, 256, 65536, splits=64, tm=128, tn=128, rm=8, rn=8),
+    "K3a_gemm_f16": lambda s: s.matmul(4096, 8192, 2048, dtype="f16", out_dtype="f16", bias=True,
+                                       relu=True, tm=128, tn=128, rm=8, rn=8),
+    "K3b_bmm_f16": lambda s: s.matmul(512, 512, 512, batch=64, dtype="f16", out_dtype="f16",
+                                      tm=128, tn=128, rm=8, rn=8),
+    "K5_attention_f16": lambda s: s.attention(8, 32, 512, 128, dtype="f16"),
+    "F8a_pointwise_add": lambda s: s.pointwise(1 << 26, ("add", "x0", "x1"), "f32"),
+}
+
+
+def _compile(ref: Path, ir_path: Path):
+    env = dict(os.environ)
+    env["PYTHONPATH"] = os.pathsep.join([str(ref), str(HERE / "emmy_shim"), str(PKG)])
+    r = subprocess.run([sys.executable, str(ref / "compile.py"), str(ir_path)], env=env,
+                       capture_output=True, text=True, timeout=600)
+    return r.returncode, r.stdout, r.stderr.strip()
+
+
+def main(ref: Path) -> int:
+    sys.path[:0] = [str(PKG)]
+    from emmy_ir import synth
+    from emmy_ir.serialize import write_package
+    OUT.mkdir(exist_ok=True)
+    jobs = []
+    for d in sorted(p for p in (ref / "tests" / "variants").iterdir() if (p / "meta.json").exists()):
+        jobs.append((d.name, next(d.glob("*.ir.json")), d / "meta.json"))
+    tmp = Path(tempfile.mkdtemp(prefix="emmy_ref_"))
+    for name, make in BENCH_CASES.items():
+        kop, meta = make(synth)
+        ir = write_package(tmp / name, kop, meta)
+        jobs.append((name, ir, tmp / name / "meta.json"))
+    report = {}
+    for name, ir, meta in jobs:
+        rc, ptx, err = _compile(ref, ir)
+        dst = OUT / name
+        if dst.exists():
+            shutil.rmtree(dst)
+        dst.mkdir()
+        shutil.copy(meta, dst / "meta.json")
+        if rc == 0:
+            (dst / "kernel.ptx").write_text(ptx)
+        report[name] = {"rc": rc, "error": err.splitlines()[-1] if err else ""}
+        print(f"{name}: rc {rc} {report[name]['error']}")
+    (OUT / "report.json").write_text(json.dumps(report, indent=1, sort_keys=True) + "\n")
+    shutil.rmtree(tmp, ignore_errors=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")))
