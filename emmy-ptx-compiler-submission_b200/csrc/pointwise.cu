@@ -72,10 +72,10 @@ template <typename T> __device__ __noinline__ T pw_slow(int op, T a, T b) {
   }
 }
 
-// One program step over the VEC lanes of this thread: RD[j] = op(RA[j], RB[j], RC[j]).
-template <typename T, int VEC>
+// One program step over the VEC lanes of this thread: RD[j*S] = op(RA[j*S], ...),
+// S the lane stride (the shared-memory register file's, or 1 for registers).
+template <typename T, int VEC, int S = kPwThreads>
 __device__ __forceinline__ void pw_step(int op, T *RD, const T *RA, const T *RB, const T *RC) {
-  constexpr int S = kPwThreads;
   const T zero = T(0), one = T(1), half = T(0.5);
 #define PW_LANES(EXPR)                                                              \
   _Pragma("unroll") for (int j = 0; j < VEC; ++j) {                                 \
@@ -260,14 +260,115 @@ pointwise_kernel(const PwProgram p, void *out, int out_dtype, int64_t n) {
   }
 }
 
+template <typename T>
+__device__ __forceinline__ void pw_step_lane(int op, T *RD, const T *RA, const T *RB, const T *RC) {
+  pw_step<T, 1, 1>(op, RD, RA, RB, RC);
+}
+
+// One-step programs (the commonest pointwise shape: x op y, x op c, op x):
+// operands straight from the loaded registers, no shared register file.
+// Operand kinds: 0 = input tensor, 1 = one-element scalar tensor, 2 = immediate.
+struct PwSimple {
+  const void *ptr[3];
+  int dtype[3];
+  int kind[3];
+  double imm[3];
+  int nops, op;
+};
+
+template <typename T>
+__device__ __forceinline__ void pw_simple_operand_f32(const PwSimple &q, int k, int64_t base,
+                                                      bool full, int64_t n, T v[4]) {
+  if (q.kind[k] == 0) {
+    const float *p = static_cast<const float *>(q.ptr[k]) + base;
+    if (full) {
+      const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
+      v[0] = T(a.x); v[1] = T(a.y); v[2] = T(a.z); v[3] = T(a.w);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = base + j < n ? T(p[j]) : T(0);
+    }
+  } else {
+    const T c = q.kind[k] == 1 ? T(*static_cast<const float *>(q.ptr[k])) : T(q.imm[k]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = c;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void pw_simple_operand(const PwSimple &q, int k, int64_t base, bool full,
+                                                  int64_t n, T v[4]) {
+  if (q.kind[k] == 0) {
+    if (full) {
+      pw_load4<T>(q.ptr[k], q.dtype[k], base, v);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = base + j < n ? pw_load1<T>(q.ptr[k], q.dtype[k], base + j) : T(0);
+    }
+  } else {
+    const T c = q.kind[k] == 1 ? pw_load1<T>(q.ptr[k], q.dtype[k], 0) : T(q.imm[k]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = c;
+  }
+}
+
+// OPC >= 0 fixes the op at compile time (the six arithmetic ops) and F32IO
+// fixes every tensor operand and the output to f32: a small kernel that stays
+// at full occupancy.  OPC < 0 dispatches q.op at run time.
+template <typename T, int OPC, bool F32IO>
+__global__ void __launch_bounds__(kPwThreads)
+pointwise_simple_kernel(const PwSimple q, void *out, int out_dtype, int64_t n) {
+  const int64_t groups = (n + 3) / 4;
+  const int64_t stride = (int64_t)gridDim.x * kPwThreads;
+  for (int64_t g = (int64_t)blockIdx.x * kPwThreads + threadIdx.x; g < groups; g += stride) {
+    const int64_t base = g * 4;
+    const bool full = base + 4 <= n;
+    T a[4], b[4], c[4];
+    if (F32IO) {
+      pw_simple_operand_f32(q, 0, base, full, n, a);
+      if (q.nops > 1) pw_simple_operand_f32(q, 1, base, full, n, b);
+      if (q.nops > 2) pw_simple_operand_f32(q, 2, base, full, n, c);
+    } else {
+      pw_simple_operand<T>(q, 0, base, full, n, a);
+      if (q.nops > 1) pw_simple_operand<T>(q, 1, base, full, n, b);
+      if (q.nops > 2) pw_simple_operand<T>(q, 2, base, full, n, c);
+    }
+    T o[4];
+    // pw_step on single lanes: registers in place of the shared-memory file
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      T ra[1] = {a[j]}, rb[1] = {q.nops > 1 ? b[j] : T(0)}, rc[1] = {q.nops > 2 ? c[j] : T(0)}, rd[1];
+      pw_step_lane<T>(OPC >= 0 ? OPC : q.op, rd, ra, rb, rc);
+      o[j] = rd[0];
+    }
+    if (F32IO) {
+      float *dst = static_cast<float *>(out) + base;
+      if (full) {
+        *reinterpret_cast<float4 *>(dst) = make_float4(float(o[0]), float(o[1]), float(o[2]), float(o[3]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (base + j < n) dst[j] = float(o[j]);
+      }
+    } else if (full) {
+      pw_store4<T>(out, out_dtype, base, o);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (base + j < n) pw_store1<T>(out, out_dtype, base + j, o[j]);
+    }
+  }
+}
+
 template <typename T, int VEC, int NIN, int G>
 void launch_pointwise(const PwProgram &p, int nregs, void *out, int out_dtype, int64_t n,
                       cudaStream_t st) {
   const int64_t groups = (n + VEC - 1) / VEC;
-  int64_t blocks = (groups + kPwThreads - 1) / kPwThreads;
-  // enough resident blocks to cover HBM latency; the grid-stride loop does the rest
-  const int64_t cap = (int64_t)sm_count() * 8;
-  if (blocks > cap) blocks = cap;
+  // one pass: each thread takes G groups (their loads issued together) and the
+  // grid covers the data once -- many short CTAs keep every SM streaming to
+  // the end, where a capped grid-stride loop ran slower on B200
+  int64_t blocks = (groups + (int64_t)kPwThreads * G - 1) / ((int64_t)kPwThreads * G);
+  if (blocks > INT32_MAX) blocks = INT32_MAX;          // the grid-stride loop covers the rest
   const size_t smem = (size_t)nregs * VEC * kPwThreads * sizeof(T);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(pointwise_kernel<T, VEC, NIN, G>,
@@ -351,6 +452,55 @@ extern "C" int emmy_pointwise(const void *const *inputs, const int *input_dtypes
   // would not fit; such programs run one element per thread
   if ((size_t)nregs * 4 * kPwThreads * (compute_f64 ? 8 : 4) > 160 * 1024) vec_ok = false;
   cudaStream_t st = as_stream(stream);
+  const int nleaf = n_inputs + n_scalars + n_imm;
+  if (vec_ok && n_instr == 1 && result_reg == nleaf) {
+    // one step on leaves only: the register kernel
+    const int op = program[0];
+    const int arity = (op == PW_WHERE || op == PW_FMA) ? 3
+                      : (op == PW_ADD || op == PW_SUB || op == PW_MUL || op == PW_DIV ||
+                         op == PW_MAX || op == PW_MIN || op == PW_GT || op == PW_LT ||
+                         op == PW_GE || op == PW_LE || op == PW_EQ || op == PW_POW)
+                          ? 2
+                          : 1;
+    PwSimple q{};
+    q.op = op;
+    q.nops = arity;
+    for (int k = 0; k < arity; ++k) {
+      const int r = program[2 + k];
+      if (r < n_inputs) {
+        q.kind[k] = 0; q.ptr[k] = inputs[r]; q.dtype[k] = input_dtypes[r];
+      } else if (r < n_inputs + n_scalars) {
+        q.kind[k] = 1; q.ptr[k] = scalars[r - n_inputs]; q.dtype[k] = scalar_dtypes[r - n_inputs];
+      } else {
+        q.kind[k] = 2; q.imm[k] = immediates[r - n_inputs - n_scalars];
+      }
+    }
+    int64_t blocks = ((n + 3) / 4 + kPwThreads - 1) / kPwThreads;
+    if (blocks > INT32_MAX) blocks = INT32_MAX;
+    const unsigned gb = (unsigned)blocks;
+    bool f32io = !compute_f64 && out_dtype == EMMY_DT_F32;
+    for (int k = 0; k < arity; ++k)
+      if (q.kind[k] != 2 && q.dtype[k] != EMMY_DT_F32) f32io = false;
+#define EMMY_PW_LAUNCH(T, OPC, IO) \
+    pointwise_simple_kernel<T, OPC, IO><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n)
+    if (f32io) {
+      switch (op) {
+        case PW_ADD: EMMY_PW_LAUNCH(float, PW_ADD, true); break;
+        case PW_SUB: EMMY_PW_LAUNCH(float, PW_SUB, true); break;
+        case PW_MUL: EMMY_PW_LAUNCH(float, PW_MUL, true); break;
+        case PW_DIV: EMMY_PW_LAUNCH(float, PW_DIV, true); break;
+        case PW_MAX: EMMY_PW_LAUNCH(float, PW_MAX, true); break;
+        case PW_MIN: EMMY_PW_LAUNCH(float, PW_MIN, true); break;
+        default: EMMY_PW_LAUNCH(float, -1, true); break;
+      }
+    } else if (compute_f64) {
+      EMMY_PW_LAUNCH(double, -1, false);
+    } else {
+      EMMY_PW_LAUNCH(float, -1, false);
+    }
+#undef EMMY_PW_LAUNCH
+    return check_launch("emmy_pointwise (one step)");
+  }
   if (compute_f64) {
     if (vec_ok) dispatch_inputs<double, 4>(p, nregs, out, out_dtype, n, st);
     else dispatch_inputs<double, 1>(p, nregs, out, out_dtype, n, st);
