@@ -225,6 +225,18 @@ def run(plan: dict, tensors: dict, stream=None, workspace=None, check: bool = Tr
     return launches
 
 
+_PIPE = {}
+
+
+def _pipe_streams(device):
+    """The upload, kernel and download streams ``Executor.run_pipelined`` uses on ``device``."""
+    import torch
+    key = torch.device(device).index
+    if key not in _PIPE:
+        _PIPE[key] = tuple(torch.cuda.Stream(device=device) for _ in range(3))
+    return _PIPE[key]
+
+
 class Executor:
     """Device buffers for one plan, reused across calls (H2D -> kernel -> D2H)."""
 
@@ -253,6 +265,86 @@ class Executor:
 
     def launch(self, stream=None) -> int:
         return run(self.plan, self.tensors, stream=stream, workspace=self.workspace, check=False)
+
+    def inputs(self) -> list:
+        """Plan tensors the kernels read.
+
+        Outputs are written whole (or zeroed first, ``zero_outputs``) and are
+        not read -- except the C of a split-K matmul whose atomic partial sums
+        add onto what C already holds (``gemm.accumulate``).
+        """
+        outs = set(self.plan["outputs"])
+        if self.plan.get("gemm", {}).get("accumulate"):
+            outs.discard(self.plan["args"]["c"])
+        return [n for n in self.plan["tensors"] if n not in outs]
+
+    def run_pipelined(self, host: dict, out: dict, chunks: int | None = None, stream=None,
+                      join: bool = True) -> int:
+        """Host inputs in, host outputs out, with the copies overlapping the kernels.
+
+        The plan is split into ``chunks`` independent sub-plans along its own
+        shard axis (rows, batches, heads or element ranges, as ``ptxc.dist``
+        shards it across GPUs).  Chunk i's inputs go up on one stream while
+        chunk i-1 computes on a second and chunk i-2's outputs come down on a
+        third, so both PCIe directions and the kernels run at once; tensors
+        every chunk reads whole (weights, scalars) go up once, first.  Outputs
+        are written whole by the kernels and never uploaded.  ``chunks``
+        defaults to one per ~32 MiB of input.  ``host``/``out`` tensors should
+        be pinned for the copies to be asynchronous.
+
+        Ordered after ``stream`` (default: the current stream).  The three
+        streams are shared by every Executor on the device, so consecutive
+        calls with ``join=False`` queue behind one another without a stall;
+        the last call of a step passes ``join=True`` (the default), which makes
+        ``stream`` wait for every download.  Returns the library launches.
+        """
+        import torch
+        from .dist import shard_plan
+        cur = stream if stream is not None else torch.cuda.current_stream(self.device)
+        s_in, s_k, s_out = _pipe_streams(self.device)
+        outs = set(self.plan["outputs"])
+        ins = self.inputs()
+        if chunks is None:
+            in_bytes = sum(self.tensors[n].numel() * self.tensors[n].element_size() for n in ins)
+            chunks = max(1, min(64, -(-in_bytes // (32 << 20))))
+        try:
+            subs = [shard_plan(self.plan, i, chunks) for i in range(chunks)] if chunks > 1 else None
+        except ValueError:
+            subs = None
+        if subs is None:
+            subs = [(self.plan, {n: (0, t.numel()) for n, t in self.tensors.items()})]
+        full = {n for n in ins if all(sl[n] == (0, self.tensors[n].numel()) for _, sl in subs)}
+        for s in (s_in, s_k, s_out):
+            s.wait_stream(cur)
+        flat = {n: torch.as_tensor(host[n]).reshape(-1) for n in ins}
+        launches = 0
+        with torch.cuda.stream(s_in):
+            for n in full:
+                self.tensors[n].copy_(flat[n], non_blocking=True)
+        for sub, sl in subs:
+            with torch.cuda.stream(s_in):
+                for n in ins:
+                    if n not in full:
+                        off, cnt = sl[n]
+                        self.tensors[n][off:off + cnt].copy_(flat[n][off:off + cnt],
+                                                             non_blocking=True)
+                ev_in = torch.cuda.Event()
+                ev_in.record(s_in)
+            s_k.wait_event(ev_in)
+            views = {n: self.tensors[n][sl[n][0]:sl[n][0] + sl[n][1]] for n in self.plan["tensors"]}
+            launches += run(sub, views, stream=s_k, workspace=self.workspace, check=False)
+            ev_k = torch.cuda.Event()
+            ev_k.record(s_k)
+            s_out.wait_event(ev_k)
+            with torch.cuda.stream(s_out):
+                for n in outs:
+                    if n in out:
+                        off, cnt = sl[n]
+                        out[n].reshape(-1)[off:off + cnt].copy_(self.tensors[n][off:off + cnt],
+                                                                non_blocking=True)
+        if join:
+            cur.wait_stream(s_out)
+        return launches
 
     def download(self, names=None, out=None) -> dict:
         names = list(names or self.plan["outputs"])
