@@ -334,6 +334,35 @@ def family_extras(device, peak):
             else:
                 out[name]["frac_tensor"] = round(tf / tensor_peak()[0], 3)
         del ex
+    # the matmul + bias + ReLU package at the K3a size: two kernels (product
+    # written as f16, then bias + ReLU) against the fused epilogue launch
+    from ptxc.package import Chain, ChainExecutor
+    chain = Chain.from_kernels(synth.mm_bias_relu_chain(
+        4096, 8192, 2048, dtype="f16", c_dtype="f16", out_dtype="f16", tm=128, tn=128, rm=8, rn=8))
+    row = {}
+    for fuse in (True, False):
+        ex = ChainExecutor(chain, device=device, fuse=fuse)
+        for t in ex.buffers.values():
+            t.normal_(std=0.02)
+        for _ in range(3):
+            ex.launch()
+        times = []
+        for _ in range(10):
+            flush()
+            torch.cuda._sleep(SPIN_CYCLES)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            n = ex.launch()
+            e1.record()
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        ms = statistics.median(times)
+        key = "fused" if fuse else "two_launches"
+        row[key + "_us"] = round(ms * 1000, 2)
+        row[key + "_launches"] = n
+        row[key + "_tflops"] = round(2.0 * 4096 * 8192 * 2048 / (ms * 1e-3) / 1e12, 2)
+        del ex
+    out["F2_chain_mm_bias_relu_f16_4096x2048x8192"] = row
     del flush
     torch.cuda.empty_cache()
     return out

@@ -64,8 +64,9 @@ __device__ __forceinline__ TileCoord gemm16_tile(int t, int mt, int nt) {
 // runs every chunk and only the stores are masked.
 __device__ __forceinline__ void gemm16_drain_row(uint32_t base, int row, TileCoord tc, int M,
                                                  int N, int ktiles, const float *__restrict__ bias,
-                                                 bool add_bias, bool relu, int out_f16,
-                                                 void *__restrict__ C, int64_t c_batch_stride) {
+                                                 bool add_bias, bool relu, bool round16,
+                                                 int out_f16, void *__restrict__ C,
+                                                 int64_t c_batch_stride) {
 #pragma unroll 1
   for (int c = 0; c < 256 / 32; ++c) {
     float v[32];
@@ -76,6 +77,10 @@ __device__ __forceinline__ void gemm16_drain_row(uint32_t base, int row, TileCoo
     if (ktiles == 0) {
 #pragma unroll
       for (int k = 0; k < 32; ++k) v[k] = 0.f;
+    }
+    if (round16) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] = __half2float(__float2half_rn(v[k]));
     }
     if (add_bias) {
 #pragma unroll
@@ -231,6 +236,7 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
     const int q = warp & 3;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     const bool relu = epilogue & EMMY_EPI_RELU;
+    const bool round16 = epilogue & EMMY_EPI_ROUND_F16;
     const bool add_bias = (epilogue & EMMY_EPI_BIAS) && bias != nullptr;
     int i = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
@@ -240,7 +246,7 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
       __syncwarp();
       tc_fence_after();
       gemm16_drain_row(tmem + lane_off + a * BN, tc.m0 + q * 32 + lane, tc, M, N, ktiles,
-                       bias, add_bias, relu, out_f16, C, c_batch_stride);
+                       bias, add_bias, relu, round16, out_f16, C, c_batch_stride);
       // the accumulator's TMEM reads are complete (tcgen05.wait::ld in tmem_ld32)
       tc_fence_before();
       __syncwarp();
@@ -303,8 +309,8 @@ __device__ __forceinline__ TileCoord gemm16p_tile(int t, int mt, int nt) {
 __device__ __forceinline__ void gemm16_drain_warp_tma(uint32_t tbase, int lane, int row0,
                                                       TileCoord tc, int N,
                                                       const float *__restrict__ bias,
-                                                      bool add_bias, bool relu, int out_f16,
-                                                      const CUtensorMap *tmC,
+                                                      bool add_bias, bool relu, bool round16,
+                                                      int out_f16, const CUtensorMap *tmC,
                                                       unsigned char *stage, int &seq) {
   const int step = out_f16 ? 64 : 32;                // columns per 128-byte row piece
 #pragma unroll 1
@@ -317,6 +323,10 @@ __device__ __forceinline__ void gemm16_drain_warp_tma(uint32_t tbase, int lane, 
     if (out_f16) {
       float v[64];
       tmem_ld64(tbase + c0, v);
+      if (round16) {
+#pragma unroll
+        for (int k = 0; k < 64; ++k) v[k] = __half2float(__float2half_rn(v[k]));
+      }
       if (add_bias) {
 #pragma unroll
         for (int k = 0; k < 64; ++k) v[k] += (n + k < N) ? __ldg(bias + n + k) : 0.f;
@@ -338,6 +348,10 @@ __device__ __forceinline__ void gemm16_drain_warp_tma(uint32_t tbase, int lane, 
     } else {
       float v[32];
       tmem_ld32(tbase + c0, v);
+      if (round16) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) v[k] = __half2float(__float2half_rn(v[k]));
+      }
       if (add_bias) {
 #pragma unroll
         for (int k = 0; k < 32; ++k) v[k] += (n + k < N) ? __ldg(bias + n + k) : 0.f;
@@ -484,6 +498,7 @@ gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
     const int q = warp & 3;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     const bool relu = epilogue & EMMY_EPI_RELU;
+    const bool round16 = epilogue & EMMY_EPI_ROUND_F16;
     const bool add_bias = (epilogue & EMMY_EPI_BIAS) && bias != nullptr;
     unsigned char *stage = smem + STAGES * STAGE_BYTES + q * 2 * OUT_BOX_BYTES;
     int i = 0, seq = 0;
@@ -494,7 +509,7 @@ gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
       __syncwarp();
       tc_fence_after();
       gemm16_drain_warp_tma(tmem + lane_off + a * BN, lane, tc.m0 + BMH * (int)rank + q * 32, tc,
-                            N, bias, add_bias, relu, out_f16, &tmC, stage, seq);
+                            N, bias, add_bias, relu, round16, out_f16, &tmC, stage, seq);
       // the accumulator's TMEM reads are complete (tcgen05.wait::ld)
       tc_fence_before();
       __syncwarp();
@@ -548,6 +563,7 @@ gemm_f16_plain_kernel(const __half *__restrict__ A, const __half *__restrict__ B
       const int n = n0 + tx + 16 * j;
       if (n >= N) continue;
       float v = acc[i][j];
+      if (epilogue & EMMY_EPI_ROUND_F16) v = __half2float(__float2half_rn(v));
       if ((epilogue & EMMY_EPI_BIAS) && bias) v += bias[n];
       if (epilogue & EMMY_EPI_RELU) v = fmaxf(v, 0.f);
       const int64_t off = (int64_t)b * sc + (int64_t)m * N + n;
@@ -574,6 +590,8 @@ extern "C" int emmy_gemm_f16(const void *A, const void *B, const float *bias, vo
     return set_error(EMMY_ERR_INVALID, "emmy_gemm_f16: bad output dtype %d", out_dtype);
   if (accumulate)
     return set_error(EMMY_ERR_UNSUPPORTED, "emmy_gemm_f16: accumulating into C is not supported");
+  if (epilogue & ~(EMMY_EPI_BIAS | EMMY_EPI_RELU | EMMY_EPI_ROUND_F16))
+    return set_error(EMMY_ERR_INVALID, "emmy_gemm_f16: unknown epilogue bits %d", epilogue);
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || batch > 65535)
     return set_error(EMMY_ERR_UNSUPPORTED, "emmy_gemm_f16: size beyond 32-bit tile indexing");
   cudaStream_t st = as_stream(stream);

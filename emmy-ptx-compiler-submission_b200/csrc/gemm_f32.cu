@@ -229,6 +229,8 @@ extern "C" int emmy_gemm_f32(const float *A, const float *B, const float *bias, 
   if (!A || !B || !C) return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32: null operand");
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || batch > 65535)
     return set_error(EMMY_ERR_UNSUPPORTED, "emmy_gemm_f32: size beyond 32-bit tile indexing");
+  if (epilogue & ~(EMMY_EPI_BIAS | EMMY_EPI_RELU))
+    return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32: unknown epilogue bits %d", epilogue);
   if ((epilogue & EMMY_EPI_RELU) && (splits > 1 || accumulate))
     return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32: relu cannot follow a partial sum");
   cudaStream_t st = as_stream(stream);

@@ -16,6 +16,8 @@
 // the output move as 16-byte (f32, f64) or 8-byte (f16) vectors when every
 // pointer allows it; HBM traffic is then the algorithmic minimum.
 
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace emmy {
@@ -29,7 +31,35 @@ enum PwOp {
   PW_GELU_TANH, PW_SOFTPLUS, PW_EXP2, PW_SILU, PW_POW, PW_FLOOR, PW_CEIL, PW_SIGN, PW_NOPS
 };
 
+// A broadcast input is read at ((first + e) / div) % mod for element e (mod
+// 0: no modulo).  The quotients use the round-up multiply-shift method for
+// division by an invariant integer (Granlund & Montgomery, PLDI 1994, fig.
+// 4.1): q = (t + ((x - t) >> 1)) >> (l - 1), t = mulhi(magic, x), l =
+// ceil(log2 d), magic = floor(2^64 (2^l - d) / d) + 1; exact for all 64-bit x.
+struct PwDiv {
+  unsigned long long d, magic;
+  int shift;                       // l - 1; -1 when d == 1
+};
+
+struct PwIndex {
+  PwDiv div, mod;
+  int bcast;                       // 0: input read at e (contiguous)
+  int has_mod;
+};
+
+__host__ __device__ inline unsigned long long pw_div(const PwDiv &v, unsigned long long x) {
+#ifdef __CUDA_ARCH__
+  if (v.shift < 0) return x;
+  const unsigned long long t = __umul64hi(v.magic, x);
+  return (t + ((x - t) >> 1)) >> v.shift;
+#else
+  return x / v.d;
+#endif
+}
+
 struct PwProgram {
+  PwIndex idx[kPwMaxIn];
+  long long first;
   const void *inputs[kPwMaxIn];
   const void *scalars[kPwMaxIn];
   int in_dtype[kPwMaxIn];
@@ -175,7 +205,42 @@ template <typename T> __device__ __forceinline__ void pw_store4(void *p, int dt,
 // NIN >= 0: the input count is a compile-time constant and each thread loads
 // all inputs of G groups before evaluating any of them (G * NIN vector loads
 // in flight per thread).  NIN < 0: any input count, one group at a time.
-template <typename T, int VEC, int NIN, int G>
+// Element e of broadcast input k.
+template <typename T> __device__ __forceinline__ T pw_load_bcast(const PwProgram &p, int k, int64_t e) {
+  const PwIndex &x = p.idx[k];
+  unsigned long long q = pw_div(x.div, (unsigned long long)(p.first + e));
+  if (x.has_mod) q -= pw_div(x.mod, q) * x.mod.d;
+  return pw_load1<T>(p.inputs[k], p.in_dtype[k], (int64_t)q);
+}
+
+// Elements e .. e+VEC-1 of broadcast input k: one quotient per group, the
+// other lanes step from it (the quotient moves by at most one per lane when
+// div >= VEC; smaller divisors divide per lane).
+template <typename T, int VEC>
+__device__ __forceinline__ void pw_load_bcast_vec(const PwProgram &p, int k, int64_t e, int64_t n,
+                                                  T v[VEC]) {
+  const PwIndex &x = p.idx[k];
+  if (VEC == 1 || x.div.d < (unsigned long long)VEC) {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) v[j] = e + j < n ? pw_load_bcast<T>(p, k, e + j) : T(0);
+    return;
+  }
+  const unsigned long long x0 = (unsigned long long)(p.first + e);
+  const unsigned long long q0 = pw_div(x.div, x0);
+  const unsigned long long r0 = x0 - q0 * x.div.d;
+  unsigned long long m0 = q0;
+  if (x.has_mod) m0 = q0 - pw_div(x.mod, q0) * x.mod.d;
+  unsigned long long m1 = m0 + 1;
+  if (x.has_mod && m1 == x.mod.d) m1 = 0;
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) {
+    const unsigned long long idx = r0 + j < x.div.d ? m0 : m1;
+    v[j] = e + j < n ? pw_load1<T>(p.inputs[k], p.in_dtype[k], (int64_t)idx) : T(0);
+  }
+}
+
+// BC: some inputs are broadcast (read through PwIndex).
+template <typename T, int VEC, int NIN, int G, bool BC = false>
 __global__ void __launch_bounds__(kPwThreads)
 pointwise_kernel(const PwProgram p, void *out, int out_dtype, int64_t n) {
   constexpr int S = kPwThreads;
@@ -203,7 +268,9 @@ pointwise_kernel(const PwProgram p, void *out, int out_dtype, int64_t n) {
 #pragma unroll
         for (int k = 0; k < NI; ++k) {
           if (k >= NIN) break;
-          if (VEC == 4 && base + VEC <= n) {
+          if (BC && p.idx[k].bcast) {
+            pw_load_bcast_vec<T, VEC>(p, k, base, n, v[q][k]);
+          } else if (VEC == 4 && base + VEC <= n) {
             pw_load4<T>(p.inputs[k], p.in_dtype[k], base, v[q][k]);
           } else {
 #pragma unroll
@@ -228,7 +295,12 @@ pointwise_kernel(const PwProgram p, void *out, int out_dtype, int64_t n) {
         }
       } else {
         for (int k = 0; k < n_in; ++k) {
-          if (VEC == 4 && full) {
+          if (BC && p.idx[k].bcast) {
+            T w[VEC];
+            pw_load_bcast_vec<T, VEC>(p, k, base, n, w);
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) R[(k * VEC + j) * S] = w[j];
+          } else if (VEC == 4 && full) {
             T w[4];
             pw_load4<T>(p.inputs[k], p.in_dtype[k], base, w);
 #pragma unroll
@@ -258,11 +330,6 @@ pointwise_kernel(const PwProgram p, void *out, int out_dtype, int64_t n) {
       }
     }
   }
-}
-
-template <typename T>
-__device__ __forceinline__ void pw_step_lane(int op, T *RD, const T *RA, const T *RB, const T *RC) {
-  pw_step<T, 1, 1>(op, RD, RA, RB, RC);
 }
 
 // One-step programs (the commonest pointwise shape: x op y, x op c, op x):
@@ -333,14 +400,19 @@ pointwise_simple_kernel(const PwSimple q, void *out, int out_dtype, int64_t n) {
       if (q.nops > 1) pw_simple_operand<T>(q, 1, base, full, n, b);
       if (q.nops > 2) pw_simple_operand<T>(q, 2, base, full, n, c);
     }
-    T o[4];
-    // pw_step on single lanes: registers in place of the shared-memory file
+    if (q.nops < 2) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      T ra[1] = {a[j]}, rb[1] = {q.nops > 1 ? b[j] : T(0)}, rc[1] = {q.nops > 2 ? c[j] : T(0)}, rd[1];
-      pw_step_lane<T>(OPC >= 0 ? OPC : q.op, rd, ra, rb, rc);
-      o[j] = rd[0];
+      for (int j = 0; j < 4; ++j) b[j] = T(0);
     }
+    if (q.nops < 3) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) c[j] = T(0);
+    }
+    // one dispatch for the four lanes (registers in place of the shared-memory
+    // file, lane stride 1): a per-lane dispatch would unroll four copies of
+    // every op's code and run out of instruction cache
+    T o[4];
+    pw_step<T, 4, 1>(OPC >= 0 ? OPC : q.op, o, a, b, c);
     if (F32IO) {
       float *dst = static_cast<float *>(out) + base;
       if (full) {
@@ -360,7 +432,7 @@ pointwise_simple_kernel(const PwSimple q, void *out, int out_dtype, int64_t n) {
   }
 }
 
-template <typename T, int VEC, int NIN, int G>
+template <typename T, int VEC, int NIN, int G, bool BC = false>
 void launch_pointwise(const PwProgram &p, int nregs, void *out, int out_dtype, int64_t n,
                       cudaStream_t st) {
   const int64_t groups = (n + VEC - 1) / VEC;
@@ -371,14 +443,22 @@ void launch_pointwise(const PwProgram &p, int nregs, void *out, int out_dtype, i
   if (blocks > INT32_MAX) blocks = INT32_MAX;          // the grid-stride loop covers the rest
   const size_t smem = (size_t)nregs * VEC * kPwThreads * sizeof(T);
   if (smem > 48 * 1024)
-    cudaFuncSetAttribute(pointwise_kernel<T, VEC, NIN, G>,
+    cudaFuncSetAttribute(pointwise_kernel<T, VEC, NIN, G, BC>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  pointwise_kernel<T, VEC, NIN, G><<<(unsigned)blocks, kPwThreads, smem, st>>>(p, out, out_dtype, n);
+  pointwise_kernel<T, VEC, NIN, G, BC><<<(unsigned)blocks, kPwThreads, smem, st>>>(p, out, out_dtype, n);
 }
 
 template <typename T, int VEC>
 void dispatch_inputs(const PwProgram &p, int nregs, void *out, int out_dtype, int64_t n,
-                     cudaStream_t st) {
+                     cudaStream_t st, bool bcast) {
+  if (bcast) {
+    switch (p.n_in) {
+      case 2: launch_pointwise<T, VEC, 2, 2, true>(p, nregs, out, out_dtype, n, st); break;
+      case 3: launch_pointwise<T, VEC, 3, 2, true>(p, nregs, out, out_dtype, n, st); break;
+      default: launch_pointwise<T, VEC, -1, 1, true>(p, nregs, out, out_dtype, n, st); break;
+    }
+    return;
+  }
   switch (p.n_in) {
     case 0: launch_pointwise<T, VEC, 0, 1>(p, nregs, out, out_dtype, n, st); break;
     case 1: launch_pointwise<T, VEC, 1, 2>(p, nregs, out, out_dtype, n, st); break;
@@ -389,17 +469,34 @@ void dispatch_inputs(const PwProgram &p, int nregs, void *out, int out_dtype, in
   }
 }
 
+// Host: the multiply-shift constants for division by d (1 <= d < 2^62).
+static PwDiv make_div(unsigned long long d) {
+  PwDiv v{};
+  v.d = d;
+  if (d == 1) {
+    v.shift = -1;
+    return v;
+  }
+  int l = 0;
+  while ((1ull << l) < d) ++l;
+  const unsigned __int128 num = ((unsigned __int128)((1ull << l) - d)) << 64;
+  v.magic = (unsigned long long)(num / d) + 1;
+  v.shift = l - 1;
+  return v;
+}
+
 }  // namespace emmy
 
 using namespace emmy;
 
-extern "C" int emmy_pointwise(const void *const *inputs, const int *input_dtypes, int n_inputs,
-                              const void *const *scalars, const int *scalar_dtypes, int n_scalars,
-                              const double *immediates, int n_imm, const int *program, int n_instr,
-                              int result_reg, int compute_f64, void *out, int out_dtype, int64_t n,
-                              void *stream) {
+static int pointwise_impl(const void *const *inputs, const int *input_dtypes,
+                          const int64_t *input_index, int n_inputs, const void *const *scalars,
+                          const int *scalar_dtypes, int n_scalars, const double *immediates,
+                          int n_imm, const int *program, int n_instr, int result_reg,
+                          int compute_f64, void *out, int out_dtype, int64_t first, int64_t n,
+                          void *stream) {
   clear_error();
-  if (n < 0) return set_error(EMMY_ERR_INVALID, "emmy_pointwise: negative size");
+  if (n < 0 || first < 0) return set_error(EMMY_ERR_INVALID, "emmy_pointwise: negative size");
   if (n == 0) return EMMY_OK;
   if (!out) return set_error(EMMY_ERR_INVALID, "emmy_pointwise: null output");
   if (n_inputs < 0 || n_inputs > kPwMaxIn || n_scalars < 0 || n_scalars > kPwMaxIn || n_imm < 0 ||
@@ -421,11 +518,30 @@ extern "C" int emmy_pointwise(const void *const *inputs, const int *input_dtypes
   p.n_instr = n_instr;
   p.result_reg = result_reg;
   bool vec_ok = aligned16(out) || (out_dtype == EMMY_DT_F16 && ((uintptr_t)out & 7) == 0);
+  bool bcast = false;
+  p.first = first;
   for (int i = 0; i < n_inputs; ++i) {
     if (!inputs[i]) return set_error(EMMY_ERR_INVALID, "emmy_pointwise: null input %d", i);
     if (!dt_ok(input_dtypes[i])) return set_error(EMMY_ERR_INVALID, "emmy_pointwise: bad input dtype");
     p.inputs[i] = inputs[i];
     p.in_dtype[i] = input_dtypes[i];
+    const int64_t dv = input_index ? input_index[3 * i] : 0;
+    if (dv != 0) {
+      // broadcast input: ((first + e) / div) % mod must stay inside its numel
+      const int64_t md = input_index[3 * i + 1], numel = input_index[3 * i + 2];
+      if (dv < 1 || dv >= (int64_t(1) << 62) || md < 0 || md >= (int64_t(1) << 62) || numel < 1)
+        return set_error(EMMY_ERR_INVALID, "emmy_pointwise: bad index of input %d", i);
+      const int64_t top = md > 0 ? std::min<int64_t>(md - 1, (first + n - 1) / dv) : (first + n - 1) / dv;
+      if (top >= numel)
+        return set_error(EMMY_ERR_INVALID, "emmy_pointwise: input %d read past its %lld elements", i,
+                         (long long)numel);
+      p.idx[i].bcast = 1;
+      p.idx[i].div = make_div((unsigned long long)dv);
+      p.idx[i].has_mod = md > 0;
+      if (md > 0) p.idx[i].mod = make_div((unsigned long long)md);
+      bcast = true;
+      continue;
+    }
     const uintptr_t need = input_dtypes[i] == EMMY_DT_F16 ? 8 : 16;
     vec_ok = vec_ok && ((uintptr_t)inputs[i] % need) == 0;
   }
@@ -453,7 +569,12 @@ extern "C" int emmy_pointwise(const void *const *inputs, const int *input_dtypes
   if ((size_t)nregs * 4 * kPwThreads * (compute_f64 ? 8 : 4) > 160 * 1024) vec_ok = false;
   cudaStream_t st = as_stream(stream);
   const int nleaf = n_inputs + n_scalars + n_imm;
-  if (vec_ok && n_instr == 1 && result_reg == nleaf) {
+  // Transcendental steps (exp, log, tanh, gelu, ...) are issue-bound; they
+  // run faster in the general kernel, whose threads take two groups each.
+  const int op0 = program[0];
+  const bool cheap = op0 <= PW_ABS || (op0 >= PW_RELU && op0 <= PW_FMA) || op0 == PW_FLOOR ||
+                     op0 == PW_CEIL || op0 == PW_SIGN || op0 == PW_SQRT;
+  if (vec_ok && !bcast && n_instr == 1 && result_reg == nleaf && cheap) {
     // one step on leaves only: the register kernel
     const int op = program[0];
     const int arity = (op == PW_WHERE || op == PW_FMA) ? 3
@@ -502,11 +623,33 @@ extern "C" int emmy_pointwise(const void *const *inputs, const int *input_dtypes
     return check_launch("emmy_pointwise (one step)");
   }
   if (compute_f64) {
-    if (vec_ok) dispatch_inputs<double, 4>(p, nregs, out, out_dtype, n, st);
-    else dispatch_inputs<double, 1>(p, nregs, out, out_dtype, n, st);
+    if (vec_ok) dispatch_inputs<double, 4>(p, nregs, out, out_dtype, n, st, bcast);
+    else dispatch_inputs<double, 1>(p, nregs, out, out_dtype, n, st, bcast);
   } else {
-    if (vec_ok) dispatch_inputs<float, 4>(p, nregs, out, out_dtype, n, st);
-    else dispatch_inputs<float, 1>(p, nregs, out, out_dtype, n, st);
+    if (vec_ok) dispatch_inputs<float, 4>(p, nregs, out, out_dtype, n, st, bcast);
+    else dispatch_inputs<float, 1>(p, nregs, out, out_dtype, n, st, bcast);
   }
   return check_launch("emmy_pointwise");
+}
+
+extern "C" int emmy_pointwise(const void *const *inputs, const int *input_dtypes, int n_inputs,
+                              const void *const *scalars, const int *scalar_dtypes, int n_scalars,
+                              const double *immediates, int n_imm, const int *program, int n_instr,
+                              int result_reg, int compute_f64, void *out, int out_dtype, int64_t n,
+                              void *stream) {
+  return pointwise_impl(inputs, input_dtypes, nullptr, n_inputs, scalars, scalar_dtypes, n_scalars,
+                        immediates, n_imm, program, n_instr, result_reg, compute_f64, out, out_dtype,
+                        0, n, stream);
+}
+
+extern "C" int emmy_pointwise_indexed(const void *const *inputs, const int *input_dtypes,
+                                      const int64_t *input_index, int n_inputs,
+                                      const void *const *scalars, const int *scalar_dtypes,
+                                      int n_scalars, const double *immediates, int n_imm,
+                                      const int *program, int n_instr, int result_reg,
+                                      int compute_f64, void *out, int out_dtype, int64_t first,
+                                      int64_t n, void *stream) {
+  return pointwise_impl(inputs, input_dtypes, input_index, n_inputs, scalars, scalar_dtypes,
+                        n_scalars, immediates, n_imm, program, n_instr, result_reg, compute_f64, out,
+                        out_dtype, first, n, stream);
 }

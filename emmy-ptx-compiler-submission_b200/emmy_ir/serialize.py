@@ -89,3 +89,22 @@ def write_package(directory, kernel: KernelOp, meta_kernel: dict, package: dict 
     meta["kernels"] = [meta_kernel]
     (d / "meta.json").write_text(json.dumps(meta, indent=1))
     return ir_path
+
+
+def write_chain(directory, pairs, package: dict | None = None) -> list:
+    """A package of several kernels: one ``<entry>.ir.json`` each and one
+    ``meta.json`` listing them in launch order; returns the IR paths."""
+    d = Path(directory)
+    d.mkdir(parents=True, exist_ok=True)
+    paths = []
+    for kernel, mk in pairs:
+        outs = [a["name"] for a in mk["args"] if a.get("output")]
+        doc = graph_dict(kernel, mk["args"], outs[0])
+        path = d / f"{kernel.name}.ir.json"
+        path.write_text(json.dumps(doc, indent=1))
+        paths.append(path)
+    meta = dict(package or {})
+    meta.setdefault("id", pairs[-1][0].name)
+    meta["kernels"] = [mk for _, mk in pairs]
+    (d / "meta.json").write_text(json.dumps(meta, indent=1))
+    return paths

@@ -403,7 +403,7 @@ def _B(op, left, right):
 
 def matmul(M, N, K, batch=1, splits=1, dtype="f32", out_dtype=None, bias=False, relu=False,
            tm=64, tn=64, rm=4, rn=4, bk=None, entry="k_matmul", a_init=None, b_init=None,
-           bias_init=None):
+           bias_init=None, c_name="C"):
     """``C = A @ B`` (+ bias, relu) in the reference's cp.async tiled-matmul shape.
 
     Tile axes ``(_aS_ks?, a0? (batch), a1_b, a2_b, a1_u, a2_u)``: per split and
@@ -486,7 +486,7 @@ def matmul(M, N, K, batch=1, splits=1, dtype="f32", out_dtype=None, bias=False, 
                 body.append(Let(name=f"zero__c{i}_{j}", value=L(0.0), dtype=DT["f32"]))
                 body.append(A(f"v1__c{i}_{j}", "maximum", (val, f"zero__c{i}_{j}")))
                 val = f"v1__c{i}_{j}"
-            body.append(Write(output="C", index=bidx + (row, col), values=(val,), value_dtype=DT[out_dtype],
+            body.append(Write(output=c_name, index=bidx + (row, col), values=(val,), value_dtype=DT[out_dtype],
                               atomic=splits > 1, swizzle="NONE"))
     tile = Tile(axes=tuple(axes), body=tuple(body), block_threads=threads, aux_threads=0,
                 raster_axes=("a1_b", "a2_b"), raster_group=None, raster_orient="m")
@@ -496,9 +496,9 @@ def matmul(M, N, K, batch=1, splits=1, dtype="f32", out_dtype=None, bias=False, 
             _arg("A", dtype, lead + [M, K], seed=0, **({"init": a_init} if a_init else {}))]
     if bias:
         args.append(_arg("bias", "f32", [N], seed=2, **({"init": bias_init} if bias_init else {})))
-    args.append(_arg("C", out_dtype, lead + [M, N], output=True))
+    args.append(_arg(c_name, out_dtype, lead + [M, N], output=True))
     nblocks = splits * batch * (M // tm) * (N // tn)
-    return kop, _meta(entry, args, nblocks, threads, zero=["C"] if splits > 1 else [])
+    return kop, _meta(entry, args, nblocks, threads, zero=[c_name] if splits > 1 else [])
 
 
 # ---------------------------------------------------------------------------
@@ -585,7 +585,8 @@ _COMPARE = {"greater", "less", "greater_equal", "less_equal", "equal"}
 
 
 def pointwise(n, expr, dtype="f32", shape=None, block=256, unroll=None, entry="k_pointwise",
-              vector_write=True, inits=None, out="out", seeds=None):
+              vector_write=True, inits=None, out="out", seeds=None, tile_shape=None, dtypes=None,
+              out_dtype=None):
     """The reference pointwise shape: ``Tile(a0 : n/U)`` with U unrolled copies.
 
     Each copy u loads its element ``a0*U + u`` of every input, loads the
@@ -595,18 +596,27 @@ def pointwise(n, expr, dtype="f32", shape=None, block=256, unroll=None, entry="k
     ``v_p_big`` / ``w_p_f64`` respectively.  ``expr`` is a nested tuple:
     ``"x0"`` names an input tensor of ``shape`` (default ``[n]``),
     ``("const", name, value)`` a one-element constant tensor, ``("imm", value)``
-    an immediate (Let), and ``(op, arg, ...)`` an elementwise op.  Inputs get
-    seeds 0, 1, ... in order of first use unless ``seeds`` names them.
+    an immediate (Let), and ``(op, arg, ...)`` an elementwise op.  Broadcast
+    inputs: ``("bcast", name, numel, D, M)`` reads ``name[(e // D) % M]`` for
+    element e (``M = 0``: no ``%``); with ``tile_shape`` (a multi-axis Tile,
+    one element per thread, axes ``a0, a1, ...``), ``("axis", name, (i, ...))``
+    reads ``name[a_i, ...]``.  Inputs get seeds 0, 1, ... in order of first
+    use unless ``seeds`` names them; ``dtypes`` overrides an input's dtype and
+    ``out_dtype`` the output's (Assigns stay ``dtype``).
     """
     shape = list(shape) if shape else [int(n)]
     if math.prod(shape) != n:
         raise ValueError("shape does not hold n elements")
+    if tile_shape is not None:
+        if math.prod(tile_shape) != n:
+            raise ValueError("tile_shape does not hold n elements")
+        unroll = 1
     if unroll is None:
         unroll = next(u for u in (4, 3, 2, 1) if n % u == 0)
     if n % unroll:
         raise ValueError("unroll must divide n")
     T = n // unroll
-    inputs, consts = [], {}
+    inputs, consts, bshapes = [], {}, {}
 
     def walk(e):
         if isinstance(e, str):
@@ -614,13 +624,31 @@ def pointwise(n, expr, dtype="f32", shape=None, block=256, unroll=None, entry="k
                 inputs.append(e)
         elif e[0] == "const":
             consts[e[1]] = float(e[2])
+        elif e[0] == "bcast":
+            if e[1] not in inputs:
+                inputs.append(e[1])
+            bshapes[e[1]] = [int(e[2])]
+        elif e[0] == "axis":
+            if e[1] not in inputs:
+                inputs.append(e[1])
+            bshapes[e[1]] = [int(tile_shape[i]) for i in e[2]]
         elif e[0] != "imm":
             for a in e[1:]:
                 walk(a)
     walk(expr)
 
+    def lin_of(u):
+        if tile_shape is not None:
+            lin = V("a0")
+            for i in range(1, len(tile_shape)):
+                lin = _B("+", _B("*", lin, L(int(tile_shape[i]))), V(f"a{i}"))
+            return lin
+        return _B("+", _B("*", V("a0"), L(unroll)), L(u)) if T > 1 else L(u)
+
     def flat_index(u):
-        lin = _B("+", _B("*", V("a0"), L(unroll)), L(u)) if T > 1 else L(u)
+        if tile_shape is not None and list(tile_shape) == list(shape):
+            return tuple(V(f"a{i}") for i in range(len(shape)))
+        lin = lin_of(u)
         if len(shape) == 1:
             return (lin,)
         idx = []
@@ -636,13 +664,28 @@ def pointwise(n, expr, dtype="f32", shape=None, block=256, unroll=None, entry="k
         counter = [0]
         loaded = {}
 
+        def in_dt(name):
+            return DT[dtypes[name]] if dtypes and name in dtypes else DT[dtype]
+
         def emit(e):
             if isinstance(e, str):
                 if e not in loaded:
                     nm = f"in{inputs.index(e)}__u{u}"
-                    body.append(Load(names=(nm,), input=e, index=flat_index(u), dtype=DT[dtype]))
+                    body.append(Load(names=(nm,), input=e, index=flat_index(u), dtype=in_dt(e)))
                     loaded[e] = nm
                 return loaded[e]
+            if e[0] in ("bcast", "axis"):
+                key = (e[0], e[1])
+                if key not in loaded:
+                    nm = f"in{inputs.index(e[1])}b__u{u}"
+                    if e[0] == "axis":
+                        idx = tuple(V(f"a{i}") for i in e[2])
+                    else:
+                        q = _B("//", lin_of(u), L(int(e[3]))) if int(e[3]) > 1 else lin_of(u)
+                        idx = (_B("%", q, L(int(e[4]))) if int(e[4]) else q,)
+                    body.append(Load(names=(nm,), input=e[1], index=idx, dtype=in_dt(e[1])))
+                    loaded[key] = nm
+                return loaded[key]
             if e[0] == "const":
                 nm = f"c_{e[1]}__u{u}"
                 if nm not in loaded:
@@ -662,20 +705,67 @@ def pointwise(n, expr, dtype="f32", shape=None, block=256, unroll=None, entry="k
             return nm
         results.append(emit(expr))
     base = _B("*", V("a0"), L(unroll)) if T > 1 else L(0)
-    if vector_write:
+    odt = DT[out_dtype or dtype]
+    if tile_shape is not None:
+        body.append(Write(output=out, index=flat_index(0), values=(results[0],), value_dtype=odt,
+                          atomic=False, swizzle="NONE"))
+    elif vector_write:
         body.append(Write(output=out, index=(_B("+", base, L(0)) if T > 1 else L(0),),
-                          values=tuple(results), value_dtype=DT[dtype], atomic=False,
+                          values=tuple(results), value_dtype=odt, atomic=False,
                           swizzle="NONE"))
     else:
         for u, r in enumerate(results):
             body.append(Write(output=out, index=(_B("+", base, L(u)) if T > 1 else L(u),),
-                              values=(r,), value_dtype=DT[dtype], atomic=False, swizzle="NONE"))
-    axes = [ax("a0", T)]
+                              values=(r,), value_dtype=odt, atomic=False, swizzle="NONE"))
+    axes = ([ax(f"a{i}", int(e)) for i, e in enumerate(tile_shape)] if tile_shape is not None
+            else [ax("a0", T)])
     kop = KernelOp(name=entry, body=(_tile(axes, body, block),))
     args = [_arg(c, dtype, [1], data=[v]) for c, v in consts.items()]
     for i, name in enumerate(inputs):
         kw = {"init": inits[name]} if inits and name in inits else {}
         seed = seeds[name] if seeds and name in seeds else i
-        args.append(_arg(name, dtype, shape, seed=seed, **kw))
-    args.append(_arg(out, dtype, shape, output=True))
+        dt = dtypes[name] if dtypes and name in dtypes else dtype
+        args.append(_arg(name, dt, bshapes.get(name, shape), seed=seed, **kw))
+    args.append(_arg(out, out_dtype or dtype, shape, output=True))
     return kop, _meta(entry, args, (T + block - 1) // block, block)
+
+
+def mm_bias_relu_chain(M, N, K, dtype="f32", c_dtype=None, out_dtype=None, compute=None,
+                       bias=True, relu=True, batch=1, axis_form=True, **mm_kw):
+    """The two-kernel matmul + bias + ReLU package (the reference's
+    ``adv_mm_bias_relu``: ``k_relu__partial`` -> ``k_relu``).
+
+    Kernel 1 (``final: false``) writes the product ``mm`` (dtype ``c_dtype``);
+    kernel 2 reads it as an intermediate and writes
+    ``out = relu(mm + bias[n])`` (``out_dtype``), its Assigns typed
+    ``compute`` (default f32).  ``axis_form``: kernel 2 is a two-axis Tile
+    reading ``bias[a1]``; else a flat Tile reading ``bias[e % N]``.
+    Returns ``[(KernelOp, meta kernel entry), ...]``.
+    """
+    c_dtype = c_dtype or dtype
+    out_dtype = out_dtype or c_dtype
+    compute = compute or "f32"
+    k1, m1 = matmul(M, N, K, batch=batch, dtype=dtype, out_dtype=c_dtype, entry="k_relu__partial",
+                    c_name="mm", **mm_kw)
+    m1["final"] = False
+    shape = ([batch] if batch > 1 else []) + [M, N]
+    n = math.prod(shape)
+    if axis_form:
+        b = ("axis", "bias", (len(shape) - 1,))
+        tile = shape
+    else:
+        b = ("bcast", "bias", N, 1, N)
+        tile = None
+    expr = ("add", "mm", b) if bias else "mm"
+    if relu:
+        expr = ("relu", expr)
+    if expr == "mm":
+        expr = ("copy", "mm")
+    k2, m2 = pointwise(n, expr, compute, shape=shape, entry="k_relu", tile_shape=tile,
+                       dtypes={"mm": c_dtype, "bias": "f32"}, out_dtype=out_dtype,
+                       seeds={"bias": 2})
+    for a in m2["args"]:
+        if a["name"] == "mm":
+            a["intermediate"] = True
+            a.pop("seed", None)
+    return [(k1, m1), (k2, m2)]

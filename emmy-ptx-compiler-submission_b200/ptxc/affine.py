@@ -54,6 +54,8 @@ def affine_of(e, rename=None):
         v = e.name
         if rename and v in rename:
             v = rename[v]
+            if isinstance(v, Affine):       # an axis standing for a decoded flat id
+                return Affine(v)
         return Affine({v: 1})
     if name in ("Literal", "Dim") or isinstance(e, int):
         c = const_int(e)
@@ -76,13 +78,15 @@ def affine_of(e, rename=None):
                 return _scale(left, right.const())
             return None
         if e.op in ("/", "//", "divide", "floor_divide", "%", "mod", "remainder"):
-            # (E // c) and (E % c) of an affine E stay symbolic atoms; a flat
-            # index that holds c*k*(E//c) + k*(E%c) recombines to k*E below.
+            # (E // c) and (E % c) of an affine E (itself possibly holding
+            # such atoms) stay symbolic atoms; a flat index that holds
+            # c*k*(E//c) + k*(E%c) recombines to k*E below.
             c = right.const() if not right.vars() else None
-            if c is None or c <= 0 or not left.atoms_ok():
+            if c is None or c <= 0:
                 return None
-            kind = "div" if e.op in ("/", "//", "divide", "floor_divide") else "mod"
-            return Affine({(kind, _frozen(left), c): 1})
+            if e.op in ("/", "//", "divide", "floor_divide"):
+                return Affine({_div_key(left, c): 1})
+            return Affine({("mod", _frozen(left), c): 1})
         return None
     return None
 
@@ -91,19 +95,79 @@ def _frozen(a: Affine) -> tuple:
     return tuple(sorted(((k, v) for k, v in a.items() if v), key=repr))
 
 
-def _recombine(a: Affine):
+def _div_key(left: Affine, c: int) -> tuple:
+    """The atom ``left // c``, with ``(E // a) // c`` kept as ``E // (a*c)``
+    (equal for non-negative E), so every quotient of E has one spelling."""
+    ks = [k for k, v in left.items() if v]
+    if len(ks) == 1 and isinstance(ks[0], tuple) and ks[0][0] == "div" and left[ks[0]] == 1:
+        return ("div", ks[0][1], ks[0][2] * c)
+    return ("div", _frozen(left), c)
+
+
+def _recombine(a: Affine, keep_atoms: bool = False):
+    """Fold every ``c*k*(E//c) + k*(E%c)`` pair into ``k*E``, repeatedly (a
+    multi-axis decode nests them).  Atoms left over make the form non-affine:
+    None, unless ``keep_atoms``."""
     out = Affine(a)
-    for key in list(out):
-        if isinstance(key, tuple) and key[0] == "div" and out.get(key):
-            mod = ("mod", key[1], key[2])
-            k2 = out.get(mod, 0)
-            if k2 and out[key] == key[2] * k2:
-                del out[key]
-                del out[mod]
-                out = _add(out, _scale(Affine(dict(key[1])), k2))
-    if not out.atoms_ok():
+    changed = True
+    while changed:
+        changed = False
+        for key in list(out):
+            if isinstance(key, tuple) and key[0] == "mod" and out.get(key):
+                k2 = out[key]
+                left = Affine(dict(key[1]))
+                div = _div_key(left, key[2])
+                if out.get(div, 0) == key[2] * k2:
+                    del out[key]
+                    del out[div]
+                    out = _add(out, _scale(left, k2))
+                    changed = True
+                    break
+    out = Affine({k: v for k, v in out.items() if v or k == ""})
+    if not keep_atoms and not out.atoms_ok():
         return None
     return out
+
+
+def decode_axes(axes, flat: str = "__g") -> dict:
+    """Each Tile axis as a form of the flat work id, as the reference decodes
+    it: ``idx_i = (gid / suffix_i) % extent_i`` (``ptxc/lower.py:787-812``),
+    written as nested divisions so that the flat index of a row-major load
+    recombines to the flat id.  The first axis needs no ``%`` (the gid guard
+    keeps it in range)."""
+    out = {}
+    cur = Affine({flat: 1})
+    for i in range(len(axes) - 1, -1, -1):
+        name, ext = axes[i]
+        if i == 0:
+            out[name] = Affine(cur)
+        else:
+            out[name] = Affine({("mod", _frozen(cur), int(ext)): 1})
+            cur = Affine({_div_key(cur, int(ext)): 1})
+    return out
+
+
+def broadcast_form(a: Affine):
+    """``(E, D, M)`` when the offset ``a`` is ``(E // D) % M`` (``M = 0``: no
+    ``%``; ``D = 1``: no ``//``) of an atom-free affine ``E``, else None."""
+    keys = [k for k, v in a.items() if v and k != ""]
+    if a.const() or len(keys) != 1 or not isinstance(keys[0], tuple) or a[keys[0]] != 1:
+        return None
+    kind, left, c = keys[0]
+    D, M = 1, 0
+    if kind == "mod":
+        M = c
+        inner = Affine(dict(left))
+    else:
+        inner = Affine({keys[0]: 1})
+    ks = [k for k, v in inner.items() if v and k != ""]
+    if len(ks) == 1 and isinstance(ks[0], tuple) and ks[0][0] == "div" \
+            and inner[ks[0]] == 1 and not inner.const():
+        D = ks[0][2]
+        inner = Affine(dict(ks[0][1]))
+    if not inner.atoms_ok():
+        return None
+    return inner, D, M
 
 
 def strides_of(shape, ncoords: int) -> list:
@@ -119,17 +183,18 @@ def strides_of(shape, ncoords: int) -> list:
     return out
 
 
-def flat_affine(index, shape, rename=None):
-    """Affine flat element offset of ``buffer[index]`` for a buffer of ``shape``."""
+def flat_affine(index, shape, rename=None, keep_atoms=False):
+    """Affine flat element offset of ``buffer[index]`` for a buffer of ``shape``
+    (``keep_atoms``: also return forms with ``//`` / ``%`` atoms left over)."""
     if index is None or len(index) == 0:
         return Affine({"": 0})
     if len(index) == 1:
         a = affine_of(index[0], rename)
-        return None if a is None else _recombine(a)
+        return None if a is None else _recombine(a, keep_atoms)
     acc = Affine()
     for coord, stride in zip(index, strides_of(shape, len(index))):
         a = affine_of(coord, rename)
         if a is None:
             return None
         acc = _add(acc, _scale(a, stride))
-    return _recombine(acc)
+    return _recombine(acc, keep_atoms)

@@ -10,7 +10,8 @@ the data path:
   otherwise rows of A and C (B and the bias replicated);
 * attention: (batch, head) slices of q, k, v and o;
 * pointwise: contiguous element ranges of every input and the output (the
-  one-element constant tensors replicated).
+  one-element constant tensors and broadcast inputs replicated; the shard's
+  first element index keeps the broadcast reads in place).
 
 The one family with an exchange step is split-K matmul spread over ranks:
 each rank multiplies its K slice into a full-size partial C, and the partials
@@ -107,9 +108,17 @@ def shard_plan(plan: dict, rank: int, world: int):
         g = plan["pointwise"]
         lo, hi = shard_ranges(g["n"], world)[rank]
         sub["pointwise"]["n"] = hi - lo
+        index = g.get("input_index") or [[0, 0]] * len(g["inputs"])
+        bcast = {n for n, (d, _) in zip(g["inputs"], index) if d}
+        if bcast & ({n for n, (d, _) in zip(g["inputs"], index) if not d} | {a["out"]}):
+            raise ValueError("a pointwise tensor read both whole and broadcast")
+        if bcast:
+            # broadcast inputs stay whole; the shard numbers its elements from lo
+            sub["pointwise"]["first"] = g.get("first", 0) + lo
         for name in list(g["inputs"]) + [a["out"]]:
-            slices[name] = (lo, hi - lo)
-            set_shape(name, [hi - lo])
+            if name not in bcast:
+                slices[name] = (lo, hi - lo)
+                set_shape(name, [hi - lo])
     else:
         raise ValueError(f"family {fam!r} has no sharding rule")
     sub["shard"] = {"rank": rank, "world": world}

@@ -42,6 +42,8 @@ SIGNATURES = {
     "emmy_attention_f16": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _vp],
     "emmy_pointwise": [_vp, _vp, _int, _vp, _vp, _int, _vp, _int, _vp, _int, _int, _int, _vp, _int,
                        _i64, _vp],
+    "emmy_pointwise_indexed": [_vp, _vp, _vp, _int, _vp, _vp, _int, _vp, _int, _vp, _int, _int, _int,
+                               _vp, _int, _i64, _i64, _vp],
 }
 RESTYPES = {"emmy_reduce_workspace_bytes": _sz}
 
@@ -215,10 +217,22 @@ def run(plan: dict, tensors: dict, stream=None, workspace=None, check: bool = Tr
         imm = (ctypes.c_double * max(1, len(imms)))(*[float(v) for v in imms])
         flat = [int(x) for row in g["program"] for x in row]
         prog = (_int * len(flat))(*flat)
-        _check(lib.emmy_pointwise(in_ptrs, in_dts, len(ins), sc_ptrs, sc_dts, len(scs), imm,
-                                  len(imms), prog, len(g["program"]), g["result_reg"],
-                                  int(g["compute"] == "f64"), _ptr(T("out")),
-                                  DT_CODE[g["out_dtype"]], g["n"], st), "emmy_pointwise")
+        if "input_index" in g:
+            idx = []
+            for n, (d, m) in zip(ins, g["input_index"]):
+                idx += [int(d), int(m), tensors[n].numel()]
+            idx_arr = (ctypes.c_int64 * len(idx))(*idx)
+            _check(lib.emmy_pointwise_indexed(in_ptrs, in_dts, idx_arr, len(ins), sc_ptrs, sc_dts,
+                                              len(scs), imm, len(imms), prog, len(g["program"]),
+                                              g["result_reg"], int(g["compute"] == "f64"),
+                                              _ptr(T("out")), DT_CODE[g["out_dtype"]],
+                                              int(g.get("first", 0)), g["n"], st),
+                   "emmy_pointwise_indexed")
+        else:
+            _check(lib.emmy_pointwise(in_ptrs, in_dts, len(ins), sc_ptrs, sc_dts, len(scs), imm,
+                                      len(imms), prog, len(g["program"]), g["result_reg"],
+                                      int(g["compute"] == "f64"), _ptr(T("out")),
+                                      DT_CODE[g["out_dtype"]], g["n"], st), "emmy_pointwise")
         launches += 1
     else:
         raise ValueError(f"plan family {fam!r} has no launcher")

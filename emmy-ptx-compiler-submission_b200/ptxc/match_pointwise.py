@@ -21,7 +21,7 @@ from __future__ import annotations
 
 import math
 
-from .affine import flat_affine
+from .affine import Affine, broadcast_form, decode_axes, flat_affine
 from .common import norm_dtype, op_name, stmt_name
 from .match_reduce import NoMatch, need
 
@@ -54,9 +54,14 @@ MAX_INSTR = 48
 def match_pointwise(kop, tile, meta) -> dict:
     shapes, dtypes = meta.shapes, meta.dtypes
     axes = [(a.name, int(a.extent.value)) for a in tile.axes]
-    need(len(axes) <= 1, "pointwise Tile has more than one axis")
-    T = axes[0][1] if axes else 1
-    avar = axes[0][0] if axes else None
+    rename = None
+    if len(axes) > 1:
+        # a multi-axis Tile: each axis is a decode of the flat work id "__g"
+        rename = decode_axes(axes)
+        T, avar = math.prod(e for _, e in axes), "__g"
+    else:
+        T = axes[0][1] if axes else 1
+        avar = axes[0][0] if axes else None
     stmts = list(tile.body)
     need(stmts, "empty Tile")
     for st in stmts:
@@ -74,10 +79,10 @@ def match_pointwise(kop, tile, meta) -> dict:
         k = stmt_name(st)
         if k == "Load":
             need(st.input in shapes, f"load of unknown buffer {st.input!r}")
-            aff = flat_affine(st.index, shapes[st.input])
+            aff = flat_affine(st.index, shapes[st.input], rename, keep_atoms=True)
             need(aff is not None, "non-affine pointwise index")
             for i, nm in enumerate(st.names):
-                a2 = dict(aff)
+                a2 = Affine(aff)
                 a2[""] = a2.get("", 0) + i
                 defs[nm] = ("load", st.input, a2)
         elif k == "Let":
@@ -91,7 +96,7 @@ def match_pointwise(kop, tile, meta) -> dict:
     # written elements: (offset affine, value name)
     elems = []
     for w in writes:
-        aff = flat_affine(w.index, shapes[out])
+        aff = flat_affine(w.index, shapes[out], rename)
         need(aff is not None, "non-affine output index")
         for i, v in enumerate(w.values):
             a2 = dict(aff)
@@ -124,14 +129,24 @@ def match_pointwise(kop, tile, meta) -> dict:
         elif d[0] == "load":
             tensor, aff = d[1], d[2]
             tn = math.prod(shapes[tensor]) if shapes[tensor] else 1
+            bc = None if aff.atoms_ok() else broadcast_form(aff)
             if tn == 1 and not {k for k, c in aff.items() if k and c} and aff.get("", 0) == 0:
                 r = ("scalar", tensor)
+            elif not aff.atoms_ok():
+                # broadcast: the element's own offset E, read at (E // D) % M
+                need(bc is not None, f"{tensor!r} index is neither the element nor a broadcast of it")
+                E, D, M = bc
+                need({k: c for k, c in E.items() if c} == {k: c for k, c in elem_aff.items() if c},
+                     f"{tensor!r} is not a broadcast of the written element")
+                top = min(M - 1, (numel - 1) // D) if M else (numel - 1) // D
+                need(top < tn, f"{tensor!r} broadcast reads past its {tn} elements")
+                r = ("input", (tensor, D, M))
             else:
                 rel = {k: c for k, c in aff.items() if c}
                 want = {k: c for k, c in elem_aff.items() if c}
                 need(rel == want, f"{tensor!r} is not read at the written element")
-                need(tn == numel, f"{tensor!r} does not match the output size (no broadcasting)")
-                r = ("input", tensor)
+                need(tn == numel, f"{tensor!r} does not match the output size")
+                r = ("input", (tensor, 0, 0))
         else:
             r = ("op", d[1], tuple(canon(a, elem_aff, memo, depth + 1) for a in d[2]), d[3])
         memo[name] = r
@@ -187,6 +202,8 @@ def match_pointwise(kop, tile, meta) -> dict:
         program.append([OPCODES[op], ntmp0 + i] + rs)
     need(ntmp0 + len(prog) <= MAX_REGS and len(prog) <= MAX_INSTR, "pointwise program too large")
 
+    in_index = [[D, M] for _, D, M in inputs]
+    inputs = [t for t, _, _ in inputs]
     in_dts = {dtypes[t] for t in inputs + scalars}
     need(in_dts <= {"f32", "f16", "f64"} and dtypes[out] in ("f32", "f16", "f64"),
          "pointwise dtypes must be f16/f32/f64")
@@ -196,6 +213,8 @@ def match_pointwise(kop, tile, meta) -> dict:
         "args": {"out": out},
         "pointwise": {"n": numel, "inputs": inputs, "scalars": scalars, "immediates": imms,
                       "program": program, "result_reg": ntmp0 + len(prog) - 1,
-                      "compute": compute, "out_dtype": dtypes[out]},
+                      "compute": compute, "out_dtype": dtypes[out],
+                      **({"input_index": in_index, "first": 0}
+                         if any(D for D, _ in in_index) else {})},
         "params": {}, "dtypes": {"out": dtypes[out]},
     }

@@ -56,9 +56,12 @@ extern "C" {
 #define EMMY_DT_F16 1
 #define EMMY_DT_F64 2
 
-/* GEMM epilogue bits */
+/* GEMM epilogue bits, applied in this order: round the f32 product to f16
+ * (ROUND_F16; emmy_gemm_f16 only: the f16 intermediate of a matmul kernel
+ * followed by a separate bias/ReLU kernel), add bias[n], ReLU. */
 #define EMMY_EPI_BIAS 1
 #define EMMY_EPI_RELU 2
+#define EMMY_EPI_ROUND_F16 4
 
 /* Library version (major*10000 + minor*100 + patch). */
 int emmy_version(void);
@@ -205,6 +208,26 @@ int emmy_pointwise(const void *const *inputs, const int *input_dtypes, int n_inp
                    const double *immediates, int n_imm, const int *program, int n_instr,
                    int result_reg, int compute_f64, void *out, int out_dtype, int64_t n,
                    void *stream);
+
+/*
+ * emmy_pointwise with broadcast inputs (the bias of a matmul + bias + ReLU
+ * chain, a per-row scale): input i is read at
+ *   ((first + e) / div_i) % mod_i        (mod_i = 0: no modulo)
+ * for element e of [0, n), or at e when div_i = 0 (contiguous, as in
+ * emmy_pointwise).  input_index holds {div_i, mod_i, numel_i} per input;
+ * numel_i bounds the broadcast reads (checked on the host).  first offsets
+ * the element numbering, so a range [first, first + n) of a larger launch
+ * (a shard, a pipeline chunk) reads the same broadcast elements.  The
+ * reference reads such inputs through the decoded Tile axes
+ * (ptxc/lower.py:787-812) at a flat index that is a row-major form of them
+ * (ptxc/memory.py:150-186).
+ */
+int emmy_pointwise_indexed(const void *const *inputs, const int *input_dtypes,
+                           const int64_t *input_index, int n_inputs,
+                           const void *const *scalars, const int *scalar_dtypes, int n_scalars,
+                           const double *immediates, int n_imm, const int *program, int n_instr,
+                           int result_reg, int compute_f64, void *out, int out_dtype,
+                           int64_t first, int64_t n, void *stream);
 
 /*
  * Long-row reduction that allocates nothing: y[0] = fold_op(pre(x[0..n))) [* 1/count].

@@ -800,3 +800,29 @@ def run_ir(kernel_op, meta: dict, inputs: dict, blocks=None, threads=None) -> di
     with torch.no_grad():
         IRInterpreter(kernel_op, meta, bufs, blocks=blocks).run()
     return {k: v.numpy() for k, v in bufs.items()}
+
+
+def run_chain(pairs, host: dict, blocks=None) -> dict:
+    """Evaluate a package of several kernels in order, as the reference harness
+    runs them (``tools/localrun.py:160-195``): each kernel's outputs start at
+    zero, an ``intermediate`` argument takes the values an earlier kernel wrote
+    under that name converted to this argument's dtype, every other input comes
+    from ``host``.  ``pairs``: ``[(KernelOp, meta kernel entry), ...]``.
+    Returns every output of every kernel by name (the last writer's values)."""
+    produced = {}
+    for kop, meta in pairs:
+        ins = {}
+        for a in meta["args"]:
+            n = int(np.prod(a["shape"])) if a["shape"] else 1
+            dt = NP_DT[a["dtype"]]
+            if a.get("output"):
+                ins[a["name"]] = np.zeros(n, dtype=dt)
+            elif a.get("intermediate"):
+                ins[a["name"]] = np.asarray(produced[a["name"]]).reshape(-1).astype(dt)
+            else:
+                ins[a["name"]] = np.asarray(host[a["name"]]).reshape(-1)
+        out = run_ir(kop, meta, ins, blocks=blocks)
+        for a in meta["args"]:
+            if a.get("output"):
+                produced[a["name"]] = out[a["name"]]
+    return produced

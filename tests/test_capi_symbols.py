@@ -85,6 +85,44 @@ def test_pointwise_program_checks_need_no_gpu(lib):
     assert b"result register" in lib.emmy_last_error()
 
 
+def test_pointwise_broadcast_bounds_checked_on_the_host(lib):
+    vp, i32, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+    lib.emmy_pointwise_indexed.argtypes = [vp, vp, vp, i32, vp, vp, i32, vp, i32, vp, i32, i32, i32,
+                                           vp, i32, i64, i64, vp]
+    lib.emmy_last_error.restype = ctypes.c_char_p
+    ins = (vp * 2)(vp(16), vp(32))
+    dts = (i32 * 2)(0, 0)
+    prog = (i32 * 5)(1, 2, 0, 1, 0)
+    # input 1 read at (first + e) % 128 but holding only 100 elements
+    idx = (i64 * 6)(0, 0, 0, 1, 128, 100)
+    assert lib.emmy_pointwise_indexed(ins, dts, idx, 2, None, None, 0, None, 0, prog, 1, 2, 0,
+                                      vp(64), 0, 0, 4096, None) == 1
+    assert b"read past" in lib.emmy_last_error()
+    # (first + e) / 32 for e < 4096 from first 1024 reaches element 159 of 128
+    idx = (i64 * 6)(0, 0, 0, 32, 0, 128)
+    assert lib.emmy_pointwise_indexed(ins, dts, idx, 2, None, None, 0, None, 0, prog, 1, 2, 0,
+                                      vp(64), 0, 1024, 4096, None) == 1
+    # a negative divisor
+    idx = (i64 * 6)(0, 0, 0, -3, 0, 128)
+    assert lib.emmy_pointwise_indexed(ins, dts, idx, 2, None, None, 0, None, 0, prog, 1, 2, 0,
+                                      vp(64), 0, 0, 4096, None) == 1
+    assert b"bad index" in lib.emmy_last_error()
+
+
+def test_gemm_epilogue_bits_checked_on_the_host(lib):
+    vp, i32, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+    lib.emmy_gemm_f16.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i32, i32, i32, vp]
+    lib.emmy_gemm_f32.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, i32, i32,
+                                  i32, vp]
+    lib.emmy_last_error.restype = ctypes.c_char_p
+    assert lib.emmy_gemm_f16(vp(16), vp(16), None, vp(16), 1, 64, 64, 64, 1, 8, 0, None) == 1
+    assert b"epilogue" in lib.emmy_last_error()
+    # rounding to f16 first is an f16-matmul step only
+    assert lib.emmy_gemm_f32(vp(16), vp(16), None, vp(16), 1, 64, 64, 64, 0, 0, 0, 1, 0, 4,
+                             None) == 1
+    assert b"epilogue" in lib.emmy_last_error()
+
+
 def test_launcher_refuses_to_run_without_the_library(tmp_path, monkeypatch):
     import ptxc.launch as L
     monkeypatch.setattr(L, "_LIB", None)
