@@ -27,17 +27,18 @@ from .meta import read_meta
 
 PLAN_FORMAT = "emmy-b200-plan/1"
 
-_BLOCK_COLLECTIVES = {"Sync", "TreeHalve"}
-_WARP_COLLECTIVES = {"WarpShuffle"}
+def _has_block_collective(stmts) -> bool:
+    """A block-wide combine or barrier anywhere below (``ptxc/lower.py:704-717``)."""
+    return any(stmt_name(st) == "TreeHalve"
+               or (stmt_name(st) == "Sync" and not getattr(st, "warp", False))
+               for st in iter_stmts(stmts))
 
 
-def _has(stmts, names) -> bool:
-    for st in iter_stmts(stmts):
-        if stmt_name(st) in names:
-            return True
-        if stmt_name(st) == "Sync" and getattr(st, "warp", False) and "WarpSync" in names:
-            return True
-    return False
+def _has_warp_collective(stmts) -> bool:
+    """A warp shuffle or warp barrier anywhere below (``ptxc/lower.py:720-733``)."""
+    return any(stmt_name(st) == "WarpShuffle"
+               or (stmt_name(st) == "Sync" and getattr(st, "warp", False))
+               for st in iter_stmts(stmts))
 
 
 def _matchers():
@@ -93,12 +94,12 @@ class Lowerer:
         threads = math.prod(self.meta.block)
         launch = threads * math.prod(self.meta.grid)
         if n < launch:
-            if n % threads and _has(self.tile.body, _BLOCK_COLLECTIVES):
+            if n % threads and _has_block_collective(self.tile.body):
                 raise CompileError(
                     f"block collective under a partial block: {n} tiles, "
                     f"{threads} threads per block, {launch} launched. "
                     "The gid guard would skip part of the barrier.")
-            if n % 32 and _has(self.tile.body, _WARP_COLLECTIVES):
+            if n % 32 and _has_warp_collective(self.tile.body):
                 raise CompileError(
                     f"warp collective under a partial warp: {n} tiles, "
                     f"{launch} launched. The full mask would include inactive lanes.")
