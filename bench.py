@@ -44,6 +44,8 @@ UNIT = "GB/s"
 FALLBACK_HBM_GBS = 6650.0
 # FP32 CUDA-core peak, nominal: 148 SMs x 128 FMA/clk x 2 flops x 1.965 GHz
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+# FP64 CUDA-core peak, nominal: 148 SMs x 64 DFMA/clk x 2 flops x 1.965 GHz
+FP64_NOMINAL_TFLOPS = 148 * 64 * 2 * 1.965e9 / 1e12
 L2_FLUSH_BYTES = 256 << 20
 # A short device spin queued before each timed region keeps the GPU busy while
 # the host enqueues the launches, so the CUDA events bracket device work only.
@@ -291,6 +293,8 @@ def family_extras(device, peak):
         "K3b_bmm_f16_64x512": synth.matmul(512, 512, 512, batch=64, dtype="f16", out_dtype="f16",
                                            tm=128, tn=128, rm=8, rn=8),
         "K5_attention_f16_8x32x512x128": synth.attention(8, 32, 512, 128, dtype="f16"),
+        "X_gemm_f64_2048x2048x2048": synth.matmul(2048, 2048, 2048, dtype="f64", tm=128, tn=128,
+                                                  rm=8, rn=8, bk=16),
         "F8a_pointwise_add_f32_2^26": synth.pointwise(1 << 26, ("add", "x0", "x1"), "f32"),
         "F8b_pointwise_gelu_tanh_f16_16384x4096": synth.pointwise(
             16384 * 4096, ("gelu_tanh", "x0"), "f16", shape=[16384, 4096]),
@@ -331,6 +335,8 @@ def family_extras(device, peak):
             out[name]["tflops"] = round(tf, 2)
             if plan["family"] == "gemm_f32":
                 out[name]["frac_fp32_nominal"] = round(tf / FP32_NOMINAL_TFLOPS, 3)
+            elif plan["family"] == "gemm_f64":
+                out[name]["frac_fp64_nominal"] = round(tf / FP64_NOMINAL_TFLOPS, 3)
             else:
                 out[name]["frac_tensor"] = round(tf / tensor_peak()[0], 3)
         del ex

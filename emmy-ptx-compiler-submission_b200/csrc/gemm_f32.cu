@@ -1,4 +1,4 @@
-// f32 GEMM / batched GEMM / split-K on sm_100a CUDA cores.
+// f32 and f64 GEMM / batched GEMM / split-K on sm_100a CUDA cores.
 //
 // Replaces the entry the reference emits for its tiled-matmul IR shape: a
 // Tile over (m-block, n-block, m-lane, n-lane) axes, cp.async.cg 16-byte
@@ -16,8 +16,14 @@
 // split-K launch gives each CTA a K range and combines partials with 128-bit
 // vector atomics (red.global.add.v4.f32), the reference's atomic Write.
 //
-// Shapes TMA cannot describe (K or N not a multiple of 4, unaligned bases)
-// take a plain shared-memory tiled kernel instead.
+// f64 (the reference's fma.rn.f64 accumulate, ptxc/expr.py:1179-1309) runs
+// the same kernel on doubles: BK = 8 keeps A's shared rows at 64 bytes, the
+// 8x8 register tile holds 64 doubles (one CTA of 256 threads per SM), and
+// split-K partials meet in f64 atomic adds.  The tcgen05 tensor cores have no
+// f64 kind; DFMA on the CUDA cores is the f64 path.
+//
+// Shapes TMA cannot describe (K or N not a multiple of 16 bytes, unaligned
+// bases) take a plain shared-memory tiled kernel instead.
 
 #include "common.cuh"
 #include "tma.cuh"
@@ -25,19 +31,60 @@
 namespace emmy {
 
 namespace gemm32 {
-constexpr int BM = 128, BN = 128, BK = 16, STAGES = 4, THREADS = 256;
-constexpr int A_BYTES = BM * BK * 4, B_BYTES = BK * BN * 4, STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+constexpr int BM = 128, BN = 128, STAGES = 4, THREADS = 256;
+template <typename T> struct Cfg {
+  static constexpr int BK = 64 / (int)sizeof(T);        // 64-byte rows of A in shared memory
+  static constexpr int VK = 16 / (int)sizeof(T);        // elements per 16-byte shared load
+  static constexpr int A_BYTES = BM * BK * (int)sizeof(T);
+  static constexpr int B_BYTES = BK * BN * (int)sizeof(T);
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+};
 }  // namespace gemm32
+
+// 16-byte shared loads of VK consecutive elements, and four consecutive
+// elements (one or two 16-byte loads).
+__device__ __forceinline__ void lds_vk(const float *p, float v[4]) {
+  const float4 a = *reinterpret_cast<const float4 *>(p);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+}
+__device__ __forceinline__ void lds_vk(const double *p, double v[2]) {
+  const double2 a = *reinterpret_cast<const double2 *>(p);
+  v[0] = a.x; v[1] = a.y;
+}
+__device__ __forceinline__ void lds4(const float *p, float v[4]) { lds_vk(p, v); }
+__device__ __forceinline__ void lds4(const double *p, double v[4]) {
+  lds_vk(p, v);
+  lds_vk(p + 2, v + 2);
+}
+__device__ __forceinline__ float fma_t(float a, float b, float c) { return fmaf(a, b, c); }
+__device__ __forceinline__ double fma_t(double a, double b, double c) { return fma(a, b, c); }
+__device__ __forceinline__ void atomic_add4(float *dst, const float v[4]) {
+  atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(v[0], v[1], v[2], v[3]));
+}
+__device__ __forceinline__ void atomic_add4(double *dst, const double v[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) atomicAdd(dst + j, v[j]);
+}
+__device__ __forceinline__ void st4(float *dst, const float v[4]) {
+  *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+}
+__device__ __forceinline__ void st4(double *dst, const double v[4]) {
+  reinterpret_cast<double2 *>(dst)[0] = make_double2(v[0], v[1]);
+  reinterpret_cast<double2 *>(dst)[1] = make_double2(v[2], v[3]);
+}
 
 enum GemmMode { GEMM_STORE = 0, GEMM_ACCUMULATE = 1, GEMM_ATOMIC = 2 };
 
-__global__ void __launch_bounds__(gemm32::THREADS, 2)
-gemm_f32_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const float *__restrict__ bias, float *__restrict__ C, int M, int N, int K,
-                    int64_t c_batch_stride, int splits, int k_per_split, int epilogue, int mode,
-                    int *status) {
+template <typename T>
+__global__ void __launch_bounds__(gemm32::THREADS, sizeof(T) == 4 ? 2 : 1)
+gemm_simt_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const T *__restrict__ bias, T *__restrict__ C, int M, int N, int K,
+                     int64_t c_batch_stride, int splits, int k_per_split, int epilogue, int mode,
+                     int *status) {
   using namespace gemm32;
+  constexpr int BK = Cfg<T>::BK, VK = Cfg<T>::VK;
+  constexpr int A_BYTES = Cfg<T>::A_BYTES, STAGE_BYTES = Cfg<T>::STAGE_BYTES;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -61,8 +108,8 @@ gemm_f32_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 
   auto issue = [&](int t) {
     const int s = t % STAGES;
-    float *As = reinterpret_cast<float *>(smem + s * STAGE_BYTES);
-    float *Bs = reinterpret_cast<float *>(smem + s * STAGE_BYTES + A_BYTES);
+    T *As = reinterpret_cast<T *>(smem + s * STAGE_BYTES);
+    T *Bs = reinterpret_cast<T *>(smem + s * STAGE_BYTES + A_BYTES);
     mbar_expect_tx(&full[s], STAGE_BYTES);
     const int k = kb + t * BK;
     tma_load_3d(As, &tmA, &full[s], k, m0, batch);
@@ -71,36 +118,33 @@ gemm_f32_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   if (tid == 0)
     for (int t = 0; t < STAGES - 1 && t < ntiles; ++t) issue(t);
 
-  float acc[8][8];
+  T acc[8][8];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < 8; ++j) acc[i][j] = T(0);
 
   int failed_at = -1;
   for (int t = 0; t < ntiles; ++t) {
     const int s = t % STAGES;
     if (tid == 0 && t + STAGES - 1 < ntiles) issue(t + STAGES - 1);
     const bool ok = mbar_wait(&full[s], (t / STAGES) & 1, status, kStatusMbarTimeout);
-    const float *As = reinterpret_cast<const float *>(smem + s * STAGE_BYTES);
-    const float *Bs = reinterpret_cast<const float *>(smem + s * STAGE_BYTES + A_BYTES);
+    const T *As = reinterpret_cast<const T *>(smem + s * STAGE_BYTES);
+    const T *Bs = reinterpret_cast<const T *>(smem + s * STAGE_BYTES + A_BYTES);
 #pragma unroll
-    for (int kk = 0; kk < BK; kk += 4) {
-      float a[8][4];
+    for (int kk = 0; kk < BK; kk += VK) {
+      T a[8][VK];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 v = *reinterpret_cast<const float4 *>(As + (ty + 16 * i) * BK + kk);
-        a[i][0] = v.x; a[i][1] = v.y; a[i][2] = v.z; a[i][3] = v.w;
-      }
+      for (int i = 0; i < 8; ++i) lds_vk(As + (ty + 16 * i) * BK + kk, a[i]);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 b0 = *reinterpret_cast<const float4 *>(Bs + (kk + q) * BN + 4 * tx);
-        const float4 b1 = *reinterpret_cast<const float4 *>(Bs + (kk + q) * BN + 64 + 4 * tx);
-        const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      for (int q = 0; q < VK; ++q) {
+        T b[8];
+        lds4(Bs + (kk + q) * BN + 4 * tx, b);
+        lds4(Bs + (kk + q) * BN + 64 + 4 * tx, b + 4);
 #pragma unroll
         for (int i = 0; i < 8; ++i)
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i][q], b[j], acc[i][j]);
+          for (int j = 0; j < 8; ++j) acc[i][j] = fma_t(a[i][q], b[j], acc[i][j]);
       }
     }
     // every thread is done with stage s before thread 0 refills it next trip;
@@ -122,7 +166,7 @@ gemm_f32_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     return;
   }
 
-  float *Cb = C + (int64_t)batch * c_batch_stride;
+  T *Cb = C + (int64_t)batch * c_batch_stride;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int m = m0 + ty + 16 * i;
@@ -131,24 +175,26 @@ gemm_f32_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     for (int h = 0; h < 2; ++h) {
       const int n = n0 + 64 * h + 4 * tx;
       if (n >= N) continue;
-      float v[4] = {acc[i][4 * h], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]};
+      T v[4] = {acc[i][4 * h], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]};
       if ((epilogue & EMMY_EPI_BIAS) && bias && (mode != GEMM_ATOMIC || split == 0)) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] += (n + j < N) ? __ldg(bias + n + j) : 0.f;
+        for (int j = 0; j < 4; ++j) v[j] += (n + j < N) ? __ldg(bias + n + j) : T(0);
       }
       if (epilogue & EMMY_EPI_RELU) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] = fmaxf(v[j], 0.f);
+        for (int j = 0; j < 4; ++j) v[j] = fmax(v[j], T(0));
       }
-      float *dst = Cb + (int64_t)m * N + n;
+      T *dst = Cb + (int64_t)m * N + n;
       if (n + 3 < N) {
         if (mode == GEMM_ATOMIC) {
-          atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(v[0], v[1], v[2], v[3]));
+          atomic_add4(dst, v);
         } else if (mode == GEMM_ACCUMULATE) {
-          float4 o = *reinterpret_cast<float4 *>(dst);
-          *reinterpret_cast<float4 *>(dst) = make_float4(o.x + v[0], o.y + v[1], o.z + v[2], o.w + v[3]);
+          T o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) o[j] = dst[j] + v[j];
+          st4(dst, o);
         } else {
-          *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+          st4(dst, v);
         }
       } else {
         for (int j = 0; j < 4 && n + j < N; ++j) {
@@ -163,28 +209,29 @@ gemm_f32_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 
 // Plain shared-memory tiled kernel for shapes TMA cannot describe.
 // 64x64 CTA tile, 256 threads, 4x4 outputs per thread, BK = 16.
+template <typename T>
 __global__ void __launch_bounds__(256)
-gemm_f32_plain_kernel(const float *__restrict__ A, const float *__restrict__ B,
-                      const float *__restrict__ bias, float *__restrict__ C, int M, int N, int K,
-                      int64_t sa, int64_t sb, int64_t sc, int splits, int k_per_split,
-                      int epilogue, int mode) {
-  __shared__ float As[16][64 + 1];
-  __shared__ float Bs[16][64 + 1];
+gemm_simt_plain_kernel(const T *__restrict__ A, const T *__restrict__ B,
+                       const T *__restrict__ bias, T *__restrict__ C, int M, int N, int K,
+                       int64_t sa, int64_t sb, int64_t sc, int splits, int k_per_split,
+                       int epilogue, int mode) {
+  __shared__ T As[16][64 + 1];
+  __shared__ T Bs[16][64 + 1];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int m0 = blockIdx.x * 64, n0 = blockIdx.y * 64;
   const int batch = blockIdx.z / splits, split = blockIdx.z - batch * splits;
   const int kb = split * k_per_split, ke = min(K, kb + k_per_split);
-  const float *Ab = A + (int64_t)batch * sa;
-  const float *Bb = B + (int64_t)batch * sb;
-  float acc[4][4] = {};
+  const T *Ab = A + (int64_t)batch * sa;
+  const T *Bb = B + (int64_t)batch * sb;
+  T acc[4][4] = {};
   for (int k0 = kb; k0 < ke; k0 += 16) {
     for (int i = tid; i < 16 * 64; i += 256) {
       const int r = i / 16, c = i % 16;          // A tile: 64 rows x 16 k
       const int m = m0 + r, k = k0 + c;
-      As[c][r] = (m < M && k < ke) ? Ab[(int64_t)m * K + k] : 0.f;
+      As[c][r] = (m < M && k < ke) ? Ab[(int64_t)m * K + k] : T(0);
       const int kr = i / 64, nc = i % 64;        // B tile: 16 k x 64 cols
       const int kk = k0 + kr, n = n0 + nc;
-      Bs[kr][nc] = (kk < ke && n < N) ? Bb[(int64_t)kk * N + n] : 0.f;
+      Bs[kr][nc] = (kk < ke && n < N) ? Bb[(int64_t)kk * N + n] : T(0);
     }
     __syncthreads();
 #pragma unroll
@@ -192,20 +239,20 @@ gemm_f32_plain_kernel(const float *__restrict__ A, const float *__restrict__ B,
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(As[k][ty + 16 * i], Bs[k][tx + 16 * j], acc[i][j]);
+        for (int j = 0; j < 4; ++j) acc[i][j] = fma_t(As[k][ty + 16 * i], Bs[k][tx + 16 * j], acc[i][j]);
     __syncthreads();
   }
-  float *Cb = C + (int64_t)batch * sc;
+  T *Cb = C + (int64_t)batch * sc;
   for (int i = 0; i < 4; ++i) {
     const int m = m0 + ty + 16 * i;
     if (m >= M) continue;
     for (int j = 0; j < 4; ++j) {
       const int n = n0 + tx + 16 * j;
       if (n >= N) continue;
-      float v = acc[i][j];
+      T v = acc[i][j];
       if ((epilogue & EMMY_EPI_BIAS) && bias && (mode != GEMM_ATOMIC || split == 0)) v += bias[n];
-      if (epilogue & EMMY_EPI_RELU) v = fmaxf(v, 0.f);
-      float *dst = Cb + (int64_t)m * N + n;
+      if (epilogue & EMMY_EPI_RELU) v = fmax(v, T(0));
+      T *dst = Cb + (int64_t)m * N + n;
       if (mode == GEMM_ATOMIC) atomicAdd(dst, v);
       else if (mode == GEMM_ACCUMULATE) *dst += v;
       else *dst = v;
@@ -217,22 +264,25 @@ gemm_f32_plain_kernel(const float *__restrict__ A, const float *__restrict__ B,
 
 using namespace emmy;
 
-extern "C" int emmy_gemm_f32(const float *A, const float *B, const float *bias, float *C,
-                             int64_t batch, int64_t M, int64_t N, int64_t K, int64_t a_batch_stride,
-                             int64_t b_batch_stride, int64_t c_batch_stride, int splits,
-                             int accumulate, int epilogue, void *stream) {
+template <typename T>
+static int gemm_simt(const char *name, const T *A, const T *B, const T *bias, T *C, int64_t batch,
+                     int64_t M, int64_t N, int64_t K, int64_t a_batch_stride,
+                     int64_t b_batch_stride, int64_t c_batch_stride, int splits, int accumulate,
+                     int epilogue, void *stream) {
   using namespace gemm32;
+  constexpr int BK = Cfg<T>::BK, SMEM_BYTES = Cfg<T>::SMEM_BYTES;
+  constexpr int ES = (int)sizeof(T), VEC = 16 / ES;
   clear_error();
   if (batch < 0 || M < 0 || N < 0 || K < 0 || splits < 0)
-    return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32: negative size");
+    return set_error(EMMY_ERR_INVALID, "%s: negative size", name);
   if (batch == 0 || M == 0 || N == 0) return EMMY_OK;
-  if (!A || !B || !C) return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32: null operand");
+  if (!A || !B || !C) return set_error(EMMY_ERR_INVALID, "%s: null operand", name);
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || batch > 65535)
-    return set_error(EMMY_ERR_UNSUPPORTED, "emmy_gemm_f32: size beyond 32-bit tile indexing");
+    return set_error(EMMY_ERR_UNSUPPORTED, "%s: size beyond 32-bit tile indexing", name);
   if (epilogue & ~(EMMY_EPI_BIAS | EMMY_EPI_RELU))
-    return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32: unknown epilogue bits %d", epilogue);
+    return set_error(EMMY_ERR_INVALID, "%s: unknown epilogue bits %d", name, epilogue);
   if ((epilogue & EMMY_EPI_RELU) && (splits > 1 || accumulate))
-    return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32: relu cannot follow a partial sum");
+    return set_error(EMMY_ERR_INVALID, "%s: relu cannot follow a partial sum", name);
   cudaStream_t st = as_stream(stream);
   const int sms = sm_count();
   const int64_t mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
@@ -260,49 +310,67 @@ extern "C" int emmy_gemm_f32(const float *A, const float *B, const float *bias, 
   if (sp < 1) sp = 1;
   const int mode = sp > 1 ? GEMM_ATOMIC : (accumulate ? GEMM_ACCUMULATE : GEMM_STORE);
   if (batch > 1 && c_batch_stride < M * N)
-    return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32: batch stride of C overlaps its batches");
+    return set_error(EMMY_ERR_INVALID, "%s: batch stride of C overlaps its batches", name);
   if (mode == GEMM_ATOMIC && !accumulate) {
     const size_t elems = (size_t)((batch - 1) * c_batch_stride + M * N);
-    cudaError_t e = cudaMemsetAsync(C, 0, elems * sizeof(float), st);
-    if (e != cudaSuccess) return set_error(EMMY_ERR_CUDA, "emmy_gemm_f32: %s", cudaGetErrorString(e));
+    cudaError_t e = cudaMemsetAsync(C, 0, elems * sizeof(T), st);
+    if (e != cudaSuccess) return set_error(EMMY_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
   }
   if ((int64_t)batch * sp > 65535)
-    return set_error(EMMY_ERR_UNSUPPORTED, "emmy_gemm_f32: batch x splits beyond the grid limit");
+    return set_error(EMMY_ERR_UNSUPPORTED, "%s: batch x splits beyond the grid limit", name);
 
-  const bool tma_ok = K % 4 == 0 && N % 4 == 0 && aligned16(A) && aligned16(B) && aligned16(C) &&
-                      (a_batch_stride * 4) % 16 == 0 && (b_batch_stride * 4) % 16 == 0 &&
-                      (c_batch_stride % 4) == 0 && K > 0;
+  const bool tma_ok = K % VEC == 0 && N % 4 == 0 && aligned16(A) && aligned16(B) &&
+                      aligned16(C) && (a_batch_stride * ES) % 16 == 0 &&
+                      (b_batch_stride * ES) % 16 == 0 && (c_batch_stride % 4) == 0 && K > 0;
+  const CUtensorMapDataType tdt =
+      ES == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT64;
   if (tma_ok) {
     CUtensorMap ta, tb;
     const uint64_t adims[3] = {(uint64_t)K, (uint64_t)M, (uint64_t)batch};
-    const uint64_t astr[2] = {(uint64_t)K * 4, (uint64_t)(batch > 1 ? a_batch_stride : M * K) * 4};
+    const uint64_t astr[2] = {(uint64_t)K * ES, (uint64_t)(batch > 1 ? a_batch_stride : M * K) * ES};
     const uint32_t abox[3] = {BK, BM, 1};
     const uint64_t bdims[3] = {(uint64_t)N, (uint64_t)K, (uint64_t)batch};
-    const uint64_t bstr[2] = {(uint64_t)N * 4, (uint64_t)(batch > 1 ? b_batch_stride : K * N) * 4};
+    const uint64_t bstr[2] = {(uint64_t)N * ES, (uint64_t)(batch > 1 ? b_batch_stride : K * N) * ES};
     const uint32_t bbox[3] = {BN, BK, 1};
-    int rc = make_tensor_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, A, adims, astr, abox,
+    int rc = make_tensor_map(&ta, tdt, 3, A, adims, astr, abox,
                              CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
-    rc = make_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, B, bdims, bstr, bbox,
+    rc = make_tensor_map(&tb, tdt, 3, B, bdims, bstr, bbox,
                          CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-      cudaFuncSetAttribute(gemm_f32_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      cudaFuncSetAttribute(gemm_simt_tma_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            SMEM_BYTES);
       attr_set[dev] = true;
     }
     dim3 grid((unsigned)mt, (unsigned)nt, (unsigned)(batch * sp));
-    gemm_f32_tma_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(
+    gemm_simt_tma_kernel<T><<<grid, THREADS, SMEM_BYTES, st>>>(
         ta, tb, bias, C, (int)M, (int)N, (int)K, c_batch_stride, sp, (int)kps, epilogue, mode,
         device_status_ptr());
-    return check_launch("emmy_gemm_f32 (tma)");
+    return check_launch(name);
   }
   dim3 grid((unsigned)((M + 63) / 64), (unsigned)((N + 63) / 64), (unsigned)(batch * sp));
-  gemm_f32_plain_kernel<<<grid, 256, 0, st>>>(A, B, bias, C, (int)M, (int)N, (int)K, a_batch_stride,
-                                              b_batch_stride, c_batch_stride, sp, (int)kps,
-                                              epilogue, mode);
-  return check_launch("emmy_gemm_f32 (plain)");
+  gemm_simt_plain_kernel<T><<<grid, 256, 0, st>>>(A, B, bias, C, (int)M, (int)N, (int)K,
+                                                  a_batch_stride, b_batch_stride, c_batch_stride,
+                                                  sp, (int)kps, epilogue, mode);
+  return check_launch(name);
+}
+
+extern "C" int emmy_gemm_f32(const float *A, const float *B, const float *bias, float *C,
+                             int64_t batch, int64_t M, int64_t N, int64_t K, int64_t a_batch_stride,
+                             int64_t b_batch_stride, int64_t c_batch_stride, int splits,
+                             int accumulate, int epilogue, void *stream) {
+  return gemm_simt<float>("emmy_gemm_f32", A, B, bias, C, batch, M, N, K, a_batch_stride,
+                          b_batch_stride, c_batch_stride, splits, accumulate, epilogue, stream);
+}
+
+extern "C" int emmy_gemm_f64(const double *A, const double *B, const double *bias, double *C,
+                             int64_t batch, int64_t M, int64_t N, int64_t K, int64_t a_batch_stride,
+                             int64_t b_batch_stride, int64_t c_batch_stride, int splits,
+                             int accumulate, int epilogue, void *stream) {
+  return gemm_simt<double>("emmy_gemm_f64", A, B, bias, C, batch, M, N, K, a_batch_stride,
+                           b_batch_stride, c_batch_stride, splits, accumulate, epilogue, stream);
 }

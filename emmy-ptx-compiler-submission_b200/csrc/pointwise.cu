@@ -408,11 +408,21 @@ pointwise_simple_kernel(const PwSimple q, void *out, int out_dtype, int64_t n) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) c[j] = T(0);
     }
-    // one dispatch for the four lanes (registers in place of the shared-memory
-    // file, lane stride 1): a per-lane dispatch would unroll four copies of
-    // every op's code and run out of instruction cache
+    // registers in place of the shared-memory file (lane stride 1).  A
+    // run-time op is dispatched once for the four lanes: a per-lane dispatch
+    // would unroll four copies of every op's code.  A compile-time op is
+    // applied lane by lane (measured faster for the streaming ops).
     T o[4];
-    pw_step<T, 4, 1>(OPC >= 0 ? OPC : q.op, o, a, b, c);
+    if (OPC >= 0) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        T ra[1] = {a[j]}, rb[1] = {b[j]}, rc[1] = {c[j]}, rd[1];
+        pw_step<T, 1, 1>(OPC, rd, ra, rb, rc);
+        o[j] = rd[0];
+      }
+    } else {
+      pw_step<T, 4, 1>(q.op, o, a, b, c);
+    }
     if (F32IO) {
       float *dst = static_cast<float *>(out) + base;
       if (full) {

@@ -415,6 +415,7 @@ def matmul(M, N, K, batch=1, splits=1, dtype="f32", out_dtype=None, bias=False, 
     split (``zero_outputs`` names C), as in ``tests/variants/w_m_batch``.
     """
     out_dtype = out_dtype or dtype
+    bias_dt = "f64" if dtype == "f64" else "f32"
     esz = {"f32": 4, "f16": 2, "f64": 8}[dtype]
     vec = 16 // esz                                # elements per 16-byte copy
     bk = bk or (16 if dtype == "f32" else 32)
@@ -479,7 +480,7 @@ def matmul(M, N, K, batch=1, splits=1, dtype="f32", out_dtype=None, bias=False, 
             col = _B("+", _B("+", _B("*", V("a2_b"), L(tn)), _B("*", V("a2_u"), L(rn))), L(j))
             val = f"acc0__c{i}_{j}"
             if bias:
-                body.append(Load(names=(f"bias__c{i}_{j}",), input="bias", index=(col,), dtype=DT["f32"]))
+                body.append(Load(names=(f"bias__c{i}_{j}",), input="bias", index=(col,), dtype=DT[bias_dt]))
                 body.append(A(f"v0__c{i}_{j}", "add", (val, f"bias__c{i}_{j}")))
                 val = f"v0__c{i}_{j}"
             if relu:
@@ -495,7 +496,7 @@ def matmul(M, N, K, batch=1, splits=1, dtype="f32", out_dtype=None, bias=False, 
     args = [_arg("B", dtype, lead + [K, N], seed=1, **({"init": b_init} if b_init else {})),
             _arg("A", dtype, lead + [M, K], seed=0, **({"init": a_init} if a_init else {}))]
     if bias:
-        args.append(_arg("bias", "f32", [N], seed=2, **({"init": bias_init} if bias_init else {})))
+        args.append(_arg("bias", bias_dt, [N], seed=2, **({"init": bias_init} if bias_init else {})))
     args.append(_arg(c_name, out_dtype, lead + [M, N], output=True))
     nblocks = splits * batch * (M // tm) * (N // tn)
     return kop, _meta(entry, args, nblocks, threads, zero=[c_name] if splits > 1 else [])

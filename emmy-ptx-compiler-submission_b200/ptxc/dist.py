@@ -69,7 +69,7 @@ def shard_plan(plan: dict, rank: int, world: int):
         set_shape(a["y"], ([rows, v["inner"]] if v["inner"] > 1 else [rows])
                   if fam in ("reduce", "matvec") else
                   ([rows, v["n"], v["inner"]] if v["inner"] > 1 else [rows, v["n"]]))
-    elif fam in ("gemm_f32", "gemm_f16"):
+    elif fam in ("gemm_f32", "gemm_f64", "gemm_f16"):
         g = plan["gemm"]
         if g["batch"] >= world:
             lo, hi = shard_ranges(g["batch"], world)[rank]
@@ -134,7 +134,7 @@ def splitk_plan(plan: dict, rank: int, world: int):
     rows of B the rank reads (A's K slice is strided: the caller passes
     A[:, k0:k1] as its own contiguous tensor).
     """
-    if plan["family"] not in ("gemm_f32", "gemm_f16"):
+    if plan["family"] not in ("gemm_f32", "gemm_f64", "gemm_f16"):
         raise ValueError("split-K sharding applies to matmul plans")
     g = plan["gemm"]
     if g["batch"] != 1:

@@ -37,6 +37,7 @@ SIGNATURES = {
     "emmy_softmax_f32": [_vp, _vp, _i64, _i64, _i64, _vp],
     "emmy_matvec_f64": [_vp, _vp, _vp, _i64, _i64, _vp],
     "emmy_gemm_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _int, _vp],
+    "emmy_gemm_f64": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _int, _vp],
     "emmy_gemm_f16": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _int, _vp],
     "emmy_attention_f32": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _int, _vp],
     "emmy_attention_f16": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _vp],
@@ -181,12 +182,13 @@ def run(plan: dict, tensors: dict, stream=None, workspace=None, check: bool = Tr
         _check(lib.emmy_matvec_f64(_ptr(T("x")), _ptr(T("v")), _ptr(T("y")), v["outer"], v["n"], st),
                "emmy_matvec_f64")
         launches += 1
-    elif fam == "gemm_f32":
+    elif fam in ("gemm_f32", "gemm_f64"):
         g = plan["gemm"]
-        _check(lib.emmy_gemm_f32(_ptr(T("a")), _ptr(T("b")), _ptr(T("bias")), _ptr(T("c")),
-                                 g["batch"], g["m"], g["n"], g["k"], g["a_batch_stride"],
-                                 g["b_batch_stride"], g["c_batch_stride"], g["splits"],
-                                 int(g["accumulate"]), g["epilogue"], st), "emmy_gemm_f32")
+        fn = lib.emmy_gemm_f32 if fam == "gemm_f32" else lib.emmy_gemm_f64
+        _check(fn(_ptr(T("a")), _ptr(T("b")), _ptr(T("bias")), _ptr(T("c")),
+                  g["batch"], g["m"], g["n"], g["k"], g["a_batch_stride"],
+                  g["b_batch_stride"], g["c_batch_stride"], g["splits"],
+                  int(g["accumulate"]), g["epilogue"], st), "emmy_" + fam)
         launches += 1
     elif fam == "gemm_f16":
         g = plan["gemm"]

@@ -201,9 +201,12 @@ def match_gemm(kop, tile, meta) -> dict:
     args = {"a": a_name, "b": b_name, "c": c_name}
     if bias_name is not None:
         args["bias"] = bias_name
-    if adt == "f32":
-        need(cdt == "f32", "f32 matmul with a non-f32 output")
-        return {"family": "gemm_f32", "symbol": "emmy_gemm_f32", "args": args, "gemm": g,
+    if bias_name is not None:
+        need(dtypes[bias_name] == ("f64" if adt == "f64" else "f32"),
+             "bias vector dtype (f32, or f64 for an f64 matmul)")
+    if adt in ("f32", "f64"):
+        need(cdt == adt, f"{adt} matmul with a non-{adt} output")
+        return {"family": f"gemm_{adt}", "symbol": f"emmy_gemm_{adt}", "args": args, "gemm": g,
                 "params": {}, "dtypes": {"ab": adt, "c": cdt}}
     if adt == "f16":
         need(cdt in ("f32", "f16"), "f16 matmul output must be f16 or f32")

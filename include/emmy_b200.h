@@ -146,6 +146,18 @@ int emmy_gemm_f32(const float *A, const float *B, const float *bias, float *C, i
                   int epilogue, void *stream);
 
 /*
+ * f64 GEMM on CUDA cores (DFMA; the tensor cores have no f64 kind on sm_100a):
+ * the emmy_gemm_f32 contract on doubles -- C[b] (+)= A[b] @ B[b] (+ bias[n])
+ * (ReLU), split-K partials combined with f64 atomic adds.  Replaces the entry
+ * the reference emits for the tiled matmul shape with f64 operands
+ * (fma.rn.f64 accumulate, reference ptxc/expr.py:1179-1309, ptxc/stmts.py:614-632).
+ */
+int emmy_gemm_f64(const double *A, const double *B, const double *bias, double *C, int64_t batch,
+                  int64_t M, int64_t N, int64_t K, int64_t a_batch_stride,
+                  int64_t b_batch_stride, int64_t c_batch_stride, int splits, int accumulate,
+                  int epilogue, void *stream);
+
+/*
  * f16 GEMM with f32 accumulation on the tcgen05 tensor cores:
  * C[b] = A[b] @ B[b] (+ bias[n]) (ReLU), A [M,K] f16, B [K,N] f16 row-major,
  * C [M,N] f32 or f16 (out_dtype), bias f32 (nullable), dense batches.

@@ -1,4 +1,4 @@
-"""GPU parity of the f32 CUDA-core GEMM family (plain, batched, split-K, epilogue).
+"""GPU parity of the f32 and f64 CUDA-core GEMM family (plain, batched, split-K, epilogue).
 
 IR cases are the reference fixture shapes (``v_m_*``, ``w_m_*``), the K4a
 benchmark (split-K 256x65536x256 in 64 partitions, U(-1,1) inputs) and an
@@ -6,7 +6,9 @@ epilogue case, compiled to plans and run through the C-ABI; direct C-ABI
 cases cover shapes the TMA path cannot take (K or N not a multiple of 4).
 
 Tolerance per output element: ``|got - ref| <= 1e-5 * (|A| @ |B|)`` (the
-dot product's own scale, f64 reference), plus ``|bias|`` when a bias is added.
+dot product's own scale, f64 reference), plus ``|bias|`` when a bias is added;
+f64 operands (the reference's fma.rn.f64 accumulate): ``1e-13`` of the same
+scale against an exact-as-possible reference (``math.fsum`` rows).
 """
 
 from __future__ import annotations
@@ -95,3 +97,80 @@ def test_gemm_f32_rejects_relu_on_partial_sums():
     rc = lib.emmy_gemm_f32(ctypes.c_void_p(16), ctypes.c_void_p(16), None, ctypes.c_void_p(16),
                            1, 8, 8, 8, 0, 0, 0, 4, 0, 2, None)
     assert rc == 1
+
+
+F64_CASES = [
+    ("v_m_256_f64", dict(M=256, N=256, K=256)),
+    ("tall_split2_f64", dict(M=512, N=64, K=128, splits=2)),
+    ("batch4_split16_f64", dict(M=64, N=64, K=64, batch=4, splits=16, bk=4)),
+    ("bias_relu_f64", dict(M=192, N=320, K=200, bias=True, relu=True, tm=64, tn=64, bk=8)),
+    ("odd_k_f64", dict(M=96, N=80, K=50, tm=32, tn=16, rm=2, rn=2, bk=2)),
+    ("splitk_f64_4096", dict(M=128, N=128, K=4096, splits=8, tm=128, tn=128, rm=8, rn=8, bk=16)),
+]
+
+
+def _exact_matmul(A, B):
+    """float64 product with every dot product summed exactly (then rounded once)."""
+    import math
+    out = np.empty((A.shape[0], B.shape[1]))
+    for i in range(A.shape[0]):
+        prod = A[i][:, None] * B            # products: exact only to f64, like an fma chain
+        out[i] = [math.fsum(prod[:, j]) for j in range(B.shape[1])]
+    return out
+
+
+@pytest.mark.parametrize("name,kw", F64_CASES, ids=[c[0] for c in F64_CASES])
+def test_gemm_f64_ir(name, kw):
+    kop, meta = synth.matmul(dtype="f64", **kw)
+    plan, host, out = run_on_gpu(kop, meta)
+    assert plan["family"] == "gemm_f64"
+    x = shaped(meta, host)
+    A, B = x["A"], x["B"]
+    if A.ndim == 2:
+        A, B = A[None], B[None]
+    ref = np.stack([_exact_matmul(a, b) for a, b in zip(A, B)])
+    scale = np.stack([np.abs(a) @ np.abs(b) for a, b in zip(A, B)])
+    if "bias" in x:
+        ref = ref + x["bias"]
+        scale = scale + np.abs(x["bias"])
+    if kw.get("relu"):
+        ref = np.maximum(ref, 0)
+    got = out["C"].reshape(ref.shape)
+    assert np.all(np.abs(got - ref) <= 1e-13 * scale + 1e-300), name
+
+
+@pytest.mark.parametrize("M,N,K,batch", [(33, 30, 17, 1), (5, 7, 9, 2), (130, 4, 1024, 1),
+                                         (1, 1, 1, 1), (129, 257, 64, 1)])
+def test_gemm_f64_cabi_odd_shapes(M, N, K, batch):
+    import torch
+    from ptxc.launch import load_library
+    lib = load_library()
+    g = torch.Generator(device="cuda").manual_seed(M * 1000 + N)
+    A = torch.randn(batch, M, K, device="cuda", generator=g, dtype=torch.float64)
+    B = torch.randn(batch, K, N, device="cuda", generator=g, dtype=torch.float64)
+    C = torch.full((batch, M, N), float("nan"), device="cuda", dtype=torch.float64)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    rc = lib.emmy_gemm_f64(P(A), P(B), None, P(C), batch, M, N, K, M * K, K * N, M * N, 0, 0, 0, None)
+    assert rc == 0, lib.emmy_last_error()
+    torch.cuda.synchronize()
+    ref = torch.bmm(A, B)
+    scale = torch.bmm(A.abs(), B.abs())
+    assert torch.all((C - ref).abs() <= 1e-13 * scale + 1e-300)
+
+
+def test_gemm_f64_accumulate_adds_into_c():
+    import torch
+    from ptxc.launch import load_library
+    lib = load_library()
+    A = torch.randn(96, 64, device="cuda", dtype=torch.float64)
+    B = torch.randn(64, 80, device="cuda", dtype=torch.float64)
+    C0 = torch.randn(96, 80, device="cuda", dtype=torch.float64)
+    C = C0.clone()
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    for splits in (1, 4):
+        C.copy_(C0)
+        assert lib.emmy_gemm_f64(P(A), P(B), None, P(C), 1, 96, 80, 64, 0, 0, 0, splits, 1, 0, None) == 0
+        torch.cuda.synchronize()
+        ref = C0 + A @ B
+        scale = C0.abs() + A.abs() @ B.abs()
+        assert torch.all((C - ref).abs() <= 1e-13 * scale)
