@@ -770,3 +770,40 @@ def mm_bias_relu_chain(M, N, K, dtype="f32", c_dtype=None, out_dtype=None, compu
             a["intermediate"] = True
             a.pop("seed", None)
     return [(k1, m1), (k2, m2)]
+
+
+_ACC_NODES = {"Accum", "WarpShuffle", "TreeHalve", "Smem", "Init"}
+
+
+def retype(kop, meta, dtype, acc=None):
+    """The same IR over ``dtype`` tensors: every f32 type in the statements and
+    every f32 argument becomes ``dtype``; accumulators and the combine
+    statements that move them (Accum, WarpShuffle, TreeHalve, Smem, Init)
+    become ``acc`` (default ``dtype``).  ``acc="f32"`` over ``dtype="f16"``
+    is the f16 tensor / f32 accumulator form; ``acc="f16"`` rounds every fold
+    to f16."""
+    import dataclasses
+    acc = acc or dtype
+    to_t, to_a = DT[dtype], DT[acc]
+
+    def walk(o, target):
+        if isinstance(o, DataType):
+            return target if o.name == "f32" else o
+        if isinstance(o, tuple):
+            return tuple(walk(v, target) for v in o)
+        if dataclasses.is_dataclass(o) and not isinstance(o, type):
+            t = to_a if type(o).__name__ in _ACC_NODES else target
+            fields = {}
+            for f in dataclasses.fields(o):
+                v = getattr(o, f.name)
+                if f.name == "dtype" and v == "float":          # shared buffers name C types
+                    fields[f.name] = {"f32": "float", "f64": "double", "f16": "half"}[t.name]
+                else:
+                    fields[f.name] = walk(v, t)
+            return dataclasses.replace(o, **fields)
+        return o
+
+    new = walk(kop, to_t)
+    m = dict(meta)
+    m["args"] = [dict(a, dtype=dtype) if a["dtype"] == "f32" else dict(a) for a in meta["args"]]
+    return new, m

@@ -56,18 +56,20 @@ def shard_plan(plan: dict, rank: int, world: int):
     def set_shape(name, shape):
         sub["tensors"][name]["shape"] = list(shape)
 
-    if fam in ("reduce", "rownorm", "softmax", "matvec"):
+    if fam in ("reduce", "rownorm", "softmax", "matvec", "rowop"):
         v = plan["view"]
         lo, hi = shard_ranges(v["outer"], world)[rank]
         rows = hi - lo
         sub["view"]["outer"] = rows
         x_row = v["n"] * v["inner"]
-        y_row = v["inner"] if fam in ("reduce", "matvec") else x_row
+        reduces = fam in ("reduce", "matvec") or (
+            fam == "rowop" and plan["params"]["mode"] in ("sum", "max", "min", "dot"))
+        y_row = v["inner"] if reduces else x_row
         slices[a["x"]] = (lo * x_row, rows * x_row)
         slices[a["y"]] = (lo * y_row, rows * y_row)
         set_shape(a["x"], [rows, v["n"], v["inner"]] if v["inner"] > 1 else [rows, v["n"]])
         set_shape(a["y"], ([rows, v["inner"]] if v["inner"] > 1 else [rows])
-                  if fam in ("reduce", "matvec") else
+                  if reduces else
                   ([rows, v["n"], v["inner"]] if v["inner"] > 1 else [rows, v["n"]]))
     elif fam in ("gemm_f32", "gemm_f64", "gemm_f16"):
         g = plan["gemm"]

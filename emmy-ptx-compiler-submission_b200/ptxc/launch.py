@@ -36,6 +36,8 @@ SIGNATURES = {
     "emmy_rownorm_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _int, _vp],
     "emmy_softmax_f32": [_vp, _vp, _i64, _i64, _i64, _vp],
     "emmy_matvec_f64": [_vp, _vp, _vp, _i64, _i64, _vp],
+    "emmy_rowop": [_vp, _int, _vp, _vp, _int, _vp, _int, _i64, _i64, _i64, _int, _int, _vp, _vp,
+                   _int, _int, _vp],
     "emmy_gemm_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _int, _vp],
     "emmy_gemm_f64": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _int, _vp],
     "emmy_gemm_f16": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _int, _vp],
@@ -176,6 +178,16 @@ def run(plan: dict, tensors: dict, stream=None, workspace=None, check: bool = Tr
         v = plan["view"]
         _check(lib.emmy_softmax_f32(_ptr(T("x")), _ptr(T("y")), v["outer"], v["n"], v["inner"], st),
                "emmy_softmax_f32")
+        launches += 1
+    elif fam == "rowop":
+        v, pr, dt = plan["view"], plan["params"], plan["tensors"]
+        mode = {"sum": 0, "max": 1, "min": 2, "softmax": 3, "rms": 4, "l2": 5, "layer": 6,
+                "dot": 7}[pr["mode"]]
+        _check(lib.emmy_rowop(_ptr(T("x")), DT_CODE[dt[a["x"]]["dtype"]], _ptr(T("w")), _ptr(T("b")),
+                              DT_CODE[pr["wb_dtype"]], _ptr(T("y")), DT_CODE[dt[a["y"]]["dtype"]],
+                              v["outer"], v["n"], v["inner"], mode, REDUCE_PRE[pr["pre"]],
+                              _ptr(T("eps")), _ptr(T("count")), DT_CODE[pr["const_dtype"]],
+                              int(pr["compute"] == "f64"), st), "emmy_rowop")
         launches += 1
     elif fam == "matvec":
         v = plan["view"]

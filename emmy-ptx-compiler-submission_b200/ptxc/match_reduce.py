@@ -529,6 +529,12 @@ def match_reduction(kop, tile, meta) -> dict:
         "args": {"x": x_name, "y": y_name},
         "dtypes": {"x": xdt, "y": ydt, "acc": acc_dt},
     }
+    vec_names = list(vperm) + ([loads_v[0][0].input] if form == "dot" else [])
+    dts = {xdt, ydt, acc_dt} | {meta.dtypes[nm] for nm in list(cmap.values()) + vec_names}
+    need(dts <= {"f32", "f16", "f64"}, "row family dtypes must be f16 / f32 / f64")
+    f64_dot = form == "dot" and {xdt, ydt, meta.dtypes[loads_v[0][0].input]} == {"f64"}
+    if (dts != {"f32"} or form == "dot") and not f64_dot:
+        return _rowop_plan(plan, form, system, cmap, vec_names, view, meta, dts)
     if form in ("sum", "mean", "max", "min"):
         need(xdt == "f32" and ydt == "f32", "only f32 reductions have a B200 kernel")
         plan["family"] = "reduce"
@@ -566,6 +572,44 @@ def match_reduction(kop, tile, meta) -> dict:
             plan["args"]["w"] = vperm[0]
         if len(vperm) >= 2:
             plan["args"]["b"] = vperm[1]
+    return plan
+
+
+def _rowop_plan(plan, form, system, cmap, vec_names, view, meta, dts):
+    """Any row family over f16 / f64 (or mixed) tensors: ``emmy_rowop``,
+    computed in f64 when any tensor or the accumulator is f64, else in f32."""
+    mode = {"sum": "sum", "mean": "sum", "max": "max", "min": "min", "softmax": "softmax",
+            "dot": "dot", "rms": "rms", "rms_w": "rms", "l2": "l2", "ln": "layer",
+            "ln_w": "layer", "ln_wb": "layer"}[form]
+    if mode in ("rms", "l2", "layer", "dot"):
+        need(view["inner"] == 1, "row normalisation over a strided axis")
+    wb = {meta.dtypes[nm] for nm in vec_names}
+    need(len(wb) <= 1, "weight and bias dtypes differ")
+    consts = {meta.dtypes[nm] for nm in cmap.values()}
+    need(len(consts) <= 1, "eps and count dtypes differ")
+    plan["family"] = "rowop"
+    plan["symbol"] = "emmy_rowop"
+    plan["params"] = {
+        "mode": mode,
+        "pre": {"sumsq": "square", "sumabs": "abs"}.get(system, "identity")
+        if mode in ("sum", "max", "min") else "identity",
+        "compute": "f64" if "f64" in dts else "f32",
+        "wb_dtype": wb.pop() if wb else "f32",
+        "const_dtype": consts.pop() if consts else "f32",
+    }
+    if form == "mean":
+        plan["args"]["count"] = cmap["count"]
+    elif mode in ("rms", "layer"):
+        if "eps" in cmap:
+            plan["args"]["eps"] = cmap["eps"]
+        if "count" in cmap:
+            plan["args"]["count"] = cmap["count"]
+    if mode == "dot":
+        plan["args"]["w"] = vec_names[0]
+    elif len(vec_names) >= 1:
+        plan["args"]["w"] = vec_names[0]
+        if len(vec_names) >= 2:
+            plan["args"]["b"] = vec_names[1]
     return plan
 
 

@@ -55,6 +55,9 @@ EXACT = {
     "pointwise_gelu_f16": lambda: synth.pointwise(
         1 << 20, ("gelu_tanh", "x0"), "f16"),
     "attention_f16": lambda: synth.attention(2, 8, 256, 128, dtype="f16"),
+    "softmax_f16_rows": lambda: synth.retype(*synth.softmax([300, 1024]), "f16", acc="f32"),
+    "broadcast_bias": lambda: synth.pointwise(512 * 768, ("add", "x0", ("bcast", "b", 768, 1, 768)),
+                                              "f32", shape=[512, 768]),
 }
 
 

@@ -130,7 +130,14 @@ def test_partial_block_collective_is_refused():
         Lowerer(kop, meta).plan()
 
 
-def test_unsupported_dtype_is_refused_not_guessed():
+def test_non_f32_row_families_take_the_typed_kernel():
     kop, meta = synth.reduce([4, 64], -1, "sum", dtype="f64")
-    with pytest.raises(CompileError, match="only f32 reductions"):
+    plan = Lowerer(kop, meta).plan()
+    assert plan["family"] == "rowop" and plan["params"]["compute"] == "f64"
+
+
+def test_unsupported_dtype_is_refused_not_guessed():
+    kop, meta = synth.reduce([4, 64], -1, "sum", dtype="f32")
+    meta["args"] = [dict(a, dtype="i32") if a["name"] == "x" else a for a in meta["args"]]
+    with pytest.raises(CompileError, match="f16 / f32 / f64"):
         Lowerer(kop, meta).plan()
