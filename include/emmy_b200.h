@@ -122,6 +122,26 @@ int emmy_softmax_f32(const float *x, float *y, int64_t outer, int64_t n, int64_t
                      void *stream);
 
 /*
+ * Row families over f16 / f32 / f64 tensors in any mix, x viewed as
+ * [outer, n, inner] (inner > 1: reductions and softmax only):
+ *   mode 0/1/2  y[o, i] = sum / max / min over n of pre(x)   (pre: EMMY_PRE_*;
+ *               count non-null: y = sum * 1/count, the IR's mean)
+ *   mode 3      softmax over n
+ *   mode 4/5/6  rms / l2 / layer normalisation of each row (w, b nullable;
+ *               eps, count one-element buffers as in emmy_rownorm_f32)
+ *   mode 7      y[o] = sum_j x[o, j] * w[j]  (dot with a row-invariant vector)
+ * Dtypes are EMMY_DT_*: x_dtype, y_dtype, wb_dtype (w and b), const_dtype
+ * (eps, count).  compute_f64 computes in double, else float; the result is
+ * rounded once, at the store.  Replaces the entries the reference emits for
+ * these IR shapes with f16 or f64 types (f16 widened to f32,
+ * reference ptxc/expr.py:168-180; f64 arithmetic ptxc/expr.py:1179-1309).
+ */
+int emmy_rowop(const void *x, int x_dtype, const void *w, const void *b, int wb_dtype, void *y,
+               int y_dtype, int64_t outer, int64_t n, int64_t inner, int mode, int pre,
+               const void *eps, const void *count, int const_dtype, int compute_f64,
+               void *stream);
+
+/*
  * f64 matrix-vector product y[rows] = A[rows, cols] @ v[cols].
  * Replaces the entry the reference emits for the dot-with-vector reduction
  * shape (StridedLoop over a row with Load A, Load v, multiply, Accum add, then
