@@ -28,7 +28,7 @@ enum PwOp {
   PW_COPY = 0, PW_ADD, PW_SUB, PW_MUL, PW_DIV, PW_MAX, PW_MIN, PW_NEG, PW_ABS, PW_EXP, PW_LOG,
   PW_SQRT, PW_RSQRT, PW_RECIP, PW_TANH, PW_SIGMOID, PW_RELU, PW_GT, PW_LT, PW_GE, PW_LE, PW_EQ,
   PW_WHERE, PW_ROUND_F16, PW_FMA, PW_LOG2, PW_LOG10, PW_COS, PW_SIN, PW_TAN, PW_ERF, PW_GELU,
-  PW_GELU_TANH, PW_SOFTPLUS, PW_EXP2, PW_SILU, PW_POW, PW_FLOOR, PW_CEIL, PW_SIGN, PW_NOPS
+  PW_GELU_TANH, PW_SOFTPLUS, PW_EXP2, PW_SILU, PW_POW, PW_FLOOR, PW_CEIL, PW_SIGN, PW_NE, PW_NOPS
 };
 
 // A broadcast input is read at ((first + e) / div) % mod for element e (mod
@@ -137,6 +137,7 @@ __device__ __forceinline__ void pw_step(int op, T *RD, const T *RA, const T *RB,
     case PW_GE: PW_LANES(a >= b ? one : zero)
     case PW_LE: PW_LANES(a <= b ? one : zero)
     case PW_EQ: PW_LANES(a == b ? one : zero)
+    case PW_NE: PW_LANES(a != b ? one : zero)     // unordered: true when either is NaN (setp.neu)
     case PW_WHERE: PW_LANES(a != zero ? b : c)
     case PW_ROUND_F16: PW_LANES(T(__half2float(__float2half_rn(float(a)))))
     case PW_FMA: PW_LANES(fma_rn(a, b, c))
@@ -583,14 +584,15 @@ static int pointwise_impl(const void *const *inputs, const int *input_dtypes,
   // run faster in the general kernel, whose threads take two groups each.
   const int op0 = program[0];
   const bool cheap = op0 <= PW_ABS || (op0 >= PW_RELU && op0 <= PW_FMA) || op0 == PW_FLOOR ||
-                     op0 == PW_CEIL || op0 == PW_SIGN || op0 == PW_SQRT;
+                     op0 == PW_CEIL || op0 == PW_SIGN || op0 == PW_SQRT || op0 == PW_NE;
   if (vec_ok && !bcast && n_instr == 1 && result_reg == nleaf && cheap) {
     // one step on leaves only: the register kernel
     const int op = program[0];
     const int arity = (op == PW_WHERE || op == PW_FMA) ? 3
                       : (op == PW_ADD || op == PW_SUB || op == PW_MUL || op == PW_DIV ||
                          op == PW_MAX || op == PW_MIN || op == PW_GT || op == PW_LT ||
-                         op == PW_GE || op == PW_LE || op == PW_EQ || op == PW_POW)
+                         op == PW_GE || op == PW_LE || op == PW_EQ || op == PW_NE ||
+                         op == PW_POW)
                           ? 2
                           : 1;
     PwSimple q{};

@@ -35,10 +35,14 @@ struct Args {
   int64_t outer, n, inner;
 };
 
+// Plain loads on purpose: the half-precision __ldg is a non-volatile inline
+// asm statement, which the compiler may speculate out of an `if (ptr)` or a
+// dtype switch -- a load through a null weight pointer that faulted.  A plain
+// load is never speculated through a pointer not known to be valid.
 template <typename TC> __device__ __forceinline__ TC ld(const void *p, int dt, int64_t i) {
-  if (dt == EMMY_DT_F16) return TC(__half2float(__ldg(static_cast<const __half *>(p) + i)));
-  if (dt == EMMY_DT_F64) return TC(__ldg(static_cast<const double *>(p) + i));
-  return TC(__ldg(static_cast<const float *>(p) + i));
+  if (dt == EMMY_DT_F16) return TC(__half2float(static_cast<const __half *>(p)[i]));
+  if (dt == EMMY_DT_F64) return TC(static_cast<const double *>(p)[i]);
+  return TC(static_cast<const float *>(p)[i]);
 }
 
 __device__ __forceinline__ __half to_half(float v) { return __float2half_rn(v); }

@@ -518,7 +518,7 @@ def attention(B, H, S, D, dtype="f16", out_dtype=None, scale_div=None, entry="k_
     out_dtype = out_dtype or dtype
     Dv = Dv or D
     div = float(scale_div if scale_div is not None else math.sqrt(D))
-    rows_u, cols_u = 1, min(Dv, 64)
+    rows_u, cols_u = 1, max(c for c in range(1, min(Dv, 64) + 1) if Dv % c == 0)
     threads = rows_u * cols_u
     axes = [ax("a6", B), ax("a7", H),
             Axis(name="a0_b", extent=Dim(S // rows_u), window=None),
@@ -582,7 +582,7 @@ def attention(B, H, S, D, dtype="f16", out_dtype=None, scale_div=None, entry="k_
 # pointwise (v_p_* / w_p_* shape)
 
 BOOL = DataType(name="bool", np=NpDType("bool"), nbytes=1)
-_COMPARE = {"greater", "less", "greater_equal", "less_equal", "equal"}
+_COMPARE = {"greater", "less", "greater_equal", "less_equal", "equal", "not_equal"}
 
 
 def pointwise(n, expr, dtype="f32", shape=None, block=256, unroll=None, entry="k_pointwise",

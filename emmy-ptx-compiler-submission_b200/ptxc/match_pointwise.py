@@ -35,18 +35,18 @@ OPCODES = {
     "greater_equal": 19, "less_equal": 20, "equal": 21, "where": 22, "round_f16": 23,
     "fma": 24, "log2": 25, "log10": 26, "cos": 27, "sin": 28, "tan": 29, "erf": 30,
     "gelu": 31, "gelu_tanh": 32, "softplus": 33, "exp2": 34, "silu": 35, "pow": 36,
-    "floor": 37, "ceil": 38, "sign": 39,
+    "floor": 37, "ceil": 38, "sign": 39, "not_equal": 40,
 }
 ALIASES = {"sum": "add", "sub": "subtract", "prod": "multiply", "true_divide": "divide",
            "divide_rn_f32": "divide", "amax": "maximum", "max": "maximum", "min": "minimum",
            "negate": "negative", "fabs": "abs", "gt": "greater", "lt": "less",
-           "ge": "greater_equal", "le": "less_equal", "eq": "equal", "exp_fast": "exp",
+           "ge": "greater_equal", "le": "less_equal", "eq": "equal", "ne": "not_equal", "exp_fast": "exp",
            "pad": "copy", "bitcast": "copy"}
 ARITY = {"where": 3, "fma": 3}
 UNARY = {"copy", "negative", "abs", "exp", "log", "sqrt", "rsqrt", "reciprocal", "tanh",
          "sigmoid", "relu", "round_f16", "log2", "log10", "cos", "sin", "tan", "erf", "gelu",
          "gelu_tanh", "softplus", "exp2", "silu", "floor", "ceil", "sign"}
-COMPARES = {"greater", "less", "greater_equal", "less_equal", "equal"}
+COMPARES = {"greater", "less", "greater_equal", "less_equal", "equal", "not_equal"}
 MAX_REGS = 32
 MAX_INSTR = 48
 

@@ -230,7 +230,8 @@ int emmy_attention_f16(const void *q, const void *k, const void *v, void *o,
  * 18 less, 19 greater_equal, 20 less_equal, 21 equal, 22 where(a, b, c),
  * 23 round to f16, 24 fma, 25 log2, 26 log10, 27 cos, 28 sin, 29 tan, 30 erf,
  * 31 gelu, 32 gelu_tanh, 33 softplus, 34 exp2, 35 silu, 36 pow, 37 floor,
- * 38 ceil, 39 sign.  Comparisons give 1 or 0.  compute_f64 selects double
+ * 38 ceil, 39 sign, 40 not_equal (unordered: true when either side is NaN).
+ * Comparisons give 1 or 0.  compute_f64 selects double
  * arithmetic, else f32; add/subtract/multiply/divide/sqrt/fma are correctly
  * rounded and never contracted.  Limits: 8 inputs, 8 scalars, 8 immediates,
  * 48 steps, 32 registers in all.

@@ -749,6 +749,8 @@ def _elementwise(opname, args, kinds, kind):
         return (a <= b), "pred"
     if opname in ("equal", "eq"):
         return (a == b), "pred"
+    if opname in ("not_equal", "ne"):
+        return (a != b), "pred"          # unordered, as setp.neu (ptxc/expr.py:785-786)
     if opname == "where":
         c = args[0]
         c = c if c.dtype == torch.bool else (c != 0)

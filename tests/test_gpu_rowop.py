@@ -112,6 +112,17 @@ def test_rmsnorm_and_l2(dt, acc):
     _run(kop, meta, "norm", lambda x: F.l2norm(x["x"].astype(np.float64), out_dtype=np.float64))
 
 
+@pytest.mark.parametrize("dt", ["f16", "f64"])
+def test_norms_without_weights(dt):
+    """Null weight / bias / eps pointers: nothing may be loaded through them."""
+    kop, meta = synth.retype(*synth.rmsnorm(64, 512, eps=1e-5, weight=False), dt, acc="f32" if dt == "f16" else dt)
+    _run(kop, meta, "norm", lambda x: F.rmsnorm(x["x"].astype(np.float64), None, 1e-5,
+                                                out_dtype=np.float64))
+    kop, meta = synth.retype(*synth.layernorm(64, 512, affine=False), dt)
+    _run(kop, meta, "norm", lambda x: F.layernorm(x["x"].astype(np.float64), None, None, 1e-5,
+                                                  out_dtype=np.float64))
+
+
 @pytest.mark.parametrize("dt", ["f32", "f16"])
 def test_dot_with_vector(dt):
     kop, meta = synth.matvec(512, 1000, dtype=dt)
