@@ -369,6 +369,45 @@ def family_extras(device, peak):
         row[key + "_tflops"] = round(2.0 * 4096 * 8192 * 2048 / (ms * 1e-3) / 1e12, 2)
         del ex
     out["F2_chain_mm_bias_relu_f16_4096x2048x8192"] = row
+    # K1 is launch-bound as one launch (16 MB): the same kernel replayed from a
+    # CUDA graph, back to back over 8 separate input/output pairs (256 MB in
+    # all, so every launch reads from HBM), amortises the launch
+    kop, meta = synth.rmsnorm(4096, 512, eps=1e-6)
+    plan = Lowerer(kop, meta).plan()
+    exs = [Executor(plan, device=device) for _ in range(8)]
+    for ex in exs:
+        for t in ex.tensors.values():
+            t.normal_()
+        for a in meta["args"]:
+            if "data" in a:
+                ex.tensors[a["name"]].fill_(float(a["data"][0]))
+    side = torch.cuda.Stream(device=device)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for ex in exs:
+            ex.launch()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for ex in exs:
+            ex.launch()
+    for _ in range(3):
+        graph.replay()
+    times = []
+    for _ in range(10):
+        flush()
+        torch.cuda._sleep(SPIN_CYCLES)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = statistics.median(times) / len(exs)
+    gbs = plan_bytes(plan) / (ms * 1e-3) / 1e9
+    out["K1_rmsnorm_4096x512_graph8"] = {"us_per_launch": round(ms * 1000, 2), "gbs": round(gbs, 1),
+                                         "frac_hbm": round(gbs / peak, 3), "launches": len(exs)}
+    del graph, exs
     del flush
     torch.cuda.empty_cache()
     return out

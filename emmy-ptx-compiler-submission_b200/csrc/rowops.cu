@@ -38,6 +38,33 @@ __device__ __forceinline__ float group_sum(float v, float *red) {
   return v;
 }
 
+// two sums reduced together (one shared-memory stage for both)
+template <int TPR>
+__device__ __forceinline__ void group_sum2(float &a, float &b, float *red) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  if constexpr (TPR > 32) {
+    constexpr int W = TPR / 32;
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) {
+      red[w] = a;
+      red[16 + w] = b;
+    }
+    __syncthreads();
+    a = l < W ? red[l] : 0.f;
+    b = l < W ? red[16 + l] : 0.f;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      a += __shfl_xor_sync(0xffffffffu, a, o);
+      b += __shfl_xor_sync(0xffffffffu, b, o);
+    }
+  }
+}
+
 template <int TPR>
 __device__ __forceinline__ float group_max(float v, float *red) {
   v = warp_max(v);
@@ -169,26 +196,24 @@ row_resident_kernel(const float *__restrict__ x, const float *__restrict__ w,
           else __stcs(yr + idx, o[0]);
         }
       }
-    } else {  // MODE_LN: two register passes, mean then centred variance
-      float s = 0.f;
+    } else {  // MODE_LN: the IR's two moments in one pass, var = E[x^2] - mean^2
+      float s = 0.f, q2 = 0.f;
 #pragma unroll
       for (int c = 0; c < NCH; ++c)
 #pragma unroll
-        for (int k = 0; k < VEC; ++k) s += v[c][k];
-      s = group_sum<TPR>(s, red);
-      const float mean = s * inv_count;
-      float q2 = 0.f;
-#pragma unroll
-      for (int c = 0; c < NCH; ++c)
-        if (((int64_t)c * TPR + t) * VEC < cols) {
-#pragma unroll
-          for (int k = 0; k < VEC; ++k) {
-            v[c][k] = v[c][k] - mean;
-            q2 = fmaf(v[c][k], v[c][k], q2);
-          }
+        for (int k = 0; k < VEC; ++k) {
+          s += v[c][k];
+          q2 = fmaf(v[c][k], v[c][k], q2);
         }
-      q2 = group_sum<TPR>(q2, red);
-      const float r = 1.0f / sqrtf(q2 * inv_count + eps);
+      group_sum2<TPR>(s, q2, red);
+      const float mean = s * inv_count;
+#pragma unroll
+      for (int c = 0; c < NCH; ++c)
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) v[c][k] = v[c][k] - mean;
+      // rounded op by op like the IR (mul, mul, sub, add: no contraction)
+      const float var = __fsub_rn(__fmul_rn(q2, inv_count), __fmul_rn(mean, mean));
+      const float r = 1.0f / sqrtf(__fadd_rn(var, eps));
 #pragma unroll
       for (int c = 0; c < NCH; ++c) {
         const int64_t idx = ((int64_t)c * TPR + t) * VEC;
