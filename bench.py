@@ -598,6 +598,14 @@ PROFILE_CASES = {
                                       tm=128, tn=128, rm=8, rn=8),
     "rmsnorm_K1": lambda s: s.rmsnorm(4096, 512, eps=1e-6),
     "pointwise_gelu_f16_2^26": lambda s: s.pointwise(1 << 26, ("gelu_tanh", "x0"), "f16"),
+    "pointwise_bias_relu_f32_16384x4096": lambda s: s.pointwise(
+        16384 * 4096, ("relu", ("add", "x0", ("bcast", "b", 4096, 1, 4096))), "f32",
+        shape=[16384, 4096]),
+    "gemm_f64_2048": lambda s: s.matmul(2048, 2048, 2048, dtype="f64", tm=128, tn=128, rm=8, rn=8,
+                                        bk=16),
+    "rowop_softmax_f16_16384x4096": lambda s: s.retype(*s.softmax([16384, 4096]), "f16", acc="f32"),
+    "rowop_layernorm_f16_16384x1024": lambda s: s.retype(*s.layernorm(16384, 1024), "f16",
+                                                         acc="f32"),
 }
 
 
