@@ -298,6 +298,10 @@ def family_extras(device, peak):
         "F8a_pointwise_add_f32_2^26": synth.pointwise(1 << 26, ("add", "x0", "x1"), "f32"),
         "F8b_pointwise_gelu_tanh_f16_16384x4096": synth.pointwise(
             16384 * 4096, ("gelu_tanh", "x0"), "f16", shape=[16384, 4096]),
+        "F8c_pointwise_bias_relu_f32_16384x4096": synth.pointwise(
+            16384 * 4096, ("relu", ("add", "x0", ("bcast", "b", 4096, 1, 4096))), "f32",
+            shape=[16384, 4096]),
+        "X_softmax_f16_16384x4096": synth.retype(*synth.softmax([16384, 4096]), "f16", acc="f32"),
     }
     for name, (kop, meta) in cases.items():
         plan = Lowerer(kop, meta).plan()

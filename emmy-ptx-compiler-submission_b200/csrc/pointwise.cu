@@ -214,19 +214,35 @@ template <typename T> __device__ __forceinline__ T pw_load_bcast(const PwProgram
   return pw_load1<T>(p.inputs[k], p.in_dtype[k], (int64_t)q);
 }
 
-// Elements e .. e+VEC-1 of broadcast input k: one quotient per group, the
+// Elements e .. e+VEC-1 of a broadcast input: one quotient per group, the
 // other lanes step from it (the quotient moves by at most one per lane when
 // div >= VEC; smaller divisors divide per lane).
 template <typename T, int VEC>
-__device__ __forceinline__ void pw_load_bcast_vec(const PwProgram &p, int k, int64_t e, int64_t n,
-                                                  T v[VEC]) {
-  const PwIndex &x = p.idx[k];
-  if (VEC == 1 || x.div.d < (unsigned long long)VEC) {
+__device__ __forceinline__ void pw_bcast_group(const void *ptr, int dt, const PwIndex &x,
+                                               long long first, int64_t e, int64_t n, T v[VEC]) {
+  if (VEC > 1 && x.div.d == 1 && (!x.has_mod || x.mod.d >= (unsigned long long)VEC)) {
+    // e % M: one remainder per group, consecutive lanes wrap at most once
+    const unsigned long long x0 = (unsigned long long)(first + e);
+    unsigned long long m0 = x0;
+    if (x.has_mod) m0 = x0 - pw_div(x.mod, x0) * x.mod.d;
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) v[j] = e + j < n ? pw_load_bcast<T>(p, k, e + j) : T(0);
+    for (int j = 0; j < VEC; ++j) {
+      unsigned long long idx = m0 + j;
+      if (x.has_mod && idx >= x.mod.d) idx -= x.mod.d;
+      v[j] = e + j < n ? pw_load1<T>(ptr, dt, (int64_t)idx) : T(0);
+    }
     return;
   }
-  const unsigned long long x0 = (unsigned long long)(p.first + e);
+  if (VEC == 1 || x.div.d < (unsigned long long)VEC) {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      unsigned long long q = pw_div(x.div, (unsigned long long)(first + e + j));
+      if (x.has_mod) q -= pw_div(x.mod, q) * x.mod.d;
+      v[j] = e + j < n ? pw_load1<T>(ptr, dt, (int64_t)q) : T(0);
+    }
+    return;
+  }
+  const unsigned long long x0 = (unsigned long long)(first + e);
   const unsigned long long q0 = pw_div(x.div, x0);
   const unsigned long long r0 = x0 - q0 * x.div.d;
   unsigned long long m0 = q0;
@@ -236,8 +252,14 @@ __device__ __forceinline__ void pw_load_bcast_vec(const PwProgram &p, int k, int
 #pragma unroll
   for (int j = 0; j < VEC; ++j) {
     const unsigned long long idx = r0 + j < x.div.d ? m0 : m1;
-    v[j] = e + j < n ? pw_load1<T>(p.inputs[k], p.in_dtype[k], (int64_t)idx) : T(0);
+    v[j] = e + j < n ? pw_load1<T>(ptr, dt, (int64_t)idx) : T(0);
   }
+}
+
+template <typename T, int VEC>
+__device__ __forceinline__ void pw_load_bcast_vec(const PwProgram &p, int k, int64_t e, int64_t n,
+                                                  T v[VEC]) {
+  pw_bcast_group<T, VEC>(p.inputs[k], p.in_dtype[k], p.idx[k], p.first, e, n, v);
 }
 
 // BC: some inputs are broadcast (read through PwIndex).
@@ -336,15 +358,20 @@ pointwise_kernel(const PwProgram p, void *out, int out_dtype, int64_t n) {
 // One-step programs (the commonest pointwise shape: x op y, x op c, op x):
 // operands straight from the loaded registers, no shared register file.
 // Operand kinds: 0 = input tensor, 1 = one-element scalar tensor, 2 = immediate.
+// Operand kinds: 0 = input tensor, 1 = one-element scalar tensor,
+// 2 = immediate, 3 = broadcast input (read through idx).  `post` (>= 0) is a
+// unary op applied to the step's result (x + b then ReLU).
 struct PwSimple {
   const void *ptr[3];
   int dtype[3];
   int kind[3];
   double imm[3];
-  int nops, op;
+  PwIndex idx[3];
+  long long first;
+  int nops, op, post;
 };
 
-template <typename T>
+template <typename T, bool BC>
 __device__ __forceinline__ void pw_simple_operand_f32(const PwSimple &q, int k, int64_t base,
                                                       bool full, int64_t n, T v[4]) {
   if (q.kind[k] == 0) {
@@ -356,6 +383,8 @@ __device__ __forceinline__ void pw_simple_operand_f32(const PwSimple &q, int k, 
 #pragma unroll
       for (int j = 0; j < 4; ++j) v[j] = base + j < n ? T(p[j]) : T(0);
     }
+  } else if (BC && q.kind[k] == 3) {
+    pw_bcast_group<T, 4>(q.ptr[k], EMMY_DT_F32, q.idx[k], q.first, base, n, v);
   } else {
     const T c = q.kind[k] == 1 ? T(*static_cast<const float *>(q.ptr[k])) : T(q.imm[k]);
 #pragma unroll
@@ -363,7 +392,7 @@ __device__ __forceinline__ void pw_simple_operand_f32(const PwSimple &q, int k, 
   }
 }
 
-template <typename T>
+template <typename T, bool BC>
 __device__ __forceinline__ void pw_simple_operand(const PwSimple &q, int k, int64_t base, bool full,
                                                   int64_t n, T v[4]) {
   if (q.kind[k] == 0) {
@@ -373,6 +402,8 @@ __device__ __forceinline__ void pw_simple_operand(const PwSimple &q, int k, int6
 #pragma unroll
       for (int j = 0; j < 4; ++j) v[j] = base + j < n ? pw_load1<T>(q.ptr[k], q.dtype[k], base + j) : T(0);
     }
+  } else if (BC && q.kind[k] == 3) {
+    pw_bcast_group<T, 4>(q.ptr[k], q.dtype[k], q.idx[k], q.first, base, n, v);
   } else {
     const T c = q.kind[k] == 1 ? pw_load1<T>(q.ptr[k], q.dtype[k], 0) : T(q.imm[k]);
 #pragma unroll
@@ -383,7 +414,23 @@ __device__ __forceinline__ void pw_simple_operand(const PwSimple &q, int k, int6
 // OPC >= 0 fixes the op at compile time (the six arithmetic ops) and F32IO
 // fixes every tensor operand and the output to f32: a small kernel that stays
 // at full occupancy.  OPC < 0 dispatches q.op at run time.
-template <typename T, int OPC, bool F32IO>
+// The cheap unary ops a one-step program may be followed by.
+template <typename T> __device__ __forceinline__ T pw_post(int op, T v) {
+  switch (op) {
+    case PW_RELU: return fmax(v, T(0));
+    case PW_NEG: return -v;
+    case PW_ABS: return fabs(v);
+    case PW_ROUND_F16: return T(__half2float(__float2half_rn(float(v))));
+    case PW_SQRT: return sqrt_rn(v);
+    case PW_FLOOR: return floor(v);
+    case PW_CEIL: return ceil(v);
+    case PW_SIGN: return v > T(0) ? T(1) : (v < T(0) ? T(-1) : v);
+    default: return v;                                  // PW_COPY
+  }
+}
+
+// POST: a unary op follows the step; BC: some operand is a broadcast input.
+template <typename T, int OPC, bool F32IO, bool POST, bool BC>
 __global__ void __launch_bounds__(kPwThreads)
 pointwise_simple_kernel(const PwSimple q, void *out, int out_dtype, int64_t n) {
   const int64_t groups = (n + 3) / 4;
@@ -393,13 +440,13 @@ pointwise_simple_kernel(const PwSimple q, void *out, int out_dtype, int64_t n) {
     const bool full = base + 4 <= n;
     T a[4], b[4], c[4];
     if (F32IO) {
-      pw_simple_operand_f32(q, 0, base, full, n, a);
-      if (q.nops > 1) pw_simple_operand_f32(q, 1, base, full, n, b);
-      if (q.nops > 2) pw_simple_operand_f32(q, 2, base, full, n, c);
+      pw_simple_operand_f32<T, BC>(q, 0, base, full, n, a);
+      if (q.nops > 1) pw_simple_operand_f32<T, BC>(q, 1, base, full, n, b);
+      if (q.nops > 2) pw_simple_operand_f32<T, BC>(q, 2, base, full, n, c);
     } else {
-      pw_simple_operand<T>(q, 0, base, full, n, a);
-      if (q.nops > 1) pw_simple_operand<T>(q, 1, base, full, n, b);
-      if (q.nops > 2) pw_simple_operand<T>(q, 2, base, full, n, c);
+      pw_simple_operand<T, BC>(q, 0, base, full, n, a);
+      if (q.nops > 1) pw_simple_operand<T, BC>(q, 1, base, full, n, b);
+      if (q.nops > 2) pw_simple_operand<T, BC>(q, 2, base, full, n, c);
     }
     if (q.nops < 2) {
 #pragma unroll
@@ -423,6 +470,10 @@ pointwise_simple_kernel(const PwSimple q, void *out, int out_dtype, int64_t n) {
       }
     } else {
       pw_step<T, 4, 1>(q.op, o, a, b, c);
+    }
+    if (POST) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = pw_post<T>(q.post, o[j]);
     }
     if (F32IO) {
       float *dst = static_cast<float *>(out) + base;
@@ -499,6 +550,18 @@ static PwDiv make_div(unsigned long long d) {
 }  // namespace emmy
 
 using namespace emmy;
+
+template <typename T, int OPC, bool IO>
+static void launch_simple(const PwSimple &q, void *out, int out_dtype, int64_t n, unsigned gb,
+                          cudaStream_t st, bool has_bc) {
+  if (q.post >= 0) {
+    if (has_bc) pointwise_simple_kernel<T, OPC, IO, true, true><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+    else pointwise_simple_kernel<T, OPC, IO, true, false><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+  } else {
+    if (has_bc) pointwise_simple_kernel<T, OPC, IO, false, true><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+    else pointwise_simple_kernel<T, OPC, IO, false, false><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+  }
+}
 
 static int pointwise_impl(const void *const *inputs, const int *input_dtypes,
                           const int64_t *input_index, int n_inputs, const void *const *scalars,
@@ -582,26 +645,38 @@ static int pointwise_impl(const void *const *inputs, const int *input_dtypes,
   const int nleaf = n_inputs + n_scalars + n_imm;
   // Transcendental steps (exp, log, tanh, gelu, ...) are issue-bound; they
   // run faster in the general kernel, whose threads take two groups each.
-  const int op0 = program[0];
-  const bool cheap = op0 <= PW_ABS || (op0 >= PW_RELU && op0 <= PW_FMA) || op0 == PW_FLOOR ||
-                     op0 == PW_CEIL || op0 == PW_SIGN || op0 == PW_SQRT || op0 == PW_NE;
-  if (vec_ok && !bcast && n_instr == 1 && result_reg == nleaf && cheap) {
-    // one step on leaves only: the register kernel
+  auto cheap = [](int op) {
+    return op <= PW_ABS || (op >= PW_RELU && op <= PW_FMA) || op == PW_FLOOR || op == PW_CEIL ||
+           op == PW_SIGN || op == PW_SQRT || op == PW_NE;
+  };
+  auto arity_of = [](int op) {
+    return (op == PW_WHERE || op == PW_FMA) ? 3
+           : (op == PW_ADD || op == PW_SUB || op == PW_MUL || op == PW_DIV || op == PW_MAX ||
+              op == PW_MIN || op == PW_GT || op == PW_LT || op == PW_GE || op == PW_LE ||
+              op == PW_EQ || op == PW_NE || op == PW_POW)
+               ? 2
+               : 1;
+  };
+  // one step on leaves, optionally followed by one unary step on its result
+  // (the bias + ReLU shape): the register kernel
+  const bool one = n_instr == 1 && result_reg == nleaf;
+  const bool two = n_instr == 2 && result_reg == nleaf + 1 && arity_of(program[5]) == 1 &&
+                   program[7] == nleaf && cheap(program[5]);
+  bool leaves_only = true;
+  for (int k = 0; k < arity_of(program[0]); ++k) leaves_only = leaves_only && program[2 + k] < nleaf;
+  if (vec_ok && (one || two) && leaves_only && cheap(program[0])) {
     const int op = program[0];
-    const int arity = (op == PW_WHERE || op == PW_FMA) ? 3
-                      : (op == PW_ADD || op == PW_SUB || op == PW_MUL || op == PW_DIV ||
-                         op == PW_MAX || op == PW_MIN || op == PW_GT || op == PW_LT ||
-                         op == PW_GE || op == PW_LE || op == PW_EQ || op == PW_NE ||
-                         op == PW_POW)
-                          ? 2
-                          : 1;
+    const int arity = arity_of(op);
     PwSimple q{};
     q.op = op;
     q.nops = arity;
+    q.post = two ? program[5] : -1;
+    q.first = first;
     for (int k = 0; k < arity; ++k) {
       const int r = program[2 + k];
       if (r < n_inputs) {
-        q.kind[k] = 0; q.ptr[k] = inputs[r]; q.dtype[k] = input_dtypes[r];
+        q.kind[k] = p.idx[r].bcast ? 3 : 0; q.ptr[k] = inputs[r]; q.dtype[k] = input_dtypes[r];
+        q.idx[k] = p.idx[r];
       } else if (r < n_inputs + n_scalars) {
         q.kind[k] = 1; q.ptr[k] = scalars[r - n_inputs]; q.dtype[k] = scalar_dtypes[r - n_inputs];
       } else {
@@ -615,7 +690,8 @@ static int pointwise_impl(const void *const *inputs, const int *input_dtypes,
     for (int k = 0; k < arity; ++k)
       if (q.kind[k] != 2 && q.dtype[k] != EMMY_DT_F32) f32io = false;
 #define EMMY_PW_LAUNCH(T, OPC, IO) \
-    pointwise_simple_kernel<T, OPC, IO><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n)
+    launch_simple<T, OPC, IO>(q, out, out_dtype, n, gb, st, has_bc)
+    const bool has_bc = q.kind[0] == 3 || q.kind[1] == 3 || q.kind[2] == 3;
     if (f32io) {
       switch (op) {
         case PW_ADD: EMMY_PW_LAUNCH(float, PW_ADD, true); break;

@@ -11,12 +11,13 @@
 // rounded once, at the store, to the output dtype.  That is at least as
 // accurate as the reference's per-step f16 rounding, and within its checked
 // tolerances.  The f32-only path (rowops.cu) stays the fast path for f32
-// tensors; this one trades 128-bit vector loads for dtype generality: loads
-// are per element, coalesced across the threads of a row, and the statistics
-// pass re-reads the row from L1/L2 for the map pass.
+// tensors; this one is written for dtype generality: 4-element vector loads
+// (8 bytes of f16, 16 of f32, 32 of f64) when the rows are aligned for them,
+// coalesced across the threads of a row, and the statistics passes re-read
+// the row from L1/L2 for the map pass.
 //
 // Layout: x viewed as [outer, n, inner] row-major.  inner == 1: a warp per row
-// (n <= 2048) or a 256-thread block per row; inner > 1 (reductions and
+// (n <= 2048, or 8192 with vector loads) or a 256-thread block per row; inner > 1 (reductions and
 // softmax over a strided axis): one thread per (outer, inner) column,
 // consecutive threads on consecutive inner positions.
 
@@ -105,14 +106,63 @@ template <int MODE, int TPR, typename TC> __device__ __forceinline__ TC group(TC
   return v;
 }
 
-// inner == 1: TPR threads per row (a warp, 8 rows per block; or the block)
-template <typename TC, int MODE, int TPR>
+// VEC consecutive elements (VEC = 4: one 8-byte f16, 16-byte f32 or two
+// 16-byte f64 plain loads; the caller guarantees alignment)
+template <typename TC, int VEC>
+__device__ __forceinline__ void ldv(const void *p, int dt, int64_t i, TC v[VEC]) {
+  if constexpr (VEC == 1) {
+    v[0] = ld<TC>(p, dt, i);
+  } else {
+    if (dt == EMMY_DT_F16) {
+      const uint2 u = *reinterpret_cast<const uint2 *>(static_cast<const __half *>(p) + i);
+      const __half2 h0 = *reinterpret_cast<const __half2 *>(&u.x);
+      const __half2 h1 = *reinterpret_cast<const __half2 *>(&u.y);
+      v[0] = TC(__low2float(h0)); v[1] = TC(__high2float(h0));
+      v[2] = TC(__low2float(h1)); v[3] = TC(__high2float(h1));
+    } else if (dt == EMMY_DT_F64) {
+      const double2 *q = reinterpret_cast<const double2 *>(static_cast<const double *>(p) + i);
+      const double2 x0 = q[0], x1 = q[1];
+      v[0] = TC(x0.x); v[1] = TC(x0.y); v[2] = TC(x1.x); v[3] = TC(x1.y);
+    } else {
+      const float4 x = *reinterpret_cast<const float4 *>(static_cast<const float *>(p) + i);
+      v[0] = TC(x.x); v[1] = TC(x.y); v[2] = TC(x.z); v[3] = TC(x.w);
+    }
+  }
+}
+
+template <typename TC, int VEC>
+__device__ __forceinline__ void stv(void *p, int dt, int64_t i, const TC v[VEC]) {
+  if constexpr (VEC == 1) {
+    st<TC>(p, dt, i, v[0]);
+  } else {
+    if (dt == EMMY_DT_F16) {
+      __half2 h0 = __halves2half2(to_half(v[0]), to_half(v[1]));
+      __half2 h1 = __halves2half2(to_half(v[2]), to_half(v[3]));
+      uint2 u;
+      u.x = *reinterpret_cast<unsigned *>(&h0);
+      u.y = *reinterpret_cast<unsigned *>(&h1);
+      *reinterpret_cast<uint2 *>(static_cast<__half *>(p) + i) = u;
+    } else if (dt == EMMY_DT_F64) {
+      double2 *q = reinterpret_cast<double2 *>(static_cast<double *>(p) + i);
+      q[0] = make_double2(double(v[0]), double(v[1]));
+      q[1] = make_double2(double(v[2]), double(v[3]));
+    } else {
+      *reinterpret_cast<float4 *>(static_cast<float *>(p) + i) =
+          make_float4(float(v[0]), float(v[1]), float(v[2]), float(v[3]));
+    }
+  }
+}
+
+// inner == 1: TPR threads per row (a warp, 8 rows per block; or the block),
+// VEC elements per thread per step
+template <typename TC, int MODE, int TPR, int VEC>
 __global__ void __launch_bounds__(256) rows_kernel(const Args a) {
   constexpr int RPB = TPR > 32 ? 1 : 256 / 32;
   __shared__ TC red[32];
   const int g = TPR > 32 ? 0 : (threadIdx.x >> 5);
   const int t = TPR > 32 ? threadIdx.x : (threadIdx.x & 31);
   const int64_t n = a.n;
+  const int64_t i0 = (int64_t)t * VEC, step = (int64_t)TPR * VEC;
   TC eps = TC(0), inv_count = TC(0);
   if (a.eps) eps = ld<TC>(a.eps, a.cdt, 0);
   if (a.count) inv_count = TC(1) / ld<TC>(a.count, a.cdt, 0);
@@ -120,57 +170,103 @@ __global__ void __launch_bounds__(256) rows_kernel(const Args a) {
   for (int64_t row = (int64_t)blockIdx.x * RPB + g; row < a.outer;
        row += (int64_t)gridDim.x * RPB) {
     const int64_t base = row * n;
+    TC v[VEC];
     if constexpr (MODE == M_SUM || MODE == M_MAX || MODE == M_MIN) {
       TC acc = seed<MODE, TC>();
-      for (int64_t i = t; i < n; i += TPR) acc = fold<MODE, TC>(acc, ld<TC>(a.x, a.xdt, base + i), a.pre);
+      for (int64_t i = i0; i < n; i += step) {
+        ldv<TC, VEC>(a.x, a.xdt, base + i, v);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) acc = fold<MODE, TC>(acc, v[j], a.pre);
+      }
       acc = group<MODE, TPR, TC>(acc, red);
       if (t == 0) st<TC>(a.y, a.ydt, row, a.count ? acc * inv_count : acc);
     } else if constexpr (MODE == M_DOT) {
-      TC acc = TC(0);
-      for (int64_t i = t; i < n; i += TPR)
-        acc = fma_c(ld<TC>(a.x, a.xdt, base + i), ld<TC>(a.w, a.wdt, i), acc);
+      TC acc = TC(0), u[VEC];
+      for (int64_t i = i0; i < n; i += step) {
+        ldv<TC, VEC>(a.x, a.xdt, base + i, v);
+        ldv<TC, VEC>(a.w, a.wdt, i, u);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) acc = fma_c(v[j], u[j], acc);
+      }
       acc = group<M_SUM, TPR, TC>(acc, red);
       if (t == 0) st<TC>(a.y, a.ydt, row, acc);
     } else if constexpr (MODE == M_SOFTMAX) {
       TC m = max_seed<TC>();
-      for (int64_t i = t; i < n; i += TPR) m = fmax(m, ld<TC>(a.x, a.xdt, base + i));
+      for (int64_t i = i0; i < n; i += step) {
+        ldv<TC, VEC>(a.x, a.xdt, base + i, v);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) m = fmax(m, v[j]);
+      }
       m = group<M_MAX, TPR, TC>(m, red);
       TC s = TC(0);
-      for (int64_t i = t; i < n; i += TPR) s += exp_c(ld<TC>(a.x, a.xdt, base + i) - m);
+      for (int64_t i = i0; i < n; i += step) {
+        ldv<TC, VEC>(a.x, a.xdt, base + i, v);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) s += exp_c(v[j] - m);
+      }
       s = group<M_SUM, TPR, TC>(s, red);
       const TC r = TC(1) / s;
-      for (int64_t i = t; i < n; i += TPR)
-        st<TC>(a.y, a.ydt, base + i, exp_c(ld<TC>(a.x, a.xdt, base + i) - m) * r);
+      for (int64_t i = i0; i < n; i += step) {
+        ldv<TC, VEC>(a.x, a.xdt, base + i, v);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) v[j] = exp_c(v[j] - m) * r;
+        stv<TC, VEC>(a.y, a.ydt, base + i, v);
+      }
     } else if constexpr (MODE == M_RMS || MODE == M_L2) {
-      TC s = TC(0);
-      for (int64_t i = t; i < n; i += TPR) {
-        const TC v = ld<TC>(a.x, a.xdt, base + i);
-        s = fma_c(v, v, s);
+      TC s = TC(0), u[VEC];
+      for (int64_t i = i0; i < n; i += step) {
+        ldv<TC, VEC>(a.x, a.xdt, base + i, v);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) s = fma_c(v[j], v[j], s);
       }
       s = group<M_SUM, TPR, TC>(s, red);
       const TC r = MODE == M_RMS ? TC(1) / sqrt(eps + s * inv_count) : TC(1) / sqrt(s);
-      for (int64_t i = t; i < n; i += TPR) {
-        TC o = ld<TC>(a.x, a.xdt, base + i) * r;
-        if (MODE == M_RMS && a.w) o *= ld<TC>(a.w, a.wdt, i);
-        st<TC>(a.y, a.ydt, base + i, o);
+      for (int64_t i = i0; i < n; i += step) {
+        ldv<TC, VEC>(a.x, a.xdt, base + i, v);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) v[j] = v[j] * r;
+        if (MODE == M_RMS && a.w) {
+          ldv<TC, VEC>(a.w, a.wdt, i, u);
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) v[j] *= u[j];
+        }
+        stv<TC, VEC>(a.y, a.ydt, base + i, v);
       }
     } else {  // M_LN: mean, then the centred variance
-      TC s = TC(0);
-      for (int64_t i = t; i < n; i += TPR) s += ld<TC>(a.x, a.xdt, base + i);
+      TC s = TC(0), u[VEC];
+      for (int64_t i = i0; i < n; i += step) {
+        ldv<TC, VEC>(a.x, a.xdt, base + i, v);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) s += v[j];
+      }
       s = group<M_SUM, TPR, TC>(s, red);
       const TC mean = s * inv_count;
       TC q = TC(0);
-      for (int64_t i = t; i < n; i += TPR) {
-        const TC d = ld<TC>(a.x, a.xdt, base + i) - mean;
-        q = fma_c(d, d, q);
+      for (int64_t i = i0; i < n; i += step) {
+        ldv<TC, VEC>(a.x, a.xdt, base + i, v);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const TC d = v[j] - mean;
+          q = fma_c(d, d, q);
+        }
       }
       q = group<M_SUM, TPR, TC>(q, red);
       const TC r = TC(1) / sqrt(q * inv_count + eps);
-      for (int64_t i = t; i < n; i += TPR) {
-        TC o = (ld<TC>(a.x, a.xdt, base + i) - mean) * r;
-        if (a.w) o *= ld<TC>(a.w, a.wdt, i);
-        if (a.b) o += ld<TC>(a.b, a.wdt, i);
-        st<TC>(a.y, a.ydt, base + i, o);
+      for (int64_t i = i0; i < n; i += step) {
+        ldv<TC, VEC>(a.x, a.xdt, base + i, v);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) v[j] = (v[j] - mean) * r;
+        if (a.w) {
+          ldv<TC, VEC>(a.w, a.wdt, i, u);
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) v[j] *= u[j];
+        }
+        if (a.b) {
+          ldv<TC, VEC>(a.b, a.wdt, i, u);
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) v[j] += u[j];
+        }
+        stv<TC, VEC>(a.y, a.ydt, base + i, v);
       }
     }
   }
@@ -213,15 +309,26 @@ void launch(const Args &a, cudaStream_t st) {
     }
     return;
   }
-  if (a.n <= 2048) {
-    int64_t blocks = (a.outer + 7) / 8;
-    if (blocks > (int64_t)sms * 32) blocks = (int64_t)sms * 32;
-    rows_kernel<TC, MODE, 32><<<(unsigned)blocks, 256, 0, st>>>(a);
+  // 4 elements per access when every row start is aligned for it
+  auto al = [](const void *ptr, int dt) {
+    const uintptr_t need = dt == EMMY_DT_F16 ? 8 : 16;
+    return ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) % need) == 0;
+  };
+  const bool v4 = a.n % 4 == 0 && al(a.x, a.xdt) && al(a.y, a.ydt) && al(a.w, a.wdt) &&
+                  al(a.b, a.wdt);
+  const bool warp_rows = a.n <= (v4 ? 8192 : 2048);
+  int64_t blocks = warp_rows ? (a.outer + 7) / 8 : a.outer;
+  const int64_t cap = (int64_t)sms * (warp_rows ? 32 : 8);
+  if (blocks > cap) blocks = cap;
+#define EMMY_ROWT(TPR, V) rows_kernel<TC, MODE, TPR, V><<<(unsigned)blocks, 256, 0, st>>>(a)
+  if (warp_rows) {
+    if (v4) EMMY_ROWT(32, 4);
+    else EMMY_ROWT(32, 1);
   } else {
-    int64_t blocks = a.outer;
-    if (blocks > (int64_t)sms * 8) blocks = (int64_t)sms * 8;
-    rows_kernel<TC, MODE, 256><<<(unsigned)blocks, 256, 0, st>>>(a);
+    if (v4) EMMY_ROWT(256, 4);
+    else EMMY_ROWT(256, 1);
   }
+#undef EMMY_ROWT
 }
 
 template <typename TC>
