@@ -46,6 +46,10 @@ FALLBACK_HBM_GBS = 6650.0
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 # FP64 CUDA-core peak, nominal: 148 SMs x 64 DFMA/clk x 2 flops x 1.965 GHz
 FP64_NOMINAL_TFLOPS = 148 * 64 * 2 * 1.965e9 / 1e12
+# measured once on this pool's B200s (independent FFMA / DFMA chains on every
+# SM at 1965 MHz): 70.86 and 33.35 TFLOP/s
+FP32_MEASURED_TFLOPS = 70.86
+FP64_MEASURED_TFLOPS = 33.35
 L2_FLUSH_BYTES = 256 << 20
 # A short device spin queued before each timed region keeps the GPU busy while
 # the host enqueues the launches, so the CUDA events bracket device work only.
@@ -292,7 +296,14 @@ def family_extras(device, peak):
             rm=8, rn=8),
         "K3b_bmm_f16_64x512": synth.matmul(512, 512, 512, batch=64, dtype="f16", out_dtype="f16",
                                            tm=128, tn=128, rm=8, rn=8),
+        "K3a_gemm_f16_f32out_4096x2048x8192_bias_relu": synth.matmul(
+            4096, 8192, 2048, dtype="f16", out_dtype="f32", bias=True, relu=True, tm=128, tn=128,
+            rm=8, rn=8),
+        "K3b_bmm_f16_f32out_64x512": synth.matmul(512, 512, 512, batch=64, dtype="f16",
+                                                  out_dtype="f32", tm=128, tn=128, rm=8, rn=8),
         "K5_attention_f16_8x32x512x128": synth.attention(8, 32, 512, 128, dtype="f16"),
+        **{f"K5_sweep_f16_8x32_S{S}_D{D}": synth.attention(8, 32, S, D, dtype="f16")
+           for D in (16, 64, 256) for S in (16, 128, 512)},
         "X_gemm_f64_2048x2048x2048": synth.matmul(2048, 2048, 2048, dtype="f64", tm=128, tn=128,
                                                   rm=8, rn=8, bk=16),
         "F8a_pointwise_add_f32_2^26": synth.pointwise(1 << 26, ("add", "x0", "x1"), "f32"),
@@ -339,8 +350,10 @@ def family_extras(device, peak):
             out[name]["tflops"] = round(tf, 2)
             if plan["family"] == "gemm_f32":
                 out[name]["frac_fp32_nominal"] = round(tf / FP32_NOMINAL_TFLOPS, 3)
+                out[name]["frac_fp32_measured"] = round(tf / FP32_MEASURED_TFLOPS, 3)
             elif plan["family"] == "gemm_f64":
                 out[name]["frac_fp64_nominal"] = round(tf / FP64_NOMINAL_TFLOPS, 3)
+                out[name]["frac_fp64_measured"] = round(tf / FP64_MEASURED_TFLOPS, 3)
             else:
                 out[name]["frac_tensor"] = round(tf / tensor_peak()[0], 3)
         del ex

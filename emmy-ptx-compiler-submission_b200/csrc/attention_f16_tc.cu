@@ -473,6 +473,10 @@ extern "C" int emmy_attention_f16(const void *q, const void *k, const void *v, v
     if (d == 128) return launch_attention_tc<128>(q, k, v, o, scale_div, batch, sq, out_f16, st);
     return launch_attention_tc<256>(q, k, v, o, scale_div, batch, sq, out_f16, st);
   }
+  // head dims up to 96: one thread per query row (any key count)
+  const int rc = launch_attention_rows(q, k, v, o, scale_div, batch, sq, sk, d, d, 1, out_f16,
+                                       k_transposed, st);
+  if (rc >= 0) return rc;
   const size_t smem = (size_t)(d + sk) * sizeof(float);
   if (smem > 200 * 1024)
     return set_error(EMMY_ERR_UNSUPPORTED, "emmy_attention_f16: %lld keys exceed shared memory",

@@ -98,6 +98,10 @@ extern "C" int emmy_attention_f32(const float *q, const float *k, const float *v
   if (!q || !k || !v || !o) return set_error(EMMY_ERR_INVALID, "emmy_attention_f32: null operand");
   if (batch > 65535 || sq > INT32_MAX)
     return set_error(EMMY_ERR_UNSUPPORTED, "emmy_attention_f32: grid too large");
+  // head dims up to 96 (d == dv): one thread per query row (any key count)
+  const int rc = launch_attention_rows(q, k, v, o, scale_div, batch, sq, sk, d, dv, 0, 0,
+                                       k_transposed, as_stream(stream));
+  if (rc >= 0) return rc;
   const size_t smem = (size_t)(d + sk) * sizeof(float);
   if (smem > 200 * 1024)
     return set_error(EMMY_ERR_UNSUPPORTED, "emmy_attention_f32: %lld keys exceed shared memory",

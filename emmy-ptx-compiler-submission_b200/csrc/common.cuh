@@ -40,6 +40,13 @@ inline int sm_count() {
   return cached[dev];
 }
 
+// Attention on CUDA cores with one thread per query row (attention_rows.cu):
+// -1 when there is no kernel for (d, dv), else the launch status.
+int launch_attention_rows(const void *q, const void *k, const void *v, void *o,
+                          const float *scale_div, int64_t batch, int64_t sq, int64_t sk,
+                          int64_t d, int64_t dv, int in_f16, int out_f16, int k_transposed,
+                          cudaStream_t st);
+
 // Device address of the library's status word on the current device.  Kernels
 // with bounded waits receive it as an argument and write a nonzero code there
 // instead of hanging or trapping; emmy_get_device_status() reads and clears it.
