@@ -112,3 +112,65 @@ extern "C" int emmy_zero(void *ptr, size_t bytes, void *stream) {
   if (e != cudaSuccess) return set_error(EMMY_ERR_CUDA, "emmy_zero: %s", cudaGetErrorString(e));
   return EMMY_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Peer mappings of device buffers between the processes of one node (CUDA
+// IPC), for kernels that write another GPU's memory over NVLink.  A buffer is
+// exported as the handle of the allocation that holds it plus the offset into
+// it (an allocator may hand out pieces of a larger allocation).
+
+namespace {
+typedef int (*PFN_getAddressRange)(unsigned long long *base, size_t *size, unsigned long long ptr);
+PFN_getAddressRange address_range_fn() {
+  static PFN_getAddressRange fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_getAddressRange>(p);
+  }
+  return fn;
+}
+}  // namespace
+
+extern "C" int emmy_ipc_export(const void *ptr, void *handle, int64_t *offset) {
+  clear_error();
+  if (!ptr || !handle || !offset) return set_error(EMMY_ERR_INVALID, "emmy_ipc_export: null argument");
+  auto range = address_range_fn();
+  if (!range) return set_error(EMMY_ERR_CUDA, "cuMemGetAddressRange is unavailable");
+  unsigned long long base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<unsigned long long>(ptr)) != 0)
+    return set_error(EMMY_ERR_INVALID, "emmy_ipc_export: not a device allocation");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base));
+  if (e != cudaSuccess) return set_error(EMMY_ERR_CUDA, "emmy_ipc_export: %s", cudaGetErrorString(e));
+  memcpy(handle, &h, sizeof(h));
+  *offset = (int64_t)(reinterpret_cast<unsigned long long>(ptr) - base);
+  return EMMY_OK;
+}
+
+extern "C" int emmy_ipc_import(const void *handle, int64_t offset, void **peer_ptr,
+                               void **peer_base) {
+  clear_error();
+  if (!handle || !peer_ptr || !peer_base || offset < 0)
+    return set_error(EMMY_ERR_INVALID, "emmy_ipc_import: bad argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void *base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return set_error(EMMY_ERR_CUDA, "emmy_ipc_import: %s", cudaGetErrorString(e));
+  *peer_base = base;
+  *peer_ptr = static_cast<char *>(base) + offset;
+  return EMMY_OK;
+}
+
+extern "C" int emmy_ipc_close(void *peer_base) {
+  clear_error();
+  if (!peer_base) return EMMY_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(peer_base);
+  if (e != cudaSuccess) return set_error(EMMY_ERR_CUDA, "emmy_ipc_close: %s", cudaGetErrorString(e));
+  return EMMY_OK;
+}

@@ -74,14 +74,47 @@ __device__ __forceinline__ void st4(double *dst, const double v[4]) {
   reinterpret_cast<double2 *>(dst)[1] = make_double2(v[2], v[3]);
 }
 
-enum GemmMode { GEMM_STORE = 0, GEMM_ACCUMULATE = 1, GEMM_ATOMIC = 2 };
+enum GemmMode { GEMM_STORE = 0, GEMM_ACCUMULATE = 1, GEMM_ATOMIC = 2, GEMM_PEER = 3 };
+
+// GEMM_PEER: a matmul and the reduce-scatter of its partial sums in one
+// kernel.  Row m of this rank's partial product is stored (plain 16-byte
+// stores; over NVLink when another GPU owns the row) into owner
+// o = m / rows_per_rank's slot buffer, in slot `me`, row m % rows_per_rank:
+// slots[o] is [world, rows_per_rank, N] and each rank writes only its own
+// slot, so nothing needs zeroing and no remote atomics are issued.  The owner
+// then sums its world slots (emmy_reduce_f32 over the slot axis).  With a K
+// split inside the rank, the splits of a tile first meet in a local workspace
+// (vector atomics); the last split to finish the tile (a per-tile arrival
+// counter) stores the summed tile and clears the workspace tile and the
+// counter for the next call, so each element crosses NVLink once.
+struct PeerRows {
+  void *rows[8];      // slot buffers of the owners, in this process's address space
+  long long rows_per_rank;
+  float *ws;          // M x N, zero between calls (the kernel leaves it zero)
+  int *counters;      // one per 128 x 128 tile, zero between calls
+  int me;             // this rank: the slot it writes
+};
+
+template <typename T>
+__device__ __forceinline__ T *gemm_dst(T *Cb, const PeerRows &pr, int mode, int m, int n, int N) {
+  if (mode == GEMM_PEER) {
+    const int owner = (int)(m / pr.rows_per_rank);
+    void *base = pr.rows[0];
+#pragma unroll
+    for (int r = 1; r < 8; ++r)            // a select chain: no local copy of the array
+      if (owner == r) base = pr.rows[r];
+    return static_cast<T *>(base) +
+           ((int64_t)pr.me * pr.rows_per_rank + (m - owner * pr.rows_per_rank)) * N + n;
+  }
+  return Cb + (int64_t)m * N + n;
+}
 
 template <typename T>
 __global__ void __launch_bounds__(gemm32::THREADS, sizeof(T) == 4 ? 2 : 1)
 gemm_simt_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const T *__restrict__ bias, T *__restrict__ C, int M, int N, int K,
                      int64_t c_batch_stride, int splits, int k_per_split, int epilogue, int mode,
-                     int *status) {
+                     const PeerRows peers, int *status) {
   using namespace gemm32;
   constexpr int BK = Cfg<T>::BK, VK = Cfg<T>::VK;
   constexpr int A_BYTES = Cfg<T>::A_BYTES, STAGE_BYTES = Cfg<T>::STAGE_BYTES;
@@ -167,6 +200,7 @@ gemm_simt_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
   }
 
   T *Cb = C + (int64_t)batch * c_batch_stride;
+  const bool peer_ws = mode == GEMM_PEER && splits > 1 && sizeof(T) == 4;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int m = m0 + ty + 16 * i;
@@ -176,7 +210,7 @@ gemm_simt_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
       const int n = n0 + 64 * h + 4 * tx;
       if (n >= N) continue;
       T v[4] = {acc[i][4 * h], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]};
-      if ((epilogue & EMMY_EPI_BIAS) && bias && (mode != GEMM_ATOMIC || split == 0)) {
+      if ((epilogue & EMMY_EPI_BIAS) && bias && (mode < GEMM_ATOMIC || split == 0)) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) v[j] += (n + j < N) ? __ldg(bias + n + j) : T(0);
       }
@@ -184,8 +218,17 @@ gemm_simt_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
 #pragma unroll
         for (int j = 0; j < 4; ++j) v[j] = fmax(v[j], T(0));
       }
-      T *dst = Cb + (int64_t)m * N + n;
-      if (n + 3 < N) {
+      T *dst = peer_ws ? reinterpret_cast<T *>(peers.ws) + (int64_t)m * N + n
+                       : gemm_dst(Cb, peers, mode, m, n, N);
+      if (mode == GEMM_PEER && !peer_ws) {
+        if (n + 3 < N) st4(dst, v);
+        else
+          for (int j = 0; j < 4 && n + j < N; ++j) dst[j] = v[j];
+      } else if (peer_ws) {
+        if (n + 3 < N) atomic_add4(dst, v);
+        else
+          for (int j = 0; j < 4 && n + j < N; ++j) atomicAdd(dst + j, v[j]);
+      } else if (n + 3 < N) {
         if (mode == GEMM_ATOMIC) {
           atomic_add4(dst, v);
         } else if (mode == GEMM_ACCUMULATE) {
@@ -205,6 +248,43 @@ gemm_simt_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
       }
     }
   }
+  if constexpr (sizeof(T) == 4) {
+    if (peer_ws) {
+      // the last split of this tile pushes the summed tile to its owner
+      __shared__ int s_last;
+      __syncthreads();
+      const int tile = blockIdx.x + blockIdx.y * gridDim.x;
+      if (tid == 0) {
+        __threadfence();                                // this CTA's adds are visible
+        s_last = atomicAdd(peers.counters + tile, 1) == splits - 1;
+      }
+      __syncthreads();
+      if (s_last) {
+        __threadfence();
+#pragma unroll 1
+        for (int i = 0; i < 8; ++i) {
+          const int m = m0 + ty + 16 * i;
+          if (m >= M) continue;
+          for (int h = 0; h < 2; ++h) {
+            const int n = n0 + 64 * h + 4 * tx;
+            if (n >= N) continue;
+            float *w = peers.ws + (int64_t)m * N + n;
+            float *dst = gemm_dst(reinterpret_cast<float *>(Cb), peers, GEMM_PEER, m, n, N);
+            if (n + 3 < N) {
+              *reinterpret_cast<float4 *>(dst) = __ldcg(reinterpret_cast<const float4 *>(w));
+              *reinterpret_cast<float4 *>(w) = make_float4(0.f, 0.f, 0.f, 0.f);
+            } else {
+              for (int j = 0; j < 4 && n + j < N; ++j) {
+                dst[j] = __ldcg(w + j);
+                w[j] = 0.f;
+              }
+            }
+          }
+        }
+        if (tid == 0) peers.counters[tile] = 0;
+      }
+    }
+  }
 }
 
 // Plain shared-memory tiled kernel for shapes TMA cannot describe.
@@ -214,7 +294,7 @@ __global__ void __launch_bounds__(256)
 gemm_simt_plain_kernel(const T *__restrict__ A, const T *__restrict__ B,
                        const T *__restrict__ bias, T *__restrict__ C, int M, int N, int K,
                        int64_t sa, int64_t sb, int64_t sc, int splits, int k_per_split,
-                       int epilogue, int mode) {
+                       int epilogue, int mode, const PeerRows peers) {
   __shared__ T As[16][64 + 1];
   __shared__ T Bs[16][64 + 1];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -243,17 +323,20 @@ gemm_simt_plain_kernel(const T *__restrict__ A, const T *__restrict__ B,
     __syncthreads();
   }
   T *Cb = C + (int64_t)batch * sc;
+#pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int m = m0 + ty + 16 * i;
     if (m >= M) continue;
+#pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int n = n0 + tx + 16 * j;
       if (n >= N) continue;
       T v = acc[i][j];
-      if ((epilogue & EMMY_EPI_BIAS) && bias && (mode != GEMM_ATOMIC || split == 0)) v += bias[n];
+      if ((epilogue & EMMY_EPI_BIAS) && bias && (mode < GEMM_ATOMIC || split == 0)) v += bias[n];
       if (epilogue & EMMY_EPI_RELU) v = fmax(v, T(0));
-      T *dst = Cb + (int64_t)m * N + n;
-      if (mode == GEMM_ATOMIC) atomicAdd(dst, v);
+      T *dst = gemm_dst(Cb, peers, mode, m, n, N);
+      if (mode == GEMM_PEER) *dst = v;
+      else if (mode == GEMM_ATOMIC) atomicAdd(dst, v);
       else if (mode == GEMM_ACCUMULATE) *dst += v;
       else *dst = v;
     }
@@ -268,7 +351,7 @@ template <typename T>
 static int gemm_simt(const char *name, const T *A, const T *B, const T *bias, T *C, int64_t batch,
                      int64_t M, int64_t N, int64_t K, int64_t a_batch_stride,
                      int64_t b_batch_stride, int64_t c_batch_stride, int splits, int accumulate,
-                     int epilogue, void *stream) {
+                     int epilogue, void *stream, const PeerRows *peers = nullptr) {
   using namespace gemm32;
   constexpr int BK = Cfg<T>::BK, SMEM_BYTES = Cfg<T>::SMEM_BYTES;
   constexpr int ES = (int)sizeof(T), VEC = 16 / ES;
@@ -308,7 +391,9 @@ static int gemm_simt(const char *name, const T *A, const T *B, const T *bias, T 
   if (kps == 0) kps = BK;
   sp = (int)((K + kps - 1) / kps);
   if (sp < 1) sp = 1;
-  const int mode = sp > 1 ? GEMM_ATOMIC : (accumulate ? GEMM_ACCUMULATE : GEMM_STORE);
+  const int mode = peers ? GEMM_PEER
+                         : (sp > 1 ? GEMM_ATOMIC : (accumulate ? GEMM_ACCUMULATE : GEMM_STORE));
+  const PeerRows pr = peers ? *peers : PeerRows{};
   if (batch > 1 && c_batch_stride < M * N)
     return set_error(EMMY_ERR_INVALID, "%s: batch stride of C overlaps its batches", name);
   if (mode == GEMM_ATOMIC && !accumulate) {
@@ -349,13 +434,18 @@ static int gemm_simt(const char *name, const T *A, const T *B, const T *bias, T 
     dim3 grid((unsigned)mt, (unsigned)nt, (unsigned)(batch * sp));
     gemm_simt_tma_kernel<T><<<grid, THREADS, SMEM_BYTES, st>>>(
         ta, tb, bias, C, (int)M, (int)N, (int)K, c_batch_stride, sp, (int)kps, epilogue, mode,
-        device_status_ptr());
+        pr, device_status_ptr());
     return check_launch(name);
+  }
+  if (peers && sp > 1) {
+    // the plain kernel stores partial rows without a tile reduction: one split
+    sp = 1;
+    kps = K;
   }
   dim3 grid((unsigned)((M + 63) / 64), (unsigned)((N + 63) / 64), (unsigned)(batch * sp));
   gemm_simt_plain_kernel<T><<<grid, 256, 0, st>>>(A, B, bias, C, (int)M, (int)N, (int)K,
                                                   a_batch_stride, b_batch_stride, c_batch_stride,
-                                                  sp, (int)kps, epilogue, mode);
+                                                  sp, (int)kps, epilogue, mode, pr);
   return check_launch(name);
 }
 
@@ -373,4 +463,31 @@ extern "C" int emmy_gemm_f64(const double *A, const double *B, const double *bia
                              int accumulate, int epilogue, void *stream) {
   return gemm_simt<double>("emmy_gemm_f64", A, B, bias, C, batch, M, N, K, a_batch_stride,
                            b_batch_stride, c_batch_stride, splits, accumulate, epilogue, stream);
+}
+
+
+extern "C" int emmy_gemm_f32_rows_to_peers(const float *A, const float *B, const float *bias,
+                                           float *const *rows, int world, int me,
+                                           int64_t rows_per_rank, int64_t M, int64_t N, int64_t K,
+                                           int splits, float *workspace, int *tile_counters,
+                                           int64_t n_counters, void *stream) {
+  clear_error();
+  if (world < 1 || world > 8 || !rows || me < 0 || me >= world)
+    return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32_rows_to_peers: 1 to 8 row owners");
+  if (rows_per_rank < 1 || rows_per_rank * world < M)
+    return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32_rows_to_peers: rows do not cover M");
+  if (!workspace || !tile_counters || n_counters < ((M + 63) / 64) * ((N + 63) / 64))
+    return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32_rows_to_peers: workspace or counters");
+  PeerRows pr{};
+  pr.rows_per_rank = rows_per_rank;
+  pr.ws = workspace;
+  pr.counters = tile_counters;
+  pr.me = me;
+  for (int r = 0; r < world; ++r) {
+    if (!rows[r] && r * rows_per_rank < M)
+      return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32_rows_to_peers: null rows of owner %d", r);
+    pr.rows[r] = rows[r];
+  }
+  return gemm_simt<float>("emmy_gemm_f32_rows_to_peers", A, B, bias, rows[0], 1, M, N, K, M * K,
+                          K * N, M * N, splits, 0, bias ? EMMY_EPI_BIAS : 0, stream, &pr);
 }

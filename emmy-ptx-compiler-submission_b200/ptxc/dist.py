@@ -181,3 +181,125 @@ def reduce_scatter_rows(partial, group=None):
     full = partial.clone()
     dist.all_reduce(full, op=dist.ReduceOp.SUM, group=group)
     return full[lo:hi].contiguous()
+
+
+class PeerRows:
+    """Every rank's slot buffer, mapped into this rank's address space.
+
+    Each rank owns ``slots``, a CUDA tensor ``[world, M / world, N]``: slot r
+    receives rank r's partial sums of the rows this rank owns.  The buffers
+    are exchanged as CUDA IPC handles (``emmy_ipc_export`` /
+    ``emmy_ipc_import``) so a kernel on any rank can store into any owner's
+    slot over NVLink.  ``ptrs`` lists the owners' slot buffers in rank order
+    (this rank's own at its index).  ``close()`` unmaps the peers' buffers;
+    call it on every rank before the process group goes away.
+    """
+
+    def __init__(self, slots, group=None):
+        import ctypes
+        import torch.distributed as dist
+        from .launch import LibraryError, load_library
+        self.lib = load_library()
+        self.slots = slots
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if slots.dim() != 3 or slots.shape[0] != self.world or not slots.is_contiguous():
+            raise ValueError("slots must be a contiguous [world, rows per rank, N] tensor")
+        handle = (ctypes.c_ubyte * 64)()
+        offset = ctypes.c_int64()
+        rc = self.lib.emmy_ipc_export(ctypes.c_void_p(slots.data_ptr()), handle,
+                                      ctypes.byref(offset))
+        if rc:
+            raise LibraryError("emmy_ipc_export: " + self.lib.emmy_last_error().decode())
+        mine = (bytes(handle), int(offset.value))
+        allh = [None] * self.world
+        dist.all_gather_object(allh, mine, group=group)
+        self.ptrs, self._bases = [], []
+        for r, (h, off) in enumerate(allh):
+            if r == self.rank:
+                self.ptrs.append(slots.data_ptr())
+                continue
+            hb = (ctypes.c_ubyte * 64).from_buffer_copy(h)
+            p, base = ctypes.c_void_p(), ctypes.c_void_p()
+            rc = self.lib.emmy_ipc_import(hb, ctypes.c_int64(off), ctypes.byref(p),
+                                          ctypes.byref(base))
+            if rc:
+                self.close()
+                raise LibraryError("emmy_ipc_import: " + self.lib.emmy_last_error().decode())
+            self.ptrs.append(p.value)
+            self._bases.append(base.value)
+
+    def workspace(self, M, N):
+        """The local tile workspace and arrival counters (zero; kernels leave them zero)."""
+        import torch
+        key = (M, N)
+        if getattr(self, "_ws_key", None) != key:
+            tiles = ((M + 63) // 64) * ((N + 63) // 64)
+            self._ws = torch.zeros(M * N, dtype=torch.float32, device=self.slots.device)
+            self._counters = torch.zeros(tiles, dtype=torch.int32, device=self.slots.device)
+            self._ws_key = key
+        return self._ws, self._counters
+
+    def close(self):
+        import ctypes
+        for b in self._bases:
+            self.lib.emmy_ipc_close(ctypes.c_void_p(b))
+        self._bases = []
+
+
+def splitk_to_peers(a_slice, b_slice, peers, M, N, splits=0, bias=None, stream=None):
+    """This rank's K slice of ``A @ B``, its rows stored straight into their
+    owners' slots: the matmul and the scatter of its partial sums in one
+    kernel (``emmy_gemm_f32_rows_to_peers``; rows of other owners travel over
+    NVLink as plain 16-byte stores, no partial C is stored locally).
+
+    Every rank's previous sums must be done reading the slots before any rank
+    launches, and every rank's launch must be finished before an owner sums
+    its slots: ``splitk_step`` does both.
+    """
+    import ctypes
+    import torch
+    from .launch import _check, _stream_handle
+    lib = peers.lib
+    world = peers.world
+    ptrs = (ctypes.c_void_p * 8)(*([ctypes.c_void_p(p) for p in peers.ptrs] +
+                                   [ctypes.c_void_p(0)] * (8 - world)))
+    ws, counters = peers.workspace(M, N)
+    st = stream if stream is not None else torch.cuda.current_stream()
+    _check(lib.emmy_gemm_f32_rows_to_peers(
+        ctypes.c_void_p(a_slice.data_ptr()), ctypes.c_void_p(b_slice.data_ptr()),
+        ctypes.c_void_p(bias.data_ptr()) if bias is not None else None, ptrs, world, peers.rank,
+        M // world, M, N, a_slice.shape[-1], splits, ctypes.c_void_p(ws.data_ptr()),
+        ctypes.c_void_p(counters.data_ptr()), counters.numel(), _stream_handle(st)),
+        "emmy_gemm_f32_rows_to_peers")
+
+
+def sum_slots(peers, out=None, stream=None):
+    """This rank's rows: the sum of its ``world`` slots (``emmy_reduce_f32``
+    over the slot axis of the ``[world, rows * N]`` view)."""
+    import ctypes
+    import torch
+    from .launch import _check, _stream_handle
+    world, rows, N = peers.slots.shape
+    if out is None:
+        out = torch.empty(rows, N, dtype=torch.float32, device=peers.slots.device)
+    st = stream if stream is not None else torch.cuda.current_stream()
+    _check(peers.lib.emmy_reduce_f32(ctypes.c_void_p(peers.slots.data_ptr()),
+                                     ctypes.c_void_p(out.data_ptr()), 1, world, rows * N, 0, 0,
+                                     None, None, 0, _stream_handle(st)), "emmy_reduce_f32")
+    return out
+
+
+def splitk_step(a_slice, b_slice, peers, M, N, splits=0, bias=None, out=None):
+    """One fused split-K step: wait for every rank (the slots are free), launch
+    ``splitk_to_peers``, wait for every rank (the slots are full), sum this
+    rank's slots.  Returns this rank's rows of ``A @ B``."""
+    import torch
+    import torch.distributed as dist
+    torch.cuda.synchronize()
+    dist.barrier(group=peers.group)
+    splitk_to_peers(a_slice, b_slice, peers, M, N, splits, bias)
+    torch.cuda.synchronize()
+    dist.barrier(group=peers.group)
+    return sum_slots(peers, out)

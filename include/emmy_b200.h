@@ -178,6 +178,35 @@ int emmy_gemm_f64(const double *A, const double *B, const double *bias, double *
                   int epilogue, void *stream);
 
 /*
+ * One rank's K slice of a matmul split across the GPUs of a node, fused with
+ * the reduce-scatter of the partial sums: C_part = A[M, Kslice] @ B[Kslice, N]
+ * (+ bias on one rank) is added, element by element (atomic adds; over
+ * NVLink for rows another GPU owns), into rows[m / rows_per_rank] at row
+ * m % rows_per_rank.  rows[] holds every owner's row buffer in this process's
+ * address space (emmy_ipc_import); the owners zero their rows before any rank
+ * launches.  With splits > 1 the splits of a tile first sum in `workspace`
+ * (M x N floats) and the last one (tile_counters, one int per 64 x 64 tile,
+ * n_counters of them) pushes the tile to its owner, so each element crosses
+ * NVLink once; workspace and counters must be zero on the first call and are
+ * left zero.  The multi-GPU form of the reference's atomic split-K Write
+ * (reference ptxc/stmts.py:456-461), one kernel instead of GEMM + collective.
+ */
+int emmy_gemm_f32_rows_to_peers(const float *A, const float *B, const float *bias,
+                                float *const *rows, int world, int me, int64_t rows_per_rank,
+                                int64_t M, int64_t N, int64_t K, int splits, float *workspace,
+                                int *tile_counters, int64_t n_counters, void *stream);
+
+/*
+ * CUDA IPC for peer mappings between the processes of one node.  export: the
+ * 64-byte handle of the allocation holding ptr and ptr's offset in it.
+ * import: map a peer's handle; *peer_ptr = mapped base + offset, *peer_base
+ * the base to pass to emmy_ipc_close.
+ */
+int emmy_ipc_export(const void *ptr, void *handle, int64_t *offset);
+int emmy_ipc_import(const void *handle, int64_t offset, void **peer_ptr, void **peer_base);
+int emmy_ipc_close(void *peer_base);
+
+/*
  * f16 GEMM with f32 accumulation on the tcgen05 tensor cores:
  * C[b] = A[b] @ B[b] (+ bias[n]) (ReLU), A [M,K] f16, B [K,N] f16 row-major,
  * C [M,N] f32 or f16 (out_dtype), bias f32 (nullable), dense batches.

@@ -4,7 +4,10 @@
   head) shard of the tcgen05 attention through the C ABI on its own GPU; the
   shards are all-gathered over NCCL and compared with the float64 oracle;
 * split-K across GPUs: each rank multiplies its K slice with the f32 GEMM into
-  a full partial C, and ``reduce_scatter_rows`` sums the partials over NCCL.
+  a full partial C, and ``reduce_scatter_rows`` sums the partials over NCCL;
+  then the fused form: the GEMM stores its partial rows straight into their
+  owner's slot over NVLink and each owner sums its slots (``PeerRows`` +
+  ``splitk_step``).
 
 Tolerances as in the single-GPU tests.  NVLS is off (``NCCL_NVLS_ENABLE=0``).
 """
@@ -46,7 +49,7 @@ def _worker(rank, world, port, q):
     from emmy_ir import synth
     from oracle import formulas as F
     from ptxc import Lowerer
-    from ptxc.dist import reduce_scatter_rows, shard_plan, splitk_plan
+    from ptxc.dist import PeerRows, reduce_scatter_rows, shard_plan, splitk_plan, splitk_step
     from ptxc.launch import Executor, load_library
     import ctypes
     torch.cuda.set_device(rank)
@@ -107,6 +110,21 @@ def _worker(rank, world, port, q):
             ref = A.astype(np.float64) @ B.astype(np.float64)
             scale = np.abs(A).astype(np.float64) @ np.abs(B).astype(np.float64)
             ok &= bool(np.all(np.abs(full.cpu().numpy() - ref) <= 1e-5 * scale))
+        # --- the same split-K with the reduce-scatter fused into the GEMM:
+        # partial rows go straight into their owner's buffer over NVLink
+        slots = torch.full((world, 256 // world, 256), float("nan"), device="cuda")
+        peers = PeerRows(slots)
+        try:
+            for _ in range(2):                     # twice: the workspace is left clean
+                mine = splitk_step(a_loc, b_loc, peers, 256, 256, splits=g["splits"])
+            full2 = torch.empty(256, 256, device="cuda")
+            dist.all_gather_into_tensor(full2, mine)
+            if rank == 0:
+                ok &= bool(np.all(np.abs(full2.cpu().numpy() - ref) <= 1e-5 * scale))
+        finally:
+            torch.cuda.synchronize()
+            dist.barrier()
+            peers.close()
         torch.cuda.synchronize()
     finally:
         dist.barrier()
