@@ -59,6 +59,27 @@ __device__ __forceinline__ void lds4(const double *p, double v[4]) {
 }
 __device__ __forceinline__ float fma_t(float a, float b, float c) { return fmaf(a, b, c); }
 __device__ __forceinline__ double fma_t(double a, double b, double c) { return fma(a, b, c); }
+
+// acc[j] = fma(a, b[j], acc[j]) for j < 8.  For f32 on sm_100a this is four
+// packed fma.rn.f32x2 (two lanes' fused multiply-adds per instruction, each
+// rounded exactly as fmaf): the CUDA-core GEMM is issue-bound, and the packed
+// form halves the FMA issue slots.
+__device__ __forceinline__ void fma_row8(double acc[8], double a, const double b[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = fma(a, b[j], acc[j]);
+}
+__device__ __forceinline__ void fma_row8(float acc[8], float a, const float b[8]) {
+  unsigned long long ap;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(ap) : "f"(a));
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    unsigned long long bp, cp;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(bp) : "f"(b[2 * p]), "f"(b[2 * p + 1]));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(cp) : "f"(acc[2 * p]), "f"(acc[2 * p + 1]));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(cp) : "l"(ap), "l"(bp));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(acc[2 * p]), "=f"(acc[2 * p + 1]) : "l"(cp));
+  }
+}
 __device__ __forceinline__ void atomic_add4(float *dst, const float v[4]) {
   atomicAdd(reinterpret_cast<float4 *>(dst), make_float4(v[0], v[1], v[2], v[3]));
 }
@@ -175,9 +196,7 @@ gemm_simt_tma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_const
         lds4(Bs + (kk + q) * BN + 4 * tx, b);
         lds4(Bs + (kk + q) * BN + 64 + 4 * tx, b + 4);
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[i][j] = fma_t(a[i][q], b[j], acc[i][j]);
+        for (int i = 0; i < 8; ++i) fma_row8(acc[i], a[i][q], b);
       }
     }
     // every thread is done with stage s before thread 0 refills it next trip;
