@@ -14,11 +14,16 @@
 //               (K0, K1, V0, K2, V1, ...; no multicast, 128-byte swizzle)
 //   warp 5      one thread issues tcgen05.mma.  S = Q K^T goes to one of two
 //               TMEM score buffers, one block ahead: S[j+1] is computed while
-//               the softmax warps work on S[j].  O += P V (into TMEM) follows
-//               once P[j] is written.
+//               the softmax warps work on S[j].  O += P V (into TMEM, P read
+//               from TMEM as the A operand) follows once P[j] is written.
 //   warps 0-3   one query row per thread (TMEM lane): read the 64 scores,
-//               exponentiate against the running max, write P as f16 into
-//               swizzled shared memory, keep the running sum; finally O / l.
+//               exponentiate against the running max, write P as packed f16
+//               over the first 32 columns of the same score buffer, keep the
+//               running sum; finally O / l.
+// P[j] lives in score buffer j % 2 until O += P[j] V has read it; the next
+// product into that buffer, S[j+2], is issued after that MMA by the same
+// thread, and the tensor pipe runs one thread's MMAs in issue order.  So the
+// softmax never waits for the previous P V product, except to rescale O.
 // The running max is moved lazily: a row keeps its max until a block's max
 // exceeds it by more than 2^8 (so P <= 256, well inside f16), and only then
 // is its O row rescaled in TMEM.  The result is the same softmax; only the
@@ -40,10 +45,9 @@ struct AttnCfg {
   static constexpr int K_BOX = BN * 128;             // [BN keys][128 B]
   static constexpr int Q_BYTES = NKB * Q_BOX;
   static constexpr int SLOT_BYTES = NKB * K_BOX;     // one K or V block
-  static constexpr int SLOTS = 3;
-  static constexpr int P_BYTES = Q_BOX;              // [128 rows][64 keys] f16
-  // Q | ring slots | P, then the mbarriers
-  static constexpr int BAR_OFF = Q_BYTES + SLOTS * SLOT_BYTES + P_BYTES;
+  static constexpr int SLOTS = 4;
+  // Q | ring slots, then the mbarriers
+  static constexpr int BAR_OFF = Q_BYTES + SLOTS * SLOT_BYTES;
   static constexpr int SMEM = BAR_OFF + 128 + 1024;
   static constexpr uint32_t S_COL0 = 0;              // score buffers at columns 0 and 64
   static constexpr uint32_t O_COL = 2 * BN;
@@ -57,6 +61,18 @@ struct AttnCfg {
 constexpr int kAttnWaitQ = 0x1201, kAttnWaitSlot = 0x1202, kAttnWaitP = 0x1203,
               kAttnWaitEmpty = 0x1204, kAttnWaitS = 0x1205, kAttnWaitO = 0x1206,
               kAttnWaitOFinal = 0x1207, kAttnWaitDrain = 0x1208, kAttnWaitMma = 0x1209;
+
+// D[tmem] (+)= A[tmem] x B[smem desc]: A is M x 16 f16, row m in TMEM lane m,
+// two consecutive k packed per 32-bit column (8 columns per MMA).
+__device__ __forceinline__ void mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -78,12 +94,11 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char *sQ = smem;
   unsigned char *sRing = sQ + C::Q_BYTES;
-  unsigned char *sP = sRing + C::SLOTS * C::SLOT_BYTES;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
-  uint64_t *q_full = bars + 0, *p_full = bars + 1, *o_full = bars + 2, *mma_done = bars + 3;
-  uint64_t *s_full = bars + 4;                       // [2]
-  uint64_t *full = bars + 6, *empty = bars + 9;      // [SLOTS] each
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 12);
+  uint64_t *q_full = bars + 0, *o_full = bars + 1, *mma_done = bars + 2;
+  uint64_t *s_full = bars + 3, *p_full = bars + 5;   // [2] each: block j uses [j % 2]
+  uint64_t *full = bars + 7, *empty = bars + 7 + C::SLOTS;   // [SLOTS] each
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 7 + 2 * C::SLOTS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * 128, bh = blockIdx.y;
@@ -94,7 +109,8 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     prefetch_tensormap(&tmK);
     prefetch_tensormap(&tmV);
     mbar_init(q_full, 1);
-    mbar_init(p_full, 128);
+    mbar_init(&p_full[0], 128);
+    mbar_init(&p_full[1], 128);
     mbar_init(o_full, 1);
     mbar_init(mma_done, 1);
     mbar_init(&s_full[0], 1);
@@ -147,7 +163,6 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       constexpr uint32_t idesc_s = f16_idesc(128, BN, false, false);
       constexpr uint32_t idesc_o = f16_idesc(128, D, false, true);
       const uint32_t qa = smem_u32(sQ);
-      const uint32_t pa = smem_u32(sP);
       int taken = 0;
       // next ring item: wait until it has landed, return its shared address
       auto take = [&](uint32_t &addr) -> bool {
@@ -187,14 +202,17 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
           issue_s(j + 1, ka);
           release();
         }
-        if (!mbar_wait(p_full, j & 1, status, kAttnWaitP) || !take(va)) break;
+        // P[j] was published into score buffer j % 2 (one barrier per buffer:
+        // P[j+2] cannot be published before S[j+2] is issued below)
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, status, kAttnWaitP) || !take(va)) break;
         tc_fence_after();
-        // O += P V: P K-major over the 64 keys, V N-major (value columns contiguous)
+        // O += P V: P from TMEM (16 keys = 8 columns per MMA), V N-major
+        // (value columns contiguous)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_f16(tmem + C::O_COL, sw128_desc(pa + kk * 32, 16, 1024),
-                  sw128_desc(va + kk * 16 * 128, C::K_BOX, 1024), idesc_o,
-                  (j | kk) != 0 ? 1u : 0u);
+          mma_f16_tmem_a(tmem + C::O_COL, tmem + C::S_COL0 + (j & 1) * BN + kk * 8,
+                         sw128_desc(va + kk * 16 * 128, C::K_BOX, 1024), idesc_o,
+                         (j | kk) != 0 ? 1u : 0u);
         mma_commit(o_full);
         release();
       }
@@ -261,42 +279,39 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         h[i] = *reinterpret_cast<uint32_t *>(&hh);
       }
       const float ps = (psum[0] + psum[1]) + (psum[2] + psum[3]);
-      if (j > 0) {
-        // P and O are still in use by the previous block's P V product
+      // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp
+      // rescales when any of its rows moved its max (alpha is 1 for the others)
+      if (j > 0 && __any_sync(0xffffffffu, move)) {
+        // O is still being accumulated by P[j-1] V.  Waiting for phase j-1 of
+        // o_full is unambiguous here: S[j] was issued after P[j-2] V, so its
+        // completion (waited above) means phases up to j-2 are done, and P[j] V
+        // has not been issued yet.
         ok = __all_sync(0xffffffffu, mbar_wait(o_full, (j - 1) & 1, status, kAttnWaitO));
         if (!ok) break;
         tc_fence_after();
-        // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp
-        // rescales when any of its rows moved its max (alpha is 1 for the others)
-        if (__any_sync(0xffffffffu, move)) {
 #pragma unroll 1
-          for (int cc = 0; cc < D / 32; ++cc) {
-            float ov[32];
-            __syncwarp();
-            tmem_ld32(lane_base + C::O_COL + cc * 32, ov);
+        for (int cc = 0; cc < D / 32; ++cc) {
+          float ov[32];
+          __syncwarp();
+          tmem_ld32(lane_base + C::O_COL + cc * 32, ov);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-            tmem_st32(lane_base + C::O_COL + cc * 32, ov);
-          }
+          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+          tmem_st32(lane_base + C::O_COL + cc * 32, ov);
         }
       }
-      // 64 keys = eight 16-byte chunks of this row's 128-byte line; chunk
-      // index XOR (row % 8) is the 128-byte swizzle
-      unsigned char *rowp = sP + r * 128;
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        *reinterpret_cast<uint4 *>(rowp + ((q ^ (r & 7)) * 16)) =
-            make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+      // P over the first 32 columns of this block's score buffer (already read)
+      tmem_st32_u(lane_base + C::S_COL0 + (j & 1) * BN, h);
       l = l * alpha + ps;
       m = m_use;
-      fence_proxy_async();      // P (generic-proxy writes) visible to the tensor core
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[j & 1]);
     }
     // epilogue: O / l, staged through shared memory (the Q and ring space,
     // free once every MMA is done) in 32-row x 128-byte swizzled boxes and
     // written by TMA stores; rows beyond S are dropped by the TMA
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_full, (nblk - 1) & 1, status, kAttnWaitOFinal));
+    // the MMA thread commits mma_done after its last product (o_full may be
+    // two phases behind here, so its parity would be ambiguous)
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(mma_done, 0, status, kAttnWaitOFinal));
     if (ok) {
       tc_fence_after();
       const float rl = 1.0f / l;

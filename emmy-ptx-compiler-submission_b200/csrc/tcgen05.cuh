@@ -167,11 +167,8 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
   for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Store 32 consecutive f32 columns of this thread's TMEM lane (waits for completion).
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
-  uint32_t r[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(v[i]);
+// Store 32 consecutive 32-bit columns of this thread's TMEM lane (waits for completion).
+__device__ __forceinline__ void tmem_st32_u(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
       "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
@@ -182,6 +179,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Store 32 consecutive f32 columns of this thread's TMEM lane (waits for completion).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  uint32_t r[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(v[i]);
+  tmem_st32_u(taddr, r);
 }
 
 }  // namespace emmy
