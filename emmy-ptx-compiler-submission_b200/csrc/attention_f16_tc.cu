@@ -222,9 +222,8 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     }
     __syncwarp();
   } else {
-    // softmax / epilogue: thread r owns query row m0 + r (TMEM lane r).
+    // softmax / epilogue: thread t owns query row m0 + t (TMEM lane t).
     // Scores are kept as t = s * scale * log2(e), so p = 2^(t - m).
-    const int r = threadIdx.x;
     const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
     const float c = (scale_div ? 1.0f / __ldg(scale_div) : 1.0f) * 1.4426950408889634f;
     float m = -INFINITY, l = 0.f;
