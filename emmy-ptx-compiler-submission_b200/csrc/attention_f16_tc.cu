@@ -7,21 +7,29 @@
 // 564-611, 1311-1392, ptxc/expr.py:891-895), here with f16 operands as the
 // benchmark configuration asks.
 //
-// One CTA owns 128 query rows of one (batch, head) and walks the keys in
-// blocks of 64; up to D = 128 two CTAs share an SM.  Warp roles:
-//   warp 4      TMA producer: Q once, then K and V blocks through one 3-slot
-//               ring in the order the MMA thread consumes them
-//               (K0, K1, V0, K2, V1, ...; no multicast, 128-byte swizzle)
+// Persistent CTAs (as many as fit on the SMs, two per SM up to D = 128) walk
+// the 128-query tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... in (batch,
+// head)-major order; each tile's keys go in blocks of 64.  Warp roles:
+//   warp 4      TMA producer: K and V blocks through one ring in the order the
+//               MMA thread consumes them (K0, K1, V0, K2, V1, ..., then the next
+//               tile's), and each tile's Q once the previous tile's last score
+//               product is done with it (no multicast, 128-byte swizzle)
 //   warp 5      one thread issues tcgen05.mma.  S = Q K^T goes to one of two
-//               TMEM score buffers, one block ahead: S[j+1] is computed while
-//               the softmax warps work on S[j].  O += P V (into TMEM, P read
-//               from TMEM as the A operand) follows once P[j] is written.
+//               TMEM score buffers, one block ahead: S[g+1] is computed while
+//               the softmax warps work on S[g].  O += P V (into TMEM, P read
+//               from TMEM as the A operand) follows once P[g] is written.
 //   warps 0-3   one query row per thread (TMEM lane): read the 64 scores,
 //               exponentiate against the running max, write P as packed f16
 //               over the first 32 columns of the same score buffer, keep the
-//               running sum; finally O / l.
-// P[j] lives in score buffer j % 2 until O += P[j] V has read it; the next
-// product into that buffer, S[j+2], is issued after that MMA by the same
+//               running sum; at the end of a tile O / l, staged in shared
+//               memory and written by TMA stores.
+// g counts key blocks over all of a CTA's tiles, so the score buffers and
+// their barriers simply continue from one tile into the next: the next tile's
+// Q, K and V loads and its first score products overlap the current tile's
+// last blocks and epilogue.  The next tile's first P V product (which starts
+// O afresh) waits until the epilogue has read O out of TMEM.
+// P[g] lives in score buffer g % 2 until O += P[g] V has read it; the next
+// product into that buffer, S[g+2], is issued after that MMA by the same
 // thread, and the tensor pipe runs one thread's MMAs in issue order.  So the
 // softmax never waits for the previous P V product, except to rescale O.
 // The running max is moved lazily: a row keeps its max until a block's max
@@ -45,10 +53,12 @@ struct AttnCfg {
   static constexpr int K_BOX = BN * 128;             // [BN keys][128 B]
   static constexpr int Q_BYTES = NKB * Q_BOX;
   static constexpr int SLOT_BYTES = NKB * K_BOX;     // one K or V block
-  static constexpr int SLOTS = 4;
-  // Q | ring slots, then the mbarriers
-  static constexpr int BAR_OFF = Q_BYTES + SLOTS * SLOT_BYTES;
-  static constexpr int SMEM = BAR_OFF + 128 + 1024;
+  static constexpr int SLOTS = 3;
+  static constexpr int STAGE_BYTES = 4 * 4096;       // one 32-row x 128-byte box per softmax warp
+  // Q | ring slots | epilogue staging, then the mbarriers
+  static constexpr int STAGE_OFF = Q_BYTES + SLOTS * SLOT_BYTES;
+  static constexpr int BAR_OFF = STAGE_OFF + STAGE_BYTES;
+  static constexpr int SMEM = BAR_OFF + 256 + 1024;
   static constexpr uint32_t S_COL0 = 0;              // score buffers at columns 0 and 64
   static constexpr uint32_t O_COL = 2 * BN;
   static constexpr uint32_t TMEM_COLS = O_COL + D <= 256 ? 256 : 512;
@@ -60,7 +70,8 @@ struct AttnCfg {
 // status codes of the waits that can give up (first one recorded wins)
 constexpr int kAttnWaitQ = 0x1201, kAttnWaitSlot = 0x1202, kAttnWaitP = 0x1203,
               kAttnWaitEmpty = 0x1204, kAttnWaitS = 0x1205, kAttnWaitO = 0x1206,
-              kAttnWaitOFinal = 0x1207, kAttnWaitDrain = 0x1208, kAttnWaitMma = 0x1209;
+              kAttnWaitOFinal = 0x1207, kAttnWaitDrain = 0x1208, kAttnWaitMma = 0x1209,
+              kAttnWaitQEmpty = 0x120a, kAttnWaitOFree = 0x120b;
 
 // D[tmem] (+)= A[tmem] x B[smem desc]: A is M x 16 f16, row m in TMEM lane m,
 // two consecutive k packed per 32-bit column (8 columns per MMA).
@@ -86,7 +97,8 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV,
                         const __grid_constant__ CUtensorMap tmO,
-                        const float *__restrict__ scale_div, int S, int out_f16, int *status) {
+                        const float *__restrict__ scale_div, int S, int ntiles, int out_f16,
+                        int *status) {
   using C = AttnCfg<D>;
   constexpr int BN = C::BN;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -95,26 +107,36 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
   unsigned char *sQ = smem;
   unsigned char *sRing = sQ + C::Q_BYTES;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
-  uint64_t *q_full = bars + 0, *o_full = bars + 1, *mma_done = bars + 2;
-  uint64_t *s_full = bars + 3, *p_full = bars + 5;   // [2] each: block j uses [j % 2]
-  uint64_t *full = bars + 7, *empty = bars + 7 + C::SLOTS;   // [SLOTS] each
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 7 + 2 * C::SLOTS);
+  // per tile: q_full (Q landed), q_empty (the tile's last S product is done
+  // with Q), o_done (the tile's last P V product is done), o_free (the
+  // epilogue has read O); per block: s_full / p_full [g % 2], o_full
+  uint64_t *q_full = bars + 0, *q_empty = bars + 1, *o_done = bars + 2, *o_free = bars + 3;
+  uint64_t *o_full = bars + 4, *mma_done = bars + 5;
+  uint64_t *s_full = bars + 6, *p_full = bars + 8;   // [2] each
+  uint64_t *full = bars + 10, *empty = bars + 10 + C::SLOTS;   // [SLOTS] each
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 10 + 2 * C::SLOTS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * 128, bh = blockIdx.y;
   const int nblk = (S + BN - 1) / BN;
+  const int qtiles = (S + 127) / 128;
+  // this CTA's tiles: blockIdx.x + i * gridDim.x for i < my_tiles
+  const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tmQ);
     prefetch_tensormap(&tmK);
     prefetch_tensormap(&tmV);
+    prefetch_tensormap(&tmO);
     mbar_init(q_full, 1);
-    mbar_init(&p_full[0], 128);
-    mbar_init(&p_full[1], 128);
+    mbar_init(q_empty, 1);
+    mbar_init(o_done, 1);
+    mbar_init(o_free, 128);
     mbar_init(o_full, 1);
     mbar_init(mma_done, 1);
-    mbar_init(&s_full[0], 1);
-    mbar_init(&s_full[1], 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 128);
+    }
     for (int s = 0; s < C::SLOTS; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -130,12 +152,10 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
   if (warp == 4) {
     if (lane == 0) {
       // TMA producer: ring item i goes to slot i % SLOTS once item i - SLOTS
-      // has been consumed.  Order: K0, then per block j: K[j+1] (if any), V[j].
-      mbar_expect_tx(q_full, C::Q_BYTES);
-      for (int kb = 0; kb < C::NKB; ++kb)
-        tma_load_3d(sQ + kb * C::Q_BOX, &tmQ, q_full, kb * 64, m0, bh);
+      // has been consumed.  Per tile: Q (once the previous tile's Q is free),
+      // K0, then per block j: K[j+1] (if any), V[j].
       int issued = 0;
-      auto load = [&](const CUtensorMap *map, int key_block) -> bool {
+      auto load = [&](const CUtensorMap *map, int key_block, int bh) -> bool {
         const int slot = issued % C::SLOTS;
         if (issued >= C::SLOTS &&
             !mbar_wait(&empty[slot], ((issued / C::SLOTS) - 1) & 1, status, kAttnWaitEmpty))
@@ -147,13 +167,25 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         ++issued;
         return true;
       };
-      bool ok = load(&tmK, 0);
-      for (int j = 0; ok && j < nblk; ++j) {
-        if (j + 1 < nblk) ok = load(&tmK, j + 1);
-        if (ok) ok = load(&tmV, j);
+      bool ok = true;
+      int qloads = 0;
+      for (int i = 0; ok && i < my_tiles; ++i) {
+        const int t = blockIdx.x + i * gridDim.x;
+        const int bh = t / qtiles, m0 = (t - bh * qtiles) * 128;
+        // Q of tile i - 1 is free once that tile's last S product is done
+        if (i > 0 && !mbar_wait(q_empty, (i - 1) & 1, status, kAttnWaitQEmpty)) break;
+        mbar_expect_tx(q_full, C::Q_BYTES);
+        for (int kb = 0; kb < C::NKB; ++kb)
+          tma_load_3d(sQ + kb * C::Q_BOX, &tmQ, q_full, kb * 64, m0, bh);
+        ++qloads;
+        ok = load(&tmK, 0, bh);
+        for (int j = 0; ok && j < nblk; ++j) {
+          if (j + 1 < nblk) ok = load(&tmK, j + 1, bh);
+          if (ok) ok = load(&tmV, j, bh);
+        }
       }
       // drain: every issued copy has landed before the CTA may exit
-      mbar_wait(q_full, 0, status, kAttnWaitDrain);
+      if (qloads > 0) mbar_wait(q_full, (qloads - 1) & 1, status, kAttnWaitDrain);
       for (int i = issued - C::SLOTS > 0 ? issued - C::SLOTS : 0; i < issued; ++i)
         mbar_wait(&full[i % C::SLOTS], (i / C::SLOTS) & 1, status, kAttnWaitDrain);
     }
@@ -175,46 +207,57 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       // descriptors built once; a byte offset d inside a 1024-byte-aligned tile
       // adds d >> 4 to the start-address field
       const uint64_t dq = sw128_desc(qa, 16, 1024);
-      auto issue_s = [&](int j, uint32_t ka) {
-        // S[j & 1] = Q K^T: both operands K-major (head dim contiguous)
+      auto issue_s = [&](int g, uint32_t ka) {
+        // S[g % 2] = Q K^T: both operands K-major (head dim contiguous)
         const uint64_t dk = sw128_desc(ka, 16, 1024);
 #pragma unroll
         for (int kb = 0; kb < C::NKB; ++kb)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_f16(tmem + C::S_COL0 + (j & 1) * BN, dq + ((kb * C::Q_BOX + kk * 32) >> 4),
+            mma_f16(tmem + C::S_COL0 + (g & 1) * BN, dq + ((kb * C::Q_BOX + kk * 32) >> 4),
                     dk + ((kb * C::K_BOX + kk * 32) >> 4), idesc_s, (kb | kk) != 0 ? 1u : 0u);
-        mma_commit(&s_full[j & 1]);
+        mma_commit(&s_full[g & 1]);
       };
-      uint32_t ka = 0, va = 0;
       // Q, K and V come from TMA: their barriers need no tcgen05 fence; P and
       // the rescaled O come from the softmax threads and do
-      bool ok = mbar_wait(q_full, 0, status, kAttnWaitQ) && take(ka);
-      if (ok) {
-        issue_s(0, ka);
+      uint32_t ka = 0, va = 0;
+      bool ok = true;
+      int g = 0;                                   // key blocks over all tiles
+      for (int i = 0; ok && i < my_tiles; ++i) {
+        ok = mbar_wait(q_full, i & 1, status, kAttnWaitQ) && take(ka);
+        if (!ok) break;
+        issue_s(g, ka);
         release();
-      }
-      for (int j = 0; ok && j < nblk; ++j) {
-        if (j + 1 < nblk) {
-          // S[j+1] into the other buffer: its previous contents (S[j-1]) were
-          // read before P[j-1] was published, which was waited for below
-          if (!take(ka)) break;
-          issue_s(j + 1, ka);
+        if (nblk == 1) mma_commit(q_empty);
+        for (int j = 0; j < nblk; ++j, ++g) {
+          if (j + 1 < nblk) {
+            // S[g+1] into the other buffer: its previous contents (P[g-1]) were
+            // read by the P V product issued before it
+            if (!(ok = take(ka))) break;
+            issue_s(g + 1, ka);
+            release();
+            if (j + 2 == nblk) mma_commit(q_empty);   // the tile's last use of Q
+          }
+          // P[g] was published into score buffer g % 2 (one barrier per buffer:
+          // P[g+2] cannot be published before S[g+2] is issued)
+          if (!(ok = mbar_wait(&p_full[g & 1], (g >> 1) & 1, status, kAttnWaitP) && take(va)))
+            break;
+          // the tile's first product overwrites O: the previous tile's
+          // epilogue must have read it
+          if (j == 0 && i > 0 && !(ok = mbar_wait(o_free, (i - 1) & 1, status, kAttnWaitOFree)))
+            break;
+          tc_fence_after();
+          // O += P V: P from TMEM (16 keys = 8 columns per MMA), V N-major
+          // (value columns contiguous)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f16_tmem_a(tmem + C::O_COL, tmem + C::S_COL0 + (g & 1) * BN + kk * 8,
+                           sw128_desc(va + kk * 16 * 128, C::K_BOX, 1024), idesc_o,
+                           (j | kk) != 0 ? 1u : 0u);
+          mma_commit(o_full);
           release();
         }
-        // P[j] was published into score buffer j % 2 (one barrier per buffer:
-        // P[j+2] cannot be published before S[j+2] is issued below)
-        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, status, kAttnWaitP) || !take(va)) break;
-        tc_fence_after();
-        // O += P V: P from TMEM (16 keys = 8 columns per MMA), V N-major
-        // (value columns contiguous)
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_f16_tmem_a(tmem + C::O_COL, tmem + C::S_COL0 + (j & 1) * BN + kk * 8,
-                         sw128_desc(va + kk * 16 * 128, C::K_BOX, 1024), idesc_o,
-                         (j | kk) != 0 ? 1u : 0u);
-        mma_commit(o_full);
-        release();
+        if (ok) mma_commit(o_done);
       }
       // every MMA this thread issued has finished before TMEM is freed
       mma_commit(mma_done);
@@ -226,137 +269,144 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     // Scores are kept as t = s * scale * log2(e), so p = 2^(t - m).
     const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
     const float c = (scale_div ? 1.0f / __ldg(scale_div) : 1.0f) * 1.4426950408889634f;
-    float m = -INFINITY, l = 0.f;
+    unsigned char *stage = smem + C::STAGE_OFF + warp * 4096;   // this warp's 4 KB box
     bool ok = true;
-    for (int j = 0; j < nblk; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, status, kAttnWaitS));
-      if (!ok) break;
-      tc_fence_after();
-      const int key0 = j * BN;
-      // raw scores v; t = v * c is folded into one FFMA below.  With c > 0 the
-      // row max of t is c * max(v), with c < 0 it is c * min(v); masked keys
-      // get the value whose t is -inf.
-      float v[64];
-      tmem_ld64(lane_base + C::S_COL0 + (j & 1) * BN, v);
-      if (key0 + BN > S) {
-        const float far = c > 0.f ? -INFINITY : INFINITY;
-#pragma unroll
-        for (int i = 0; i < 64; ++i)
-          if (key0 + i >= S) v[i] = far;
-      }
-      float ext[8];
-#pragma unroll
-      for (int q = 0; q < 8; ++q) ext[q] = v[q];
-      if (c > 0.f) {
-#pragma unroll
-        for (int i = 8; i < 64; ++i) ext[i & 7] = fmaxf(ext[i & 7], v[i]);
-#pragma unroll
-        for (int w = 4; w >= 1; w >>= 1)
-#pragma unroll
-          for (int q = 0; q < w; ++q) ext[q] = fmaxf(ext[q], ext[q + w]);
-      } else {
-#pragma unroll
-        for (int i = 8; i < 64; ++i) ext[i & 7] = fminf(ext[i & 7], v[i]);
-#pragma unroll
-        for (int w = 4; w >= 1; w >>= 1)
-#pragma unroll
-          for (int q = 0; q < w; ++q) ext[q] = fminf(ext[q], ext[q + w]);
-      }
-      const float mb = ext[0] * c;
-      // lazy max: move only when the block's max is more than 2^8 above it
-      const bool move = mb > m + C::RESCALE_LOG2;
-      const float m_use = move ? mb : m;
-      const float alpha = move ? ex2_approx(m - mb) : 1.0f;
-      float psum[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t h[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float p0 = ex2_approx(fmaf(v[2 * i], c, -m_use));
-        const float p1 = ex2_approx(fmaf(v[2 * i + 1], c, -m_use));
-        psum[i & 3] += p0 + p1;
-        __half2 hh = __floats2half2_rn(p0, p1);
-        h[i] = *reinterpret_cast<uint32_t *>(&hh);
-      }
-      const float ps = (psum[0] + psum[1]) + (psum[2] + psum[3]);
-      // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp
-      // rescales when any of its rows moved its max (alpha is 1 for the others)
-      if (j > 0 && __any_sync(0xffffffffu, move)) {
-        // O is still being accumulated by P[j-1] V.  Waiting for phase j-1 of
-        // o_full is unambiguous here: S[j] was issued after P[j-2] V, so its
-        // completion (waited above) means phases up to j-2 are done, and P[j] V
-        // has not been issued yet.
-        ok = __all_sync(0xffffffffu, mbar_wait(o_full, (j - 1) & 1, status, kAttnWaitO));
+    int g = 0;
+    for (int i = 0; ok && i < my_tiles; ++i) {
+      const int t = blockIdx.x + i * gridDim.x;
+      const int bh = t / qtiles, m0 = (t - bh * qtiles) * 128;
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < nblk; ++j, ++g) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&s_full[g & 1], (g >> 1) & 1, status, kAttnWaitS));
         if (!ok) break;
         tc_fence_after();
-#pragma unroll 1
-        for (int cc = 0; cc < D / 32; ++cc) {
-          float ov[32];
-          __syncwarp();
-          tmem_ld32(lane_base + C::O_COL + cc * 32, ov);
+        const int key0 = j * BN;
+        // raw scores v; t = v * c is folded into one FFMA below.  With c > 0 the
+        // row max of t is c * max(v), with c < 0 it is c * min(v); masked keys
+        // get the value whose t is -inf.
+        float v[64];
+        tmem_ld64(lane_base + C::S_COL0 + (g & 1) * BN, v);
+        if (key0 + BN > S) {
+          const float far = c > 0.f ? -INFINITY : INFINITY;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-          tmem_st32(lane_base + C::O_COL + cc * 32, ov);
+          for (int k = 0; k < 64; ++k)
+            if (key0 + k >= S) v[k] = far;
         }
+        float ext[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) ext[q] = v[q];
+        if (c > 0.f) {
+#pragma unroll
+          for (int k = 8; k < 64; ++k) ext[k & 7] = fmaxf(ext[k & 7], v[k]);
+#pragma unroll
+          for (int w = 4; w >= 1; w >>= 1)
+#pragma unroll
+            for (int q = 0; q < w; ++q) ext[q] = fmaxf(ext[q], ext[q + w]);
+        } else {
+#pragma unroll
+          for (int k = 8; k < 64; ++k) ext[k & 7] = fminf(ext[k & 7], v[k]);
+#pragma unroll
+          for (int w = 4; w >= 1; w >>= 1)
+#pragma unroll
+            for (int q = 0; q < w; ++q) ext[q] = fminf(ext[q], ext[q + w]);
+        }
+        const float mb = ext[0] * c;
+        // lazy max: move only when the block's max is more than 2^8 above it
+        const bool move = mb > m + C::RESCALE_LOG2;
+        const float m_use = move ? mb : m;
+        const float alpha = move ? ex2_approx(m - mb) : 1.0f;
+        float psum[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t h[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const float p0 = ex2_approx(fmaf(v[2 * k], c, -m_use));
+          const float p1 = ex2_approx(fmaf(v[2 * k + 1], c, -m_use));
+          psum[k & 3] += p0 + p1;
+          __half2 hh = __floats2half2_rn(p0, p1);
+          h[k] = *reinterpret_cast<uint32_t *>(&hh);
+        }
+        const float ps = (psum[0] + psum[1]) + (psum[2] + psum[3]);
+        // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp
+        // rescales when any of its rows moved its max (alpha is 1 for the others)
+        if (j > 0 && __any_sync(0xffffffffu, move)) {
+          // O is still being accumulated by P[g-1] V.  Waiting for phase g-1 of
+          // o_full is unambiguous here: S[g] was issued after P[g-2] V, so its
+          // completion (waited above) means phases up to g-2 are done, and P[g] V
+          // has not been issued yet.
+          ok = __all_sync(0xffffffffu, mbar_wait(o_full, (g - 1) & 1, status, kAttnWaitO));
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll 1
+          for (int cc = 0; cc < D / 32; ++cc) {
+            float ov[32];
+            __syncwarp();
+            tmem_ld32(lane_base + C::O_COL + cc * 32, ov);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) ov[k] *= alpha;
+            tmem_st32(lane_base + C::O_COL + cc * 32, ov);
+          }
+        }
+        // P over the first 32 columns of this block's score buffer (already read)
+        tmem_st32_u(lane_base + C::S_COL0 + (g & 1) * BN, h);
+        l = l * alpha + ps;
+        m = m_use;
+        tc_fence_before();
+        mbar_arrive(&p_full[g & 1]);
       }
-      // P over the first 32 columns of this block's score buffer (already read)
-      tmem_st32_u(lane_base + C::S_COL0 + (j & 1) * BN, h);
-      l = l * alpha + ps;
-      m = m_use;
-      tc_fence_before();
-      mbar_arrive(&p_full[j & 1]);
-    }
-    // epilogue: O / l, staged through shared memory (the Q and ring space,
-    // free once every MMA is done) in 32-row x 128-byte swizzled boxes and
-    // written by TMA stores; rows beyond S are dropped by the TMA
-    // the MMA thread commits mma_done after its last product (o_full may be
-    // two phases behind here, so its parity would be ambiguous)
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(mma_done, 0, status, kAttnWaitOFinal));
-    if (ok) {
+      if (!ok) break;
+      // epilogue: O / l, staged through this warp's 4 KB box in 32-row x
+      // 128-byte swizzled pieces and written by TMA stores; rows beyond S are
+      // dropped by the TMA.  Once O has been read out of TMEM, o_free lets the
+      // next tile's first P V product start.
+      ok = __all_sync(0xffffffffu, mbar_wait(o_done, i & 1, status, kAttnWaitOFinal));
+      if (!ok) break;
       tc_fence_after();
       const float rl = 1.0f / l;
-      unsigned char *stage = smem + warp * 2 * 4096;   // two 4 KB boxes per warp
       const int step = out_f16 ? 64 : 32;               // columns per 128-byte row piece
-      int seq = 0;
 #pragma unroll 1
-      for (int c0 = 0; c0 < D; c0 += step, ++seq) {
-        unsigned char *buf = stage + (seq & 1) * 4096;
-        if (seq >= 2 && lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
+      for (int c0 = 0; c0 < D; c0 += step) {
         uint4 w[8];
         if (out_f16) {
           float v[64];
           tmem_ld64(lane_base + C::O_COL + c0, v);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            uint32_t h[4];
+          for (int q = 0; q < 8; ++q) {
+            uint32_t hq[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              __half2 hh = __floats2half2_rn(v[8 * j + 2 * i] * rl, v[8 * j + 2 * i + 1] * rl);
-              h[i] = *reinterpret_cast<uint32_t *>(&hh);
+            for (int k = 0; k < 4; ++k) {
+              __half2 hh = __floats2half2_rn(v[8 * q + 2 * k] * rl, v[8 * q + 2 * k + 1] * rl);
+              hq[k] = *reinterpret_cast<uint32_t *>(&hh);
             }
-            w[j] = make_uint4(h[0], h[1], h[2], h[3]);
+            w[q] = make_uint4(hq[0], hq[1], hq[2], hq[3]);
           }
         } else {
           float v[32];
           tmem_ld32(lane_base + C::O_COL + c0, v);
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            w[j] = make_uint4(__float_as_uint(v[4 * j] * rl), __float_as_uint(v[4 * j + 1] * rl),
-                              __float_as_uint(v[4 * j + 2] * rl), __float_as_uint(v[4 * j + 3] * rl));
+          for (int q = 0; q < 8; ++q)
+            w[q] = make_uint4(__float_as_uint(v[4 * q] * rl), __float_as_uint(v[4 * q + 1] * rl),
+                              __float_as_uint(v[4 * q + 2] * rl), __float_as_uint(v[4 * q + 3] * rl));
         }
+        if (c0 + step >= D) {
+          tc_fence_before();
+          mbar_arrive(o_free);                          // O fully read out of TMEM
+        }
+        // the box is free once the previous TMA store has read it
+        if (lane == 0) bulk_wait_group_read<0>();
+        __syncwarp();
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          *reinterpret_cast<uint4 *>(buf + lane * 128 + ((j ^ (lane & 7)) * 16)) = w[j];
+        for (int q = 0; q < 8; ++q)
+          *reinterpret_cast<uint4 *>(stage + lane * 128 + ((q ^ (lane & 7)) * 16)) = w[q];
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
-          tma_store_3d(&tmO, buf, c0, m0 + warp * 32, bh);
+          tma_store_3d(&tmO, stage, c0, m0 + warp * 32, bh);
           bulk_commit_group();
         }
       }
-      if (lane == 0) bulk_wait_group<0>();
-      __syncwarp();
     }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -453,9 +503,13 @@ int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
                          Cfg::SMEM);
     attr_set[dev] = true;
   }
-  dim3 grid((unsigned)((S + 127) / 128), (unsigned)batch);
+  // persistent CTAs: as many as are resident at once, each walking its tiles
+  const int64_t ntiles = (S + 127) / 128 * batch;
+  if (ntiles > INT32_MAX) return set_error(EMMY_ERR_INVALID, "emmy_attention_f16: too many query tiles");
+  const int64_t slots = (int64_t)Cfg::MIN_BLOCKS * sm_count();
+  const unsigned grid = (unsigned)(ntiles < slots ? ntiles : slots);
   attention_f16_tc_kernel<D><<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(
-      tq, tk, tv, to, scale_div, (int)S, out_f16, device_status_ptr());
+      tq, tk, tv, to, scale_div, (int)S, (int)ntiles, out_f16, device_status_ptr());
   return check_launch("emmy_attention_f16 (tcgen05)");
 }
 

@@ -61,6 +61,9 @@ F16_CASES = [
     for D in (16, 64, 256) for S in (16, 128, 512)
 ] + [
     ("ragged_S200_D64", dict(B=1, H=3, S=200, D=64, out_dtype="f32")),
+    # more query tiles than resident CTAs: each persistent CTA walks several
+    ("tiles_S200_D64_x1200", dict(B=6, H=100, S=200, D=64, out_dtype="f32")),
+    ("tiles_S512_D256_x320", dict(B=2, H=40, S=512, D=256, out_dtype="f16")),
     ("kt_f16_fallback", dict(B=1, H=2, S=64, D=32, out_dtype="f32", k_transposed=True)),
 ]
 
