@@ -10,10 +10,12 @@
 // Persistent CTAs (as many as fit on the SMs, two per SM up to D = 128) walk
 // the 128-query tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... in (batch,
 // head)-major order; each tile's keys go in blocks of 64.  Warp roles:
-//   warp 4      TMA producer: K and V blocks through one ring in the order the
-//               MMA thread consumes them (K0, K1, V0, K2, V1, ..., then the next
-//               tile's), and each tile's Q once the previous tile's last score
-//               product is done with it (no multicast, 128-byte swizzle)
+//   warp 4      TMA producer: the first tile's Q, then K and V blocks through
+//               one ring in the order the MMA thread consumes them (K0, K1, V0,
+//               K2, V1, ..., then the next tile's; no multicast, 128-byte
+//               swizzle).  The next tile's Q is loaded by softmax thread 0 as
+//               soon as the current tile's last score product is done (the
+//               last reader of Q).
 //   warp 5      one thread issues tcgen05.mma.  S = Q K^T goes to one of two
 //               TMEM score buffers, one block ahead: S[g+1] is computed while
 //               the softmax warps work on S[g].  O += P V (into TMEM, P read
@@ -71,7 +73,7 @@ struct AttnCfg {
 constexpr int kAttnWaitQ = 0x1201, kAttnWaitSlot = 0x1202, kAttnWaitP = 0x1203,
               kAttnWaitEmpty = 0x1204, kAttnWaitS = 0x1205, kAttnWaitO = 0x1206,
               kAttnWaitOFinal = 0x1207, kAttnWaitDrain = 0x1208, kAttnWaitMma = 0x1209,
-              kAttnWaitQEmpty = 0x120a, kAttnWaitOFree = 0x120b;
+              kAttnWaitOFree = 0x120b;
 
 // D[tmem] (+)= A[tmem] x B[smem desc]: A is M x 16 f16, row m in TMEM lane m,
 // two consecutive k packed per 32-bit column (8 columns per MMA).
@@ -107,10 +109,10 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
   unsigned char *sQ = smem;
   unsigned char *sRing = sQ + C::Q_BYTES;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
-  // per tile: q_full (Q landed), q_empty (the tile's last S product is done
-  // with Q), o_done (the tile's last P V product is done), o_free (the
-  // epilogue has read O); per block: s_full / p_full [g % 2], o_full
-  uint64_t *q_full = bars + 0, *q_empty = bars + 1, *o_done = bars + 2, *o_free = bars + 3;
+  // per tile: q_full (Q landed), o_done (the tile's last P V product is
+  // done), o_free (the epilogue has read O); per block: s_full / p_full
+  // [g % 2], o_full
+  uint64_t *q_full = bars + 0, *o_done = bars + 2, *o_free = bars + 3;
   uint64_t *o_full = bars + 4, *mma_done = bars + 5;
   uint64_t *s_full = bars + 6, *p_full = bars + 8;   // [2] each
   uint64_t *full = bars + 10, *empty = bars + 10 + C::SLOTS;   // [SLOTS] each
@@ -128,7 +130,6 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     prefetch_tensormap(&tmV);
     prefetch_tensormap(&tmO);
     mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
     mbar_init(o_done, 1);
     mbar_init(o_free, 128);
     mbar_init(o_full, 1);
@@ -152,8 +153,7 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
   if (warp == 4) {
     if (lane == 0) {
       // TMA producer: ring item i goes to slot i % SLOTS once item i - SLOTS
-      // has been consumed.  Per tile: Q (once the previous tile's Q is free),
-      // K0, then per block j: K[j+1] (if any), V[j].
+      // has been consumed.  Per tile: K0, then per block j: K[j+1] (if any), V[j].
       int issued = 0;
       auto load = [&](const CUtensorMap *map, int key_block, int bh) -> bool {
         const int slot = issued % C::SLOTS;
@@ -168,24 +168,24 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         return true;
       };
       bool ok = true;
-      int qloads = 0;
-      for (int i = 0; ok && i < my_tiles; ++i) {
-        const int t = blockIdx.x + i * gridDim.x;
-        const int bh = t / qtiles, m0 = (t - bh * qtiles) * 128;
-        // Q of tile i - 1 is free once that tile's last S product is done
-        if (i > 0 && !mbar_wait(q_empty, (i - 1) & 1, status, kAttnWaitQEmpty)) break;
+      if (my_tiles > 0) {
+        const int bh = blockIdx.x / qtiles, m0 = (blockIdx.x - bh * qtiles) * 128;
         mbar_expect_tx(q_full, C::Q_BYTES);
         for (int kb = 0; kb < C::NKB; ++kb)
           tma_load_3d(sQ + kb * C::Q_BOX, &tmQ, q_full, kb * 64, m0, bh);
-        ++qloads;
+      }
+      for (int i = 0; ok && i < my_tiles; ++i) {
+        const int t = blockIdx.x + i * gridDim.x;
+        const int bh = t / qtiles;
         ok = load(&tmK, 0, bh);
         for (int j = 0; ok && j < nblk; ++j) {
           if (j + 1 < nblk) ok = load(&tmK, j + 1, bh);
           if (ok) ok = load(&tmV, j, bh);
         }
       }
-      // drain: every issued copy has landed before the CTA may exit
-      if (qloads > 0) mbar_wait(q_full, (qloads - 1) & 1, status, kAttnWaitDrain);
+      // drain: every issued copy has landed before the CTA may exit (the
+      // first Q with the MMA thread's wait or here; later ones by thread 0)
+      if (my_tiles == 1) mbar_wait(q_full, 0, status, kAttnWaitDrain);
       for (int i = issued - C::SLOTS > 0 ? issued - C::SLOTS : 0; i < issued; ++i)
         mbar_wait(&full[i % C::SLOTS], (i / C::SLOTS) & 1, status, kAttnWaitDrain);
     }
@@ -228,7 +228,6 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         if (!ok) break;
         issue_s(g, ka);
         release();
-        if (nblk == 1) mma_commit(q_empty);
         for (int j = 0; j < nblk; ++j, ++g) {
           if (j + 1 < nblk) {
             // S[g+1] into the other buffer: its previous contents (P[g-1]) were
@@ -236,7 +235,6 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
             if (!(ok = take(ka))) break;
             issue_s(g + 1, ka);
             release();
-            if (j + 2 == nblk) mma_commit(q_empty);   // the tile's last use of Q
           }
           // P[g] was published into score buffer g % 2 (one barrier per buffer:
           // P[g+2] cannot be published before S[g+2] is issued)
@@ -271,7 +269,7 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     const float c = (scale_div ? 1.0f / __ldg(scale_div) : 1.0f) * 1.4426950408889634f;
     unsigned char *stage = smem + C::STAGE_OFF + warp * 4096;   // this warp's 4 KB box
     bool ok = true;
-    int g = 0;
+    int g = 0, qloads = 0;
     for (int i = 0; ok && i < my_tiles; ++i) {
       const int t = blockIdx.x + i * gridDim.x;
       const int bh = t / qtiles, m0 = (t - bh * qtiles) * 128;
@@ -280,6 +278,17 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[g & 1], (g >> 1) & 1, status, kAttnWaitS));
         if (!ok) break;
         tc_fence_after();
+        if (j + 1 == nblk && threadIdx.x == 0 && i + 1 < my_tiles) {
+          // the tile's last score product is done, and with it every read of
+          // Q: load the next tile's (its phase i + 1 of q_full cannot complete
+          // before the MMA thread has waited for phase i)
+          const int tn = t + gridDim.x;
+          const int bhn = tn / qtiles, m0n = (tn - bhn * qtiles) * 128;
+          mbar_expect_tx(q_full, C::Q_BYTES);
+          for (int kb = 0; kb < C::NKB; ++kb)
+            tma_load_3d(sQ + kb * C::Q_BOX, &tmQ, q_full, kb * 64, m0n, bhn);
+          ++qloads;
+        }
         const int key0 = j * BN;
         // raw scores v; t = v * c is folded into one FFMA below.  With c > 0 the
         // row max of t is c * max(v), with c < 0 it is c * min(v); masked keys
@@ -406,6 +415,8 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       }
     }
     if (lane == 0) bulk_wait_group<0>();
+    // the last Q this thread loaded has landed before the CTA may exit
+    if (threadIdx.x == 0 && qloads > 0) mbar_wait(q_full, qloads & 1, status, kAttnWaitDrain);
     __syncwarp();
   }
   tc_fence_before();
