@@ -652,11 +652,11 @@ extern "C" int emmy_softmax_f32(const float *x, float *y, int64_t outer, int64_t
 //
 // emmy_reduce_f32 splits one long row over many CTAs only when the caller
 // hands it a device workspace for the per-CTA partials.  Some callers cannot
-// allocate device memory at the point of the call: code recorded into a CUDA
-// graph (cudaMalloc is not allowed while a stream is being captured), hosts
-// whose device memory is owned by a pool or budget fixed at start-up, and
-// latency-critical loops where an allocation's implicit device
-// synchronisation is not acceptable.  emmy_reduce_f32_noalloc serves them by
+// allocate device memory at the point of the call: hosts whose device memory
+// is owned by a pool or budget fixed at start-up, code running inside an
+// allocator or pool callback that must not re-enter it, and latency-critical
+// loops where an allocation's implicit device synchronisation is not
+// acceptable.  emmy_reduce_f32_noalloc serves them by
 // keeping the partials in a fixed array in the library's own device memory.
 
 namespace emmy {

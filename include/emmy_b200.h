@@ -294,10 +294,10 @@ int emmy_pointwise_indexed(const void *const *inputs, const int *input_dtypes,
 /*
  * Long-row reduction that allocates nothing: y[0] = fold_op(pre(x[0..n))) [* 1/count].
  * No counterpart in the reference: it exists for callers that cannot allocate
- * device memory when they call -- work recorded into a CUDA graph (no
- * cudaMalloc while a stream is being captured), hosts whose device memory is
- * a pool fixed at start-up, and loops that cannot afford an allocation's
- * implicit synchronisation.  The per-CTA partials live in a 4096-float array
+ * device memory when they call -- hosts whose device memory is a pool or
+ * budget fixed at start-up and owned by someone else, code that runs inside
+ * an allocator or pool callback and must not re-enter it, and loops that
+ * cannot afford an allocation's implicit device synchronisation.  The per-CTA partials live in a 4096-float array
  * inside the library (16 KB on every device that loads it, kept until exit).
  * Limit: n <= 4096 * 16384 = 67,108,864 elements; longer rows are rejected
  * with EMMY_ERR_INVALID (use emmy_reduce_f32 with a workspace instead).

@@ -1,7 +1,9 @@
 """The no-allocation long-row reduction (``emmy_reduce_f32_noalloc``).
 
-Callers that cannot allocate device memory at call time (CUDA-graph capture,
-fixed memory pools, latency-critical loops) use this entry point: its per-CTA
+Callers that cannot allocate device memory at call time (a memory pool fixed at
+start-up and owned by the host program, allocator callbacks that must not
+re-enter the allocator, loops that cannot afford an allocation's implicit
+synchronisation) use this entry point: its per-CTA
 partials live in a fixed array inside the library instead of a workspace the
 caller passes.  This test calls it through the C ABI and checks it against the
 workspace entry point (``emmy_reduce_f32``) on the same input, within the
