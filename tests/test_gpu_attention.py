@@ -64,6 +64,11 @@ F16_CASES = [
     # more query tiles than resident CTAs: each persistent CTA walks several
     ("tiles_S200_D64_x1200", dict(B=6, H=100, S=200, D=64, out_dtype="f32")),
     ("tiles_S512_D256_x320", dict(B=2, H=40, S=512, D=256, out_dtype="f16")),
+    # D = 128, ragged: a last key block with a single valid key, one partial
+    # block, and ragged tiles over several passes of the persistent CTAs
+    ("ragged_S129_D128", dict(B=1, H=3, S=129, D=128, out_dtype="f32")),
+    ("ragged_S65_D128", dict(B=2, H=2, S=65, D=128, out_dtype="f16")),
+    ("ragged_S200_D128_x600", dict(B=3, H=100, S=200, D=128, out_dtype="f16")),
     ("kt_f16_fallback", dict(B=1, H=2, S=64, D=32, out_dtype="f32", k_transposed=True)),
 ]
 
