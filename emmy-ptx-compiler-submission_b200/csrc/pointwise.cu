@@ -383,6 +383,10 @@ struct PwSimple {
   const void *ptr[3];
   int dtype[3];
   int kind[3];
+  // broadcast operand k read as b[(first + e) % M] with M and first multiples
+  // of 4 and b 16-byte aligned: a 4-element group's values are b[m .. m+3]
+  // for one m, read with one 16-byte load
+  int row4[3];
   double imm[3];
   PwIndex idx[3];
   long long first;
@@ -402,7 +406,15 @@ __device__ __forceinline__ void pw_simple_operand_f32(const PwSimple &q, int k, 
       for (int j = 0; j < 4; ++j) v[j] = base + j < n ? T(p[j]) : T(0);
     }
   } else if (BC && q.kind[k] == 3) {
-    pw_bcast_group<T, 4>(q.ptr[k], EMMY_DT_F32, q.idx[k], q.first, base, n, v);
+    if (q.row4[k] && full) {
+      const PwDiv &md = q.idx[k].mod;
+      const unsigned long long x0 = (unsigned long long)(q.first + base);
+      const unsigned long long m = x0 - pw_div(md, x0) * md.d;
+      const float4 a = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(q.ptr[k]) + m));
+      v[0] = T(a.x); v[1] = T(a.y); v[2] = T(a.z); v[3] = T(a.w);
+    } else {
+      pw_bcast_group<T, 4>(q.ptr[k], EMMY_DT_F32, q.idx[k], q.first, base, n, v);
+    }
   } else {
     const T c = q.kind[k] == 1 ? T(*static_cast<const float *>(q.ptr[k])) : T(q.imm[k]);
 #pragma unroll
@@ -447,8 +459,10 @@ template <typename T> __device__ __forceinline__ T pw_post(int op, T v) {
   }
 }
 
-// POST: a unary op follows the step; BC: some operand is a broadcast input.
-template <typename T, int OPC, bool F32IO, bool POST, bool BC>
+// POST: 0 no unary step after the op, 1 one chosen at run time (q.post),
+// 2 ReLU (the bias + ReLU shape, fixed at compile time); BC: some operand is
+// a broadcast input.
+template <typename T, int OPC, bool F32IO, int POST, bool BC>
 __global__ void __launch_bounds__(kPwThreads)
 pointwise_simple_kernel(const PwSimple q, void *out, int out_dtype, int64_t n) {
   const int64_t groups = (n + 3) / 4;
@@ -489,7 +503,10 @@ pointwise_simple_kernel(const PwSimple q, void *out, int out_dtype, int64_t n) {
     } else {
       pw_step<T, 4, 1>(q.op, o, a, b, c);
     }
-    if (POST) {
+    if (POST == 2) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = fmax(o[j], T(0));
+    } else if (POST == 1) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) o[j] = pw_post<T>(q.post, o[j]);
     }
@@ -572,12 +589,15 @@ using namespace emmy;
 template <typename T, int OPC, bool IO>
 static void launch_simple(const PwSimple &q, void *out, int out_dtype, int64_t n, unsigned gb,
                           cudaStream_t st, bool has_bc) {
-  if (q.post >= 0) {
-    if (has_bc) pointwise_simple_kernel<T, OPC, IO, true, true><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
-    else pointwise_simple_kernel<T, OPC, IO, true, false><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+  if (q.post == PW_RELU) {
+    if (has_bc) pointwise_simple_kernel<T, OPC, IO, 2, true><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+    else pointwise_simple_kernel<T, OPC, IO, 2, false><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+  } else if (q.post >= 0) {
+    if (has_bc) pointwise_simple_kernel<T, OPC, IO, 1, true><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+    else pointwise_simple_kernel<T, OPC, IO, 1, false><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
   } else {
-    if (has_bc) pointwise_simple_kernel<T, OPC, IO, false, true><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
-    else pointwise_simple_kernel<T, OPC, IO, false, false><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+    if (has_bc) pointwise_simple_kernel<T, OPC, IO, 0, true><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+    else pointwise_simple_kernel<T, OPC, IO, 0, false><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
   }
 }
 
@@ -712,6 +732,8 @@ static int pointwise_impl(const void *const *inputs, const int *input_dtypes,
       if (r < n_inputs) {
         q.kind[k] = p.idx[r].bcast ? 3 : 0; q.ptr[k] = inputs[r]; q.dtype[k] = input_dtypes[r];
         q.idx[k] = p.idx[r];
+        q.row4[k] = p.idx[r].bcast && p.idx[r].div.d == 1 && p.idx[r].has_mod &&
+                    p.idx[r].mod.d % 4 == 0 && first % 4 == 0 && aligned16(inputs[r]);
       } else if (r < n_inputs + n_scalars) {
         q.kind[k] = 1; q.ptr[k] = scalars[r - n_inputs]; q.dtype[k] = scalar_dtypes[r - n_inputs];
       } else {
