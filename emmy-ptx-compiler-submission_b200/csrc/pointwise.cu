@@ -23,6 +23,7 @@
 namespace emmy {
 
 constexpr int kPwMaxRegs = 32, kPwMaxInstr = 48, kPwMaxIn = 8, kPwThreads = 256;
+constexpr int kPwSimpleGroups = 2;     // most 4-element groups per thread in the register kernel
 
 enum PwOp {
   PW_COPY = 0, PW_ADD, PW_SUB, PW_MUL, PW_DIV, PW_MAX, PW_MIN, PW_NEG, PW_ABS, PW_EXP, PW_LOG,
@@ -461,70 +462,84 @@ template <typename T> __device__ __forceinline__ T pw_post(int op, T v) {
 
 // POST: 0 no unary step after the op, 1 one chosen at run time (q.post),
 // 2 ReLU (the bias + ReLU shape, fixed at compile time); BC: some operand is
-// a broadcast input.
-template <typename T, int OPC, bool F32IO, int POST, bool BC>
+// a broadcast input; GS: 4-element groups per thread.
+template <typename T, int OPC, bool F32IO, int POST, bool BC, int GS>
 __global__ void __launch_bounds__(kPwThreads)
 pointwise_simple_kernel(const PwSimple q, void *out, int out_dtype, int64_t n) {
+  // each thread takes GS 4-element groups a grid apart (coalesced), with
+  // every group's operands loaded before any is computed
   const int64_t groups = (n + 3) / 4;
   const int64_t stride = (int64_t)gridDim.x * kPwThreads;
-  for (int64_t g = (int64_t)blockIdx.x * kPwThreads + threadIdx.x; g < groups; g += stride) {
-    const int64_t base = g * 4;
-    const bool full = base + 4 <= n;
-    T a[4], b[4], c[4];
-    if (F32IO) {
-      pw_simple_operand_f32<T, BC>(q, 0, base, full, n, a);
-      if (q.nops > 1) pw_simple_operand_f32<T, BC>(q, 1, base, full, n, b);
-      if (q.nops > 2) pw_simple_operand_f32<T, BC>(q, 2, base, full, n, c);
-    } else {
-      pw_simple_operand<T, BC>(q, 0, base, full, n, a);
-      if (q.nops > 1) pw_simple_operand<T, BC>(q, 1, base, full, n, b);
-      if (q.nops > 2) pw_simple_operand<T, BC>(q, 2, base, full, n, c);
-    }
-    if (q.nops < 2) {
+  for (int64_t g0 = (int64_t)blockIdx.x * kPwThreads + threadIdx.x; g0 < groups;
+       g0 += GS * stride) {
+    T a[GS][4], b[GS][4], c[GS][4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = T(0);
-    }
-    if (q.nops < 3) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) c[j] = T(0);
-    }
-    // registers in place of the shared-memory file (lane stride 1).  A
-    // run-time op is dispatched once for the four lanes: a per-lane dispatch
-    // would unroll four copies of every op's code.  A compile-time op is
-    // applied lane by lane (measured faster for the streaming ops).
-    T o[4];
-    if (OPC >= 0) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        T ra[1] = {a[j]}, rb[1] = {b[j]}, rc[1] = {c[j]}, rd[1];
-        pw_step<T, 1, 1>(OPC, rd, ra, rb, rc);
-        o[j] = rd[0];
+    for (int u = 0; u < GS; ++u) {
+      const int64_t base = (g0 + u * stride) * 4;
+      if (base >= n) break;
+      const bool full = base + 4 <= n;
+      if (F32IO) {
+        pw_simple_operand_f32<T, BC>(q, 0, base, full, n, a[u]);
+        if (q.nops > 1) pw_simple_operand_f32<T, BC>(q, 1, base, full, n, b[u]);
+        if (q.nops > 2) pw_simple_operand_f32<T, BC>(q, 2, base, full, n, c[u]);
+      } else {
+        pw_simple_operand<T, BC>(q, 0, base, full, n, a[u]);
+        if (q.nops > 1) pw_simple_operand<T, BC>(q, 1, base, full, n, b[u]);
+        if (q.nops > 2) pw_simple_operand<T, BC>(q, 2, base, full, n, c[u]);
       }
-    } else {
-      pw_step<T, 4, 1>(q.op, o, a, b, c);
-    }
-    if (POST == 2) {
+      if (q.nops < 2) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) o[j] = fmax(o[j], T(0));
-    } else if (POST == 1) {
+        for (int j = 0; j < 4; ++j) b[u][j] = T(0);
+      }
+      if (q.nops < 3) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) o[j] = pw_post<T>(q.post, o[j]);
+        for (int j = 0; j < 4; ++j) c[u][j] = T(0);
+      }
     }
-    if (F32IO) {
-      float *dst = static_cast<float *>(out) + base;
-      if (full) {
-        *reinterpret_cast<float4 *>(dst) = make_float4(float(o[0]), float(o[1]), float(o[2]), float(o[3]));
+#pragma unroll
+    for (int u = 0; u < GS; ++u) {
+      const int64_t base = (g0 + u * stride) * 4;
+      if (base >= n) break;
+      const bool full = base + 4 <= n;
+      // registers in place of the shared-memory file (lane stride 1).  A
+      // run-time op is dispatched once for the four lanes: a per-lane dispatch
+      // would unroll four copies of every op's code.  A compile-time op is
+      // applied lane by lane (measured faster for the streaming ops).
+      T o[4];
+      if (OPC >= 0) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          T ra[1] = {a[u][j]}, rb[1] = {b[u][j]}, rc[1] = {c[u][j]}, rd[1];
+          pw_step<T, 1, 1>(OPC, rd, ra, rb, rc);
+          o[j] = rd[0];
+        }
+      } else {
+        pw_step<T, 4, 1>(q.op, o, a[u], b[u], c[u]);
+      }
+      if (POST == 2) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = fmax(o[j], T(0));
+      } else if (POST == 1) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = pw_post<T>(q.post, o[j]);
+      }
+      if (F32IO) {
+        float *dst = static_cast<float *>(out) + base;
+        if (full) {
+          *reinterpret_cast<float4 *>(dst) =
+              make_float4(float(o[0]), float(o[1]), float(o[2]), float(o[3]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (base + j < n) dst[j] = float(o[j]);
+        }
+      } else if (full) {
+        pw_store4<T>(out, out_dtype, base, o);
       } else {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          if (base + j < n) dst[j] = float(o[j]);
+          if (base + j < n) pw_store1<T>(out, out_dtype, base + j, o[j]);
       }
-    } else if (full) {
-      pw_store4<T>(out, out_dtype, base, o);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (base + j < n) pw_store1<T>(out, out_dtype, base + j, o[j]);
     }
   }
 }
@@ -586,18 +601,25 @@ static PwDiv make_div(unsigned long long d) {
 
 using namespace emmy;
 
+template <typename T, int OPC, bool IO, int POST, bool BC>
+static void launch_simple_gs(const PwSimple &q, void *out, int out_dtype, int64_t n, unsigned gb,
+                             cudaStream_t st, int gs) {
+  if (gs > 1) pointwise_simple_kernel<T, OPC, IO, POST, BC, kPwSimpleGroups><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+  else pointwise_simple_kernel<T, OPC, IO, POST, BC, 1><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+}
+
 template <typename T, int OPC, bool IO>
 static void launch_simple(const PwSimple &q, void *out, int out_dtype, int64_t n, unsigned gb,
-                          cudaStream_t st, bool has_bc) {
+                          cudaStream_t st, bool has_bc, int gs) {
   if (q.post == PW_RELU) {
-    if (has_bc) pointwise_simple_kernel<T, OPC, IO, 2, true><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
-    else pointwise_simple_kernel<T, OPC, IO, 2, false><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+    if (has_bc) launch_simple_gs<T, OPC, IO, 2, true>(q, out, out_dtype, n, gb, st, gs);
+    else launch_simple_gs<T, OPC, IO, 2, false>(q, out, out_dtype, n, gb, st, gs);
   } else if (q.post >= 0) {
-    if (has_bc) pointwise_simple_kernel<T, OPC, IO, 1, true><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
-    else pointwise_simple_kernel<T, OPC, IO, 1, false><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+    if (has_bc) launch_simple_gs<T, OPC, IO, 1, true>(q, out, out_dtype, n, gb, st, gs);
+    else launch_simple_gs<T, OPC, IO, 1, false>(q, out, out_dtype, n, gb, st, gs);
   } else {
-    if (has_bc) pointwise_simple_kernel<T, OPC, IO, 0, true><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
-    else pointwise_simple_kernel<T, OPC, IO, 0, false><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+    if (has_bc) launch_simple_gs<T, OPC, IO, 0, true>(q, out, out_dtype, n, gb, st, gs);
+    else launch_simple_gs<T, OPC, IO, 0, false>(q, out, out_dtype, n, gb, st, gs);
   }
 }
 
@@ -740,14 +762,20 @@ static int pointwise_impl(const void *const *inputs, const int *input_dtypes,
         q.kind[k] = 2; q.imm[k] = immediates[r - n_inputs - n_scalars];
       }
     }
-    int64_t blocks = ((n + 3) / 4 + kPwThreads - 1) / kPwThreads;
+    // two groups per thread unless two or more operands stream from HBM
+    // (measured: 2 groups take a + b[e % M] from 118 to 99 us, unary
+    // activations 5-20% faster; x + y 3% slower)
+    int full_streams = 0;
+    for (int k = 0; k < arity; ++k) full_streams += q.kind[k] == 0;
+    const int gs = full_streams >= 2 ? 1 : kPwSimpleGroups;
+    int64_t blocks = ((n + 3) / 4 + (int64_t)kPwThreads * gs - 1) / ((int64_t)kPwThreads * gs);
     if (blocks > INT32_MAX) blocks = INT32_MAX;
     const unsigned gb = (unsigned)blocks;
     bool f32io = !compute_f64 && out_dtype == EMMY_DT_F32;
     for (int k = 0; k < arity; ++k)
       if (q.kind[k] != 2 && q.dtype[k] != EMMY_DT_F32) f32io = false;
 #define EMMY_PW_LAUNCH(T, OPC, IO) \
-    launch_simple<T, OPC, IO>(q, out, out_dtype, n, gb, st, has_bc)
+    launch_simple<T, OPC, IO>(q, out, out_dtype, n, gb, st, has_bc, gs)
     const bool has_bc = q.kind[0] == 3 || q.kind[1] == 3 || q.kind[2] == 3;
     if (compiled(op)) {                                // f32io holds here
       switch (op) {
