@@ -442,9 +442,11 @@ __device__ __forceinline__ void pw_simple_operand(const PwSimple &q, int k, int6
   }
 }
 
-// OPC >= 0 fixes the op at compile time (the six arithmetic ops) and F32IO
-// fixes every tensor operand and the output to f32: a small kernel that stays
-// at full occupancy.  OPC < 0 dispatches q.op at run time.
+// OPC >= 0 fixes the op at compile time (the six arithmetic ops, the common
+// activations).  IO = 1 fixes every tensor operand and the output to f32, IO =
+// 2 is a one-step program on one contiguous f16 input with an f16 output, IO =
+// 0 reads each operand in its own dtype: a small kernel that stays at full
+// occupancy.  OPC < 0 dispatches q.op at run time.
 // The cheap unary ops a one-step program may be followed by.
 template <typename T> __device__ __forceinline__ T pw_post(int op, T v) {
   switch (op) {
@@ -463,7 +465,7 @@ template <typename T> __device__ __forceinline__ T pw_post(int op, T v) {
 // POST: 0 no unary step after the op, 1 one chosen at run time (q.post),
 // 2 ReLU (the bias + ReLU shape, fixed at compile time); BC: some operand is
 // a broadcast input; GS: 4-element groups per thread.
-template <typename T, int OPC, bool F32IO, int POST, bool BC, int GS>
+template <typename T, int OPC, int IO, int POST, bool BC, int GS>
 __global__ void __launch_bounds__(kPwThreads)
 pointwise_simple_kernel(const PwSimple q, void *out, int out_dtype, int64_t n) {
   // each thread takes GS 4-element groups a grid apart (coalesced), with
@@ -478,7 +480,10 @@ pointwise_simple_kernel(const PwSimple q, void *out, int out_dtype, int64_t n) {
       const int64_t base = (g0 + u * stride) * 4;
       if (base >= n) break;
       const bool full = base + 4 <= n;
-      if (F32IO) {
+      if (IO == 2 && full) {
+        // one-step f16 program on a contiguous input (the only IO == 2 form)
+        pw_load4<T>(q.ptr[0], EMMY_DT_F16, base, a[u]);
+      } else if (IO == 1) {
         pw_simple_operand_f32<T, BC>(q, 0, base, full, n, a[u]);
         if (q.nops > 1) pw_simple_operand_f32<T, BC>(q, 1, base, full, n, b[u]);
         if (q.nops > 2) pw_simple_operand_f32<T, BC>(q, 2, base, full, n, c[u]);
@@ -523,7 +528,7 @@ pointwise_simple_kernel(const PwSimple q, void *out, int out_dtype, int64_t n) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) o[j] = pw_post<T>(q.post, o[j]);
       }
-      if (F32IO) {
+      if (IO == 1) {
         float *dst = static_cast<float *>(out) + base;
         if (full) {
           *reinterpret_cast<float4 *>(dst) =
@@ -534,7 +539,7 @@ pointwise_simple_kernel(const PwSimple q, void *out, int out_dtype, int64_t n) {
             if (base + j < n) dst[j] = float(o[j]);
         }
       } else if (full) {
-        pw_store4<T>(out, out_dtype, base, o);
+        pw_store4<T>(out, IO == 2 ? EMMY_DT_F16 : out_dtype, base, o);
       } else {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
@@ -601,14 +606,14 @@ static PwDiv make_div(unsigned long long d) {
 
 using namespace emmy;
 
-template <typename T, int OPC, bool IO, int POST, bool BC>
+template <typename T, int OPC, int IO, int POST, bool BC>
 static void launch_simple_gs(const PwSimple &q, void *out, int out_dtype, int64_t n, unsigned gb,
                              cudaStream_t st, int gs) {
   if (gs > 1) pointwise_simple_kernel<T, OPC, IO, POST, BC, kPwSimpleGroups><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
   else pointwise_simple_kernel<T, OPC, IO, POST, BC, 1><<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
 }
 
-template <typename T, int OPC, bool IO>
+template <typename T, int OPC, int IO>
 static void launch_simple(const PwSimple &q, void *out, int out_dtype, int64_t n, unsigned gb,
                           cudaStream_t st, bool has_bc, int gs) {
   if (q.post == PW_RELU) {
@@ -738,9 +743,14 @@ static int pointwise_impl(const void *const *inputs, const int *input_dtypes,
     }
     return true;
   };
-  auto compiled = [&](int op) {
-    return (op == PW_GELU_TANH || op == PW_SILU || op == PW_EXP) && all_f32();
+  // ... and, as one step on a contiguous f16 input with an f16 output, with
+  // half loads and stores fixed at compile time
+  auto all_f16_one = [&]() {
+    return !compute_f64 && one && out_dtype == EMMY_DT_F16 && program[2] < n_inputs &&
+           input_dtypes[program[2]] == EMMY_DT_F16 && !p.idx[program[2]].bcast;
   };
+  auto activation = [](int op) { return op == PW_GELU_TANH || op == PW_SILU || op == PW_EXP; };
+  auto compiled = [&](int op) { return activation(op) && (all_f32() || all_f16_one()); };
   if (vec_ok && (one || two) && leaves_only && (cheap(program[0]) || compiled(program[0]))) {
     const int op = program[0];
     const int arity = arity_of(op);
@@ -777,26 +787,41 @@ static int pointwise_impl(const void *const *inputs, const int *input_dtypes,
 #define EMMY_PW_LAUNCH(T, OPC, IO) \
     launch_simple<T, OPC, IO>(q, out, out_dtype, n, gb, st, has_bc, gs)
     const bool has_bc = q.kind[0] == 3 || q.kind[1] == 3 || q.kind[2] == 3;
-    if (compiled(op)) {                                // f32io holds here
+    if (compiled(op) && !f32io) {                      // one f16 step, no post, no broadcast
       switch (op) {
-        case PW_GELU_TANH: EMMY_PW_LAUNCH(float, PW_GELU_TANH, true); break;
-        case PW_SILU: EMMY_PW_LAUNCH(float, PW_SILU, true); break;
-        default: EMMY_PW_LAUNCH(float, PW_EXP, true); break;
+        case PW_GELU_TANH:
+          pointwise_simple_kernel<float, PW_GELU_TANH, 2, 0, false, kPwSimpleGroups>
+              <<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+          break;
+        case PW_SILU:
+          pointwise_simple_kernel<float, PW_SILU, 2, 0, false, kPwSimpleGroups>
+              <<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+          break;
+        default:
+          pointwise_simple_kernel<float, PW_EXP, 2, 0, false, kPwSimpleGroups>
+              <<<gb, kPwThreads, 0, st>>>(q, out, out_dtype, n);
+          break;
+      }
+    } else if (compiled(op)) {                         // f32io holds here
+      switch (op) {
+        case PW_GELU_TANH: EMMY_PW_LAUNCH(float, PW_GELU_TANH, 1); break;
+        case PW_SILU: EMMY_PW_LAUNCH(float, PW_SILU, 1); break;
+        default: EMMY_PW_LAUNCH(float, PW_EXP, 1); break;
       }
     } else if (f32io) {
       switch (op) {
-        case PW_ADD: EMMY_PW_LAUNCH(float, PW_ADD, true); break;
-        case PW_SUB: EMMY_PW_LAUNCH(float, PW_SUB, true); break;
-        case PW_MUL: EMMY_PW_LAUNCH(float, PW_MUL, true); break;
-        case PW_DIV: EMMY_PW_LAUNCH(float, PW_DIV, true); break;
-        case PW_MAX: EMMY_PW_LAUNCH(float, PW_MAX, true); break;
-        case PW_MIN: EMMY_PW_LAUNCH(float, PW_MIN, true); break;
-        default: EMMY_PW_LAUNCH(float, -1, true); break;
+        case PW_ADD: EMMY_PW_LAUNCH(float, PW_ADD, 1); break;
+        case PW_SUB: EMMY_PW_LAUNCH(float, PW_SUB, 1); break;
+        case PW_MUL: EMMY_PW_LAUNCH(float, PW_MUL, 1); break;
+        case PW_DIV: EMMY_PW_LAUNCH(float, PW_DIV, 1); break;
+        case PW_MAX: EMMY_PW_LAUNCH(float, PW_MAX, 1); break;
+        case PW_MIN: EMMY_PW_LAUNCH(float, PW_MIN, 1); break;
+        default: EMMY_PW_LAUNCH(float, -1, 1); break;
       }
     } else if (compute_f64) {
-      EMMY_PW_LAUNCH(double, -1, false);
+      EMMY_PW_LAUNCH(double, -1, 0);
     } else {
-      EMMY_PW_LAUNCH(float, -1, false);
+      EMMY_PW_LAUNCH(float, -1, 0);
     }
 #undef EMMY_PW_LAUNCH
     return check_launch("emmy_pointwise (one step)");
