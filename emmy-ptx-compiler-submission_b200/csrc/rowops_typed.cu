@@ -298,6 +298,62 @@ __global__ void __launch_bounds__(256) cols_kernel(const Args a) {
   }
 }
 
+// f16 softmax over rows of 256 * CH elements, the row held in registers: a
+// warp per row, each lane CH 16-byte pieces (8 halves) at piece lane + 32 k,
+// so the row is read from memory once (the kernel above reads it three
+// times).  Same arithmetic as the kernel above in f32: the max from the
+// reference's -1e30 seed, p = e^(x - max), one correctly rounded 1 / sum,
+// p * (1 / sum) rounded to f16; only the summation order differs.
+template <int CH>
+__global__ void __launch_bounds__(256)
+softmax_f16_resident_kernel(const __half *__restrict__ x, __half *__restrict__ y, int64_t outer) {
+  constexpr int N = 256 * CH;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * 8;
+  for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < outer; row += warps) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(x + row * N);
+    uint4 v[CH];
+#pragma unroll
+    for (int k = 0; k < CH; ++k) v[k] = src[lane + 32 * k];
+    float m = max_seed<float>();
+#pragma unroll
+    for (int k = 0; k < CH; ++k) {
+      const __half2 *h = reinterpret_cast<const __half2 *>(&v[k]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) m = fmaxf(m, fmaxf(__low2float(h[q]), __high2float(h[q])));
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < CH; ++k) {
+      const __half2 *h = reinterpret_cast<const __half2 *>(&v[k]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        s += exp_c(__low2float(h[q]) - m);
+        s += exp_c(__high2float(h[q]) - m);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float r = 1.0f / s;
+    uint4 *dst = reinterpret_cast<uint4 *>(y + row * N);
+#pragma unroll
+    for (int k = 0; k < CH; ++k) {
+      const __half2 *h = reinterpret_cast<const __half2 *>(&v[k]);
+      uint4 w;
+      uint32_t *wq = reinterpret_cast<uint32_t *>(&w);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        __half2 o = __floats2half2_rn(exp_c(__low2float(h[q]) - m) * r,
+                                      exp_c(__high2float(h[q]) - m) * r);
+        wq[q] = *reinterpret_cast<uint32_t *>(&o);
+      }
+      dst[lane + 32 * k] = w;
+    }
+  }
+}
+
 template <typename TC, int MODE>
 void launch(const Args &a, cudaStream_t st) {
   const int sms = sm_count();
@@ -308,6 +364,25 @@ void launch(const Args &a, cudaStream_t st) {
       cols_kernel<TC, MODE><<<(unsigned)blocks, 256, 0, st>>>(a);
     }
     return;
+  }
+  if constexpr (MODE == M_SOFTMAX && sizeof(TC) == 4) {
+    // f16 in and out, rows of 512 .. 4096 elements in steps of 256: the row
+    // in registers
+    const int64_t ch = a.n / 256;
+    if (a.xdt == EMMY_DT_F16 && a.ydt == EMMY_DT_F16 && a.n % 256 == 0 &&
+        (ch == 2 || ch == 4 || ch == 8 || ch == 16) && aligned16(a.x) && aligned16(a.y)) {
+      int64_t blocks = (a.outer + 7) / 8;
+      if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;
+      const __half *xh = static_cast<const __half *>(a.x);
+      __half *yh = static_cast<__half *>(a.y);
+      switch (ch) {
+        case 2: softmax_f16_resident_kernel<2><<<(unsigned)blocks, 256, 0, st>>>(xh, yh, a.outer); break;
+        case 4: softmax_f16_resident_kernel<4><<<(unsigned)blocks, 256, 0, st>>>(xh, yh, a.outer); break;
+        case 8: softmax_f16_resident_kernel<8><<<(unsigned)blocks, 256, 0, st>>>(xh, yh, a.outer); break;
+        default: softmax_f16_resident_kernel<16><<<(unsigned)blocks, 256, 0, st>>>(xh, yh, a.outer); break;
+      }
+      return;
+    }
   }
   // 4 elements per access when every row start is aligned for it
   auto al = [](const void *ptr, int dt) {

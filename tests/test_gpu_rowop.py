@@ -85,7 +85,8 @@ def test_reduce_f64_whole_tensor():
 
 @pytest.mark.parametrize("dt,acc", [("f16", "f16"), ("f16", "f32"), ("f64", "f64")])
 @pytest.mark.parametrize("shape,dim", [([64, 512], -1), ([64, 32], -1), ([2, 4, 64, 3000], -1),
-                                       ([96, 40], 0)])
+                                       ([96, 40], 0), ([300, 4096], -1), ([33, 1024], -1),
+                                       ([5, 2048], -1)])
 def test_softmax(shape, dim, dt, acc):
     kop, meta = synth.retype(*synth.softmax(shape, dim=dim), dt, acc=acc)
     _run(kop, meta, "softmax",
