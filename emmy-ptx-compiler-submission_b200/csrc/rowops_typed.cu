@@ -298,23 +298,32 @@ __global__ void __launch_bounds__(256) cols_kernel(const Args a) {
   }
 }
 
-// f16 softmax over rows of 256 * CH elements, the row held in registers: a
-// warp per row, each lane CH 16-byte pieces (8 halves) at piece lane + 32 k,
-// so the row is read from memory once (the kernel above reads it three
-// times).  Same arithmetic as the kernel above in f32: the max from the
-// reference's -1e30 seed, p = e^(x - max), one correctly rounded 1 / sum,
-// p * (1 / sum) rounded to f16; only the summation order differs.
-template <int CH>
+// f16 softmax over rows of 256 * CH * WPR elements, the row held in
+// registers: WPR warps per row (one, or two for the longest rows, which would
+// otherwise need ~180 registers a thread), each lane CH 16-byte pieces (8
+// halves) at piece lane + 32 k of its warp's part of the row, so the row is
+// read from memory once (the kernel above reads it three times).  Same
+// arithmetic as the kernel above in f32: the max from the reference's -1e30
+// seed, p = e^(x - max), one correctly rounded 1 / sum, p * (1 / sum)
+// rounded to f16; only the summation order differs.
+template <int CH, int WPR>
 __global__ void __launch_bounds__(256)
 softmax_f16_resident_kernel(const __half *__restrict__ x, __half *__restrict__ y, int64_t outer) {
-  constexpr int N = 256 * CH;
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = (int64_t)gridDim.x * 8;
-  for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < outer; row += warps) {
-    const uint4 *src = reinterpret_cast<const uint4 *>(x + row * N);
+  constexpr int N = 256 * CH * WPR, RPB = 8 / WPR;
+  __shared__ float red[2][8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int rib = warp / WPR, part = warp % WPR;      // row in block, part of the row
+  // every thread of the block runs the same number of iterations (the
+  // barriers below), rows past the end doing no memory work.  red[0] and
+  // red[1] are each read between two barriers that every thread passes
+  // before anyone writes the same slot again, so they need no third barrier.
+  for (int64_t r0 = (int64_t)blockIdx.x * RPB; r0 < outer; r0 += (int64_t)gridDim.x * RPB) {
+    const int64_t row = r0 + rib;
+    const bool live = row < outer;
+    const uint4 *src = reinterpret_cast<const uint4 *>(x + row * N) + part * 32 * CH;
     uint4 v[CH];
 #pragma unroll
-    for (int k = 0; k < CH; ++k) v[k] = src[lane + 32 * k];
+    for (int k = 0; k < CH; ++k) v[k] = live ? src[lane + 32 * k] : make_uint4(0, 0, 0, 0);
     float m = max_seed<float>();
 #pragma unroll
     for (int k = 0; k < CH; ++k) {
@@ -324,6 +333,12 @@ softmax_f16_resident_kernel(const __half *__restrict__ x, __half *__restrict__ y
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if constexpr (WPR > 1) {
+      if (lane == 0) red[0][warp] = m;
+      __syncthreads();
+#pragma unroll
+      for (int w = 0; w < WPR; ++w) m = fmaxf(m, red[0][rib * WPR + w]);
+    }
     float s = 0.f;
 #pragma unroll
     for (int k = 0; k < CH; ++k) {
@@ -336,20 +351,29 @@ softmax_f16_resident_kernel(const __half *__restrict__ x, __half *__restrict__ y
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if constexpr (WPR > 1) {
+      if (lane == 0) red[1][warp] = s;
+      __syncthreads();
+      s = 0.f;
+#pragma unroll
+      for (int w = 0; w < WPR; ++w) s += red[1][rib * WPR + w];
+    }
     const float r = 1.0f / s;
-    uint4 *dst = reinterpret_cast<uint4 *>(y + row * N);
+    if (live) {
+      uint4 *dst = reinterpret_cast<uint4 *>(y + row * N) + part * 32 * CH;
 #pragma unroll
-    for (int k = 0; k < CH; ++k) {
-      const __half2 *h = reinterpret_cast<const __half2 *>(&v[k]);
-      uint4 w;
-      uint32_t *wq = reinterpret_cast<uint32_t *>(&w);
+      for (int k = 0; k < CH; ++k) {
+        const __half2 *h = reinterpret_cast<const __half2 *>(&v[k]);
+        uint4 w;
+        uint32_t *wq = reinterpret_cast<uint32_t *>(&w);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        __half2 o = __floats2half2_rn(exp_c(__low2float(h[q]) - m) * r,
-                                      exp_c(__high2float(h[q]) - m) * r);
-        wq[q] = *reinterpret_cast<uint32_t *>(&o);
+        for (int q = 0; q < 4; ++q) {
+          __half2 o = __floats2half2_rn(exp_c(__low2float(h[q]) - m) * r,
+                                        exp_c(__high2float(h[q]) - m) * r);
+          wq[q] = *reinterpret_cast<uint32_t *>(&o);
+        }
+        dst[lane + 32 * k] = w;
       }
-      dst[lane + 32 * k] = w;
     }
   }
 }
@@ -371,15 +395,16 @@ void launch(const Args &a, cudaStream_t st) {
     const int64_t ch = a.n / 256;
     if (a.xdt == EMMY_DT_F16 && a.ydt == EMMY_DT_F16 && a.n % 256 == 0 &&
         (ch == 2 || ch == 4 || ch == 8 || ch == 16) && aligned16(a.x) && aligned16(a.y)) {
-      int64_t blocks = (a.outer + 7) / 8;
+      const int rpb = ch == 16 ? 4 : 8;                 // 4096: two warps per row
+      int64_t blocks = (a.outer + rpb - 1) / rpb;
       if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;
       const __half *xh = static_cast<const __half *>(a.x);
       __half *yh = static_cast<__half *>(a.y);
       switch (ch) {
-        case 2: softmax_f16_resident_kernel<2><<<(unsigned)blocks, 256, 0, st>>>(xh, yh, a.outer); break;
-        case 4: softmax_f16_resident_kernel<4><<<(unsigned)blocks, 256, 0, st>>>(xh, yh, a.outer); break;
-        case 8: softmax_f16_resident_kernel<8><<<(unsigned)blocks, 256, 0, st>>>(xh, yh, a.outer); break;
-        default: softmax_f16_resident_kernel<16><<<(unsigned)blocks, 256, 0, st>>>(xh, yh, a.outer); break;
+        case 2: softmax_f16_resident_kernel<2, 1><<<(unsigned)blocks, 256, 0, st>>>(xh, yh, a.outer); break;
+        case 4: softmax_f16_resident_kernel<4, 1><<<(unsigned)blocks, 256, 0, st>>>(xh, yh, a.outer); break;
+        case 8: softmax_f16_resident_kernel<8, 1><<<(unsigned)blocks, 256, 0, st>>>(xh, yh, a.outer); break;
+        default: softmax_f16_resident_kernel<8, 2><<<(unsigned)blocks, 256, 0, st>>>(xh, yh, a.outer); break;
       }
       return;
     }
