@@ -298,79 +298,171 @@ __global__ void __launch_bounds__(256) cols_kernel(const Args a) {
   }
 }
 
-// f16 softmax over rows of 256 * CH * WPR elements, the row held in
-// registers: WPR warps per row (one, or two for the longest rows, which would
-// otherwise need ~180 registers a thread), each lane CH 16-byte pieces (8
-// halves) at piece lane + 32 k of its warp's part of the row, so the row is
-// read from memory once (the kernel above reads it three times).  Same
-// arithmetic as the kernel above in f32: the max from the reference's -1e30
-// seed, p = e^(x - max), one correctly rounded 1 / sum, p * (1 / sum)
-// rounded to f16; only the summation order differs.
-template <int CH, int WPR>
-__global__ void __launch_bounds__(256)
-softmax_f16_resident_kernel(const __half *__restrict__ x, __half *__restrict__ y, int64_t outer) {
+// f16 rows of 256 * CH * WPR elements held in registers, for softmax and
+// rms / layer normalisation: WPR warps per row (one, or two for the longest
+// rows, which would otherwise need ~180 registers a thread), each lane CH
+// 16-byte pieces (8 halves) at piece lane + 32 k of its warp's part of the
+// row, so the row is read from memory once (the kernel above reads it two or
+// three times).  Same arithmetic as the kernel above in f32 (softmax: the max
+// from the reference's -1e30 seed, e^(x - max), one correctly rounded
+// 1 / sum; rms: 1 / sqrt(eps + sum(x^2) / n); layer norm: the mean, then
+// the centred variance; weight and bias in their own dtype), rounded once to
+// f16 at the store; only the summation order differs.
+template <int MODE, int CH, int WPR>
+__global__ void __launch_bounds__(256) rows_f16_resident_kernel(const Args a) {
   constexpr int N = 256 * CH * WPR, RPB = 8 / WPR;
   __shared__ float red[2][8];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int rib = warp / WPR, part = warp % WPR;      // row in block, part of the row
+  const __half *x = static_cast<const __half *>(a.x);
+  __half *y = static_cast<__half *>(a.y);
+  float eps = 0.f, inv_count;
+  if (a.eps) eps = ld<float>(a.eps, a.cdt, 0);
+  if (a.count) inv_count = 1.0f / ld<float>(a.count, a.cdt, 0);
+  else inv_count = 1.0f / float(N);
+  int rcount = 0;                                     // reductions so far: exchange slot parity
+  // a row's max or sum over its WPR warps, the same value in each.  Slots
+  // alternate, so a slot is rewritten only after a barrier that every thread
+  // passes once it has read the slot's previous value.
+  auto allreduce = [&](float v, bool is_max) -> float {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const float w = __shfl_xor_sync(0xffffffffu, v, o);
+      v = is_max ? fmaxf(v, w) : v + w;
+    }
+    if constexpr (WPR > 1) {
+      const int slot = rcount & 1;
+      if (lane == 0) red[slot][warp] = v;
+      __syncthreads();
+      v = red[slot][rib * WPR];
+#pragma unroll
+      for (int w = 1; w < WPR; ++w)
+        v = is_max ? fmaxf(v, red[slot][rib * WPR + w]) : v + red[slot][rib * WPR + w];
+    }
+    ++rcount;
+    return v;
+  };
   // every thread of the block runs the same number of iterations (the
-  // barriers below), rows past the end doing no memory work.  red[0] and
-  // red[1] are each read between two barriers that every thread passes
-  // before anyone writes the same slot again, so they need no third barrier.
-  for (int64_t r0 = (int64_t)blockIdx.x * RPB; r0 < outer; r0 += (int64_t)gridDim.x * RPB) {
+  // barriers in allreduce), rows past the end doing no memory work
+  for (int64_t r0 = (int64_t)blockIdx.x * RPB; r0 < a.outer; r0 += (int64_t)gridDim.x * RPB) {
     const int64_t row = r0 + rib;
-    const bool live = row < outer;
-    const uint4 *src = reinterpret_cast<const uint4 *>(x + row * N) + part * 32 * CH;
+    const bool live = row < a.outer;
+    const int64_t piece0 = (int64_t)part * 32 * CH;   // this warp's first 8-element piece
+    const uint4 *src = reinterpret_cast<const uint4 *>(x + row * N) + piece0;
     uint4 v[CH];
 #pragma unroll
     for (int k = 0; k < CH; ++k) v[k] = live ? src[lane + 32 * k] : make_uint4(0, 0, 0, 0);
-    float m = max_seed<float>();
-#pragma unroll
-    for (int k = 0; k < CH; ++k) {
-      const __half2 *h = reinterpret_cast<const __half2 *>(&v[k]);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) m = fmaxf(m, fmaxf(__low2float(h[q]), __high2float(h[q])));
-    }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if constexpr (WPR > 1) {
-      if (lane == 0) red[0][warp] = m;
-      __syncthreads();
-#pragma unroll
-      for (int w = 0; w < WPR; ++w) m = fmaxf(m, red[0][rib * WPR + w]);
-    }
-    float s = 0.f;
-#pragma unroll
-    for (int k = 0; k < CH; ++k) {
-      const __half2 *h = reinterpret_cast<const __half2 *>(&v[k]);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        s += exp_c(__low2float(h[q]) - m);
-        s += exp_c(__high2float(h[q]) - m);
-      }
-    }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if constexpr (WPR > 1) {
-      if (lane == 0) red[1][warp] = s;
-      __syncthreads();
-      s = 0.f;
-#pragma unroll
-      for (int w = 0; w < WPR; ++w) s += red[1][rib * WPR + w];
-    }
-    const float r = 1.0f / s;
-    if (live) {
-      uint4 *dst = reinterpret_cast<uint4 *>(y + row * N) + part * 32 * CH;
+    float sc = 1.f, sh = 0.f;                         // y = x * sc - sh, before weight and bias
+    if constexpr (MODE == M_SOFTMAX) {
+      float m = max_seed<float>();
 #pragma unroll
       for (int k = 0; k < CH; ++k) {
         const __half2 *h = reinterpret_cast<const __half2 *>(&v[k]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) m = fmaxf(m, fmaxf(__low2float(h[q]), __high2float(h[q])));
+      }
+      m = allreduce(m, true);
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < CH; ++k) {
+        const __half2 *h = reinterpret_cast<const __half2 *>(&v[k]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          s += exp_c(__low2float(h[q]) - m);
+          s += exp_c(__high2float(h[q]) - m);
+        }
+      }
+      s = allreduce(s, false);
+      sc = 1.0f / s;
+      sh = m;                                         // softmax: e^(x - sh) * sc
+    } else if constexpr (MODE == M_RMS) {
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < CH; ++k) {
+        const __half2 *h = reinterpret_cast<const __half2 *>(&v[k]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float lo = __low2float(h[q]), hi = __high2float(h[q]);
+          s = fmaf(lo, lo, s);
+          s = fmaf(hi, hi, s);
+        }
+      }
+      s = allreduce(s, false);
+      sc = 1.0f / sqrtf(eps + s * inv_count);
+    } else {                                          // M_LN
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < CH; ++k) {
+        const __half2 *h = reinterpret_cast<const __half2 *>(&v[k]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          s += __low2float(h[q]);
+          s += __high2float(h[q]);
+        }
+      }
+      s = allreduce(s, false);
+      const float mean = s * inv_count;
+      float qv = 0.f;
+#pragma unroll
+      for (int k = 0; k < CH; ++k) {
+        const __half2 *h = reinterpret_cast<const __half2 *>(&v[k]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float d0 = __low2float(h[q]) - mean, d1 = __high2float(h[q]) - mean;
+          qv = fmaf(d0, d0, qv);
+          qv = fmaf(d1, d1, qv);
+        }
+      }
+      qv = allreduce(qv, false);
+      sc = 1.0f / sqrtf(qv * inv_count + eps);
+      sh = mean;                                      // layer norm: (x - sh) * sc
+    }
+    if (live) {
+      uint4 *dst = reinterpret_cast<uint4 *>(y + row * N) + piece0;
+#pragma unroll
+      for (int k = 0; k < CH; ++k) {
+        const __half2 *h = reinterpret_cast<const __half2 *>(&v[k]);
+        float o[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float lo = __low2float(h[q]), hi = __high2float(h[q]);
+          if constexpr (MODE == M_SOFTMAX) {
+            o[2 * q] = exp_c(lo - sh) * sc;
+            o[2 * q + 1] = exp_c(hi - sh) * sc;
+          } else if constexpr (MODE == M_RMS) {
+            o[2 * q] = lo * sc;
+            o[2 * q + 1] = hi * sc;
+          } else {
+            o[2 * q] = (lo - sh) * sc;
+            o[2 * q + 1] = (hi - sh) * sc;
+          }
+        }
+        if constexpr (MODE != M_SOFTMAX) {
+          const int64_t e = (piece0 + lane + 32 * k) * 8;   // element index in the row
+          float u[4];
+          if (a.w) {
+            ldv<float, 4>(a.w, a.wdt, e, u);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[j] *= u[j];
+            ldv<float, 4>(a.w, a.wdt, e + 4, u);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[4 + j] *= u[j];
+          }
+          if (MODE == M_LN && a.b) {
+            ldv<float, 4>(a.b, a.wdt, e, u);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[j] += u[j];
+            ldv<float, 4>(a.b, a.wdt, e + 4, u);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[4 + j] += u[j];
+          }
+        }
         uint4 w;
         uint32_t *wq = reinterpret_cast<uint32_t *>(&w);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          __half2 o = __floats2half2_rn(exp_c(__low2float(h[q]) - m) * r,
-                                        exp_c(__high2float(h[q]) - m) * r);
-          wq[q] = *reinterpret_cast<uint32_t *>(&o);
+          __half2 hh = __floats2half2_rn(o[2 * q], o[2 * q + 1]);
+          wq[q] = *reinterpret_cast<uint32_t *>(&hh);
         }
         dst[lane + 32 * k] = w;
       }
@@ -389,22 +481,31 @@ void launch(const Args &a, cudaStream_t st) {
     }
     return;
   }
-  if constexpr (MODE == M_SOFTMAX && sizeof(TC) == 4) {
-    // f16 in and out, rows of 512 .. 4096 elements in steps of 256: the row
-    // in registers
+  if constexpr ((MODE == M_SOFTMAX || MODE == M_RMS || MODE == M_LN) && sizeof(TC) == 4) {
+    // f16 in and out, rows of 512, 1024, 2048 (and 4096 for softmax)
+    // elements: the row in registers (weight and bias, when present, aligned
+    // for 4-element loads)
     const int64_t ch = a.n / 256;
-    if (a.xdt == EMMY_DT_F16 && a.ydt == EMMY_DT_F16 && a.n % 256 == 0 &&
-        (ch == 2 || ch == 4 || ch == 8 || ch == 16) && aligned16(a.x) && aligned16(a.y)) {
+    auto wal = [&](const void *ptr) {
+      const uintptr_t need = a.wdt == EMMY_DT_F16 ? 8 : (a.wdt == EMMY_DT_F64 ? 32 : 16);
+      return ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) % need) == 0;
+    };
+    // (the norms' two-warp 4096 form needs 200+ registers and ran slower than
+    // the general kernel: norms up to 2048)
+    const bool ch_ok = ch == 2 || ch == 4 || ch == 8 || (ch == 16 && MODE == M_SOFTMAX);
+    if (a.xdt == EMMY_DT_F16 && a.ydt == EMMY_DT_F16 && a.n % 256 == 0 && ch_ok &&
+        aligned16(a.x) && aligned16(a.y) && wal(a.w) && wal(a.b)) {
       const int rpb = ch == 16 ? 4 : 8;                 // 4096: two warps per row
       int64_t blocks = (a.outer + rpb - 1) / rpb;
       if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;
-      const __half *xh = static_cast<const __half *>(a.x);
-      __half *yh = static_cast<__half *>(a.y);
       switch (ch) {
-        case 2: softmax_f16_resident_kernel<2, 1><<<(unsigned)blocks, 256, 0, st>>>(xh, yh, a.outer); break;
-        case 4: softmax_f16_resident_kernel<4, 1><<<(unsigned)blocks, 256, 0, st>>>(xh, yh, a.outer); break;
-        case 8: softmax_f16_resident_kernel<8, 1><<<(unsigned)blocks, 256, 0, st>>>(xh, yh, a.outer); break;
-        default: softmax_f16_resident_kernel<8, 2><<<(unsigned)blocks, 256, 0, st>>>(xh, yh, a.outer); break;
+        case 2: rows_f16_resident_kernel<MODE, 2, 1><<<(unsigned)blocks, 256, 0, st>>>(a); break;
+        case 4: rows_f16_resident_kernel<MODE, 4, 1><<<(unsigned)blocks, 256, 0, st>>>(a); break;
+        case 8: rows_f16_resident_kernel<MODE, 8, 1><<<(unsigned)blocks, 256, 0, st>>>(a); break;
+        default:
+          if constexpr (MODE == M_SOFTMAX)
+            rows_f16_resident_kernel<MODE, 8, 2><<<(unsigned)blocks, 256, 0, st>>>(a);
+          break;
       }
       return;
     }

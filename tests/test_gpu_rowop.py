@@ -94,7 +94,7 @@ def test_softmax(shape, dim, dt, acc):
 
 
 @pytest.mark.parametrize("dt,acc", [("f16", "f16"), ("f16", "f32"), ("f64", "f64")])
-@pytest.mark.parametrize("rows,cols", [(64, 512), (100, 4096), (7, 96)])
+@pytest.mark.parametrize("rows,cols", [(64, 512), (100, 4096), (7, 96), (33, 1024), (17, 2048)])
 def test_layernorm(rows, cols, dt, acc):
     kop, meta = synth.retype(*synth.layernorm(rows, cols), dt, acc=acc)
 
@@ -111,6 +111,14 @@ def test_rmsnorm_and_l2(dt, acc):
                                                 1e-5, out_dtype=np.float64))
     kop, meta = synth.retype(*synth.l2norm(64, 256), dt, acc=acc)
     _run(kop, meta, "norm", lambda x: F.l2norm(x["x"].astype(np.float64), out_dtype=np.float64))
+
+
+@pytest.mark.parametrize("cols", [1024, 2048, 4096])
+def test_rmsnorm_f16_wide_rows(cols):
+    """f16 rows held in registers: one warp per row up to 2048, two at 4096."""
+    kop, meta = synth.retype(*synth.rmsnorm(37, cols, eps=1e-5), "f16", acc="f32")
+    _run(kop, meta, "norm", lambda x: F.rmsnorm(x["x"].astype(np.float64), x["w"].astype(np.float64),
+                                                1e-5, out_dtype=np.float64))
 
 
 @pytest.mark.parametrize("dt", ["f16", "f64"])
