@@ -47,33 +47,49 @@
 
 namespace emmy {
 
-template <int D>
+// WIDE (D = 256): 128-key blocks (score products at N = 128, the tensor
+// core's full rate; N = 64 runs at 57% of it) and two softmax warps per TMEM
+// lane quadrant, each taking 64 of a row's 128 scores; the two halves exchange
+// their block max through shared memory and add their sums at the end.  At
+// D = 256 one CTA fills an SM's tensor memory either way.  Otherwise 64-key
+// blocks, one softmax warp per quadrant, two CTAs per SM up to D = 128 (where
+// 128-key blocks would cost the second CTA: measured slower).
+template <int D, bool WIDE>
 struct AttnCfg {
-  static constexpr int BN = 64;                      // keys per block
+  static constexpr int BN = WIDE ? 128 : 64;         // keys per block
+  static constexpr int HALVES = WIDE ? 2 : 1;        // softmax warps per lane quadrant
+  static constexpr int SM_WARPS = 4 * HALVES;        // softmax warps
   static constexpr int NKB = D / 64;                 // 64-wide head-dim blocks of Q and K
   static constexpr int Q_BOX = 128 * 128;            // [128 rows][128 B]
   static constexpr int K_BOX = BN * 128;             // [BN keys][128 B]
   static constexpr int Q_BYTES = NKB * Q_BOX;
   static constexpr int SLOT_BYTES = NKB * K_BOX;     // one K or V block
-  static constexpr int SLOTS = 3;
-  static constexpr int STAGE_BYTES = 4 * 4096;       // one 32-row x 128-byte box per softmax warp
-  // Q | ring slots | epilogue staging, then the mbarriers
+  static constexpr int SLOTS = WIDE ? 2 : 3;
+  // epilogue staging: one STAGE_ROWS-row x 128-byte box per softmax warp
+  static constexpr int STAGE_ROWS = WIDE ? 16 : 32;
+  static constexpr int STAGE_BYTES = SM_WARPS * STAGE_ROWS * 128;
+  // Q | ring slots | epilogue staging | half-row exchange, then the mbarriers
   static constexpr int STAGE_OFF = Q_BYTES + SLOTS * SLOT_BYTES;
-  static constexpr int BAR_OFF = STAGE_OFF + STAGE_BYTES;
+  static constexpr int XCH_OFF = STAGE_OFF + STAGE_BYTES;
+  static constexpr int XCH_BYTES = WIDE ? 3 * 2 * 128 * 4 : 0;   // max [2][2][128], sum [2][128]
+  static constexpr int BAR_OFF = XCH_OFF + XCH_BYTES;
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
-  static constexpr uint32_t S_COL0 = 0;              // score buffers at columns 0 and 64
+  static constexpr uint32_t S_COL0 = 0;              // score buffers at columns 0 and BN
   static constexpr uint32_t O_COL = 2 * BN;
   static constexpr uint32_t TMEM_COLS = O_COL + D <= 256 ? 256 : 512;
-  static constexpr int THREADS = 192;
-  static constexpr int MIN_BLOCKS = D <= 128 ? 2 : 1;   // two CTAs per SM
+  static constexpr int PRODUCER_WARP = SM_WARPS, MMA_WARP = SM_WARPS + 1;
+  static constexpr int THREADS = 32 * (SM_WARPS + 2);
+  static constexpr int MIN_BLOCKS = (!WIDE && D <= 128) ? 2 : 1;
   static constexpr float RESCALE_LOG2 = 8.0f;        // lazy max threshold (P <= 2^8)
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(O_COL + D <= 512, "tensor memory");
 };
 
 // status codes of the waits that can give up (first one recorded wins)
 constexpr int kAttnWaitQ = 0x1201, kAttnWaitSlot = 0x1202, kAttnWaitP = 0x1203,
               kAttnWaitEmpty = 0x1204, kAttnWaitS = 0x1205, kAttnWaitO = 0x1206,
               kAttnWaitOFinal = 0x1207, kAttnWaitDrain = 0x1208, kAttnWaitMma = 0x1209,
-              kAttnWaitOFree = 0x120b;
+              kAttnWaitOFree = 0x120b, kAttnWaitHalf = 0x120c;
 
 // D[tmem] (+)= A[tmem] x B[smem desc]: A is M x 16 f16, row m in TMEM lane m,
 // two consecutive k packed per 32-bit column (8 columns per MMA).
@@ -93,15 +109,15 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-template <int D>
-__global__ void __launch_bounds__(192, AttnCfg<D>::MIN_BLOCKS)
+template <int D, bool WIDE>
+__global__ void __launch_bounds__(AttnCfg<D, WIDE>::THREADS, AttnCfg<D, WIDE>::MIN_BLOCKS)
 attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV,
                         const __grid_constant__ CUtensorMap tmO,
                         const float *__restrict__ scale_div, int S, int ntiles, int out_f16,
                         int *status) {
-  using C = AttnCfg<D>;
+  using C = AttnCfg<D, WIDE>;
   constexpr int BN = C::BN;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(
@@ -116,7 +132,9 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
   uint64_t *o_full = bars + 4, *mma_done = bars + 5;
   uint64_t *s_full = bars + 6, *p_full = bars + 8;   // [2] each
   uint64_t *full = bars + 10, *empty = bars + 10 + C::SLOTS;   // [SLOTS] each
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 10 + 2 * C::SLOTS);
+  // WIDE: half-row exchange, per lane quadrant: block max [g % 2], tile sum
+  uint64_t *xmax = bars + 10 + 2 * C::SLOTS, *xsum = xmax + 8;   // [4][2], [4]
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 10 + 2 * C::SLOTS + 12);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nblk = (S + BN - 1) / BN;
@@ -131,26 +149,30 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     prefetch_tensormap(&tmO);
     mbar_init(q_full, 1);
     mbar_init(o_done, 1);
-    mbar_init(o_free, 128);
+    mbar_init(o_free, 32 * C::SM_WARPS);
     mbar_init(o_full, 1);
     mbar_init(mma_done, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], 128);
+      mbar_init(&p_full[b], 32 * C::SM_WARPS);
     }
     for (int s = 0; s < C::SLOTS; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
+    if (WIDE) {
+      for (int x = 0; x < 8; ++x) mbar_init(&xmax[x], 64);   // the two warps of a quadrant
+      for (int x = 0; x < 4; ++x) mbar_init(&xsum[x], 64);
+    }
     fence_barrier_init();
   }
-  if (warp == 4) tmem_alloc(tmem_holder, C::TMEM_COLS);
+  if (warp == C::PRODUCER_WARP) tmem_alloc(tmem_holder, C::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  if (warp == 4) {
+  if (warp == C::PRODUCER_WARP) {
     if (lane == 0) {
       // TMA producer: ring item i goes to slot i % SLOTS once item i - SLOTS
       // has been consumed.  Per tile: K0, then per block j: K[j+1] (if any), V[j].
@@ -190,7 +212,7 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         mbar_wait(&full[i % C::SLOTS], (i / C::SLOTS) & 1, status, kAttnWaitDrain);
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == C::MMA_WARP) {
     if (lane == 0) {
       constexpr uint32_t idesc_s = f16_idesc(128, BN, false, false);
       constexpr uint32_t idesc_o = f16_idesc(128, D, false, true);
@@ -245,11 +267,13 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
           if (j == 0 && i > 0 && !(ok = mbar_wait(o_free, (i - 1) & 1, status, kAttnWaitOFree)))
             break;
           tc_fence_after();
-          // O += P V: P from TMEM (16 keys = 8 columns per MMA), V N-major
-          // (value columns contiguous)
+          // O += P V: P from TMEM (16 keys = 8 columns per MMA; each 64-key
+          // half of a block packed into the first 32 of its 64 score columns),
+          // V N-major (value columns contiguous)
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_f16_tmem_a(tmem + C::O_COL, tmem + C::S_COL0 + (g & 1) * BN + kk * 8,
+          for (int kk = 0; kk < BN / 16; ++kk)
+            mma_f16_tmem_a(tmem + C::O_COL,
+                           tmem + C::S_COL0 + (g & 1) * BN + (kk >> 2) * 64 + (kk & 3) * 8,
                            sw128_desc(va + kk * 16 * 128, C::K_BOX, 1024), idesc_o,
                            (j | kk) != 0 ? 1u : 0u);
           mma_commit(o_full);
@@ -263,11 +287,17 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     }
     __syncwarp();
   } else {
-    // softmax / epilogue: thread t owns query row m0 + t (TMEM lane t).
-    // Scores are kept as t = s * scale * log2(e), so p = 2^(t - m).
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    // softmax / epilogue.  Warp w reads TMEM lane quadrant w % 4: its thread
+    // owns query row m0 + r, r = 32 * (w % 4) + lane, and of each block's
+    // scores the 64 columns of half w / 4 (WIDE) or all 64.  Scores are kept
+    // as t = s * scale * log2(e), so p = 2^(t - m).
+    const int quad = warp & 3, half = warp >> 2;
+    const int r = quad * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const float c = (scale_div ? 1.0f / __ldg(scale_div) : 1.0f) * 1.4426950408889634f;
-    unsigned char *stage = smem + C::STAGE_OFF + warp * 4096;   // this warp's 4 KB box
+    unsigned char *stage = smem + C::STAGE_OFF + warp * (C::STAGE_ROWS * 128);   // this warp's box
+    float *xch = reinterpret_cast<float *>(smem + C::XCH_OFF);   // WIDE only
+    constexpr int OCOLS = D / C::HALVES;                 // O columns this warp rescales / writes
     bool ok = true;
     int g = 0, qloads = 0;
     for (int i = 0; ok && i < my_tiles; ++i) {
@@ -289,13 +319,14 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
             tma_load_3d(sQ + kb * C::Q_BOX, &tmQ, q_full, kb * 64, m0n, bhn);
           ++qloads;
         }
-        const int key0 = j * BN;
+        const int key0 = j * BN + half * 64;
+        const uint32_t scol = C::S_COL0 + (g & 1) * BN + half * 64;   // this half's columns
         // raw scores v; t = v * c is folded into one FFMA below.  With c > 0 the
         // row max of t is c * max(v), with c < 0 it is c * min(v); masked keys
         // get the value whose t is -inf.
         float v[64];
-        tmem_ld64(lane_base + C::S_COL0 + (g & 1) * BN, v);
-        if (key0 + BN > S) {
+        tmem_ld64(lane_base + scol, v);
+        if (key0 + 64 > S) {
           const float far = c > 0.f ? -INFINITY : INFINITY;
 #pragma unroll
           for (int k = 0; k < 64; ++k)
@@ -319,7 +350,21 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
 #pragma unroll
             for (int q = 0; q < w; ++q) ext[q] = fminf(ext[q], ext[q + w]);
         }
-        const float mb = ext[0] * c;
+        float mb = ext[0] * c;
+        if constexpr (WIDE) {
+          // the row's max over both halves: each half posts its own, the
+          // quadrant's barrier for this block parity completes with both.  A
+          // thread posts block g + 2 only after it has seen block g + 1, for
+          // which its partner must have read block g, so one slot per parity
+          // suffices and the barrier is never two phases ahead of a waiter.
+          float *slot = xch + (g & 1) * 256;
+          slot[half * 128 + r] = mb;
+          mbar_arrive(&xmax[quad * 2 + (g & 1)]);
+          ok = __all_sync(0xffffffffu, mbar_wait(&xmax[quad * 2 + (g & 1)], (g >> 1) & 1, status,
+                                                 kAttnWaitHalf));
+          if (!ok) break;
+          mb = fmaxf(mb, slot[(half ^ 1) * 128 + r]);
+        }
         // lazy max: move only when the block's max is more than 2^8 above it
         const bool move = mb > m + C::RESCALE_LOG2;
         const float m_use = move ? mb : m;
@@ -346,24 +391,32 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
           if (!ok) break;
           tc_fence_after();
 #pragma unroll 1
-          for (int cc = 0; cc < D / 32; ++cc) {
+          for (int cc = 0; cc < OCOLS / 32; ++cc) {
             float ov[32];
             __syncwarp();
-            tmem_ld32(lane_base + C::O_COL + cc * 32, ov);
+            tmem_ld32(lane_base + C::O_COL + half * OCOLS + cc * 32, ov);
 #pragma unroll
             for (int k = 0; k < 32; ++k) ov[k] *= alpha;
-            tmem_st32(lane_base + C::O_COL + cc * 32, ov);
+            tmem_st32(lane_base + C::O_COL + half * OCOLS + cc * 32, ov);
           }
         }
-        // P over the first 32 columns of this block's score buffer (already read)
-        tmem_st32_u(lane_base + C::S_COL0 + (g & 1) * BN, h);
-        l = l * alpha + ps;
+        // P over the first 32 of this half's score columns (already read)
+        tmem_st32_u(lane_base + scol, h);
+        l = l * alpha + ps;                // this half's share of the row sum
         m = m_use;
         tc_fence_before();
         mbar_arrive(&p_full[g & 1]);
       }
       if (!ok) break;
-      // epilogue: O / l, staged through this warp's 4 KB box in 32-row x
+      if constexpr (WIDE) {
+        // the row sum: this half's share plus the partner's (one phase per tile)
+        xch[512 + half * 128 + r] = l;
+        mbar_arrive(&xsum[quad]);
+        ok = __all_sync(0xffffffffu, mbar_wait(&xsum[quad], i & 1, status, kAttnWaitHalf));
+        if (!ok) break;
+        l += xch[512 + (half ^ 1) * 128 + r];
+      }
+      // epilogue: O / l, staged through this warp's box in STAGE_ROWS-row x
       // 128-byte swizzled pieces and written by TMA stores; rows beyond S are
       // dropped by the TMA.  Once O has been read out of TMEM, o_free lets the
       // next tile's first P V product start.
@@ -373,7 +426,7 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       const float rl = 1.0f / l;
       const int step = out_f16 ? 64 : 32;               // columns per 128-byte row piece
 #pragma unroll 1
-      for (int c0 = 0; c0 < D; c0 += step) {
+      for (int c0 = half * OCOLS; c0 < (half + 1) * OCOLS; c0 += step) {
         uint4 w[8];
         if (out_f16) {
           float v[64];
@@ -396,21 +449,28 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
             w[q] = make_uint4(__float_as_uint(v[4 * q] * rl), __float_as_uint(v[4 * q + 1] * rl),
                               __float_as_uint(v[4 * q + 2] * rl), __float_as_uint(v[4 * q + 3] * rl));
         }
-        if (c0 + step >= D) {
+        if (c0 + step >= (half + 1) * OCOLS) {
           tc_fence_before();
           mbar_arrive(o_free);                          // O fully read out of TMEM
         }
-        // the box is free once the previous TMA store has read it
-        if (lane == 0) bulk_wait_group_read<0>();
-        __syncwarp();
+        // the warp's 32 rows in 32 / STAGE_ROWS boxes; the box is free once
+        // the previous TMA store has read it
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
-          *reinterpret_cast<uint4 *>(stage + lane * 128 + ((q ^ (lane & 7)) * 16)) = w[q];
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_3d(&tmO, stage, c0, m0 + warp * 32, bh);
-          bulk_commit_group();
+        for (int hb = 0; hb < 32 / C::STAGE_ROWS; ++hb) {
+          if (lane == 0) bulk_wait_group_read<0>();
+          __syncwarp();
+          const int row = lane - hb * C::STAGE_ROWS;
+          if (row >= 0 && row < C::STAGE_ROWS) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              *reinterpret_cast<uint4 *>(stage + row * 128 + ((q ^ (row & 7)) * 16)) = w[q];
+          }
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tmO, stage, c0, m0 + quad * 32 + hb * C::STAGE_ROWS, bh);
+            bulk_commit_group();
+          }
         }
       }
     }
@@ -421,7 +481,7 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) tmem_dealloc(tmem, C::TMEM_COLS);
+  if (warp == C::PRODUCER_WARP) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
 // CUDA-core fallback (any head dim, pre-transposed k, S beyond one block of
@@ -481,11 +541,11 @@ attention_f16_simt_kernel(const __half *__restrict__ q, const __half *__restrict
 
 namespace {
 
-template <int D>
+template <int D, bool WIDE>
 int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
                         const float *scale_div, int64_t batch, int64_t S, int out_f16,
                         cudaStream_t st) {
-  using Cfg = AttnCfg<D>;
+  using Cfg = AttnCfg<D, WIDE>;
   CUtensorMap tq, tk, tv;
   const uint64_t dims[3] = {(uint64_t)D, (uint64_t)S, (uint64_t)batch};
   const uint64_t str[2] = {(uint64_t)D * 2, (uint64_t)S * D * 2};
@@ -497,11 +557,11 @@ int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   if (!rc) rc = make_tensor_map(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, v, dims, str, kbox,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
-  // O written by TMA stores of 32-row x 128-byte boxes
+  // O written by TMA stores of STAGE_ROWS-row x 128-byte boxes
   CUtensorMap to;
   const uint64_t esize = out_f16 ? 2 : 4;
   const uint64_t ostr[2] = {(uint64_t)D * esize, (uint64_t)S * D * esize};
-  const uint32_t obox[3] = {(uint32_t)(128 / esize), 32, 1};
+  const uint32_t obox[3] = {(uint32_t)(128 / esize), (uint32_t)Cfg::STAGE_ROWS, 1};
   if (!rc) rc = make_tensor_map(&to, out_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                                 3, o, dims, ostr, obox, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -510,8 +570,8 @@ int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaFuncSetAttribute(attention_f16_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         Cfg::SMEM);
+    cudaFuncSetAttribute(attention_f16_tc_kernel<D, WIDE>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     attr_set[dev] = true;
   }
   // persistent CTAs: as many as are resident at once, each walking its tiles
@@ -519,7 +579,7 @@ int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
   if (ntiles > INT32_MAX) return set_error(EMMY_ERR_INVALID, "emmy_attention_f16: too many query tiles");
   const int64_t slots = (int64_t)Cfg::MIN_BLOCKS * sm_count();
   const unsigned grid = (unsigned)(ntiles < slots ? ntiles : slots);
-  attention_f16_tc_kernel<D><<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(
+  attention_f16_tc_kernel<D, WIDE><<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(
       tq, tk, tv, to, scale_div, (int)S, (int)ntiles, out_f16, device_status_ptr());
   return check_launch("emmy_attention_f16 (tcgen05)");
 }
@@ -548,9 +608,14 @@ extern "C" int emmy_attention_f16(const void *q, const void *k, const void *v, v
   const bool tc = !k_transposed && sq == sk && aligned16(q) && aligned16(k) && aligned16(v) &&
                   aligned16(o) && (d == 64 || d == 128 || d == 256);
   if (tc) {
-    if (d == 64) return launch_attention_tc<64>(q, k, v, o, scale_div, batch, sq, out_f16, st);
-    if (d == 128) return launch_attention_tc<128>(q, k, v, o, scale_div, batch, sq, out_f16, st);
-    return launch_attention_tc<256>(q, k, v, o, scale_div, batch, sq, out_f16, st);
+    // D = 256: 128-key blocks once there is more than one 64-key block
+    if (d == 64)
+      return launch_attention_tc<64, false>(q, k, v, o, scale_div, batch, sq, out_f16, st);
+    if (d == 128)
+      return launch_attention_tc<128, false>(q, k, v, o, scale_div, batch, sq, out_f16, st);
+    if (sq > 64)
+      return launch_attention_tc<256, true>(q, k, v, o, scale_div, batch, sq, out_f16, st);
+    return launch_attention_tc<256, false>(q, k, v, o, scale_div, batch, sq, out_f16, st);
   }
   // head dims up to 96: one thread per query row (any key count)
   const int rc = launch_attention_rows(q, k, v, o, scale_div, batch, sq, sk, d, d, 1, out_f16,

@@ -69,6 +69,8 @@ F16_CASES = [
     ("ragged_S129_D128", dict(B=1, H=3, S=129, D=128, out_dtype="f32")),
     ("ragged_S65_D128", dict(B=2, H=2, S=65, D=128, out_dtype="f16")),
     ("ragged_S200_D128_x600", dict(B=3, H=100, S=200, D=128, out_dtype="f16")),
+    ("ragged_S200_D256", dict(B=1, H=3, S=200, D=256, out_dtype="f32")),
+    ("ragged_S130_D256_x300", dict(B=3, H=50, S=130, D=256, out_dtype="f16")),
     ("kt_f16_fallback", dict(B=1, H=2, S=64, D=32, out_dtype="f32", k_transposed=True)),
 ]
 
