@@ -9,18 +9,20 @@
 //
 // Persistent CTAs (as many as fit on the SMs, two per SM up to D = 128) walk
 // the 128-query tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... in (batch,
-// head)-major order; each tile's keys go in blocks of 64.  Warp roles:
-//   warp 4      TMA producer: the first tile's Q, then K and V blocks through
+// head)-major order; each tile's keys go in blocks of 64 (128 at D = 256, see
+// AttnCfg).  Warp roles (W = 4 softmax warps, 8 at D = 256):
+//   warp W      TMA producer: the first tile's Q, then K and V blocks through
 //               one ring in the order the MMA thread consumes them (K0, K1, V0,
 //               K2, V1, ..., then the next tile's; no multicast, 128-byte
 //               swizzle).  The next tile's Q is loaded by softmax thread 0 as
 //               soon as the current tile's last score product is done (the
 //               last reader of Q).
-//   warp 5      one thread issues tcgen05.mma.  S = Q K^T goes to one of two
+//   warp W + 1  one thread issues tcgen05.mma.  S = Q K^T goes to one of two
 //               TMEM score buffers, one block ahead: S[g+1] is computed while
 //               the softmax warps work on S[g].  O += P V (into TMEM, P read
 //               from TMEM as the A operand) follows once P[g] is written.
-//   warps 0-3   one query row per thread (TMEM lane): read the 64 scores,
+//   warps 0..W-1 one query row per thread (TMEM lane; at D = 256 two threads
+//               per row, each with half of the block): read the 64 scores,
 //               exponentiate against the running max, write P as packed f16
 //               over the first 32 columns of the same score buffer, keep the
 //               running sum; at the end of a tile O / l, staged in shared
