@@ -49,31 +49,32 @@
 
 namespace emmy {
 
-// WIDE (D = 256): 128-key blocks (score products at N = 128, the tensor
-// core's full rate; N = 64 runs at 57% of it) and two softmax warps per TMEM
-// lane quadrant, each taking 64 of a row's 128 scores; the two halves exchange
-// their block max through shared memory and add their sums at the end.  At
-// D = 256 one CTA fills an SM's tensor memory either way.  Otherwise 64-key
-// blocks, one softmax warp per quadrant, two CTAs per SM up to D = 128 (where
-// 128-key blocks would cost the second CTA: measured slower).
-template <int D, bool WIDE>
+// BN keys per block, HALVES softmax warps per TMEM lane quadrant (each taking
+// BN / HALVES of a row's scores; with two, the halves exchange their block max
+// through shared memory and add their sums at the end).  D = 256: 128-key
+// blocks (score products at N = 128, the tensor core's full rate; N = 64 runs
+// at 57% of it) -- one CTA fills an SM's tensor memory either way.  D <= 128:
+// 64-key blocks and two CTAs per SM (128-key blocks would cost the second CTA:
+// measured slower).
+template <int D, int BN_, int HALVES_>
 struct AttnCfg {
-  static constexpr int BN = WIDE ? 128 : 64;         // keys per block
-  static constexpr int HALVES = WIDE ? 2 : 1;        // softmax warps per lane quadrant
+  static constexpr int BN = BN_;                     // keys per block
+  static constexpr int HALVES = HALVES_;             // softmax warps per lane quadrant
+  static constexpr int CPT = BN / HALVES;            // score columns per softmax thread
   static constexpr int SM_WARPS = 4 * HALVES;        // softmax warps
   static constexpr int NKB = D / 64;                 // 64-wide head-dim blocks of Q and K
   static constexpr int Q_BOX = 128 * 128;            // [128 rows][128 B]
   static constexpr int K_BOX = BN * 128;             // [BN keys][128 B]
   static constexpr int Q_BYTES = NKB * Q_BOX;
   static constexpr int SLOT_BYTES = NKB * K_BOX;     // one K or V block
-  static constexpr int SLOTS = WIDE ? 2 : 3;
+  static constexpr int SLOTS = BN == 128 ? 2 : 3;
   // epilogue staging: one STAGE_ROWS-row x 128-byte box per softmax warp
-  static constexpr int STAGE_ROWS = WIDE ? 16 : 32;
+  static constexpr int STAGE_ROWS = HALVES > 1 ? 16 : 32;
   static constexpr int STAGE_BYTES = SM_WARPS * STAGE_ROWS * 128;
   // Q | ring slots | epilogue staging | half-row exchange, then the mbarriers
   static constexpr int STAGE_OFF = Q_BYTES + SLOTS * SLOT_BYTES;
   static constexpr int XCH_OFF = STAGE_OFF + STAGE_BYTES;
-  static constexpr int XCH_BYTES = WIDE ? 3 * 2 * 128 * 4 : 0;   // max [2][2][128], sum [2][128]
+  static constexpr int XCH_BYTES = HALVES > 1 ? 3 * 2 * 128 * 4 : 0;   // max [2][2][128], sum [2][128]
   static constexpr int BAR_OFF = XCH_OFF + XCH_BYTES;
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
   static constexpr uint32_t S_COL0 = 0;              // score buffers at columns 0 and BN
@@ -81,7 +82,7 @@ struct AttnCfg {
   static constexpr uint32_t TMEM_COLS = O_COL + D <= 256 ? 256 : 512;
   static constexpr int PRODUCER_WARP = SM_WARPS, MMA_WARP = SM_WARPS + 1;
   static constexpr int THREADS = 32 * (SM_WARPS + 2);
-  static constexpr int MIN_BLOCKS = (!WIDE && D <= 128) ? 2 : 1;
+  static constexpr int MIN_BLOCKS = 2 * BN + D <= 256 ? 2 : 1;   // two CTAs per SM when TMEM allows
   static constexpr float RESCALE_LOG2 = 8.0f;        // lazy max threshold (P <= 2^8)
   static_assert(SMEM <= 227 * 1024, "shared memory");
   static_assert(O_COL + D <= 512, "tensor memory");
@@ -105,21 +106,34 @@ __device__ __forceinline__ void mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem,
       : "memory");
 }
 
+// Store 16 consecutive 32-bit columns of this thread's TMEM lane (waits for completion).
+__device__ __forceinline__ void tmem_st16_u(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
-template <int D, bool WIDE>
-__global__ void __launch_bounds__(AttnCfg<D, WIDE>::THREADS, AttnCfg<D, WIDE>::MIN_BLOCKS)
+template <int D, int BN_, int HALVES_>
+__global__ void __launch_bounds__(AttnCfg<D, BN_, HALVES_>::THREADS, AttnCfg<D, BN_, HALVES_>::MIN_BLOCKS)
 attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV,
                         const __grid_constant__ CUtensorMap tmO,
                         const float *__restrict__ scale_div, int S, int ntiles, int out_f16,
                         int *status) {
-  using C = AttnCfg<D, WIDE>;
+  using C = AttnCfg<D, BN_, HALVES_>;
+  constexpr bool SPLIT = C::HALVES > 1;              // two softmax warps per row
   constexpr int BN = C::BN;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(
@@ -134,7 +148,7 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
   uint64_t *o_full = bars + 4, *mma_done = bars + 5;
   uint64_t *s_full = bars + 6, *p_full = bars + 8;   // [2] each
   uint64_t *full = bars + 10, *empty = bars + 10 + C::SLOTS;   // [SLOTS] each
-  // WIDE: half-row exchange, per lane quadrant: block max [g % 2], tile sum
+  // SPLIT: half-row exchange, per lane quadrant: block max [g % 2], tile sum
   uint64_t *xmax = bars + 10 + 2 * C::SLOTS, *xsum = xmax + 8;   // [4][2], [4]
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 10 + 2 * C::SLOTS + 12);
 
@@ -162,7 +176,7 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    if (WIDE) {
+    if (SPLIT) {
       for (int x = 0; x < 8; ++x) mbar_init(&xmax[x], 64);   // the two warps of a quadrant
       for (int x = 0; x < 4; ++x) mbar_init(&xsum[x], 64);
     }
@@ -269,13 +283,14 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
           if (j == 0 && i > 0 && !(ok = mbar_wait(o_free, (i - 1) & 1, status, kAttnWaitOFree)))
             break;
           tc_fence_after();
-          // O += P V: P from TMEM (16 keys = 8 columns per MMA; each 64-key
-          // half of a block packed into the first 32 of its 64 score columns),
-          // V N-major (value columns contiguous)
+          // O += P V: P from TMEM (16 keys = 8 columns per MMA; each softmax
+          // thread's CPT keys packed into the first CPT / 2 of its CPT score
+          // columns), V N-major (value columns contiguous)
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk)
             mma_f16_tmem_a(tmem + C::O_COL,
-                           tmem + C::S_COL0 + (g & 1) * BN + (kk >> 2) * 64 + (kk & 3) * 8,
+                           tmem + C::S_COL0 + (g & 1) * BN + (kk * 16 / C::CPT) * C::CPT +
+                               (kk * 16 % C::CPT) / 2,
                            sw128_desc(va + kk * 16 * 128, C::K_BOX, 1024), idesc_o,
                            (j | kk) != 0 ? 1u : 0u);
           mma_commit(o_full);
@@ -291,14 +306,15 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
   } else {
     // softmax / epilogue.  Warp w reads TMEM lane quadrant w % 4: its thread
     // owns query row m0 + r, r = 32 * (w % 4) + lane, and of each block's
-    // scores the 64 columns of half w / 4 (WIDE) or all 64.  Scores are kept
+    // scores the CPT columns of half w / 4 (SPLIT) or all of them.  Scores are kept
     // as t = s * scale * log2(e), so p = 2^(t - m).
     const int quad = warp & 3, half = warp >> 2;
     const int r = quad * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const float c = (scale_div ? 1.0f / __ldg(scale_div) : 1.0f) * 1.4426950408889634f;
     unsigned char *stage = smem + C::STAGE_OFF + warp * (C::STAGE_ROWS * 128);   // this warp's box
-    float *xch = reinterpret_cast<float *>(smem + C::XCH_OFF);   // WIDE only
+    float *xch = reinterpret_cast<float *>(smem + C::XCH_OFF);   // SPLIT only
+    constexpr int CPT = C::CPT;
     constexpr int OCOLS = D / C::HALVES;                 // O columns this warp rescales / writes
     bool ok = true;
     int g = 0, qloads = 0;
@@ -321,17 +337,18 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
             tma_load_3d(sQ + kb * C::Q_BOX, &tmQ, q_full, kb * 64, m0n, bhn);
           ++qloads;
         }
-        const int key0 = j * BN + half * 64;
-        const uint32_t scol = C::S_COL0 + (g & 1) * BN + half * 64;   // this half's columns
+        const int key0 = j * BN + half * CPT;
+        const uint32_t scol = C::S_COL0 + (g & 1) * BN + half * CPT;   // this half's columns
         // raw scores v; t = v * c is folded into one FFMA below.  With c > 0 the
         // row max of t is c * max(v), with c < 0 it is c * min(v); masked keys
         // get the value whose t is -inf.
-        float v[64];
-        tmem_ld64(lane_base + scol, v);
-        if (key0 + 64 > S) {
+        float v[CPT];
+        if constexpr (CPT == 64) tmem_ld64(lane_base + scol, v);
+        else tmem_ld32(lane_base + scol, v);
+        if (key0 + CPT > S) {
           const float far = c > 0.f ? -INFINITY : INFINITY;
 #pragma unroll
-          for (int k = 0; k < 64; ++k)
+          for (int k = 0; k < CPT; ++k)
             if (key0 + k >= S) v[k] = far;
         }
         float ext[8];
@@ -339,21 +356,21 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         for (int q = 0; q < 8; ++q) ext[q] = v[q];
         if (c > 0.f) {
 #pragma unroll
-          for (int k = 8; k < 64; ++k) ext[k & 7] = fmaxf(ext[k & 7], v[k]);
+          for (int k = 8; k < CPT; ++k) ext[k & 7] = fmaxf(ext[k & 7], v[k]);
 #pragma unroll
           for (int w = 4; w >= 1; w >>= 1)
 #pragma unroll
             for (int q = 0; q < w; ++q) ext[q] = fmaxf(ext[q], ext[q + w]);
         } else {
 #pragma unroll
-          for (int k = 8; k < 64; ++k) ext[k & 7] = fminf(ext[k & 7], v[k]);
+          for (int k = 8; k < CPT; ++k) ext[k & 7] = fminf(ext[k & 7], v[k]);
 #pragma unroll
           for (int w = 4; w >= 1; w >>= 1)
 #pragma unroll
             for (int q = 0; q < w; ++q) ext[q] = fminf(ext[q], ext[q + w]);
         }
         float mb = ext[0] * c;
-        if constexpr (WIDE) {
+        if constexpr (SPLIT) {
           // the row's max over both halves: each half posts its own, the
           // quadrant's barrier for this block parity completes with both.  A
           // thread posts block g + 2 only after it has seen block g + 1, for
@@ -372,9 +389,9 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         const float m_use = move ? mb : m;
         const float alpha = move ? ex2_approx(m - mb) : 1.0f;
         float psum[4] = {0.f, 0.f, 0.f, 0.f};
-        uint32_t h[32];
+        uint32_t h[CPT / 2];
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
+        for (int k = 0; k < CPT / 2; ++k) {
           const float p0 = ex2_approx(fmaf(v[2 * k], c, -m_use));
           const float p1 = ex2_approx(fmaf(v[2 * k + 1], c, -m_use));
           psum[k & 3] += p0 + p1;
@@ -402,15 +419,16 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
             tmem_st32(lane_base + C::O_COL + half * OCOLS + cc * 32, ov);
           }
         }
-        // P over the first 32 of this half's score columns (already read)
-        tmem_st32_u(lane_base + scol, h);
+        // P over the first CPT / 2 of this half's score columns (already read)
+        if constexpr (CPT == 64) tmem_st32_u(lane_base + scol, h);
+        else tmem_st16_u(lane_base + scol, h);
         l = l * alpha + ps;                // this half's share of the row sum
         m = m_use;
         tc_fence_before();
         mbar_arrive(&p_full[g & 1]);
       }
       if (!ok) break;
-      if constexpr (WIDE) {
+      if constexpr (SPLIT) {
         // the row sum: this half's share plus the partner's (one phase per tile)
         xch[512 + half * 128 + r] = l;
         mbar_arrive(&xsum[quad]);
@@ -543,11 +561,11 @@ attention_f16_simt_kernel(const __half *__restrict__ q, const __half *__restrict
 
 namespace {
 
-template <int D, bool WIDE>
+template <int D, int BN, int HALVES>
 int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
                         const float *scale_div, int64_t batch, int64_t S, int out_f16,
                         cudaStream_t st) {
-  using Cfg = AttnCfg<D, WIDE>;
+  using Cfg = AttnCfg<D, BN, HALVES>;
   CUtensorMap tq, tk, tv;
   const uint64_t dims[3] = {(uint64_t)D, (uint64_t)S, (uint64_t)batch};
   const uint64_t str[2] = {(uint64_t)D * 2, (uint64_t)S * D * 2};
@@ -572,7 +590,7 @@ int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaFuncSetAttribute(attention_f16_tc_kernel<D, WIDE>,
+    cudaFuncSetAttribute(attention_f16_tc_kernel<D, BN, HALVES>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     attr_set[dev] = true;
   }
@@ -581,7 +599,7 @@ int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
   if (ntiles > INT32_MAX) return set_error(EMMY_ERR_INVALID, "emmy_attention_f16: too many query tiles");
   const int64_t slots = (int64_t)Cfg::MIN_BLOCKS * sm_count();
   const unsigned grid = (unsigned)(ntiles < slots ? ntiles : slots);
-  attention_f16_tc_kernel<D, WIDE><<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(
+  attention_f16_tc_kernel<D, BN, HALVES><<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(
       tq, tk, tv, to, scale_div, (int)S, (int)ntiles, out_f16, device_status_ptr());
   return check_launch("emmy_attention_f16 (tcgen05)");
 }
@@ -610,14 +628,17 @@ extern "C" int emmy_attention_f16(const void *q, const void *k, const void *v, v
   const bool tc = !k_transposed && sq == sk && aligned16(q) && aligned16(k) && aligned16(v) &&
                   aligned16(o) && (d == 64 || d == 128 || d == 256);
   if (tc) {
-    // D = 256: 128-key blocks once there is more than one 64-key block
+    // D = 256: 128-key blocks once there is more than one 64-key block.
+    // (D = 128 with two softmax warps per row, 32 scores each, at two CTAs per
+    // SM was measured slower: the per-block max exchange costs more than the
+    // halved softmax work saves.)
     if (d == 64)
-      return launch_attention_tc<64, false>(q, k, v, o, scale_div, batch, sq, out_f16, st);
+      return launch_attention_tc<64, 64, 1>(q, k, v, o, scale_div, batch, sq, out_f16, st);
     if (d == 128)
-      return launch_attention_tc<128, false>(q, k, v, o, scale_div, batch, sq, out_f16, st);
+      return launch_attention_tc<128, 64, 1>(q, k, v, o, scale_div, batch, sq, out_f16, st);
     if (sq > 64)
-      return launch_attention_tc<256, true>(q, k, v, o, scale_div, batch, sq, out_f16, st);
-    return launch_attention_tc<256, false>(q, k, v, o, scale_div, batch, sq, out_f16, st);
+      return launch_attention_tc<256, 128, 2>(q, k, v, o, scale_div, batch, sq, out_f16, st);
+    return launch_attention_tc<256, 64, 1>(q, k, v, o, scale_div, batch, sq, out_f16, st);
   }
   // head dims up to 96: one thread per query row (any key count)
   const int rc = launch_attention_rows(q, k, v, o, scale_div, batch, sq, sk, d, d, 1, out_f16,
