@@ -4,6 +4,7 @@
 #include "common.cuh"
 #include "tma.cuh"
 
+#include <mutex>
 #include <string.h>
 
 namespace emmy {
@@ -26,16 +27,68 @@ void clear_error() { t_error[0] = 0; }
 
 const char *last_error_text() { return t_error; }
 
-int *device_status_ptr() {
-  static int *cached[64] = {nullptr};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!cached[dev]) {
+namespace {
+typedef int (*PFN_ctxGetCurrent)(void **ctx);
+PFN_ctxGetCurrent ctx_get_current_fn() {
+  static PFN_ctxGetCurrent fn = []() -> PFN_ctxGetCurrent {
     void *p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
-    cached[dev] = static_cast<int *>(p);
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<PFN_ctxGetCurrent>(p);
+    return nullptr;
+  }();
+  return fn;
+}
+
+struct SymbolSlot {
+  const void *symbol;
+  int dev;
+  void *ctx;
+  void *addr;
+};
+std::mutex g_symbol_mutex;
+SymbolSlot g_symbol_slots[256];
+int g_symbol_used = 0;
+}  // namespace
+
+void *symbol_address(const void *symbol, int *rc) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    *rc = set_error(EMMY_ERR_CUDA, "no current device: %s", cudaGetErrorString(e));
+    return nullptr;
   }
-  return cached[dev];
+  // the context is part of the key: after a device reset the module is
+  // loaded afresh and its symbols may move
+  void *ctx = nullptr;
+  if (auto get = ctx_get_current_fn()) get(&ctx);
+  std::lock_guard<std::mutex> lock(g_symbol_mutex);
+  for (int i = 0; i < g_symbol_used; ++i) {
+    const SymbolSlot &s = g_symbol_slots[i];
+    if (s.symbol == symbol && s.dev == dev && s.ctx == ctx) {
+      *rc = EMMY_OK;
+      return s.addr;
+    }
+  }
+  void *p = nullptr;
+  e = cudaGetSymbolAddress(&p, symbol);
+  if (e != cudaSuccess || p == nullptr) {
+    *rc = set_error(EMMY_ERR_CUDA, "cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    return nullptr;
+  }
+  int slot = -1;
+  for (int i = 0; i < g_symbol_used; ++i)
+    if (g_symbol_slots[i].symbol == symbol && g_symbol_slots[i].dev == dev) slot = i;   // stale
+  if (slot < 0 && g_symbol_used < 256) slot = g_symbol_used++;
+  if (slot >= 0) g_symbol_slots[slot] = SymbolSlot{symbol, dev, ctx, p};
+  *rc = EMMY_OK;
+  return p;
+}
+
+int *device_status_ptr() {
+  int rc = 0;
+  return static_cast<int *>(symbol_address(reinterpret_cast<const void *>(&g_device_status), &rc));
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {

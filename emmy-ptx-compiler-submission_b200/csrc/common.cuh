@@ -47,6 +47,13 @@ int launch_attention_rows(const void *q, const void *k, const void *v, void *o,
                           int64_t d, int64_t dv, int in_f16, int out_f16, int k_transposed,
                           cudaStream_t st);
 
+// Device address of one of this library's __device__ variables in the current
+// device's current context (looked up with cudaGetSymbolAddress on first use
+// in that context and cached; thread-safe).  Host code must pass this address
+// to kernels, never the symbol itself, which on the host names a stand-in.
+// Returns nullptr and sets *rc (with the error text) on failure.
+void *symbol_address(const void *symbol, int *rc);
+
 // Device address of the library's status word on the current device.  Kernels
 // with bounded waits receive it as an argument and write a nonzero code there
 // instead of hanging or trapping; emmy_get_device_status() reads and clears it.

@@ -486,15 +486,20 @@ extern "C" int emmy_gemm_f64(const double *A, const double *B, const double *bia
 
 
 extern "C" int emmy_gemm_f32_rows_to_peers(const float *A, const float *B, const float *bias,
-                                           float *const *rows, int world, int me,
-                                           int64_t rows_per_rank, int64_t M, int64_t N, int64_t K,
-                                           int splits, float *workspace, int *tile_counters,
-                                           int64_t n_counters, void *stream) {
+                                           float *const *rows, int64_t slot_floats, int world,
+                                           int me, int64_t rows_per_rank, int64_t M, int64_t N,
+                                           int64_t K, int splits, float *workspace,
+                                           int *tile_counters, int64_t n_counters, void *stream) {
   clear_error();
   if (world < 1 || world > 8 || !rows || me < 0 || me >= world)
     return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32_rows_to_peers: 1 to 8 row owners");
   if (rows_per_rank < 1 || rows_per_rank * world < M)
     return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32_rows_to_peers: rows do not cover M");
+  if (N < 0 || slot_floats < (int64_t)world * rows_per_rank * N)
+    return set_error(EMMY_ERR_INVALID,
+                     "emmy_gemm_f32_rows_to_peers: slot buffers of %lld floats, need world x "
+                     "rows_per_rank x N = %lld", (long long)slot_floats,
+                     (long long)world * rows_per_rank * N);
   if (!workspace || !tile_counters || n_counters < ((M + 63) / 64) * ((N + 63) / 64))
     return set_error(EMMY_ERR_INVALID, "emmy_gemm_f32_rows_to_peers: workspace or counters");
   PeerRows pr{};

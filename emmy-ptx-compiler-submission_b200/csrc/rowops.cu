@@ -672,28 +672,17 @@ static __device__ __align__(256) float g_noalloc_partials[kNoallocParts];
 
 // Device address of g_noalloc_partials for the current device.  Host code may
 // not pass the symbol itself to a kernel (on the host it names a stand-in, not
-// device memory), so the address is looked up once per device, with that
-// device current, and cached.
+// device memory), so the address is looked up with cudaGetSymbolAddress, with
+// the device current, on the first call in each device context (later calls
+// reuse it; the lookup is thread-safe and repeated after a device reset).
 static float *noalloc_partials_ptr(int *rc) {
-  static float *cached[64] = {nullptr};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) {
-    *rc = set_error(EMMY_ERR_CUDA, "emmy_reduce_f32_noalloc: no current device");
-    return nullptr;
+  void *p = symbol_address(reinterpret_cast<const void *>(&g_noalloc_partials), rc);
+  if (!p) {
+    char why[256];
+    snprintf(why, sizeof(why), "%s", last_error_text());
+    set_error(*rc, "emmy_reduce_f32_noalloc: the address of the built-in scratch: %s", why);
   }
-  if (!cached[dev]) {
-    void *p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_partials);
-    if (e != cudaSuccess || p == nullptr) {
-      *rc = set_error(EMMY_ERR_CUDA, "emmy_reduce_f32_noalloc: cudaGetSymbolAddress: %s",
-                      cudaGetErrorString(e));
-      return nullptr;
-    }
-    cached[dev] = static_cast<float *>(p);
-  }
-  *rc = EMMY_OK;
-  return cached[dev];
+  return static_cast<float *>(p);
 }
 
 template <int OP, int PRE>

@@ -269,8 +269,8 @@ def splitk_to_peers(a_slice, b_slice, peers, M, N, splits=0, bias=None, stream=N
     st = stream if stream is not None else torch.cuda.current_stream()
     _check(lib.emmy_gemm_f32_rows_to_peers(
         ctypes.c_void_p(a_slice.data_ptr()), ctypes.c_void_p(b_slice.data_ptr()),
-        ctypes.c_void_p(bias.data_ptr()) if bias is not None else None, ptrs, world, peers.rank,
-        M // world, M, N, a_slice.shape[-1], splits, ctypes.c_void_p(ws.data_ptr()),
+        ctypes.c_void_p(bias.data_ptr()) if bias is not None else None, ptrs,
+        peers.slots.numel(), world, peers.rank, M // world, M, N, a_slice.shape[-1], splits, ctypes.c_void_p(ws.data_ptr()),
         ctypes.c_void_p(counters.data_ptr()), counters.numel(), _stream_handle(st)),
         "emmy_gemm_f32_rows_to_peers")
 

@@ -40,8 +40,8 @@ SIGNATURES = {
                    _int, _int, _vp],
     "emmy_gemm_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _int, _vp],
     "emmy_gemm_f64": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _int, _vp],
-    "emmy_gemm_f32_rows_to_peers": [_vp, _vp, _vp, _vp, _int, _int, _i64, _i64, _i64, _i64, _int,
-                                    _vp, _vp, _i64, _vp],
+    "emmy_gemm_f32_rows_to_peers": [_vp, _vp, _vp, _vp, _i64, _int, _int, _i64, _i64, _i64, _i64,
+                                    _int, _vp, _vp, _i64, _vp],
     "emmy_ipc_export": [_vp, _vp, _vp],
     "emmy_ipc_import": [_vp, _i64, _vp, _vp],
     "emmy_ipc_close": [_vp],

@@ -180,21 +180,29 @@ int emmy_gemm_f64(const double *A, const double *B, const double *bias, double *
 /*
  * One rank's K slice of a matmul split across the GPUs of a node, fused with
  * the reduce-scatter of the partial sums: C_part = A[M, Kslice] @ B[Kslice, N]
- * (+ bias on one rank) is added, element by element (atomic adds; over
- * NVLink for rows another GPU owns), into rows[m / rows_per_rank] at row
- * m % rows_per_rank.  rows[] holds every owner's row buffer in this process's
- * address space (emmy_ipc_import); the owners zero their rows before any rank
- * launches.  With splits > 1 the splits of a tile first sum in `workspace`
- * (M x N floats) and the last one (tile_counters, one int per 64 x 64 tile,
- * n_counters of them) pushes the tile to its owner, so each element crosses
- * NVLink once; workspace and counters must be zero on the first call and are
- * left zero.  The multi-GPU form of the reference's atomic split-K Write
- * (reference ptxc/stmts.py:456-461), one kernel instead of GEMM + collective.
+ * (+ bias: pass it on one rank only, or it joins the sum once per rank) is
+ * stored, row by row, into the owners' slot buffers.  Owner o (rows
+ * [o * rows_per_rank, (o + 1) * rows_per_rank) of C) holds a slot buffer
+ * rows[o] of [world, rows_per_rank, N] floats (slot_floats floats, checked to
+ * be at least world * rows_per_rank * N); rank `me` writes only slot `me` of
+ * each owner (plain 16-byte stores, over NVLink for another GPU's rows), so
+ * nothing needs zeroing and no atomics cross NVLink.  The owner then sums its
+ * `world` slots (emmy_reduce_f32 over the slot axis).  rows[] holds every
+ * owner's buffer in this process's address space (emmy_ipc_import).  When the
+ * K slice is split inside the rank (splits > 1, or splits = 0 and the library
+ * widens the split to fill the GPU), the splits of each 128 x 128 tile first
+ * sum in `workspace` (M x N floats, local) and the last split to arrive at
+ * the tile (tile_counters: at least ceil(M / 64) * ceil(N / 64) ints) stores
+ * it, so each element crosses NVLink once; workspace and counters must be
+ * zero before the first call and are left zero.  The multi-GPU form of the
+ * reference's atomic split-K Write (reference ptxc/stmts.py:456-461), one
+ * kernel instead of GEMM + collective.
  */
 int emmy_gemm_f32_rows_to_peers(const float *A, const float *B, const float *bias,
-                                float *const *rows, int world, int me, int64_t rows_per_rank,
-                                int64_t M, int64_t N, int64_t K, int splits, float *workspace,
-                                int *tile_counters, int64_t n_counters, void *stream);
+                                float *const *rows, int64_t slot_floats, int world, int me,
+                                int64_t rows_per_rank, int64_t M, int64_t N, int64_t K,
+                                int splits, float *workspace, int *tile_counters,
+                                int64_t n_counters, void *stream);
 
 /*
  * CUDA IPC for peer mappings between the processes of one node.  export: the

@@ -13,7 +13,11 @@ directory is git-ignored and travels to the GPU box, where
 ``oracle/ref_ptx.py`` loads and launches the PTX exactly as the reference
 harness does (``tools/localrun.py:102-142``).
 
-Usage: ``python oracle/make_ref_ptx.py [REFERENCE_DIR]``.
+Usage: ``python oracle/make_ref_ptx.py [REFERENCE_DIR]``; without the argument
+the checkout is found by ``oracle/refdir.py`` (``EMMY_REFERENCE_DIR``, else a
+``reference`` checkout beside this repository).  The test set-up
+(``tests/conftest.py``) runs it when ``oracle/_ref`` is missing or older than
+this file.
 """
 
 from __future__ import annotations
@@ -86,4 +90,12 @@ def main(ref: Path) -> int:
 
 
 if __name__ == "__main__":
-    sys.exit(main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")))
+    if len(sys.argv) > 1:
+        _ref = Path(sys.argv[1])
+    else:
+        sys.path.insert(0, str(ROOT))
+        from oracle.refdir import reference_dir
+        _ref = reference_dir()
+        if _ref is None:
+            sys.exit("make_ref_ptx: no reference checkout (set EMMY_REFERENCE_DIR)")
+    sys.exit(main(_ref))

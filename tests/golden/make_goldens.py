@@ -17,7 +17,9 @@ The tests rebuild each fixture's IR shape with ``emmy_ir.synth``
 against these values with the fixture's own rtol/atol, on the CPU oracle and
 on the GPU kernels, without needing the reference checkout.
 
-Usage: ``python tests/golden/make_goldens.py [VARIANTS_DIR]``.
+Usage: ``python tests/golden/make_goldens.py [VARIANTS_DIR]``; without the
+argument the reference checkout is found by ``oracle/refdir.py``
+(``EMMY_REFERENCE_DIR``, else a ``reference`` checkout beside this repository).
 """
 
 from __future__ import annotations
@@ -67,4 +69,12 @@ def main(variants: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference/tests/variants"))
+    if len(sys.argv) > 1:
+        main(Path(sys.argv[1]))
+    else:
+        sys.path.insert(0, str(HERE.parent.parent))
+        from oracle.refdir import reference_variants
+        _v = reference_variants()
+        if _v is None:
+            sys.exit("make_goldens: no reference checkout (set EMMY_REFERENCE_DIR)")
+        main(_v)

@@ -61,6 +61,21 @@ def test_host_side_argument_checks_run_before_any_cuda_call(lib):
     assert lib.emmy_rownorm_f32(None, None, None, None, 0, 4, None, None, 0, None) == 0
 
 
+def test_peer_slot_size_checked_on_the_host(lib):
+    # a slot buffer smaller than world x rows_per_rank x N is refused before any launch
+    lib.emmy_gemm_f32_rows_to_peers.argtypes = (
+        [ctypes.c_void_p] * 4 + [ctypes.c_int64, ctypes.c_int, ctypes.c_int] +
+        [ctypes.c_int64] * 4 + [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                ctypes.c_void_p])
+    lib.emmy_last_error.restype = ctypes.c_char_p
+    rows = (ctypes.c_void_p * 8)(*([ctypes.c_void_p(256)] * 8))
+    rc = lib.emmy_gemm_f32_rows_to_peers(ctypes.c_void_p(256), ctypes.c_void_p(256), None, rows,
+                                         2 * 128 * 64 - 1, 2, 0, 128, 256, 64, 1024, 1,
+                                         ctypes.c_void_p(256), ctypes.c_void_p(256), 64, None)
+    assert rc == 1
+    assert b"slot buffers" in lib.emmy_last_error()
+
+
 def test_pointwise_program_checks_need_no_gpu(lib):
     vp, i32, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
     lib.emmy_pointwise.argtypes = [vp, vp, i32, vp, vp, i32, vp, i32, vp, i32, i32, i32, vp, i32,

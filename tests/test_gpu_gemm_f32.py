@@ -174,3 +174,42 @@ def test_gemm_f64_accumulate_adds_into_c():
         ref = C0 + A @ B
         scale = C0.abs() + A.abs() @ B.abs()
         assert torch.all((C - ref).abs() <= 1e-13 * scale)
+
+
+@pytest.mark.parametrize("M,N,K,splits", [(200, 196, 4096, 0), (136, 260, 1000, 1),
+                                          (256, 128, 8192, 8)])
+def test_rows_to_peers_single_owner_matches_the_plain_gemm(M, N, K, splits):
+    """The fused split-K kernel with one owner (this GPU): auto-widened or
+    caller splits, a bias, ragged 128 x 128 tiles.  Its slot must equal the
+    plain f32 GEMM within the GEMM tolerance, and the tile workspace and
+    arrival counters must be left zero for the next call (checked over two
+    calls)."""
+    import torch
+    from ptxc.launch import load_library
+    lib = load_library()
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    A = torch.rand(M, K, device="cuda", generator=g) * 2 - 1
+    B = torch.rand(K, N, device="cuda", generator=g) * 2 - 1
+    bias = torch.randn(N, device="cuda", generator=g)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    plain = torch.empty(M, N, device="cuda")
+    assert lib.emmy_gemm_f32(P(A), P(B), P(bias), P(plain), 1, M, N, K, 0, 0, 0, splits, 0, 1,
+                             None) == 0, lib.emmy_last_error()
+    slots = torch.full((1, M, N), float("nan"), device="cuda")
+    ws = torch.zeros(M * N, device="cuda")
+    tiles = ((M + 63) // 64) * ((N + 63) // 64)
+    counters = torch.zeros(tiles, dtype=torch.int32, device="cuda")
+    rows = (ctypes.c_void_p * 8)(P(slots), *([ctypes.c_void_p(0)] * 7))
+    for _ in range(2):
+        slots.fill_(float("nan"))
+        rc = lib.emmy_gemm_f32_rows_to_peers(P(A), P(B), P(bias), rows, slots.numel(), 1, 0, M,
+                                             M, N, K, splits, P(ws), P(counters), tiles, None)
+        assert rc == 0, lib.emmy_last_error()
+        torch.cuda.synchronize()
+        ref = A.double() @ B.double() + bias.double()
+        scale = A.double().abs() @ B.double().abs() + bias.double().abs()
+        got = slots[0].double()
+        assert torch.all((got - ref).abs() <= RTOL * scale), "fused slot differs from float64"
+        assert torch.all((got - plain.double()).abs() <= 2 * RTOL * scale), "fused vs plain GEMM"
+        assert int(torch.count_nonzero(ws)) == 0, "tile workspace not left zero"
+        assert int(torch.count_nonzero(counters)) == 0, "arrival counters not left zero"
