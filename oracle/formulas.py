@@ -110,3 +110,29 @@ def attention_bhsd(q, k, v, scale, out_dtype=np.float32):
     s = np.matmul(_f64(q), np.swapaxes(_f64(k), -1, -2)) * float(scale)
     p = softmax(s, axis=-1, out_dtype=np.float64)
     return np.matmul(p, _f64(v)).astype(out_dtype)
+
+
+def layernorm_abs_scale(x, gamma, beta, eps):
+    """``(|x| + |mean|) * rstd * |gamma| + |beta|``: the magnitude of the terms
+    each layer-norm output is formed from, for error bounds (an output near
+    zero because beta cancels the normalised term still carries the terms'
+    rounding)."""
+    x64 = _f64(x)
+    m = x64.mean(-1, keepdims=True)
+    d = x64 - m
+    rstd = 1.0 / np.sqrt((d * d).mean(-1, keepdims=True) + eps)
+    s = (np.abs(x64) + np.abs(m)) * rstd
+    if gamma is not None:
+        s = s * np.abs(_f64(gamma))
+    if beta is not None:
+        s = s + np.abs(_f64(beta))
+    return s
+
+
+def attention_abs_scale(q, k, v, scale):
+    """``sum_j p_j |v_j|`` per output element (q, k, v ``[..., S, D]``; k not
+    transposed): the convex-combination scale of each attention output, for
+    error bounds."""
+    s = np.matmul(_f64(q), np.swapaxes(_f64(k), -1, -2)) * float(scale)
+    p = softmax(s, axis=-1, out_dtype=np.float64)
+    return np.matmul(p, np.abs(_f64(v)))

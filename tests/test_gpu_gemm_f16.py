@@ -19,6 +19,7 @@ import pytest
 from emmy_ir import synth
 from gpu_util import run_on_gpu, shaped
 from oracle import formulas as F
+from parity import check
 
 pytestmark = pytest.mark.gpu
 
@@ -45,13 +46,11 @@ IR_CASES = [
 ]
 
 
-def _check(x, got, bias=None, relu=False, f16_out=True):
+def _check(x, got, bias=None, relu=False, f16_out=True, case="gemm_f16"):
     ref = F.matmul(x["A"], x["B"], bias, relu, out_dtype=np.float64)
     scale = F.matmul_abs_bound(x["A"], x["B"], bias)
-    u = 2.0 ** -11 if f16_out else 0.0
-    err = np.abs(got.reshape(ref.shape).astype(np.float64) - ref)
-    bound = RTOL * scale + u * np.abs(ref)
-    assert np.all(err <= bound), f"max excess {np.max(err - bound)}"
+    check(got.reshape(ref.shape), ref, scale, case=case, family="gemm_f16", dtype="f16",
+          out_dtype="f16" if f16_out else "f32")
 
 
 @pytest.mark.parametrize("name,kw", IR_CASES, ids=[c[0] for c in IR_CASES])
@@ -60,7 +59,8 @@ def test_gemm_f16_ir(name, kw):
     plan, host, out = run_on_gpu(kop, meta)
     assert plan["family"] == "gemm_f16"
     x = shaped(meta, host)
-    _check(x, out["C"], x.get("bias"), kw.get("relu", False), kw["out_dtype"] == "f16")
+    _check(x, out["C"], x.get("bias"), kw.get("relu", False), kw["out_dtype"] == "f16",
+           case=f"gemm_f16 {name}")
 
 
 @pytest.mark.parametrize("M,N,K,batch,out", [(33, 30, 17, 1, 1), (5, 7, 9, 2, 0), (64, 24, 40, 1, 1),

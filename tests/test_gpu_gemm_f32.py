@@ -21,6 +21,7 @@ import pytest
 from emmy_ir import synth
 from gpu_util import run_on_gpu, shaped
 from oracle import formulas as F
+from parity import check
 
 pytestmark = pytest.mark.gpu
 
@@ -51,7 +52,7 @@ def test_gemm_f32_ir(name, kw):
     ref = F.matmul(x["A"], x["B"], x.get("bias"), kw.get("relu", False), out_dtype=np.float64)
     scale = F.matmul_abs_bound(x["A"], x["B"], x.get("bias"))
     got = out["C"].reshape(ref.shape).astype(np.float64)
-    assert np.all(np.abs(got - ref) <= RTOL * scale + 1e-30), name
+    check(got, ref, scale, case=f"gemm_f32 {name}", family="gemm_f32", dtype="f32")
 
 
 @pytest.mark.parametrize("M,N,K,batch", [(33, 30, 17, 1), (5, 7, 9, 2), (130, 4, 1024, 1),
@@ -136,7 +137,7 @@ def test_gemm_f64_ir(name, kw):
     if kw.get("relu"):
         ref = np.maximum(ref, 0)
     got = out["C"].reshape(ref.shape)
-    assert np.all(np.abs(got - ref) <= 1e-13 * scale + 1e-300), name
+    check(got, ref, scale, case=f"gemm_f64 {name}", family="gemm_f64", dtype="f64", rtol=1e-13)
 
 
 @pytest.mark.parametrize("M,N,K,batch", [(33, 30, 17, 1), (5, 7, 9, 2), (130, 4, 1024, 1),

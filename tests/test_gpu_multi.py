@@ -9,7 +9,8 @@
   owner's slot over NVLink and each owner sums its slots (``PeerRows`` +
   ``splitk_step``).
 
-Tolerances as in the single-GPU tests.  NVLS is off (``NCCL_NVLS_ENABLE=0``).
+Tolerances as in the single-GPU tests (``tests/parity.py``): softmax 1e-5
+relative, attention 1e-3 of ``sum_j p_j |v_j|``, split-K 1e-5 of ``|A| @ |B|``.  NVLS is off (``NCCL_NVLS_ENABLE=0``).
 """
 
 from __future__ import annotations
@@ -71,7 +72,7 @@ def _worker(rank, world, port, q):
         if rank == 0:
             ref = F.softmax(host["x"].reshape(64, 1024), out_dtype=np.float64).reshape(-1)
             got = out.cpu().numpy().astype(np.float64)
-            ok &= bool(np.all(np.abs(got - ref) <= 1e-5 * np.abs(ref) + 1e-6 * np.abs(ref).max()))
+            ok &= bool(np.all(np.abs(got - ref) <= 1e-5 * np.abs(ref) + 1e-30))
         # --- attention heads, sharded (tcgen05 path)
         kop, meta = synth.attention(2, 4, 256, 128, dtype="f16", out_dtype="f32")
         plan = Lowerer(kop, meta).plan()
@@ -85,8 +86,9 @@ def _worker(rank, world, port, q):
         if rank == 0:
             x = {k: v.reshape(2, 4, 256, 128) for k, v in host.items() if v.size > 1}
             ref = F.attention_bhsd(x["q"], x["k"], x["v"], 1 / np.sqrt(128), out_dtype=np.float64)
+            scale = F.attention_abs_scale(x["q"], x["k"], x["v"], 1 / np.sqrt(128))
             got = out.cpu().numpy().astype(np.float64).reshape(ref.shape)
-            ok &= bool(np.all(np.abs(got - ref) <= 1e-3 * np.abs(x["v"].astype(np.float64)).max()))
+            ok &= bool(np.all(np.abs(got - ref) <= 1e-3 * scale))
         # --- split-K f32 GEMM across ranks + NCCL reduce-scatter
         kop, meta = synth.matmul(256, 256, 8192, splits=16, tm=128, tn=128, rm=8, rn=8)
         plan = Lowerer(kop, meta).plan()
