@@ -10,12 +10,23 @@ through the C-ABI of ``libemmyb200.so``.  The metric is HBM throughput over
 the algorithmic bytes (every input read once, every output written once).
 
 Arms
-  default            the B200 kernels (one process per GPU; with torchrun every
-                     rank runs its own full-size K2 batch: weak scaling, no
-                     collective on the data path)
+  default            the B200 kernels, one process per GPU.  With N ranks the
+                     K2 rows are partitioned (``ptxc.dist.shard_plan``): each
+                     rank runs 1/N of the softmax rows and 1/N of the layernorm
+                     rows, no collective on the data path (strong scaling; the
+                     line's ``value`` is the whole workload's bytes over the
+                     slowest rank's time).  The ``weak`` key times every rank
+                     on a full K2 batch.  At N > 1 the split-K matmul K4a runs
+                     across the ranks (each rank a K slice, then the NCCL
+                     reduce-scatter, and the fused peer-store form): key
+                     ``splitk_across_gpus``.  At N = 1 the ``families`` key
+                     times every other benchmark configuration.
   --impl reference   the reference's CPU path for the same IRs: the torch-CPU
                      statement-level evaluation of the IR (``oracle/interp.py``)
-                     on every host thread, each step a bounded sample of rows
+                     over every row of both K2 IRs per step, on every host
+                     thread; beside it the torch-CPU family ops and, where a
+                     GPU and ``oracle/_ref`` exist, the reference compiler's own
+                     PTX for each benchmark configuration timed on the GPU.
 
 One JSON line is printed by rank 0.
 """
@@ -41,7 +52,9 @@ for _p in (str(ROOT), str(PKG)):
 
 METRIC = "per-family HBM GB/s (K2: softmax4d + layernorm f32)"
 UNIT = "GB/s"
+K2_WORKLOAD = "K2: softmax f32 [32,16,512,512] dim=-1 + layernorm f32 affine [16384,1024]"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_TENSOR_TFLOPS = 1590.0
 # FP32 CUDA-core peak, nominal: 148 SMs x 128 FMA/clk x 2 flops x 1.965 GHz
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 # FP64 CUDA-core peak, nominal: 148 SMs x 64 DFMA/clk x 2 flops x 1.965 GHz
@@ -51,33 +64,61 @@ FP64_NOMINAL_TFLOPS = 148 * 64 * 2 * 1.965e9 / 1e12
 FP32_MEASURED_TFLOPS = 70.86
 FP64_MEASURED_TFLOPS = 33.35
 L2_FLUSH_BYTES = 256 << 20
+# Family timings keep each launch's data out of L2: a kernel whose tensors
+# total less than this runs on several copies of them, launched back to back
+# (the per-launch time is the pass over all copies divided by their number).
+FOOTPRINT_BYTES = 256 << 20
+MAX_COPIES = 64
 # A short device spin queued before each timed region keeps the GPU busy while
 # the host enqueues the launches, so the CUDA events bracket device work only.
 SPIN_CYCLES = 200_000
 
+# ncu summary (profiles/) holding each configuration's dram bytes per launch
+PROFILE_OF = {
+    "K2a_softmax_32x16x512x512": "softmax_f32_K2a.md",
+    "K2b_layernorm_16384x1024": "layernorm_f32_K2b.md",
+    "K1_rmsnorm_4096x512": "rmsnorm_f32_K1.md",
+    "K4b_matvec_f64_16384": "matvec_f64_K4b.md",
+    "K4a_splitk_f32_256x65536x256": "gemm_f32_K4a.md",
+    "K3a_gemm_f16_4096x2048x8192_bias_relu": "gemm_f16_K3a.md",
+    "K3b_bmm_f16_64x512": "bmm_f16_K3b.md",
+    "K5_attention_f16_8x32x512x128": "attention_f16_K5.md",
+    "K5_sweep_f16_8x32_S512_D256": "attention_f16_D256.md",
+    "K5_sweep_f16_8x32_S512_D16": "attention_f16_D16.md",
+    "F8a_pointwise_add_f32_2^26": "pointwise_F8.md",
+    "F8c_pointwise_bias_relu_f32_16384x4096": "pointwise_broadcast.md",
+    "X_softmax_f16_16384x4096": "rowop_softmax_f16.md",
+}
 
-def hbm_peak():
+
+def _peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         try:
-            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
-        except (ValueError, KeyError):
+            return json.loads(p.read_text())
+        except ValueError:
             pass
-    return FALLBACK_HBM_GBS, "fallback"
+    return {}
+
+
+def hbm_peak():
+    try:
+        return float(_peaks()["hbm_gbs"]), "measured"
+    except (KeyError, TypeError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
 
 
 def tensor_peak():
-    p = ROOT / "MEASURED_PEAKS.json"
-    if p.exists():
-        try:
-            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
-        except (ValueError, KeyError):
-            pass
-    return 1590.0, "fallback"
+    try:
+        return float(_peaks()["bf16_tflops"]), "measured"
+    except (KeyError, TypeError, ValueError):
+        return FALLBACK_TENSOR_TFLOPS, "fallback"
 
 
 def profile_traffic(name):
     """dram bytes per launch recorded from an ncu capture in profiles/<name>."""
+    if not name:
+        return None
     p = ROOT / "profiles" / name
     if not p.exists():
         return None
@@ -109,6 +150,40 @@ def plan_bytes(plan):
         numel = math.prod(spec["shape"]) if spec["shape"] else 1
         total += numel * torch.empty((), dtype=torch_dtype(spec["dtype"])).element_size()
     return total
+
+
+def plan_flops(plan):
+    if "gemm" in plan:
+        g = plan["gemm"]
+        return 2.0 * g["batch"] * g["m"] * g["n"] * g["k"]
+    if "attention" in plan:
+        a = plan["attention"]
+        return 2.0 * a["batch"] * a["sq"] * a["sk"] * (a["d"] + a["dv"])
+    return 0.0
+
+
+def shard_inputs(meta, slices, rank, world):
+    """Seeded host inputs of this rank's shard: the tensors the shard slices are
+    drawn for the slice alone (seeded per rank), the replicated ones whole (the
+    same on every rank).  At world = 1 this is ``synth.make_inputs(meta)``."""
+    import numpy as np
+    from emmy_ir import synth
+    if world == 1:
+        return synth.make_inputs(meta)
+    out = {}
+    full = {a["name"]: (math.prod(a["shape"]) if a["shape"] else 1) for a in meta["args"]}
+    for a in meta["args"]:
+        name = a["name"]
+        off, cnt = slices.get(name, (0, full[name]))
+        if a.get("output"):
+            out[name] = np.zeros(cnt, dtype=synth.NP.get(a["dtype"], np.float32))
+        elif cnt == full[name] or "data" in a:
+            v = synth.make_inputs(meta, only={name})[name]
+            out[name] = v[off:off + cnt] if cnt != full[name] else v
+        else:
+            shard_meta = {"args": [dict(a, shape=[cnt])]}
+            out[name] = synth.make_inputs(shard_meta, seed_offset=1000 * rank)[name]
+    return out
 
 
 class ClockSampler:
@@ -191,6 +266,26 @@ def dist_setup():
     return world, rank, local
 
 
+def cpu_model():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# --------------------------------------------------------------------- CPU legs
+
+
 def cpu_inputs(workload, hosts=None):
     """CPU tensors for the IR evaluation (reusing the bench's host inputs when given)."""
     import torch
@@ -207,84 +302,138 @@ def cpu_inputs(workload, hosts=None):
     return out
 
 
-def cpu_sample_rate(workload, bufs_list, seconds_per_kernel, threads, rows_hint=None):
-    """Time the torch-CPU IR evaluation on a bounded sample of each kernel's rows.
+def cpu_full_step(workload, bufs_list, threads):
+    """One full K2 step of the torch-CPU IR evaluation: every row of both IRs.
 
-    Returns (GB/s over the sample bytes, description, cores, seconds, rows used).
+    Returns (GB/s over the step's algorithmic bytes, seconds, description).
     """
     import torch
     from oracle.interp import IRInterpreter
     from ptxc import Lowerer
-
     torch.set_num_threads(threads)
-    total_bytes = 0.0
-    total_s = 0.0
-    desc = []
-    rows_used = []
-    for i, ((kop, meta), bufs) in enumerate(zip(workload, bufs_list)):
+    total_bytes, total_s, desc = 0.0, 0.0, []
+    for (kop, meta), bufs in zip(workload, bufs_list):
         plan = Lowerer(kop, meta).plan()
         grid = meta["grid"][0]
-        row_bytes = plan_bytes(plan) / grid      # bytes per Tile row (one block)
-        rows = rows_hint[i] if rows_hint else 64
-        while True:
-            t0 = time.perf_counter()
-            with torch.no_grad():
-                IRInterpreter(kop, meta, bufs, blocks=(0, rows)).run()
-            dt = time.perf_counter() - t0
-            if rows_hint or dt >= seconds_per_kernel or rows >= grid:
-                break
-            rows = min(grid, rows * 4, max(rows * 2, int(rows * seconds_per_kernel / max(dt, 1e-3))))
-        total_bytes += rows * row_bytes
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            IRInterpreter(kop, meta, bufs, blocks=(0, grid)).run()
+        dt = time.perf_counter() - t0
+        total_bytes += plan_bytes(plan)
         total_s += dt
-        rows_used.append(rows)
-        desc.append(f"{kop.name}: {rows} of {grid} rows")
-    return total_bytes / total_s / 1e9, "; ".join(desc), threads, total_s, rows_used
+        desc.append(f"{kop.name}: all {grid} rows")
+    return total_bytes / total_s / 1e9, total_s, "; ".join(desc)
 
 
-def run_reference_arm(args):
-    world, rank, _ = dist_setup()
-    if rank != 0:
-        return 0
-    threads = os.cpu_count() or 1
-    workload = k2_workload()
-    bufs = cpu_inputs(workload)
-    _, _, _, _, rows = cpu_sample_rate(workload, bufs, 0.5, threads)
-    per_step = []
-    rates = []
-    desc = ""
-    for i in range(args.warmup + args.steps):
-        gbs, desc, cores, secs, _ = cpu_sample_rate(workload, bufs, 0.5, threads, rows_hint=rows)
-        if i >= args.warmup:
-            per_step.append(secs)
-            rates.append(gbs)
-    value = statistics.median(rates)
-    line = {
-        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1000 * statistics.median(per_step), 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "impl": "reference",
-        "config": {"workload": "K2: softmax f32 [32,16,512,512] dim=-1 + layernorm f32 affine [16384,1024]",
-                   "reference_path": "torch-CPU evaluation of the same IR (oracle/interp.py), "
-                                     "bounded row sample per step"},
-        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": desc},
-        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-    return 0
-
-
-def family_extras(device, peak):
-    """Kernel-only GB/s of the other memory-bound benchmark configs (K1, K4b)."""
+def cpu_warm(workload, bufs_list, threads):
+    """A few rows of each IR, to take first-call costs out of the timed step."""
     import torch
+    from oracle.interp import IRInterpreter
+    torch.set_num_threads(threads)
+    for (kop, meta), bufs in zip(workload, bufs_list):
+        with torch.no_grad():
+            IRInterpreter(kop, meta, bufs, blocks=(0, 64)).run()
+
+
+def torch_cpu_family_ops(threads, reps=5):
+    """The K2 family ops as torch's own CPU kernels (torch.softmax, layer_norm),
+    on the K2 shapes: median of ``reps`` after one warm-up; GB/s over the same
+    algorithmic bytes."""
+    import torch
+    import torch.nn.functional as Fn
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(32, 16, 512, 512, generator=g) * 2.0
+    xl = torch.randn(16384, 1024, generator=g)
+    gamma = torch.rand(1024, generator=g) + 0.5
+    beta = torch.randn(1024, generator=g) * 0.1
+    y = torch.empty_like(x)
+
+    def t(fn):
+        fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return statistics.median(ts)
+    ts = t(lambda: torch.softmax(x, dim=-1, out=y))
+    tl = t(lambda: Fn.layer_norm(xl, (1024,), gamma, beta, 1e-5))
+    sm_bytes = 2 * x.numel() * 4
+    ln_bytes = 2 * xl.numel() * 4 + 2 * 1024 * 4
+    return {"softmax_ms": round(ts * 1e3, 2), "layernorm_ms": round(tl * 1e3, 2),
+            "value": round((sm_bytes + ln_bytes) / (ts + tl) / 1e9, 3), "unit": UNIT,
+            "threads": threads,
+            "ops": "torch.softmax(x, -1) over [32,16,512,512] + F.layer_norm over [16384,1024]"}
+
+
+# ------------------------------------------------------------------ GPU timing
+
+
+def _event_pair():
+    import torch
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def time_launches(make_launch, nbytes, flush, reps=10, warmup=3):
+    """Per-launch device time (us) of one kernel configuration.
+
+    ``make_launch()`` returns a zero-argument function that launches the
+    kernel on its own copy of the tensors.  With fewer than FOOTPRINT_BYTES
+    per launch, ``copies`` such copies are launched back to back between the
+    events and the time divided by their number, so every launch reads from
+    HBM and the 1 us event resolution is spread over many launches.  L2 is
+    flushed before each timed pass.  Returns (median us per launch, copies).
+    """
+    import torch
+    copies = 1 if nbytes >= FOOTPRINT_BYTES else min(MAX_COPIES,
+                                                     -(-FOOTPRINT_BYTES // max(nbytes, 1)))
+    fns = [make_launch() for _ in range(copies)]
+    for _ in range(warmup):
+        for f in fns:
+            f()
+    samples = []
+    for _ in range(reps):
+        flush()
+        torch.cuda._sleep(SPIN_CYCLES)
+        e0, e1 = _event_pair()
+        e0.record()
+        for f in fns:
+            f()
+        e1.record()
+        e1.synchronize()
+        samples.append(e0.elapsed_time(e1) * 1e3 / copies)
+    del fns
+    return statistics.median(samples), copies
+
+
+def roofline_block(name, nbytes, flops, us, pipe):
+    """The binding roof of one configuration: t_roof = max(bytes / HBM peak,
+    flops / peak of the pipe the kernel uses); frac = t_roof / measured time."""
+    hbm, hsrc = hbm_peak()
+    t_hbm = nbytes / (hbm * 1e9)
+    pipe_peak = {"tensor": tensor_peak()[0], "fp32": FP32_MEASURED_TFLOPS,
+                 "fp64": FP64_MEASURED_TFLOPS}.get(pipe)
+    t_pipe = flops / (pipe_peak * 1e12) if pipe_peak else 0.0
+    t = us * 1e-6
+    if t_hbm >= t_pipe:
+        blk = {"bound": "hbm", "achieved": round(nbytes / t / 1e9, 1), "peak": hbm, "unit": "GB/s",
+               "peak_source": f"{hsrc} hbm_gbs"}
+    else:
+        blk = {"bound": pipe, "achieved": round(flops / t / 1e12, 2), "peak": pipe_peak,
+               "unit": "TFLOP/s",
+               "peak_source": ("measured bf16_tflops (burst)" if pipe == "tensor"
+                               else f"measured {pipe} FMA chains")}
+    blk["frac"] = round(max(t_hbm, t_pipe) / t, 4)
+    blk["algorithmic_bytes"] = int(nbytes)
+    blk["traffic"] = profile_traffic(PROFILE_OF.get(name))
+    blk["profile"] = PROFILE_OF.get(name) if blk["traffic"] is not None else None
+    return blk
+
+
+def family_cases():
     from emmy_ir import synth
-    from ptxc import Lowerer
-    from ptxc.launch import Executor
-    out = {}
-    flush = L2Flush(device)
-    cases = {
+    return {
         "K1_rmsnorm_4096x512": synth.rmsnorm(4096, 512, eps=1e-6),
         "K2a_softmax_32x16x512x512": synth.softmax([32, 16, 512, 512]),
         "K2b_layernorm_16384x1024": synth.layernorm(16384, 1024),
@@ -303,7 +452,7 @@ def family_extras(device, peak):
                                                   out_dtype="f32", tm=128, tn=128, rm=8, rn=8),
         "K5_attention_f16_8x32x512x128": synth.attention(8, 32, 512, 128, dtype="f16"),
         **{f"K5_sweep_f16_8x32_S{S}_D{D}": synth.attention(8, 32, S, D, dtype="f16")
-           for D in (16, 64, 256) for S in (16, 128, 512)},
+           for D in (16, 32, 64, 96, 256) for S in (16, 128, 512)},
         "X_gemm_f64_2048x2048x2048": synth.matmul(2048, 2048, 2048, dtype="f64", tm=128, tn=128,
                                                   rm=8, rn=8, bk=16),
         "F8a_pointwise_add_f32_2^26": synth.pointwise(1 << 26, ("add", "x0", "x1"), "f32"),
@@ -314,49 +463,60 @@ def family_extras(device, peak):
             shape=[16384, 4096]),
         "X_softmax_f16_16384x4096": synth.retype(*synth.softmax([16384, 4096]), "f16", acc="f32"),
     }
-    for name, (kop, meta) in cases.items():
+
+
+def _pipe_of(plan):
+    fam = plan["family"]
+    if fam == "gemm_f32":
+        return "fp32"
+    if fam == "gemm_f64":
+        return "fp64"
+    if fam in ("gemm_f16", "attention_f16"):
+        return "tensor"
+    return None
+
+
+def family_extras(device, only=None):
+    """Kernel-only time, throughput and roofline of every benchmark configuration."""
+    import torch
+    from emmy_ir import synth
+    from ptxc import Lowerer
+    from ptxc.launch import Executor
+    out = {}
+    flush = L2Flush(device)
+    for name, (kop, meta) in family_cases().items():
+        if only and not any(o in name for o in only):
+            continue
         plan = Lowerer(kop, meta).plan()
-        ex = Executor(plan, device=device)
-        for t in ex.tensors.values():
-            if t.is_floating_point():
-                t.normal_()
-        for a in meta["args"]:
-            if "data" in a:
-                ex.tensors[a["name"]].fill_(float(a["data"][0]))
-        for _ in range(3):
-            ex.launch()
-        times = []
-        for _ in range(10):
-            flush()
-            torch.cuda._sleep(SPIN_CYCLES)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            ex.launch()
-            e1.record()
-            e1.synchronize()
-            times.append(e0.elapsed_time(e1))
-        ms = statistics.median(times)
-        gbs = plan_bytes(plan) / (ms * 1e-3) / 1e9
-        out[name] = {"us": round(ms * 1000, 2), "gbs": round(gbs, 1), "frac_hbm": round(gbs / peak, 3),
-                     "bytes": plan_bytes(plan)}
-        if "gemm" in plan or "attention" in plan:
-            if "gemm" in plan:
-                g = plan["gemm"]
-                flops = 2.0 * g["batch"] * g["m"] * g["n"] * g["k"]
-            else:
-                a = plan["attention"]
-                flops = 2.0 * a["batch"] * a["sq"] * a["sk"] * (a["d"] + a["dv"])
-            tf = flops / (ms * 1e-3) / 1e12
-            out[name]["tflops"] = round(tf, 2)
+        nbytes = plan_bytes(plan)
+
+        def make():
+            ex = Executor(plan, device=device)
+            for t in ex.tensors.values():
+                if t.is_floating_point():
+                    t.normal_()
+            for a in meta["args"]:
+                if "data" in a:
+                    ex.tensors[a["name"]].fill_(float(a["data"][0]))
+            return ex.launch
+        us, copies = time_launches(make, nbytes, flush)
+        flops = plan_flops(plan)
+        row = {"us": round(us, 2), "gbs": round(nbytes / us / 1e3, 1), "bytes": nbytes,
+               "launches_per_sample": copies, "kernel_family": plan["family"]}
+        if flops:
+            row["tflops"] = round(flops / us / 1e6, 2)
             if plan["family"] == "gemm_f32":
-                out[name]["frac_fp32_nominal"] = round(tf / FP32_NOMINAL_TFLOPS, 3)
-                out[name]["frac_fp32_measured"] = round(tf / FP32_MEASURED_TFLOPS, 3)
+                row["frac_fp32_nominal"] = round(row["tflops"] / FP32_NOMINAL_TFLOPS, 3)
             elif plan["family"] == "gemm_f64":
-                out[name]["frac_fp64_nominal"] = round(tf / FP64_NOMINAL_TFLOPS, 3)
-                out[name]["frac_fp64_measured"] = round(tf / FP64_MEASURED_TFLOPS, 3)
-            else:
-                out[name]["frac_tensor"] = round(tf / tensor_peak()[0], 3)
-        del ex
+                row["frac_fp64_nominal"] = round(row["tflops"] / FP64_NOMINAL_TFLOPS, 3)
+            elif _pipe_of(plan) == "tensor":
+                row["frac_tensor"] = round(row["tflops"] / tensor_peak()[0], 3)
+        row["roofline"] = roofline_block(name, nbytes, flops, us, _pipe_of(plan))
+        out[name] = row
+        torch.cuda.empty_cache()
+    if only:
+        del flush
+        return out
     # the matmul + bias + ReLU package at the K3a size: two kernels (product
     # written as f16, then bias + ReLU) against the fused epilogue launch
     from ptxc.package import Chain, ChainExecutor
@@ -367,31 +527,18 @@ def family_extras(device, peak):
         ex = ChainExecutor(chain, device=device, fuse=fuse)
         for t in ex.buffers.values():
             t.normal_(std=0.02)
-        for _ in range(3):
-            ex.launch()
-        times = []
-        for _ in range(10):
-            flush()
-            torch.cuda._sleep(SPIN_CYCLES)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            n = ex.launch()
-            e1.record()
-            e1.synchronize()
-            times.append(e0.elapsed_time(e1))
-        ms = statistics.median(times)
+        n = ex.launch()
+        us, _ = time_launches(lambda: ex.launch, FOOTPRINT_BYTES, flush)
         key = "fused" if fuse else "two_launches"
-        row[key + "_us"] = round(ms * 1000, 2)
+        row[key + "_us"] = round(us, 2)
         row[key + "_launches"] = n
-        row[key + "_tflops"] = round(2.0 * 4096 * 8192 * 2048 / (ms * 1e-3) / 1e12, 2)
+        row[key + "_tflops"] = round(2.0 * 4096 * 8192 * 2048 / us / 1e6, 2)
         del ex
     out["F2_chain_mm_bias_relu_f16_4096x2048x8192"] = row
-    # K1 is launch-bound as one launch (16 MB): the same kernel replayed from a
-    # CUDA graph, back to back over 8 separate input/output pairs (256 MB in
-    # all, so every launch reads from HBM), amortises the launch
+    # K1 from a CUDA graph of 16 launches over separate input/output pairs
     kop, meta = synth.rmsnorm(4096, 512, eps=1e-6)
     plan = Lowerer(kop, meta).plan()
-    exs = [Executor(plan, device=device) for _ in range(8)]
+    exs = [Executor(plan, device=device) for _ in range(16)]
     for ex in exs:
         for t in ex.tensors.values():
             t.normal_()
@@ -408,38 +555,245 @@ def family_extras(device, peak):
     with torch.cuda.graph(graph):
         for ex in exs:
             ex.launch()
-    for _ in range(3):
-        graph.replay()
-    times = []
-    for _ in range(10):
-        flush()
-        torch.cuda._sleep(SPIN_CYCLES)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        graph.replay()
-        e1.record()
-        e1.synchronize()
-        times.append(e0.elapsed_time(e1))
-    ms = statistics.median(times) / len(exs)
-    gbs = plan_bytes(plan) / (ms * 1e-3) / 1e9
-    out["K1_rmsnorm_4096x512_graph8"] = {"us_per_launch": round(ms * 1000, 2), "gbs": round(gbs, 1),
-                                         "frac_hbm": round(gbs / peak, 3), "launches": len(exs)}
+    us, _ = time_launches(lambda: graph.replay, FOOTPRINT_BYTES, flush)
+    us /= len(exs)
+    nb = plan_bytes(plan)
+    out["K1_rmsnorm_4096x512_graph16"] = {"us_per_launch": round(us, 2),
+                                          "gbs": round(nb / us / 1e3, 1),
+                                          "launches": len(exs),
+                                          "roofline": roofline_block("K1_rmsnorm_4096x512", nb, 0,
+                                                                     us, None)}
     del graph, exs
     del flush
     torch.cuda.empty_cache()
     return out
 
 
+def splitk_across_gpus(world, rank, device, reps=10):
+    """K4a (256 x 65536 x 256 f32, 64 K partitions) split across the ranks.
+
+    Each rank multiplies its K slice (65536 / N, 64 / N partitions) into a full
+    partial C; then (a) the NCCL reduce-scatter leaves each rank its 256 / N
+    rows of C, or (b) the fused kernel stores each partial row straight into
+    its owner's slot over NVLink and the owner sums its slots.  Device times,
+    max over ranks, median of ``reps``.  The two forms' results are compared.
+    """
+    import ctypes
+    import torch
+    import torch.distributed as dist
+    from ptxc.dist import PeerRows, reduce_scatter_rows, shard_ranges, splitk_to_peers, sum_slots
+    from ptxc.launch import _check, _stream_handle, load_library
+    lib = load_library()
+    M, N, K = 256, 256, 65536
+    k0, k1 = shard_ranges(K, world)[rank]
+    kk = k1 - k0
+    splits = max(1, 64 // world)
+    g = torch.Generator(device=device).manual_seed(4242 + rank)
+    A = torch.rand(M, kk, device=device, generator=g) * 2 - 1
+    B = torch.rand(kk, N, device=device, generator=g) * 2 - 1
+    c_part = torch.empty(M, N, device=device)
+    flush = L2Flush(device)
+    st = torch.cuda.current_stream()
+
+    def gemm():
+        _check(lib.emmy_gemm_f32(ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(B.data_ptr()),
+                                 None, ctypes.c_void_p(c_part.data_ptr()), 1, M, N, kk, 0, 0, 0,
+                                 splits, 0, 0, _stream_handle(st)), "emmy_gemm_f32")
+
+    rows = None
+    for _ in range(3):
+        gemm()
+        rows = reduce_scatter_rows(c_part)
+    t_g, t_r, t_t = [], [], []
+    for _ in range(reps):
+        flush()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = _event_pair()
+        e2 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        gemm()
+        e1.record()
+        rows = reduce_scatter_rows(c_part)
+        e2.record()
+        e2.synchronize()
+        t_g.append(e0.elapsed_time(e1) * 1e3)
+        t_r.append(e1.elapsed_time(e2) * 1e3)
+        t_t.append(e0.elapsed_time(e2) * 1e3)
+    # fused: GEMM + scatter of partial rows over NVLink, then the slot sum
+    slots = torch.zeros(world, M // world, N, device=device)
+    peers = PeerRows(slots)
+    t_f, t_k, t_s = [], [], []
+    try:
+        mine = None
+        for i in range(3 + reps):
+            flush()
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = _event_pair()
+            e0.record()
+            splitk_to_peers(A, B, peers, M, N, splits=splits)
+            e1.record()
+            torch.cuda.synchronize()
+            dist.barrier()
+            e2, e3 = _event_pair()
+            e2.record()
+            mine = sum_slots(peers)
+            e3.record()
+            e3.synchronize()
+            if i >= 3:
+                t_k.append(e0.elapsed_time(e1) * 1e3)
+                t_s.append(e2.elapsed_time(e3) * 1e3)
+                t_f.append(t_k[-1] + t_s[-1])
+        diff = float((mine - rows).abs().max()) / max(float(rows.abs().max()), 1e-30)
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier()
+        peers.close()
+    med = torch.tensor([statistics.median(x) for x in (t_g, t_r, t_t, t_k, t_s, t_f)] + [diff],
+                       device=device, dtype=torch.float64)
+    dist.all_reduce(med, op=dist.ReduceOp.MAX)
+    v = [float(x) for x in med.tolist()]
+    flops = 2.0 * M * N * K
+    del flush
+    return {"config": f"{M}x{K}x{N} f32, K split over {world} GPUs ({splits} partitions per GPU)",
+            "gemm_us": round(v[0], 2), "reduce_scatter_us": round(v[1], 2),
+            "total_us": round(v[2], 2), "total_tflops": round(flops / v[2] / 1e6, 2),
+            "fused_kernel_us": round(v[3], 2), "fused_slot_sum_us": round(v[4], 2),
+            "fused_total_us": round(v[5], 2), "fused_tflops": round(flops / v[5] / 1e6, 2),
+            "forms_agree_max_rel": v[6],
+            "timing": "device events per rank, max over ranks, median of 10; L2 flushed"}
+
+
+# ------------------------------------------------------------------- the arms
+
+
+def run_reference_arm(args):
+    from ptxc import Lowerer
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return 0
+    threads = cpu_threads()
+    workload = k2_workload()
+    bufs = cpu_inputs(workload)
+    cpu_warm(workload, bufs, threads)
+    # one whole step untimed (first touch of the outputs), then the timed
+    # steps, capped so the arm ends within a few minutes on a slow host (the
+    # line reports the number actually timed)
+    _, first_s, desc = cpu_full_step(workload, bufs, threads)
+    steps = args.steps
+    budget_s = float(os.environ.get("EMMY_REFERENCE_BUDGET_S", "240"))
+    if first_s * steps > budget_s:
+        steps = max(1, int(budget_s // max(first_s, 1e-9)))
+    per_step = []
+    for _ in range(steps):
+        _, secs, desc = cpu_full_step(workload, bufs, threads)
+        per_step.append(secs)
+    total_s = sum(per_step)
+    step_bytes = sum(plan_bytes(Lowerer(k, m).plan()) for k, m in workload)
+    value = steps * step_bytes / total_s / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": steps, "steps_requested": args.steps, "warmup": 1,
+        "ms_per_step": round(1000 * total_s / steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded numpy inputs, BASELINE distributions)", "impl": "reference",
+        "config": {"workload": K2_WORKLOAD,
+                   "reference_path": "torch-CPU statement-level evaluation of the same IR "
+                                     "(oracle/interp.py) over every row of both IRs per step",
+                   "bytes_per_step": step_bytes},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": desc + " (the whole K2 step, every step)",
+                         "cpu_model": cpu_model()},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "torch_cpu_family_ops": torch_cpu_family_ops(threads),
+    }
+    if not args.no_families:
+        line["reference_ptx"] = reference_ptx_families()
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def reference_ptx_families():
+    """The reference compiler's own PTX (oracle/_ref, made by the unmodified
+    reference compiler) for each benchmark configuration, launched as the
+    reference harness launches it, timed on the GPU with the families' protocol."""
+    try:
+        import torch
+        if not torch.cuda.is_available():
+            return {"unavailable": "no GPU"}
+        from emmy_ir import synth
+        from oracle import ref_ptx
+        from oracle.make_ref_ptx import BENCH_CASES
+        from ptxc import Lowerer
+    except ImportError as e:
+        return {"unavailable": f"import failed: {e}"}
+    names = {"K1_rmsnorm": "K1_rmsnorm_4096x512", "K2a_softmax": "K2a_softmax_32x16x512x512",
+             "K2b_layernorm": "K2b_layernorm_16384x1024", "K4b_matvec_f64": "K4b_matvec_f64_16384",
+             "K4a_splitk_f32": "K4a_splitk_f32_256x65536x256",
+             "K3a_gemm_f16": "K3a_gemm_f16_4096x2048x8192_bias_relu",
+             "K3b_bmm_f16": "K3b_bmm_f16_64x512", "K5_attention_f16": "K5_attention_f16_8x32x512x128",
+             "F8a_pointwise_add": "F8a_pointwise_add_f32_2^26"}
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    flush = L2Flush(dev)
+    dts = {"f32": torch.float32, "f16": torch.float16, "f64": torch.float64}
+    out = {}
+    for name, make in BENCH_CASES.items():
+        if not ref_ptx.available(name):
+            continue
+        kop, meta = make(synth)
+        k = ref_ptx.RefKernel(name)
+        nbytes = sum((math.prod(a["shape"]) if a["shape"] else 1) *
+                     torch.empty((), dtype=dts[a["dtype"]]).element_size() for a in meta["args"])
+        # the harness zeroes these before every launch (atomic split-K outputs)
+        zero = k.k.get("zero_outputs") or []
+
+        def make_launch():
+            ts = {}
+            for a in meta["args"]:
+                n = math.prod(a["shape"]) if a["shape"] else 1
+                t = torch.empty(n, dtype=dts[a["dtype"]], device=dev)
+                if "data" in a:
+                    t.fill_(float(a["data"][0]))
+                elif a.get("output"):
+                    t.zero_()
+                else:
+                    t.normal_()
+                ts[a["name"]] = t
+            zs = [ts[z] for z in zero if z in ts]
+
+            def launch():
+                for z in zs:
+                    z.zero_()
+                k.launch(ts)
+            return launch
+        us, copies = time_launches(make_launch, nbytes, flush)
+        k.close()
+        row = {"us": round(us, 2), "gbs": round(nbytes / us / 1e3, 1),
+               "launches_per_sample": copies}
+        flops = plan_flops(Lowerer(kop, meta).plan())
+        if flops:
+            row["tflops"] = round(flops / us / 1e6, 2)
+        out[names.get(name, name)] = row
+        torch.cuda.empty_cache()
+    del flush
+    return out
+
+
 def run_b200_arm(args):
     import torch
     import torch.distributed as dist
-    from emmy_ir import synth
     from ptxc import Lowerer
+    from ptxc.dist import shard_plan
     from ptxc.launch import Executor, load_library
 
     world, rank, local = dist_setup()
     if world > 1:
         from datetime import timedelta
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
@@ -449,59 +803,65 @@ def run_b200_arm(args):
     load_library()
     peak, peak_src = hbm_peak()
 
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     workload = k2_workload()
-    plans = [Lowerer(k, m).plan() for k, m in workload]
-    step_bytes = sum(plan_bytes(p) for p in plans)
-    # inputs: seeded host arrays, pinned (they are also the e2e source)
+    full_plans = [Lowerer(k, m).plan() for k, m in workload]
+    total_bytes = sum(plan_bytes(p) for p in full_plans)
+    # this rank's rows of each IR (the whole plan at N = 1)
+    shards = [shard_plan(p, rank, world) for p in full_plans]
+    plans = [s for s, _ in shards]
+    my_bytes = sum(plan_bytes(p) for p in plans)
     hosts = []
-    for (kop, meta) in workload:
-        h = synth.make_inputs(meta, seed_offset=rank * 1000)
-        pinned = {}
-        for k, v in h.items():
-            t = torch.from_numpy(v).pin_memory()
-            pinned[k] = t
-        hosts.append(pinned)
+    for (kop, meta), (_, slices) in zip(workload, shards):
+        h = shard_inputs(meta, slices, rank, world)
+        hosts.append({k: torch.from_numpy(v).pin_memory() for k, v in h.items()})
     execs = [Executor(p, device=device) for p in plans]
     for ex, h in zip(execs, hosts):
         ex.upload(h)
     torch.cuda.synchronize()
     flush = L2Flush(device)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
+    def timed_steps(exs, steps):
+        """(total ms, softmax-launch ms per step, launches) over ``steps`` steps."""
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+               torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        launches = 0
+        for i in range(steps):
+            flush()                         # L2 flush between steps (outside the events)
+            torch.cuda._sleep(SPIN_CYCLES)
+            e0, e1, e2 = ev[i]
+            e0.record()
+            launches += exs[0].launch()     # softmax (dominant kernel)
+            e1.record()
+            launches += exs[1].launch()     # layernorm
+            e2.record()
+        torch.cuda.synchronize()
+        total = sum(a.elapsed_time(c) for a, b, c in ev)
+        return total, [a.elapsed_time(b) for a, b, c in ev], launches
 
-    # ---- device-resident timing
+    # ---- device-resident timing: this rank's partition (the headline)
     for _ in range(args.warmup):
         for ex in execs:
             ex.launch()
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    launches = 0
     clocks = ClockSampler(device.index).__enter__()
-    for i in range(args.steps):
-        flush()                             # L2 flush between steps (outside the events)
-        torch.cuda._sleep(SPIN_CYCLES)
-        e0, e1, e2 = ev[i]
-        e0.record()
-        launches += execs[0].launch()       # softmax (dominant kernel)
-        e1.record()
-        launches += execs[1].launch()       # layernorm
-        e2.record()
-    torch.cuda.synchronize()
+    total_ms, sm_ms, launches = timed_steps(execs, args.steps)
     barrier()
     torch.cuda.synchronize()
-    step_ms = [a.elapsed_time(c) for a, b, c in ev]
-    sm_ms = [a.elapsed_time(b) for a, b, c in ev]
-    total_ms = sum(step_ms)
-    if world > 1:
-        t = torch.tensor([total_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
-    value = world * args.steps * step_bytes / (total_ms * 1e-3) / 1e9
+    total_ms = max_over_ranks(total_ms)
+    value = args.steps * total_bytes / (total_ms * 1e-3) / 1e9
     sm_bytes = plan_bytes(plans[0])
     sm_avg = statistics.mean(sm_ms)
     achieved = sm_bytes / (sm_avg * 1e-3) / 1e9
@@ -522,8 +882,7 @@ def run_b200_arm(args):
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(args.steps)]
+    e2e_ev = [_event_pair() for _ in range(args.steps)]
     for i in range(args.steps):
         a, b = e2e_ev[i]
         a.record()
@@ -532,29 +891,58 @@ def run_b200_arm(args):
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    clocks.__exit__(None, None, None)
-    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = world * args.steps * step_bytes / (e2e_ms * 1e-3) / 1e9
+    e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in e2e_ev))
+    e2e_value = args.steps * total_bytes / (e2e_ms * 1e-3) / 1e9
     # spot check the e2e outputs against the device results of the same step
     for ex, o in zip(execs, outs):
         for name, t in o.items():
             assert torch.equal(t, ex.tensors[name].cpu()), "e2e output mismatch"
-
+    # bytes per step over all ranks (each rank copies its own shard)
+    h2d_all = int(round(max_over_ranks(h2d) * world)) if world > 1 else h2d
+    d2h_all = int(round(max_over_ranks(d2h) * world)) if world > 1 else d2h
     execs.clear()
+
+    # ---- weak scaling key (N > 1): every rank on a full K2 batch
+    weak = None
+    if world > 1:
+        wexecs = []
+        for (kop, meta), p in zip(workload, full_plans):
+            ex = Executor(p, device=device)
+            for t in ex.tensors.values():
+                t.normal_()
+            for a in meta["args"]:
+                if "data" in a:
+                    ex.tensors[a["name"]].fill_(float(a["data"][0]))
+            wexecs.append(ex)
+        for _ in range(args.warmup):
+            for ex in wexecs:
+                ex.launch()
+        torch.cuda.synchronize()
+        barrier()
+        wms, _, _ = timed_steps(wexecs, args.steps)
+        barrier()
+        wms = max_over_ranks(wms)
+        weak = {"value": round(world * args.steps * total_bytes / (wms * 1e-3) / 1e9, 2),
+                "unit": UNIT, "ms_per_step": round(wms / args.steps, 4),
+                "per_rank": "each rank runs one full K2 batch per step"}
+        wexecs.clear()
+    clocks.__exit__(None, None, None)
     del flush
     torch.cuda.empty_cache()
-    extras = family_extras(device, peak) if (rank == 0 and not args.no_families) else None
+
+    splitk = splitk_across_gpus(world, rank, device) if world > 1 else None
+    extras = family_extras(device) if (world == 1 and not args.no_families) else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
+        # the same measurement as the reference arm: one whole K2 step of the
+        # torch-CPU IR evaluation (every row), after a warm-up on a few rows
+        threads = cpu_threads()
         bufs = cpu_inputs(workload, hosts)
-        gbs, desc, cores, secs, _ = cpu_sample_rate(workload, bufs, 6.0, os.cpu_count() or 1)
-        cpu = {"value": round(gbs, 4), "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": desc + f" (torch-CPU IR evaluation, {secs:.1f} s)"}
+        cpu_warm(workload, bufs, threads)
+        gbs, secs, desc = cpu_full_step(workload, bufs, threads)
+        cpu = {"value": round(gbs, 4), "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": desc + f" (one whole K2 step, {secs:.1f} s)", "cpu_model": cpu_model()}
 
     if world > 1:
         dist.barrier()
@@ -565,29 +953,36 @@ def run_b200_arm(args):
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total_ms / args.steps, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded numpy inputs, BASELINE distributions)",
         "config": {
-            "workload": "K2: softmax f32 [32,16,512,512] dim=-1 + layernorm f32 affine [16384,1024]",
-            "per_rank": "each rank runs one full K2 batch per step",
-            "bytes_per_step_per_rank": step_bytes,
-            "l2": "flushed between steps (256 MiB device write outside the timed events)",
+            "workload": K2_WORKLOAD,
+            "parallelism": f"rows partitioned over {world} GPU(s) (ptxc.dist.shard_plan), "
+                           "no collective on the data path",
+            "bytes_per_step": total_bytes,
+            "bytes_per_step_rank0": my_bytes,
+            "l2": "flushed between steps (256 MiB device write + read outside the timed events)",
             "ir": "synthesised Kernel IR in the reference fixtures' reduction shapes",
         },
-        "roofline": {"bound": "hbm", "kernel": "emmy softmax (row_resident_kernel, 4x32x4)",
+        "roofline": {"bound": "hbm", "kernel": "emmy softmax (row_resident_kernel)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": UNIT,
                      "frac": round(achieved / peak, 4),
-                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
-                     else "fallback 6.65 TB/s",
+                     "peak_source": (f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)"
+                                     if peak_src == "measured" else "fallback 6.65 TB/s"),
                      "bytes_per_launch": sm_bytes, "avg_launch_us": round(sm_avg * 1000, 2),
-                     "traffic": profile_traffic("softmax_f32_K2a.md")},
-        "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h,
-                "path": ("ptxc.launch.Executor.run_pipelined: pinned host inputs -> H2D / C-ABI kernels / "
-                         "D2H overlapped per ~32 MiB chunk on three streams -> pinned host outputs")},
+                     "traffic": (profile_traffic("softmax_f32_K2a.md") if world == 1 else None)},
+        "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d_all,
+                "d2h_bytes_per_step": d2h_all,
+                "path": ("ptxc.launch.Executor.run_pipelined: pinned host inputs -> H2D / C-ABI "
+                         "kernels / D2H overlapped per ~32 MiB chunk on three streams -> pinned "
+                         "host outputs")},
         "gpu_launches": launches,
         "clocks": clocks.summary(),
     }
+    if weak:
+        line["weak"] = weak
+    if splitk:
+        line["splitk_across_gpus"] = splitk
     if cpu:
         line["cpu_baseline"] = cpu
     if extras:
@@ -597,19 +992,25 @@ def run_b200_arm(args):
 
 
 PROFILE_CASES = {
-    # name: (builder, launches) -- small cases (inputs above L2, a few hundred MB at most)
+    # name: builder -- small cases (inputs above L2, a few hundred MB at most)
     # for one-kernel ncu captures: `python bench.py --case softmax_65536x512`
     "softmax_65536x512": lambda s: s.softmax([65536, 512], x_init={"dist": "normal", "std": 2.0}),
     "softmax_K2a": lambda s: s.softmax([32, 16, 512, 512], x_init={"dist": "normal", "std": 2.0}),
     "layernorm_16384x1024": lambda s: s.layernorm(16384, 1024),
     "rmsnorm_65536x512": lambda s: s.rmsnorm(65536, 512, eps=1e-6),
     "matvec_f64_8192x4096": lambda s: s.matvec(8192, 4096),
+    "matvec_f64_K4b": lambda s: s.matvec(16384, 16384),
     "gemm_f16_K3a": lambda s: s.matmul(4096, 8192, 2048, dtype="f16", out_dtype="f16", bias=True,
                                        relu=True, tm=128, tn=128, rm=8, rn=8),
     "gemm_f16_2048": lambda s: s.matmul(2048, 2048, 2048, dtype="f16", out_dtype="f16",
                                         tm=128, tn=128, rm=8, rn=8),
     "attention_f16_K5": lambda s: s.attention(8, 32, 512, 128, dtype="f16"),
-    "gemm_f32_splitk_K4a": lambda s: s.matmul(256, 256, 65536, splits=64, tm=128, tn=128, rm=8, rn=8),
+    "attention_f16_D256": lambda s: s.attention(8, 32, 512, 256, dtype="f16"),
+    "attention_f16_D16": lambda s: s.attention(8, 32, 512, 16, dtype="f16"),
+    "attention_f16_D32": lambda s: s.attention(8, 32, 512, 32, dtype="f16"),
+    "attention_f16_D96": lambda s: s.attention(8, 32, 512, 96, dtype="f16"),
+    "gemm_f32_splitk_K4a": lambda s: s.matmul(256, 256, 65536, splits=64, tm=128, tn=128, rm=8,
+                                              rn=8),
     "pointwise_add_2^26": lambda s: s.pointwise(1 << 26, ("add", "x0", "x1"), "f32"),
     "bmm_f16_K3b": lambda s: s.matmul(512, 512, 512, batch=64, dtype="f16", out_dtype="f16",
                                       tm=128, tn=128, rm=8, rn=8),
@@ -654,9 +1055,16 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-families", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--families-only", nargs="*", default=None,
+                    help="time only the family configurations whose name contains one of these")
     args = ap.parse_args()
     if args.case:
         return run_case(args.case, args.launches)
+    if args.families_only is not None:
+        import torch
+        torch.cuda.set_device(0)
+        print(json.dumps(family_extras(torch.device("cuda", 0), only=args.families_only or None)))
+        return 0
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3
     if args.impl == "reference":
