@@ -56,8 +56,16 @@ namespace emmy {
 // at 57% of it) -- one CTA fills an SM's tensor memory either way.  D <= 128:
 // 64-key blocks and two CTAs per SM (128-key blocks would cost the second CTA:
 // measured slower).
-template <int D, int BN_, int HALVES_>
+// DQ: the head dims the score product covers (K16 steps), a multiple of 16
+// and at most D.  A head dim d below D runs the kernel of the next supported
+// width: the tensor maps carry the real d, so TMA fills the columns d..D-1 of
+// every Q, K and V box with zeros (they add nothing to the scores, and the O
+// columns they produce are never stored), and the score product issues only
+// ceil(d / 16) K16 steps.
+template <int D, int BN_, int HALVES_, int DQ_ = D>
 struct AttnCfg {
+  static constexpr int DQ = DQ_;                     // head dims the score product reads
+  static constexpr int KSTEPS = DQ / 16;             // K16 steps of the score product
   static constexpr int BN = BN_;                     // keys per block
   static constexpr int HALVES = HALVES_;             // softmax warps per lane quadrant
   static constexpr int CPT = BN / HALVES;            // score columns per softmax thread
@@ -85,6 +93,7 @@ struct AttnCfg {
   static constexpr int MIN_BLOCKS = 2 * BN + D <= 256 ? 2 : 1;   // two CTAs per SM when TMEM allows
   static constexpr float RESCALE_LOG2 = 8.0f;        // lazy max threshold (P <= 2^8)
   static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(DQ % 16 == 0 && DQ > 0 && DQ <= D, "score product width");
   static_assert(O_COL + D <= 512, "tensor memory");
 };
 
@@ -124,15 +133,16 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-template <int D, int BN_, int HALVES_>
-__global__ void __launch_bounds__(AttnCfg<D, BN_, HALVES_>::THREADS, AttnCfg<D, BN_, HALVES_>::MIN_BLOCKS)
+template <int D, int BN_, int HALVES_, int DQ_>
+__global__ void __launch_bounds__(AttnCfg<D, BN_, HALVES_, DQ_>::THREADS,
+                                  AttnCfg<D, BN_, HALVES_, DQ_>::MIN_BLOCKS)
 attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV,
                         const __grid_constant__ CUtensorMap tmO,
-                        const float *__restrict__ scale_div, int S, int ntiles, int out_f16,
-                        int *status) {
-  using C = AttnCfg<D, BN_, HALVES_>;
+                        const float *__restrict__ scale_div, int S, int dv, int ntiles,
+                        int out_f16, int *status) {
+  using C = AttnCfg<D, BN_, HALVES_, DQ_>;
   constexpr bool SPLIT = C::HALVES > 1;              // two softmax warps per row
   constexpr int BN = C::BN;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -249,11 +259,11 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         // S[g % 2] = Q K^T: both operands K-major (head dim contiguous)
         const uint64_t dk = sw128_desc(ka, 16, 1024);
 #pragma unroll
-        for (int kb = 0; kb < C::NKB; ++kb)
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_f16(tmem + C::S_COL0 + (g & 1) * BN, dq + ((kb * C::Q_BOX + kk * 32) >> 4),
-                    dk + ((kb * C::K_BOX + kk * 32) >> 4), idesc_s, (kb | kk) != 0 ? 1u : 0u);
+        for (int ks = 0; ks < C::KSTEPS; ++ks) {
+          const int kb = ks / 4, kk = ks % 4;
+          mma_f16(tmem + C::S_COL0 + (g & 1) * BN, dq + ((kb * C::Q_BOX + kk * 32) >> 4),
+                  dk + ((kb * C::K_BOX + kk * 32) >> 4), idesc_s, ks != 0 ? 1u : 0u);
+        }
         mma_commit(&s_full[g & 1]);
       };
       // Q, K and V come from TMA: their barriers need no tcgen05 fence; P and
@@ -445,8 +455,11 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       tc_fence_after();
       const float rl = 1.0f / l;
       const int step = out_f16 ? 64 : 32;               // columns per 128-byte row piece
+      // pieces that hold real output columns (c < dv); TMA clips the last one
+      const int c_top = (dv + step - 1) / step * step;
+      const int c_end = (half + 1) * OCOLS < c_top ? (half + 1) * OCOLS : c_top;
 #pragma unroll 1
-      for (int c0 = half * OCOLS; c0 < (half + 1) * OCOLS; c0 += step) {
+      for (int c0 = half * OCOLS; c0 < c_end; c0 += step) {
         uint4 w[8];
         if (out_f16) {
           float v[64];
@@ -469,7 +482,7 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
             w[q] = make_uint4(__float_as_uint(v[4 * q] * rl), __float_as_uint(v[4 * q + 1] * rl),
                               __float_as_uint(v[4 * q + 2] * rl), __float_as_uint(v[4 * q + 3] * rl));
         }
-        if (c0 + step >= (half + 1) * OCOLS) {
+        if (c0 + step >= c_end) {
           tc_fence_before();
           mbar_arrive(o_free);                          // O fully read out of TMEM
         }
@@ -561,14 +574,16 @@ attention_f16_simt_kernel(const __half *__restrict__ q, const __half *__restrict
 
 namespace {
 
-template <int D, int BN, int HALVES>
+// d: the real head dim (a multiple of 8, at most D); the maps carry it, so
+// boxes reaching past it are zero-filled on load and clipped on store.
+template <int D, int BN, int HALVES, int DQ>
 int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
-                        const float *scale_div, int64_t batch, int64_t S, int out_f16,
-                        cudaStream_t st) {
-  using Cfg = AttnCfg<D, BN, HALVES>;
+                        const float *scale_div, int64_t batch, int64_t S, int64_t d,
+                        int out_f16, cudaStream_t st) {
+  using Cfg = AttnCfg<D, BN, HALVES, DQ>;
   CUtensorMap tq, tk, tv;
-  const uint64_t dims[3] = {(uint64_t)D, (uint64_t)S, (uint64_t)batch};
-  const uint64_t str[2] = {(uint64_t)D * 2, (uint64_t)S * D * 2};
+  const uint64_t dims[3] = {(uint64_t)d, (uint64_t)S, (uint64_t)batch};
+  const uint64_t str[2] = {(uint64_t)d * 2, (uint64_t)S * d * 2};
   const uint32_t qbox[3] = {64, 128, 1};
   const uint32_t kbox[3] = {64, Cfg::BN, 1};
   int rc = make_tensor_map(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, q, dims, str, qbox,
@@ -580,7 +595,7 @@ int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
   // O written by TMA stores of STAGE_ROWS-row x 128-byte boxes
   CUtensorMap to;
   const uint64_t esize = out_f16 ? 2 : 4;
-  const uint64_t ostr[2] = {(uint64_t)D * esize, (uint64_t)S * D * esize};
+  const uint64_t ostr[2] = {(uint64_t)d * esize, (uint64_t)S * d * esize};
   const uint32_t obox[3] = {(uint32_t)(128 / esize), (uint32_t)Cfg::STAGE_ROWS, 1};
   if (!rc) rc = make_tensor_map(&to, out_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
@@ -590,7 +605,7 @@ int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaFuncSetAttribute(attention_f16_tc_kernel<D, BN, HALVES>,
+    cudaFuncSetAttribute(attention_f16_tc_kernel<D, BN, HALVES, DQ>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     attr_set[dev] = true;
   }
@@ -599,8 +614,8 @@ int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
   if (ntiles > INT32_MAX) return set_error(EMMY_ERR_INVALID, "emmy_attention_f16: too many query tiles");
   const int64_t slots = (int64_t)Cfg::MIN_BLOCKS * sm_count();
   const unsigned grid = (unsigned)(ntiles < slots ? ntiles : slots);
-  attention_f16_tc_kernel<D, BN, HALVES><<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(
-      tq, tk, tv, to, scale_div, (int)S, (int)ntiles, out_f16, device_status_ptr());
+  attention_f16_tc_kernel<D, BN, HALVES, DQ><<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(
+      tq, tk, tv, to, scale_div, (int)S, (int)d, (int)ntiles, out_f16, device_status_ptr());
   return check_launch("emmy_attention_f16 (tcgen05)");
 }
 
@@ -625,20 +640,31 @@ extern "C" int emmy_attention_f16(const void *q, const void *k, const void *v, v
     return set_error(EMMY_ERR_UNSUPPORTED, "emmy_attention_f16: grid too large");
   cudaStream_t st = as_stream(stream);
   const int out_f16 = out_dtype == EMMY_DT_F16;
+  // the tensor-core kernel: any head dim that is a multiple of 8 (16-byte rows
+  // for TMA) up to 256, run by the kernel of the next width in {64, 128, 256}
   const bool tc = !k_transposed && sq == sk && aligned16(q) && aligned16(k) && aligned16(v) &&
-                  aligned16(o) && (d == 64 || d == 128 || d == 256);
+                  aligned16(o) && d % 8 == 0 && d <= 256;
   if (tc) {
     // D = 256: 128-key blocks once there is more than one 64-key block.
     // (D = 128 with two softmax warps per row, 32 scores each, at two CTAs per
     // SM was measured slower: the per-block max exchange costs more than the
     // halved softmax work saves.)
-    if (d == 64)
-      return launch_attention_tc<64, 64, 1>(q, k, v, o, scale_div, batch, sq, out_f16, st);
-    if (d == 128)
-      return launch_attention_tc<128, 64, 1>(q, k, v, o, scale_div, batch, sq, out_f16, st);
+    if (d <= 16)
+      return launch_attention_tc<64, 64, 1, 16>(q, k, v, o, scale_div, batch, sq, d, out_f16, st);
+    if (d <= 32)
+      return launch_attention_tc<64, 64, 1, 32>(q, k, v, o, scale_div, batch, sq, d, out_f16, st);
+    if (d <= 64)
+      return launch_attention_tc<64, 64, 1, 64>(q, k, v, o, scale_div, batch, sq, d, out_f16, st);
+    if (d <= 96)
+      return launch_attention_tc<128, 64, 1, 96>(q, k, v, o, scale_div, batch, sq, d, out_f16,
+                                                 st);
+    if (d <= 128)
+      return launch_attention_tc<128, 64, 1, 128>(q, k, v, o, scale_div, batch, sq, d, out_f16,
+                                                  st);
     if (sq > 64)
-      return launch_attention_tc<256, 128, 2>(q, k, v, o, scale_div, batch, sq, out_f16, st);
-    return launch_attention_tc<256, 64, 1>(q, k, v, o, scale_div, batch, sq, out_f16, st);
+      return launch_attention_tc<256, 128, 2, 256>(q, k, v, o, scale_div, batch, sq, d, out_f16,
+                                                   st);
+    return launch_attention_tc<256, 64, 1, 256>(q, k, v, o, scale_div, batch, sq, d, out_f16, st);
   }
   // head dims up to 96: one thread per query row (any key count)
   const int rc = launch_attention_rows(q, k, v, o, scale_div, batch, sq, sk, d, d, 1, out_f16,

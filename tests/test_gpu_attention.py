@@ -65,8 +65,18 @@ F16_CASES = [
     ("K5_2x4x512x128_f32out", dict(B=2, H=4, S=512, D=128, out_dtype="f32")),
 ] + [
     (f"sweep_S{S}_D{D}", dict(B=2, H=4, S=S, D=D, out_dtype="f16"))
-    for D in (16, 64, 256) for S in (16, 128, 512)
+    for D in (16, 32, 64, 96, 256) for S in (16, 128, 512)
 ] + [
+    # head dims run by the next-wider tensor-core kernel (TMA zero-fills the
+    # columns past d): multiples of 8 that are not multiples of 16, d between
+    # the widths, f32 output, ragged key counts
+    ("d24_S130_f32out", dict(B=2, H=3, S=130, D=24, out_dtype="f32")),
+    ("d48_S200", dict(B=1, H=5, S=200, D=48, out_dtype="f16")),
+    ("d96_S512_f32out", dict(B=2, H=4, S=512, D=96, out_dtype="f32")),
+    ("d104_S77", dict(B=3, H=2, S=77, D=104, out_dtype="f16")),
+    ("d200_S256", dict(B=1, H=4, S=256, D=200, out_dtype="f16")),
+    ("d16_tiles_x600", dict(B=6, H=100, S=256, D=16, out_dtype="f16")),
+
     ("ragged_S200_D64", dict(B=1, H=3, S=200, D=64, out_dtype="f32")),
     # more query tiles than resident CTAs: each persistent CTA walks several
     ("tiles_S200_D64_x1200", dict(B=6, H=100, S=200, D=64, out_dtype="f32")),
