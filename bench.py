@@ -69,9 +69,14 @@ L2_FLUSH_BYTES = 256 << 20
 # (the per-launch time is the pass over all copies divided by their number).
 FOOTPRINT_BYTES = 256 << 20
 MAX_COPIES = 64
-# A short device spin queued before each timed region keeps the GPU busy while
-# the host enqueues the launches, so the CUDA events bracket device work only.
+# A device spin queued before each timed region keeps the GPU busy while the
+# host enqueues the launches, so the CUDA events bracket device work only.  A
+# launch through ctypes takes the host several microseconds, longer than a
+# small kernel runs, so a timed pass of many launches spins SPIN_PER_LAUNCH
+# cycles more per launch (~15 us at 1.965 GHz): every launch is queued before
+# the start event fires and the kernels run back to back.
 SPIN_CYCLES = 200_000
+SPIN_PER_LAUNCH = 30_000
 
 # ncu summary (profiles/) holding each configuration's dram bytes per launch
 PROFILE_OF = {
@@ -383,7 +388,8 @@ def time_launches(make_launch, nbytes, flush, reps=10, warmup=3):
     per launch, ``copies`` such copies are launched back to back between the
     events and the time divided by their number, so every launch reads from
     HBM and the 1 us event resolution is spread over many launches.  L2 is
-    flushed before each timed pass.  Returns (median us per launch, copies).
+    flushed before each timed pass, and the device spin before it lasts until
+    every launch of the pass is queued.  Returns (median us per launch, copies).
     """
     import torch
     copies = 1 if nbytes >= FOOTPRINT_BYTES else min(MAX_COPIES,
@@ -395,7 +401,7 @@ def time_launches(make_launch, nbytes, flush, reps=10, warmup=3):
     samples = []
     for _ in range(reps):
         flush()
-        torch.cuda._sleep(SPIN_CYCLES)
+        torch.cuda._sleep(SPIN_CYCLES + SPIN_PER_LAUNCH * copies)
         e0, e1 = _event_pair()
         e0.record()
         for f in fns:
