@@ -62,8 +62,14 @@ namespace emmy {
 // every Q, K and V box with zeros (they add nothing to the scores, and the O
 // columns they produce are never stored), and the score product issues only
 // ceil(d / 16) K16 steps.
-template <int D, int BN_, int HALVES_, int DQ_ = D>
+// POLY8: of every 8 score pairs a softmax thread exponentiates, how many go
+// through the FMA-pipe polynomial (exp2_poly2) instead of MUFU ex2 (the MUFU
+// unit runs 16 exponentials per SM per clock, the FMA pipe 128 fused
+// multiply-adds, so sharing the work shortens the exponent phase).
+// SLOTS_: depth of the K/V ring (0: the default below).
+template <int D, int BN_, int HALVES_, int DQ_ = D, int POLY8_ = 3, int SLOTS_ = 0>
 struct AttnCfg {
+  static constexpr int POLY8 = POLY8_;               // pairs of 8 on the FMA-pipe exp2
   static constexpr int DQ = DQ_;                     // head dims the score product reads
   static constexpr int KSTEPS = DQ / 16;             // K16 steps of the score product
   static constexpr int BN = BN_;                     // keys per block
@@ -75,22 +81,30 @@ struct AttnCfg {
   static constexpr int K_BOX = BN * 128;             // [BN keys][128 B]
   static constexpr int Q_BYTES = NKB * Q_BOX;
   static constexpr int SLOT_BYTES = NKB * K_BOX;     // one K or V block
-  static constexpr int SLOTS = BN == 128 ? 2 : 3;
-  // epilogue staging: one STAGE_ROWS-row x 128-byte box per softmax warp
-  static constexpr int STAGE_ROWS = HALVES > 1 ? 16 : 32;
+  static constexpr int SLOTS = SLOTS_ ? SLOTS_ : (BN == 128 ? 2 : 3);
+  // epilogue staging: one STAGE_ROWS-row x 128-byte box per softmax warp (16
+  // rows where 32 would not leave two CTAs room for Q and the ring)
+  static constexpr int STAGE_ROWS =
+      HALVES > 1 || (Q_BYTES + SLOTS * SLOT_BYTES > 96 * 1024) ? 16 : 32;
   static constexpr int STAGE_BYTES = SM_WARPS * STAGE_ROWS * 128;
   // Q | ring slots | epilogue staging | half-row exchange, then the mbarriers
   static constexpr int STAGE_OFF = Q_BYTES + SLOTS * SLOT_BYTES;
   static constexpr int XCH_OFF = STAGE_OFF + STAGE_BYTES;
   static constexpr int XCH_BYTES = HALVES > 1 ? 3 * 2 * 128 * 4 : 0;   // max [2][2][128], sum [2][128]
   static constexpr int BAR_OFF = XCH_OFF + XCH_BYTES;
-  static constexpr int SMEM = BAR_OFF + 256 + 1024;
-  static constexpr uint32_t S_COL0 = 0;              // score buffers at columns 0 and BN
-  static constexpr uint32_t O_COL = 2 * BN;
+  // mbarriers: 12 fixed, full / empty per slot, 12 for the half-row
+  // exchange, then the TMEM address word
+  static constexpr int BAR_BYTES = ((12 + 2 * SLOTS + 12) * 8 + 8 + 63) / 64 * 64;
+  static constexpr int SMEM = BAR_OFF + BAR_BYTES + 1024;
+  // score buffers: three when they and O fit two CTAs' tensor memory (then
+  // S runs two blocks ahead of the softmax), else two
+  static constexpr int NSB = (HALVES == 1 && 3 * BN + D <= 256) ? 3 : 2;
+  static constexpr uint32_t S_COL0 = 0;              // score buffer b at column b * BN
+  static constexpr uint32_t O_COL = NSB * BN;
   static constexpr uint32_t TMEM_COLS = O_COL + D <= 256 ? 256 : 512;
   static constexpr int PRODUCER_WARP = SM_WARPS, MMA_WARP = SM_WARPS + 1;
   static constexpr int THREADS = 32 * (SM_WARPS + 2);
-  static constexpr int MIN_BLOCKS = 2 * BN + D <= 256 ? 2 : 1;   // two CTAs per SM when TMEM allows
+  static constexpr int MIN_BLOCKS = NSB * BN + D <= 256 ? 2 : 1;   // two CTAs per SM when TMEM allows
   static constexpr float RESCALE_LOG2 = 8.0f;        // lazy max threshold (P <= 2^8)
   static_assert(SMEM <= 227 * 1024, "shared memory");
   static_assert(DQ % 16 == 0 && DQ > 0 && DQ <= D, "score product width");
@@ -133,16 +147,87 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-template <int D, int BN_, int HALVES_, int DQ_>
-__global__ void __launch_bounds__(AttnCfg<D, BN_, HALVES_, DQ_>::THREADS,
-                                  AttnCfg<D, BN_, HALVES_, DQ_>::MIN_BLOCKS)
+// Packed pairs of f32 (sm_100 add / sub / fma .f32x2: two lanes per
+// instruction, each rounded as its scalar form).
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t r, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// the f16x2 of a pair (lo in the low half, as __floats2half2_rn(lo, hi))
+__device__ __forceinline__ uint32_t f16x2_of(uint64_t p) {
+  float lo, hi;
+  unpack2(p, lo, hi);
+  uint32_t h;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
+  return h;
+}
+
+// 2^t for a pair, on the FMA pipe.  Range reduction: t = j + f with j the
+// nearest integer (the sum with 1.5 * 2^23 leaves j in the low mantissa bits of
+// r) and f = t - j in [-1/2, 1/2], exact; 2^f by a degree-4 polynomial fitted
+// here for least maximum relative error on [-1/2, 1/2] (Lawson-weighted least
+// squares on Chebyshev nodes; 2.7e-6 relative error in this f32 Horner form,
+// against the 2^-12 of the f16 rounding P gets next); 2^j is added into the
+// exponent field, (bits(r) << 23) being j << 23.  t is clamped to -125 first so
+// the exponent stays normal: a key far below the row max (or masked, t = -inf)
+// gets 2^-125 instead of 0, which the f16 P rounds to 0 and the f32 row sum
+// does not see.
+struct Exp2Poly {
+  uint64_t magic, c0, c1, c2, c3, c4;
+  __device__ __forceinline__ Exp2Poly()
+      : magic(pack2(0x1.8p23f, 0x1.8p23f)),
+        c0(pack2(0x1.ffffe8p-1f, 0x1.ffffe8p-1f)),
+        c1(pack2(0x1.62e0dcp-1f, 0x1.62e0dcp-1f)),
+        c2(pack2(0x1.ec06dap-3f, 0x1.ec06dap-3f)),
+        c3(pack2(0x1.ca1440p-5f, 0x1.ca1440p-5f)),
+        c4(pack2(0x1.3997d4p-7f, 0x1.3997d4p-7f)) {}
+  __device__ __forceinline__ uint64_t operator()(uint64_t t2) const {
+    float a, b;
+    unpack2(t2, a, b);
+    const uint64_t x = pack2(fmaxf(a, -125.0f), fmaxf(b, -125.0f));
+    const uint64_t r = add2(x, magic);
+    const uint64_t f = sub2(x, sub2(r, magic));
+    uint64_t p = fma2(c4, f, c3);
+    p = fma2(p, f, c2);
+    p = fma2(p, f, c1);
+    p = fma2(p, f, c0);
+    float pa, pb, ra, rb;
+    unpack2(p, pa, pb);
+    unpack2(r, ra, rb);
+    return pack2(__int_as_float(__float_as_int(pa) + (__float_as_int(ra) << 23)),
+                 __int_as_float(__float_as_int(pb) + (__float_as_int(rb) << 23)));
+  }
+};
+
+template <int D, int BN_, int HALVES_, int DQ_, int POLY8_, int SLOTS_>
+__global__ void __launch_bounds__(AttnCfg<D, BN_, HALVES_, DQ_, POLY8_, SLOTS_>::THREADS,
+                                  AttnCfg<D, BN_, HALVES_, DQ_, POLY8_, SLOTS_>::MIN_BLOCKS)
 attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV,
                         const __grid_constant__ CUtensorMap tmO,
                         const float *__restrict__ scale_div, int S, int dv, int ntiles,
                         int out_f16, int *status) {
-  using C = AttnCfg<D, BN_, HALVES_, DQ_>;
+  using C = AttnCfg<D, BN_, HALVES_, DQ_, POLY8_, SLOTS_>;
   constexpr bool SPLIT = C::HALVES > 1;              // two softmax warps per row
   constexpr int BN = C::BN;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -153,14 +238,18 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
   // per tile: q_full (Q landed), o_done (the tile's last P V product is
   // done), o_free (the epilogue has read O); per block: s_full / p_full
-  // [g % 2], o_full
-  uint64_t *q_full = bars + 0, *o_done = bars + 2, *o_free = bars + 3;
-  uint64_t *o_full = bars + 4, *mma_done = bars + 5;
-  uint64_t *s_full = bars + 6, *p_full = bars + 8;   // [2] each
-  uint64_t *full = bars + 10, *empty = bars + 10 + C::SLOTS;   // [SLOTS] each
+  // [g % NSB] (score buffer g % NSB holds S, then P), o_full [g % 2] (P V
+  // product g done: two barriers, so with S two blocks ahead a wait for
+  // product g - 1 is never two phases behind its barrier)
+  constexpr int NSB = C::NSB;
+  uint64_t *q_full = bars + 0, *o_done = bars + 1, *o_free = bars + 2, *mma_done = bars + 3;
+  uint64_t *o_full = bars + 4;                       // [2]
+  uint64_t *s_full = bars + 6, *p_full = bars + 9;   // [NSB] each (3 reserved)
+  uint64_t *full = bars + 12, *empty = bars + 12 + C::SLOTS;   // [SLOTS] each
   // SPLIT: half-row exchange, per lane quadrant: block max [g % 2], tile sum
-  uint64_t *xmax = bars + 10 + 2 * C::SLOTS, *xsum = xmax + 8;   // [4][2], [4]
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 10 + 2 * C::SLOTS + 12);
+  uint64_t *xmax = bars + 12 + 2 * C::SLOTS, *xsum = xmax + 8;   // [4][2], [4]
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 12 + 2 * C::SLOTS + 12);
+  static_assert(NSB == 2 || !SPLIT, "the half-row exchange assumes two score buffers");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nblk = (S + BN - 1) / BN;
@@ -176,9 +265,10 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     mbar_init(q_full, 1);
     mbar_init(o_done, 1);
     mbar_init(o_free, 32 * C::SM_WARPS);
-    mbar_init(o_full, 1);
+    mbar_init(&o_full[0], 1);
+    mbar_init(&o_full[1], 1);
     mbar_init(mma_done, 1);
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NSB; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&p_full[b], 32 * C::SM_WARPS);
     }
@@ -201,7 +291,8 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
   if (warp == C::PRODUCER_WARP) {
     if (lane == 0) {
       // TMA producer: ring item i goes to slot i % SLOTS once item i - SLOTS
-      // has been consumed.  Per tile: K0, then per block j: K[j+1] (if any), V[j].
+      // has been consumed.  Per tile: K0 .. K[NSB-2], then per block j:
+      // K[j+NSB-1] (if any), V[j] -- the order the MMA thread takes them.
       int issued = 0;
       auto load = [&](const CUtensorMap *map, int key_block, int bh) -> bool {
         const int slot = issued % C::SLOTS;
@@ -225,9 +316,9 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       for (int i = 0; ok && i < my_tiles; ++i) {
         const int t = blockIdx.x + i * gridDim.x;
         const int bh = t / qtiles;
-        ok = load(&tmK, 0, bh);
+        for (int j = 0; ok && j < NSB - 1 && j < nblk; ++j) ok = load(&tmK, j, bh);
         for (int j = 0; ok && j < nblk; ++j) {
-          if (j + 1 < nblk) ok = load(&tmK, j + 1, bh);
+          if (j + NSB - 1 < nblk) ok = load(&tmK, j + NSB - 1, bh);
           if (ok) ok = load(&tmV, j, bh);
         }
       }
@@ -256,15 +347,15 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       // adds d >> 4 to the start-address field
       const uint64_t dq = sw128_desc(qa, 16, 1024);
       auto issue_s = [&](int g, uint32_t ka) {
-        // S[g % 2] = Q K^T: both operands K-major (head dim contiguous)
+        // S[g % NSB] = Q K^T: both operands K-major (head dim contiguous)
         const uint64_t dk = sw128_desc(ka, 16, 1024);
 #pragma unroll
         for (int ks = 0; ks < C::KSTEPS; ++ks) {
           const int kb = ks / 4, kk = ks % 4;
-          mma_f16(tmem + C::S_COL0 + (g & 1) * BN, dq + ((kb * C::Q_BOX + kk * 32) >> 4),
+          mma_f16(tmem + C::S_COL0 + (g % NSB) * BN, dq + ((kb * C::Q_BOX + kk * 32) >> 4),
                   dk + ((kb * C::K_BOX + kk * 32) >> 4), idesc_s, ks != 0 ? 1u : 0u);
         }
-        mma_commit(&s_full[g & 1]);
+        mma_commit(&s_full[g % NSB]);
       };
       // Q, K and V come from TMA: their barriers need no tcgen05 fence; P and
       // the rescaled O come from the softmax threads and do
@@ -272,21 +363,26 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       bool ok = true;
       int g = 0;                                   // key blocks over all tiles
       for (int i = 0; ok && i < my_tiles; ++i) {
-        ok = mbar_wait(q_full, i & 1, status, kAttnWaitQ) && take(ka);
+        ok = mbar_wait(q_full, i & 1, status, kAttnWaitQ);
+        // the tile's first NSB - 1 score products
+        for (int j = 0; ok && j < NSB - 1 && j < nblk; ++j) {
+          if (!(ok = take(ka))) break;
+          issue_s(g + j, ka);
+          release();
+        }
         if (!ok) break;
-        issue_s(g, ka);
-        release();
         for (int j = 0; j < nblk; ++j, ++g) {
-          if (j + 1 < nblk) {
-            // S[g+1] into the other buffer: its previous contents (P[g-1]) were
-            // read by the P V product issued before it
+          if (j + NSB - 1 < nblk) {
+            // S[g+NSB-1] into buffer (g-1) % NSB: its previous contents
+            // (P[g-1]) were read by the P V product issued before it, and the
+            // tensor pipe runs this thread's MMAs in issue order
             if (!(ok = take(ka))) break;
-            issue_s(g + 1, ka);
+            issue_s(g + NSB - 1, ka);
             release();
           }
-          // P[g] was published into score buffer g % 2 (one barrier per buffer:
-          // P[g+2] cannot be published before S[g+2] is issued)
-          if (!(ok = mbar_wait(&p_full[g & 1], (g >> 1) & 1, status, kAttnWaitP) && take(va)))
+          // P[g] was published into score buffer g % NSB (one barrier per
+          // buffer: P[g+NSB] cannot be published before S[g+NSB] is issued)
+          if (!(ok = mbar_wait(&p_full[g % NSB], (g / NSB) & 1, status, kAttnWaitP) && take(va)))
             break;
           // the tile's first product overwrites O: the previous tile's
           // epilogue must have read it
@@ -299,11 +395,11 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk)
             mma_f16_tmem_a(tmem + C::O_COL,
-                           tmem + C::S_COL0 + (g & 1) * BN + (kk * 16 / C::CPT) * C::CPT +
+                           tmem + C::S_COL0 + (g % NSB) * BN + (kk * 16 / C::CPT) * C::CPT +
                                (kk * 16 % C::CPT) / 2,
                            sw128_desc(va + kk * 16 * 128, C::K_BOX, 1024), idesc_o,
                            (j | kk) != 0 ? 1u : 0u);
-          mma_commit(o_full);
+          mma_commit(&o_full[g & 1]);
           release();
         }
         if (ok) mma_commit(o_done);
@@ -322,6 +418,8 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     const int r = quad * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const float c = (scale_div ? 1.0f / __ldg(scale_div) : 1.0f) * 1.4426950408889634f;
+    const uint64_t c2 = pack2(c, c);
+    const Exp2Poly exp2_poly;
     unsigned char *stage = smem + C::STAGE_OFF + warp * (C::STAGE_ROWS * 128);   // this warp's box
     float *xch = reinterpret_cast<float *>(smem + C::XCH_OFF);   // SPLIT only
     constexpr int CPT = C::CPT;
@@ -333,7 +431,7 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
       const int bh = t / qtiles, m0 = (t - bh * qtiles) * 128;
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < nblk; ++j, ++g) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&s_full[g & 1], (g >> 1) & 1, status, kAttnWaitS));
+        ok = __all_sync(0xffffffffu, mbar_wait(&s_full[g % NSB], (g / NSB) & 1, status, kAttnWaitS));
         if (!ok) break;
         tc_fence_after();
         if (j + 1 == nblk && threadIdx.x == 0 && i + 1 < my_tiles) {
@@ -348,7 +446,7 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
           ++qloads;
         }
         const int key0 = j * BN + half * CPT;
-        const uint32_t scol = C::S_COL0 + (g & 1) * BN + half * CPT;   // this half's columns
+        const uint32_t scol = C::S_COL0 + (g % NSB) * BN + half * CPT;   // this half's columns
         // raw scores v; t = v * c is folded into one FFMA below.  With c > 0 the
         // row max of t is c * max(v), with c < 0 it is c * min(v); masked keys
         // get the value whose t is -inf.
@@ -398,25 +496,39 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         const bool move = mb > m + C::RESCALE_LOG2;
         const float m_use = move ? mb : m;
         const float alpha = move ? ex2_approx(m - mb) : 1.0f;
-        float psum[4] = {0.f, 0.f, 0.f, 0.f};
+        // p = 2^(v c - m) for the pairs of this thread's scores: argument and
+        // sums as packed pairs; POLY8 of every 8 pairs on the FMA pipe, the
+        // rest on MUFU
+        const uint64_t nm2 = pack2(-m_use, -m_use);
+        uint64_t psum2[2] = {0ull, 0ull};
         uint32_t h[CPT / 2];
 #pragma unroll
         for (int k = 0; k < CPT / 2; ++k) {
-          const float p0 = ex2_approx(fmaf(v[2 * k], c, -m_use));
-          const float p1 = ex2_approx(fmaf(v[2 * k + 1], c, -m_use));
-          psum[k & 3] += p0 + p1;
-          __half2 hh = __floats2half2_rn(p0, p1);
-          h[k] = *reinterpret_cast<uint32_t *>(&hh);
+          const uint64_t t2 = fma2(pack2(v[2 * k], v[2 * k + 1]), c2, nm2);
+          uint64_t p2;
+          if ((k & 7) < C::POLY8) {
+            p2 = exp2_poly(t2);
+          } else {
+            float t0, t1;
+            unpack2(t2, t0, t1);
+            p2 = pack2(ex2_approx(t0), ex2_approx(t1));
+          }
+          psum2[k & 1] = add2(psum2[k & 1], p2);
+          h[k] = f16x2_of(p2);
         }
-        const float ps = (psum[0] + psum[1]) + (psum[2] + psum[3]);
+        float ps0, ps1;
+        unpack2(add2(psum2[0], psum2[1]), ps0, ps1);
+        const float ps = ps0 + ps1;
         // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp
         // rescales when any of its rows moved its max (alpha is 1 for the others)
         if (j > 0 && __any_sync(0xffffffffu, move)) {
-          // O is still being accumulated by P[g-1] V.  Waiting for phase g-1 of
-          // o_full is unambiguous here: S[g] was issued after P[g-2] V, so its
-          // completion (waited above) means phases up to g-2 are done, and P[g] V
-          // has not been issued yet.
-          ok = __all_sync(0xffffffffu, mbar_wait(o_full, (g - 1) & 1, status, kAttnWaitO));
+          // O is still being accumulated by P[g-1] V.  That product completes
+          // phase (g-1) / 2 of o_full[(g-1) % 2], and the wait is unambiguous:
+          // S[g] was issued after P[g-NSB] V, so its completion (waited above)
+          // means every product up to g-NSB -- among them g-3, the previous
+          // one on that barrier -- is done, and P[g+1] V has not been issued.
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(&o_full[(g - 1) & 1], ((g - 1) >> 1) & 1, status, kAttnWaitO));
           if (!ok) break;
           tc_fence_after();
 #pragma unroll 1
@@ -435,7 +547,7 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
         l = l * alpha + ps;                // this half's share of the row sum
         m = m_use;
         tc_fence_before();
-        mbar_arrive(&p_full[g & 1]);
+        mbar_arrive(&p_full[g % NSB]);
       }
       if (!ok) break;
       if constexpr (SPLIT) {
@@ -576,11 +688,12 @@ namespace {
 
 // d: the real head dim (a multiple of 8, at most D); the maps carry it, so
 // boxes reaching past it are zero-filled on load and clipped on store.
-template <int D, int BN, int HALVES, int DQ>
+template <int D, int BN, int HALVES, int DQ, int POLY8 = AttnCfg<D, BN, HALVES, DQ>::POLY8,
+          int SLOTS = 0>
 int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
                         const float *scale_div, int64_t batch, int64_t S, int64_t d,
                         int out_f16, cudaStream_t st) {
-  using Cfg = AttnCfg<D, BN, HALVES, DQ>;
+  using Cfg = AttnCfg<D, BN, HALVES, DQ, POLY8, SLOTS>;
   CUtensorMap tq, tk, tv;
   const uint64_t dims[3] = {(uint64_t)d, (uint64_t)S, (uint64_t)batch};
   const uint64_t str[2] = {(uint64_t)d * 2, (uint64_t)S * d * 2};
@@ -605,7 +718,7 @@ int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaFuncSetAttribute(attention_f16_tc_kernel<D, BN, HALVES, DQ>,
+    cudaFuncSetAttribute(attention_f16_tc_kernel<D, BN, HALVES, DQ, POLY8, SLOTS>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     attr_set[dev] = true;
   }
@@ -614,7 +727,7 @@ int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
   if (ntiles > INT32_MAX) return set_error(EMMY_ERR_INVALID, "emmy_attention_f16: too many query tiles");
   const int64_t slots = (int64_t)Cfg::MIN_BLOCKS * sm_count();
   const unsigned grid = (unsigned)(ntiles < slots ? ntiles : slots);
-  attention_f16_tc_kernel<D, BN, HALVES, DQ><<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(
+  attention_f16_tc_kernel<D, BN, HALVES, DQ, POLY8, SLOTS><<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(
       tq, tk, tv, to, scale_div, (int)S, (int)d, (int)ntiles, out_f16, device_status_ptr());
   return check_launch("emmy_attention_f16 (tcgen05)");
 }
