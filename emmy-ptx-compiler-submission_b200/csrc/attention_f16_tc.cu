@@ -62,14 +62,9 @@ namespace emmy {
 // every Q, K and V box with zeros (they add nothing to the scores, and the O
 // columns they produce are never stored), and the score product issues only
 // ceil(d / 16) K16 steps.
-// POLY8: of every 8 score pairs a softmax thread exponentiates, how many go
-// through the FMA-pipe polynomial (exp2_poly2) instead of MUFU ex2 (the MUFU
-// unit runs 16 exponentials per SM per clock, the FMA pipe 128 fused
-// multiply-adds, so sharing the work shortens the exponent phase).
 // SLOTS_: depth of the K/V ring (0: the default below).
-template <int D, int BN_, int HALVES_, int DQ_ = D, int POLY8_ = 3, int SLOTS_ = 0>
+template <int D, int BN_, int HALVES_, int DQ_ = D, int SLOTS_ = 0>
 struct AttnCfg {
-  static constexpr int POLY8 = POLY8_;               // pairs of 8 on the FMA-pipe exp2
   static constexpr int DQ = DQ_;                     // head dims the score product reads
   static constexpr int KSTEPS = DQ / 16;             // K16 steps of the score product
   static constexpr int BN = BN_;                     // keys per block
@@ -147,7 +142,7 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// Packed pairs of f32 (sm_100 add / sub / fma .f32x2: two lanes per
+// Packed pairs of f32 (sm_100 add / fma .f32x2: two lanes per
 // instruction, each rounded as its scalar form).
 __device__ __forceinline__ uint64_t pack2(float lo, float hi) {
   uint64_t r;
@@ -167,11 +162,6 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
-__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
 // the f16x2 of a pair (lo in the low half, as __floats2half2_rn(lo, hi))
 __device__ __forceinline__ uint32_t f16x2_of(uint64_t p) {
   float lo, hi;
@@ -181,53 +171,17 @@ __device__ __forceinline__ uint32_t f16x2_of(uint64_t p) {
   return h;
 }
 
-// 2^t for a pair, on the FMA pipe.  Range reduction: t = j + f with j the
-// nearest integer (the sum with 1.5 * 2^23 leaves j in the low mantissa bits of
-// r) and f = t - j in [-1/2, 1/2], exact; 2^f by a degree-4 polynomial fitted
-// here for least maximum relative error on [-1/2, 1/2] (Lawson-weighted least
-// squares on Chebyshev nodes; 2.7e-6 relative error in this f32 Horner form,
-// against the 2^-12 of the f16 rounding P gets next); 2^j is added into the
-// exponent field, (bits(r) << 23) being j << 23.  t is clamped to -125 first so
-// the exponent stays normal: a key far below the row max (or masked, t = -inf)
-// gets 2^-125 instead of 0, which the f16 P rounds to 0 and the f32 row sum
-// does not see.
-struct Exp2Poly {
-  uint64_t magic, c0, c1, c2, c3, c4;
-  __device__ __forceinline__ Exp2Poly()
-      : magic(pack2(0x1.8p23f, 0x1.8p23f)),
-        c0(pack2(0x1.ffffe8p-1f, 0x1.ffffe8p-1f)),
-        c1(pack2(0x1.62e0dcp-1f, 0x1.62e0dcp-1f)),
-        c2(pack2(0x1.ec06dap-3f, 0x1.ec06dap-3f)),
-        c3(pack2(0x1.ca1440p-5f, 0x1.ca1440p-5f)),
-        c4(pack2(0x1.3997d4p-7f, 0x1.3997d4p-7f)) {}
-  __device__ __forceinline__ uint64_t operator()(uint64_t t2) const {
-    float a, b;
-    unpack2(t2, a, b);
-    const uint64_t x = pack2(fmaxf(a, -125.0f), fmaxf(b, -125.0f));
-    const uint64_t r = add2(x, magic);
-    const uint64_t f = sub2(x, sub2(r, magic));
-    uint64_t p = fma2(c4, f, c3);
-    p = fma2(p, f, c2);
-    p = fma2(p, f, c1);
-    p = fma2(p, f, c0);
-    float pa, pb, ra, rb;
-    unpack2(p, pa, pb);
-    unpack2(r, ra, rb);
-    return pack2(__int_as_float(__float_as_int(pa) + (__float_as_int(ra) << 23)),
-                 __int_as_float(__float_as_int(pb) + (__float_as_int(rb) << 23)));
-  }
-};
 
-template <int D, int BN_, int HALVES_, int DQ_, int POLY8_, int SLOTS_>
-__global__ void __launch_bounds__(AttnCfg<D, BN_, HALVES_, DQ_, POLY8_, SLOTS_>::THREADS,
-                                  AttnCfg<D, BN_, HALVES_, DQ_, POLY8_, SLOTS_>::MIN_BLOCKS)
+template <int D, int BN_, int HALVES_, int DQ_, int SLOTS_>
+__global__ void __launch_bounds__(AttnCfg<D, BN_, HALVES_, DQ_, SLOTS_>::THREADS,
+                                  AttnCfg<D, BN_, HALVES_, DQ_, SLOTS_>::MIN_BLOCKS)
 attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV,
                         const __grid_constant__ CUtensorMap tmO,
                         const float *__restrict__ scale_div, int S, int dv, int ntiles,
                         int out_f16, int *status) {
-  using C = AttnCfg<D, BN_, HALVES_, DQ_, POLY8_, SLOTS_>;
+  using C = AttnCfg<D, BN_, HALVES_, DQ_, SLOTS_>;
   constexpr bool SPLIT = C::HALVES > 1;              // two softmax warps per row
   constexpr int BN = C::BN;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -419,7 +373,6 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const float c = (scale_div ? 1.0f / __ldg(scale_div) : 1.0f) * 1.4426950408889634f;
     const uint64_t c2 = pack2(c, c);
-    const Exp2Poly exp2_poly;
     unsigned char *stage = smem + C::STAGE_OFF + warp * (C::STAGE_ROWS * 128);   // this warp's box
     float *xch = reinterpret_cast<float *>(smem + C::XCH_OFF);   // SPLIT only
     constexpr int CPT = C::CPT;
@@ -459,66 +412,84 @@ attention_f16_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
           for (int k = 0; k < CPT; ++k)
             if (key0 + k >= S) v[k] = far;
         }
-        float ext[8];
+        // the block's row max of t: c * max(v) for c > 0, c * min(v) for c < 0
+        auto block_max = [&]() -> float {
+          float ext[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) ext[q] = v[q];
-        if (c > 0.f) {
+          for (int q = 0; q < 8; ++q) ext[q] = v[q];
+          if (c > 0.f) {
 #pragma unroll
-          for (int k = 8; k < CPT; ++k) ext[k & 7] = fmaxf(ext[k & 7], v[k]);
+            for (int k = 8; k < CPT; ++k) ext[k & 7] = fmaxf(ext[k & 7], v[k]);
 #pragma unroll
-          for (int w = 4; w >= 1; w >>= 1)
+            for (int w = 4; w >= 1; w >>= 1)
 #pragma unroll
-            for (int q = 0; q < w; ++q) ext[q] = fmaxf(ext[q], ext[q + w]);
-        } else {
+              for (int q = 0; q < w; ++q) ext[q] = fmaxf(ext[q], ext[q + w]);
+          } else {
 #pragma unroll
-          for (int k = 8; k < CPT; ++k) ext[k & 7] = fminf(ext[k & 7], v[k]);
+            for (int k = 8; k < CPT; ++k) ext[k & 7] = fminf(ext[k & 7], v[k]);
 #pragma unroll
-          for (int w = 4; w >= 1; w >>= 1)
+            for (int w = 4; w >= 1; w >>= 1)
 #pragma unroll
-            for (int q = 0; q < w; ++q) ext[q] = fminf(ext[q], ext[q + w]);
-        }
-        float mb = ext[0] * c;
-        if constexpr (SPLIT) {
-          // the row's max over both halves: each half posts its own, the
-          // quadrant's barrier for this block parity completes with both.  A
-          // thread posts block g + 2 only after it has seen block g + 1, for
-          // which its partner must have read block g, so one slot per parity
-          // suffices and the barrier is never two phases ahead of a waiter.
-          float *slot = xch + (g & 1) * 256;
-          slot[half * 128 + r] = mb;
-          mbar_arrive(&xmax[quad * 2 + (g & 1)]);
-          ok = __all_sync(0xffffffffu, mbar_wait(&xmax[quad * 2 + (g & 1)], (g >> 1) & 1, status,
-                                                 kAttnWaitHalf));
+              for (int q = 0; q < w; ++q) ext[q] = fminf(ext[q], ext[q + w]);
+          }
+          return ext[0] * c;
+        };
+        // p = 2^(v c - mu) for the pairs of this thread's scores (argument and
+        // sums as packed pairs, the exponential on MUFU); P as packed f16 into
+        // h; returns the sum of p
+        uint32_t h[CPT / 2];
+        auto exponentiate = [&](float mu) -> float {
+          const uint64_t nm2 = pack2(-mu, -mu);
+          uint64_t psum2[2] = {0ull, 0ull};
+#pragma unroll
+          for (int k = 0; k < CPT / 2; ++k) {
+            const uint64_t t2 = fma2(pack2(v[2 * k], v[2 * k + 1]), c2, nm2);
+            float t0, t1;
+            unpack2(t2, t0, t1);
+            const uint64_t p2 = pack2(ex2_approx(t0), ex2_approx(t1));
+            psum2[k & 1] = add2(psum2[k & 1], p2);
+            h[k] = f16x2_of(p2);
+          }
+          float ps0, ps1;
+          unpack2(add2(psum2[0], psum2[1]), ps0, ps1);
+          return ps0 + ps1;
+        };
+        // the row's block max over both halves (SPLIT): each half posts its
+        // own, the quadrant's barrier for this block parity completes with
+        // both.  A thread posts block g + 2 only after it has seen block g + 1,
+        // for which its partner must have read block g, so one slot per parity
+        // suffices and the barrier is never two phases ahead of a waiter.
+        auto row_max = [&](float mine) -> float {
+          if constexpr (SPLIT) {
+            float *slot = xch + (g & 1) * 256;
+            slot[half * 128 + r] = mine;
+            mbar_arrive(&xmax[quad * 2 + (g & 1)]);
+            ok = __all_sync(0xffffffffu, mbar_wait(&xmax[quad * 2 + (g & 1)], (g >> 1) & 1,
+                                                   status, kAttnWaitHalf));
+            return fmaxf(mine, slot[(half ^ 1) * 128 + r]);
+          }
+          return mine;
+        };
+        // Lazy max: the row max moves only when a block's max is more than
+        // 2^8 above it (so P <= 2^8).  A tile's first block sets it.  Later
+        // blocks are exponentiated against the running max while their max is
+        // computed beside it (the two chains are independent), and a row
+        // whose max does move -- rare after the first block -- redoes its
+        // block against the new one.
+        float mb, ps;
+        if (j == 0) {
+          mb = row_max(block_max());
           if (!ok) break;
-          mb = fmaxf(mb, slot[(half ^ 1) * 128 + r]);
+          ps = exponentiate(mb);
+        } else {
+          ps = exponentiate(m);
+          mb = row_max(block_max());
+          if (!ok) break;
         }
-        // lazy max: move only when the block's max is more than 2^8 above it
         const bool move = mb > m + C::RESCALE_LOG2;
         const float m_use = move ? mb : m;
         const float alpha = move ? ex2_approx(m - mb) : 1.0f;
-        // p = 2^(v c - m) for the pairs of this thread's scores: argument and
-        // sums as packed pairs; POLY8 of every 8 pairs on the FMA pipe, the
-        // rest on MUFU
-        const uint64_t nm2 = pack2(-m_use, -m_use);
-        uint64_t psum2[2] = {0ull, 0ull};
-        uint32_t h[CPT / 2];
-#pragma unroll
-        for (int k = 0; k < CPT / 2; ++k) {
-          const uint64_t t2 = fma2(pack2(v[2 * k], v[2 * k + 1]), c2, nm2);
-          uint64_t p2;
-          if ((k & 7) < C::POLY8) {
-            p2 = exp2_poly(t2);
-          } else {
-            float t0, t1;
-            unpack2(t2, t0, t1);
-            p2 = pack2(ex2_approx(t0), ex2_approx(t1));
-          }
-          psum2[k & 1] = add2(psum2[k & 1], p2);
-          h[k] = f16x2_of(p2);
-        }
-        float ps0, ps1;
-        unpack2(add2(psum2[0], psum2[1]), ps0, ps1);
-        const float ps = ps0 + ps1;
+        if (j > 0 && move) ps = exponentiate(m_use);
         // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp
         // rescales when any of its rows moved its max (alpha is 1 for the others)
         if (j > 0 && __any_sync(0xffffffffu, move)) {
@@ -688,12 +659,11 @@ namespace {
 
 // d: the real head dim (a multiple of 8, at most D); the maps carry it, so
 // boxes reaching past it are zero-filled on load and clipped on store.
-template <int D, int BN, int HALVES, int DQ, int POLY8 = AttnCfg<D, BN, HALVES, DQ>::POLY8,
-          int SLOTS = 0>
+template <int D, int BN, int HALVES, int DQ, int SLOTS = 0>
 int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
                         const float *scale_div, int64_t batch, int64_t S, int64_t d,
                         int out_f16, cudaStream_t st) {
-  using Cfg = AttnCfg<D, BN, HALVES, DQ, POLY8, SLOTS>;
+  using Cfg = AttnCfg<D, BN, HALVES, DQ, SLOTS>;
   CUtensorMap tq, tk, tv;
   const uint64_t dims[3] = {(uint64_t)d, (uint64_t)S, (uint64_t)batch};
   const uint64_t str[2] = {(uint64_t)d * 2, (uint64_t)S * d * 2};
@@ -718,7 +688,7 @@ int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaFuncSetAttribute(attention_f16_tc_kernel<D, BN, HALVES, DQ, POLY8, SLOTS>,
+    cudaFuncSetAttribute(attention_f16_tc_kernel<D, BN, HALVES, DQ, SLOTS>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     attr_set[dev] = true;
   }
@@ -727,7 +697,7 @@ int launch_attention_tc(const void *q, const void *k, const void *v, void *o,
   if (ntiles > INT32_MAX) return set_error(EMMY_ERR_INVALID, "emmy_attention_f16: too many query tiles");
   const int64_t slots = (int64_t)Cfg::MIN_BLOCKS * sm_count();
   const unsigned grid = (unsigned)(ntiles < slots ? ntiles : slots);
-  attention_f16_tc_kernel<D, BN, HALVES, DQ, POLY8, SLOTS><<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(
+  attention_f16_tc_kernel<D, BN, HALVES, DQ, SLOTS><<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(
       tq, tk, tv, to, scale_div, (int)S, (int)d, (int)ntiles, out_f16, device_status_ptr());
   return check_launch("emmy_attention_f16 (tcgen05)");
 }
