@@ -50,6 +50,13 @@ for _p in (str(ROOT), str(PKG)):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
+# Multi-rank runs log NCCL's communicator set-up (ranks, devices, transports)
+# to stderr, keeping stdout for the JSON line; set before torch loads NCCL.
+if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+    os.environ.setdefault("NCCL_DEBUG", "INFO")
+    os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+
 METRIC = "per-family HBM GB/s (K2: softmax4d + layernorm f32)"
 UNIT = "GB/s"
 K2_WORKLOAD = "K2: softmax f32 [32,16,512,512] dim=-1 + layernorm f32 affine [16384,1024]"
@@ -63,6 +70,8 @@ FP64_NOMINAL_TFLOPS = 148 * 64 * 2 * 1.965e9 / 1e12
 # SM at 1965 MHz): 70.86 and 33.35 TFLOP/s
 FP32_MEASURED_TFLOPS = 70.86
 FP64_MEASURED_TFLOPS = 33.35
+# MUFU ex2 rate, nominal: 16 per SM per clock x 148 SMs x 1.965 GHz
+MUFU_EXP_PER_S = 16 * 148 * 1.965e9
 L2_FLUSH_BYTES = 256 << 20
 # Family timings keep each launch's data out of L2: a kernel whose tensors
 # total less than this runs on several copies of them, launched back to back
@@ -384,12 +393,13 @@ def time_launches(make_launch, nbytes, flush, reps=10, warmup=3):
     """Per-launch device time (us) of one kernel configuration.
 
     ``make_launch()`` returns a zero-argument function that launches the
-    kernel on its own copy of the tensors.  With fewer than FOOTPRINT_BYTES
-    per launch, ``copies`` such copies are launched back to back between the
-    events and the time divided by their number, so every launch reads from
-    HBM and the 1 us event resolution is spread over many launches.  L2 is
-    flushed before each timed pass, and the device spin before it lasts until
-    every launch of the pass is queued.  Returns (median us per launch, copies).
+    kernel on its own copy of the tensors (on the current stream).  With fewer
+    than FOOTPRINT_BYTES per launch, ``copies`` such copies run back to back in
+    each timed pass, captured once into a CUDA graph and replayed, so the host
+    cost of a launch through ctypes (longer than a small kernel) stays out of
+    the pass; the time is divided by the number of copies.  Every launch reads
+    from HBM, and the 1 us event resolution is spread over many launches.  L2
+    is flushed before each timed pass.  Returns (median us per launch, copies).
     """
     import torch
     copies = 1 if nbytes >= FOOTPRINT_BYTES else min(MAX_COPIES,
@@ -398,39 +408,65 @@ def time_launches(make_launch, nbytes, flush, reps=10, warmup=3):
     for _ in range(warmup):
         for f in fns:
             f()
+    torch.cuda.synchronize()
+    graph = None
+    if copies > 1:
+        try:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                for f in fns:
+                    f()
+            graph.replay()
+            torch.cuda.synchronize()
+        except RuntimeError:
+            graph = None
+            torch.cuda.synchronize()
     samples = []
     for _ in range(reps):
         flush()
-        torch.cuda._sleep(SPIN_CYCLES + SPIN_PER_LAUNCH * copies)
+        torch.cuda._sleep(SPIN_CYCLES + (0 if graph else SPIN_PER_LAUNCH * copies))
         e0, e1 = _event_pair()
         e0.record()
-        for f in fns:
-            f()
+        if graph is not None:
+            graph.replay()
+        else:
+            for f in fns:
+                f()
         e1.record()
         e1.synchronize()
         samples.append(e0.elapsed_time(e1) * 1e3 / copies)
-    del fns
+    del graph, fns
     return statistics.median(samples), copies
 
 
-def roofline_block(name, nbytes, flops, us, pipe):
+def roofline_block(name, nbytes, flops, us, pipe, n_exp=0):
     """The binding roof of one configuration: t_roof = max(bytes / HBM peak,
-    flops / peak of the pipe the kernel uses); frac = t_roof / measured time."""
+    flops / peak of the pipe the kernel uses, exponentials / MUFU rate);
+    frac = t_roof / measured time.  The exponential term (attention: one per
+    score, B*H*Sq*Sk) uses the nominal MUFU rate, 16 ex2 per SM per clock at
+    148 SMs and 1.965 GHz."""
     hbm, hsrc = hbm_peak()
     t_hbm = nbytes / (hbm * 1e9)
     pipe_peak = {"tensor": tensor_peak()[0], "fp32": FP32_MEASURED_TFLOPS,
                  "fp64": FP64_MEASURED_TFLOPS}.get(pipe)
     t_pipe = flops / (pipe_peak * 1e12) if pipe_peak else 0.0
+    t_exp = n_exp / MUFU_EXP_PER_S
     t = us * 1e-6
-    if t_hbm >= t_pipe:
+    if t_hbm >= max(t_pipe, t_exp):
         blk = {"bound": "hbm", "achieved": round(nbytes / t / 1e9, 1), "peak": hbm, "unit": "GB/s",
                "peak_source": f"{hsrc} hbm_gbs"}
+    elif t_exp > t_pipe:
+        blk = {"bound": "mufu", "achieved": round(n_exp / t / 1e12, 3),
+               "peak": round(MUFU_EXP_PER_S / 1e12, 3), "unit": "Texp/s",
+               "peak_source": "nominal: 16 ex2 / SM / clock x 148 SMs x 1.965 GHz"}
     else:
         blk = {"bound": pipe, "achieved": round(flops / t / 1e12, 2), "peak": pipe_peak,
                "unit": "TFLOP/s",
                "peak_source": ("measured bf16_tflops (burst)" if pipe == "tensor"
                                else f"measured {pipe} FMA chains")}
-    blk["frac"] = round(max(t_hbm, t_pipe) / t, 4)
+    blk["frac"] = round(max(t_hbm, t_pipe, t_exp) / t, 4)
     blk["algorithmic_bytes"] = int(nbytes)
     blk["traffic"] = profile_traffic(PROFILE_OF.get(name))
     blk["profile"] = PROFILE_OF.get(name) if blk["traffic"] is not None else None
@@ -517,7 +553,11 @@ def family_extras(device, only=None):
                 row["frac_fp64_nominal"] = round(row["tflops"] / FP64_NOMINAL_TFLOPS, 3)
             elif _pipe_of(plan) == "tensor":
                 row["frac_tensor"] = round(row["tflops"] / tensor_peak()[0], 3)
-        row["roofline"] = roofline_block(name, nbytes, flops, us, _pipe_of(plan))
+        n_exp = 0
+        if "attention" in plan:
+            at = plan["attention"]
+            n_exp = at["batch"] * at["sq"] * at["sk"]
+        row["roofline"] = roofline_block(name, nbytes, flops, us, _pipe_of(plan), n_exp)
         out[name] = row
         torch.cuda.empty_cache()
     if only:
@@ -798,8 +838,6 @@ def run_b200_arm(args):
     world, rank, local = dist_setup()
     if world > 1:
         from datetime import timedelta
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
@@ -837,20 +875,31 @@ def run_b200_arm(args):
     torch.cuda.synchronize()
     flush = L2Flush(device)
 
+    side = torch.cuda.Stream(device=device)
+
     def timed_steps(exs, steps):
-        """(total ms, softmax-launch ms per step, launches) over ``steps`` steps."""
+        """(total ms, softmax-launch ms per step, launches) over ``steps`` steps.
+
+        The two IRs of a step are independent: the layernorm runs on a second
+        stream beside the softmax (forked after the start event, joined before
+        the end event), so its short launch overlaps the long one.
+        """
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
                torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        main = torch.cuda.current_stream()
         launches = 0
         for i in range(steps):
             flush()                         # L2 flush between steps (outside the events)
             torch.cuda._sleep(SPIN_CYCLES)
             e0, e1, e2 = ev[i]
-            e0.record()
-            launches += exs[0].launch()     # softmax (dominant kernel)
-            e1.record()
-            launches += exs[1].launch()     # layernorm
-            e2.record()
+            e0.record(main)
+            side.wait_event(e0)
+            with torch.cuda.stream(side):
+                launches += exs[1].launch(stream=side)   # layernorm
+            launches += exs[0].launch(stream=main)       # softmax (dominant kernel)
+            e1.record(main)
+            main.wait_stream(side)
+            e2.record(main)
         torch.cuda.synchronize()
         total = sum(a.elapsed_time(c) for a, b, c in ev)
         return total, [a.elapsed_time(b) for a, b, c in ev], launches
