@@ -98,7 +98,11 @@ __device__ __forceinline__ float group_min(float v, float *red) {
 // `cols` contiguous floats.  Each of the TPR threads owns NCH chunks of VEC
 // consecutive elements: chunk c of thread t covers elements (c*TPR + t)*VEC.
 
-template <int MODE, int VEC, int TPR, int NCH>
+// PREF: the weight (and, for layer norm, bias) elements a thread multiplies
+// by are read into registers once, before its first row, when they number at
+// most PREF per thread -- every row uses the same ones, and read after the
+// row's reduction their L2 latency would sit on every row's path.
+template <int MODE, int VEC, int TPR, int NCH, int PREF = 32>
 __global__ void __launch_bounds__(TPR > 32 ? TPR : 256)
 row_resident_kernel(const float *__restrict__ x, const float *__restrict__ w,
                     const float *__restrict__ b, float *__restrict__ y, int64_t rows,
@@ -112,6 +116,38 @@ row_resident_kernel(const float *__restrict__ x, const float *__restrict__ w,
   if constexpr (MODE == MODE_RMS || MODE == MODE_LN) {
     eps = eps_p ? __ldg(eps_p) : 0.f;
     inv_count = 1.0f / (count_p ? __ldg(count_p) : (float)cols);
+  }
+  constexpr bool PRE_W =
+      (MODE == MODE_RMS || MODE == MODE_LN) && NCH * VEC * (MODE == MODE_LN ? 2 : 1) <= PREF;
+  constexpr bool PRE_B = PRE_W && MODE == MODE_LN;
+  float wv[PRE_W ? NCH : 1][VEC], bv[PRE_B ? NCH : 1][VEC];
+  if constexpr (PRE_W) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int64_t idx = ((int64_t)c * TPR + t) * VEC;
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) wv[c][k] = 1.f;
+      if (w != nullptr && idx < cols) {
+        if constexpr (VEC == 4) {
+          const float4 q = __ldg(reinterpret_cast<const float4 *>(w + idx));
+          wv[c][0] = q.x; wv[c][1] = q.y; wv[c][2] = q.z; wv[c][3] = q.w;
+        } else {
+          wv[c][0] = __ldg(w + idx);
+        }
+      }
+      if constexpr (PRE_B) {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) bv[c][k] = 0.f;
+        if (b != nullptr && idx < cols) {
+          if constexpr (VEC == 4) {
+            const float4 q = __ldg(reinterpret_cast<const float4 *>(b + idx));
+            bv[c][0] = q.x; bv[c][1] = q.y; bv[c][2] = q.z; bv[c][3] = q.w;
+          } else {
+            bv[c][0] = __ldg(b + idx);
+          }
+        }
+      }
+    }
   }
 
   for (int64_t row = (int64_t)blockIdx.x * RPB + g; row < rows;
@@ -185,7 +221,10 @@ row_resident_kernel(const float *__restrict__ x, const float *__restrict__ w,
 #pragma unroll
           for (int k = 0; k < VEC; ++k) o[k] = v[c][k] * r;
           if (MODE == MODE_RMS && w != nullptr) {
-            if constexpr (VEC == 4) {
+            if constexpr (PRE_W) {
+#pragma unroll
+              for (int k = 0; k < VEC; ++k) o[k] *= wv[c][k];
+            } else if constexpr (VEC == 4) {
               float4 q = __ldg(reinterpret_cast<const float4 *>(w + idx));
               o[0] *= q.x; o[1] *= q.y; o[2] *= q.z; o[3] *= q.w;
             } else {
@@ -222,7 +261,10 @@ row_resident_kernel(const float *__restrict__ x, const float *__restrict__ w,
 #pragma unroll
           for (int k = 0; k < VEC; ++k) o[k] = v[c][k] * r;
           if (w != nullptr) {
-            if constexpr (VEC == 4) {
+            if constexpr (PRE_W) {
+#pragma unroll
+              for (int k = 0; k < VEC; ++k) o[k] *= wv[c][k];
+            } else if constexpr (VEC == 4) {
               float4 q = __ldg(reinterpret_cast<const float4 *>(w + idx));
               o[0] *= q.x; o[1] *= q.y; o[2] *= q.z; o[3] *= q.w;
             } else {
@@ -230,7 +272,10 @@ row_resident_kernel(const float *__restrict__ x, const float *__restrict__ w,
             }
           }
           if (b != nullptr) {
-            if constexpr (VEC == 4) {
+            if constexpr (PRE_B) {
+#pragma unroll
+              for (int k = 0; k < VEC; ++k) o[k] += bv[c][k];
+            } else if constexpr (VEC == 4) {
               float4 q = __ldg(reinterpret_cast<const float4 *>(b + idx));
               o[0] += q.x; o[1] += q.y; o[2] += q.z; o[3] += q.w;
             } else {
@@ -482,7 +527,7 @@ softmax_cols_kernel(const float *__restrict__ x, float *__restrict__ y, int64_t 
 
 namespace {
 
-template <int MODE, int VEC, int TPR, int NCH>
+template <int MODE, int VEC, int TPR, int NCH, int PREF = 32>
 void launch_resident(const float *x, const float *w, const float *b, float *y, int64_t rows,
                      int64_t cols, const float *eps, const float *count, cudaStream_t st) {
   constexpr int RPB = TPR > 32 ? 1 : 8;
@@ -490,7 +535,7 @@ void launch_resident(const float *x, const float *w, const float *b, float *y, i
   int64_t blocks = (rows + RPB - 1) / RPB;
   const int64_t cap = (int64_t)sm_count() * 64;  // grid-stride beyond ~64 CTAs per SM
   if (blocks > cap * 16) blocks = cap * 16;
-  row_resident_kernel<MODE, VEC, TPR, NCH>
+  row_resident_kernel<MODE, VEC, TPR, NCH, PREF>
       <<<(unsigned)blocks, threads, 0, st>>>(x, w, b, y, rows, cols, eps, count);
 }
 
