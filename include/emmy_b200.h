@@ -243,9 +243,11 @@ int emmy_attention_f32(const float *q, const float *k, const float *v, float *o,
 /*
  * Attention-like chain, f16 in, f32 softmax and accumulation, per batch-head b:
  *   o[b] = softmax(q[b] @ k[b]^T * recip(*scale_div)) @ v[b]
- * q, k, v, o [B, S, D] (sq == sk and D in {64, 128, 256} run on the tcgen05
- * tensor cores: S = Q K^T and O += P V accumulate in tensor memory; other
- * shapes, or k pre-transposed [B, D, Sk], run on CUDA cores), o f16 or f32.
+ * q, k, v, o [B, S, D]; sq == sk with D a multiple of 8 up to 256 and
+ * 16-byte aligned tensors run on the tcgen05 tensor cores (S = Q K^T and
+ * O += P V accumulate in tensor memory; a D below 64 / 128 / 256 runs the
+ * kernel of that width with the missing columns zero-filled); other shapes,
+ * or k pre-transposed [B, D, Sk], run on CUDA cores; o f16 or f32.
  * Replaces the entry the reference emits for the attention IR shape
  * (reference ptxc/stmts.py:663-725, 564-611, 1311-1392) with f16 operands.
  */
