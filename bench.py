@@ -53,7 +53,8 @@ for _p in (str(ROOT), str(PKG)):
 # Multi-rank runs log NCCL's communicator set-up (ranks, devices, transports)
 # to stderr, keeping stdout for the JSON line; set before torch loads NCCL.
 if int(os.environ.get("WORLD_SIZE", "1")) > 1:
-    os.environ.setdefault("NCCL_DEBUG", "INFO")
+    if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+        os.environ["NCCL_DEBUG"] = "INFO"
     os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
     os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 

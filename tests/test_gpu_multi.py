@@ -44,7 +44,9 @@ def _worker(rank, world, port, q):
     root = Path(__file__).resolve().parent.parent
     for p in (str(root), str(root / "emmy-ptx-compiler-submission_b200")):
         sys.path.insert(0, p)
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    # NVLS off; NCCL's communicator set-up (ranks, devices) logged to stderr
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      NCCL_DEBUG="INFO", NCCL_DEBUG_SUBSYS="INIT", NCCL_DEBUG_FILE="/dev/stderr")
     import torch
     import torch.distributed as dist
     from emmy_ir import synth
