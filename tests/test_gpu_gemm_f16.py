@@ -43,6 +43,17 @@ IR_CASES = [
     ("edge_tiles_192x136x72", dict(M=192, N=136, K=72, dtype="f16", out_dtype="f32", bias=True,
                                    tm=64, tn=8, rm=4, rn=1, bk=8)),
     ("one_tile_128x256x64", dict(M=128, N=256, K=64, dtype="f16", out_dtype="f16", tm=64, tn=64)),
+    # CTA-pair kernel with a partial last round of tiles: 80 tiles on 74
+    # clusters with bias + ReLU, and the K3b shape with f32 output
+    ("pair_tail_split_40x256x512x256", dict(M=256, N=512, K=256, batch=40, dtype="f16",
+                                            out_dtype="f32", bias=True, relu=True, tm=128,
+                                            tn=128, rm=8, rn=8,
+                                            a_init={"dist": "normal", "std": STD},
+                                            b_init={"dist": "normal", "std": STD})),
+    ("pair_tail_split_K3b_f32out", dict(M=512, N=512, K=512, batch=64, dtype="f16",
+                                        out_dtype="f32", tm=128, tn=128, rm=8, rn=8,
+                                        a_init={"dist": "normal", "std": STD},
+                                        b_init={"dist": "normal", "std": STD})),
 ]
 
 
