@@ -117,6 +117,88 @@ __device__ __forceinline__ float gelu_tanh_f32(float x) {
   return __fdividef(x, 1.0f + e);
 }
 
+// gelu (tanh form) of a pair, the steps of gelu_tanh_f32 on packed f32x2
+// lanes (each lane rounded as its scalar form; sm_100 mul / fma / add
+// .f32x2), the exponential and the reciprocal on MUFU with subnormal results
+// flushed: e < 2^-126 leaves 1 + e = 1 either way, and x / (1 + e) below
+// 2^-126 rounds to 0 in any f16 output.
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t r, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float ex2_ftz(float a) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+__device__ __forceinline__ float rcp_ftz(float a) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+__device__ __forceinline__ uint64_t gelu_tanh_f32x2(uint64_t x) {
+  const uint64_t t = fma2(pk2(0.044715f, 0.044715f), mul2(mul2(x, x), x), x);
+  const uint64_t a = mul2(mul2(t, pk2(-1.5957691216057308f, -1.5957691216057308f)),
+                          pk2(1.4426950408889634f, 1.4426950408889634f));
+  float a0, a1;
+  upk2(a, a0, a1);
+  float d0, d1;
+  upk2(add2(pk2(ex2_ftz(a0), ex2_ftz(a1)), pk2(1.0f, 1.0f)), d0, d1);
+  return mul2(x, pk2(rcp_ftz(d0), rcp_ftz(d1)));
+}
+
+// One-step gelu (tanh form) on a contiguous f16 input with an f16 output: 8
+// elements per 16-byte load and store, GS groups per thread loaded before any
+// is computed, the pairs through gelu_tanh_f32x2.  n8 groups of 8.
+template <int GS>
+__global__ void __launch_bounds__(256)
+gelu_tanh_f16x8_kernel(const uint4 *__restrict__ x, uint4 *__restrict__ y, int64_t n8) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t g0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g0 < n8; g0 += GS * stride) {
+    uint4 in[GS];
+#pragma unroll
+    for (int u = 0; u < GS; ++u) {
+      const int64_t g = g0 + u * stride;
+      if (g < n8) in[u] = __ldcs(x + g);
+    }
+#pragma unroll
+    for (int u = 0; u < GS; ++u) {
+      const int64_t g = g0 + u * stride;
+      if (g >= n8) break;
+      const uint32_t w[4] = {in[u].x, in[u].y, in[u].z, in[u].w};
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[k]));
+        float lo, hi;
+        upk2(gelu_tanh_f32x2(pk2(f.x, f.y)), lo, hi);
+        const __half2 h = __floats2half2_rn(lo, hi);
+        o[k] = *reinterpret_cast<const uint32_t *>(&h);
+      }
+      __stcs(y + g, make_uint4(o[0], o[1], o[2], o[3]));
+    }
+  }
+}
+
 // One program step over the VEC lanes of this thread: RD[j*S] = op(RA[j*S], ...),
 // S the lane stride (the shared-memory register file's, or 1 for registers).
 template <typename T, int VEC, int S = kPwThreads>
@@ -787,7 +869,16 @@ static int pointwise_impl(const void *const *inputs, const int *input_dtypes,
 #define EMMY_PW_LAUNCH(T, OPC, IO) \
     launch_simple<T, OPC, IO>(q, out, out_dtype, n, gb, st, has_bc, gs)
     const bool has_bc = q.kind[0] == 3 || q.kind[1] == 3 || q.kind[2] == 3;
-    if (compiled(op) && !f32io) {                      // one f16 step, no post, no broadcast
+    if (compiled(op) && !f32io && op == PW_GELU_TANH && n % 8 == 0 && aligned16(q.ptr[0]) &&
+        aligned16(out)) {
+      // gelu on whole 8-element groups: 16-byte loads and stores, packed pairs
+      constexpr int GS = 2;
+      const int64_t n8 = n / 8;
+      int64_t blocks = (n8 + 256LL * GS - 1) / (256LL * GS);
+      if (blocks > INT32_MAX) blocks = INT32_MAX;
+      gelu_tanh_f16x8_kernel<GS><<<(unsigned)blocks, 256, 0, st>>>(
+          static_cast<const uint4 *>(q.ptr[0]), static_cast<uint4 *>(out), n8);
+    } else if (compiled(op) && !f32io) {               // one f16 step, no post, no broadcast
       switch (op) {
         case PW_GELU_TANH:
           pointwise_simple_kernel<float, PW_GELU_TANH, 2, 0, false, kPwSimpleGroups>

@@ -115,3 +115,25 @@ def test_unaligned_offsets_use_scalar_path():
     got = views["out"].cpu().numpy()
     assert np.array_equal(got, host["x0"] * host["x1"] - host["x0"])
     assert float(bufs["out"][0]) == 0.0                   # nothing written before the view
+
+
+def test_gelu_f16_whole_groups_matches_general_path_and_float64():
+    """f16 gelu (tanh form) on whole 8-element groups runs the packed 16-byte
+    kernel; one more 4-element group sends the same values through the
+    general f16 path.  Both within one f16 ulp (2e-3 * |ref| + 2e-3, as the
+    opcode test) of each other and of float64."""
+    n = 1 << 20
+    kop, meta = synth.pointwise(n, ("gelu_tanh", "x0"), "f16")
+    host = synth.make_inputs(meta)
+    _, _, out = run_on_gpu(kop, meta, host)
+    kop2, meta2 = synth.pointwise(n + 4, ("gelu_tanh", "x0"), "f16")
+    host2 = synth.make_inputs(meta2)
+    host2["x0"][:n] = host["x0"]
+    _, _, out2 = run_on_gpu(kop2, meta2, host2)
+    got = out["out"].astype(np.float64)
+    general = out2["out"][:n].astype(np.float64)
+    x = host["x0"].astype(np.float64)
+    ref = 0.5 * x * (1.0 + np.tanh(np.sqrt(2.0 / np.pi) * (x + 0.044715 * x ** 3)))
+    assert_close(got, general, 2e-3, 2e-3, "packed vs general f16 path")
+    assert_close(got, ref, 2e-3, 2e-3, "packed f16 path vs float64")
+    assert np.mean(got == general) > 0.99
