@@ -62,6 +62,48 @@ template <> __device__ __forceinline__ double fma_c(double a, double b, double c
 // the reference's exp: the fast exponential for f32 (ex2 of x*log2 e,
 // ptxc/expr.py:891-895); f64 keeps double precision
 __device__ __forceinline__ float exp_c(float v) { return __expf(v); }
+
+// Packed pairs of f32 (sm_100 sub / mul / add .f32x2, each lane rounded as
+// its scalar form) and the base-2 exponential with subnormal results flushed,
+// for the f16 softmax rows: e^(x - m) = 2^((x - m) log2 e), the subtract and
+// the multiply on pairs, as __expf(x - m) computes it lane by lane.  A
+// flushed p (below 2^-126) is 0 in the f16 output either way.
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t r, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float ex2_ftz(float a) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+// e^(x - m) for the two halves of h, as a packed pair (m2 = (m, m),
+// c2 = (log2 e, log2 e))
+__device__ __forceinline__ uint64_t exp_pair(__half2 h, uint64_t m2, uint64_t c2) {
+  const float2 f = __half22float2(h);
+  float t0, t1;
+  upk2(mul2(sub2(pk2(f.x, f.y), m2), c2), t0, t1);
+  return pk2(ex2_ftz(t0), ex2_ftz(t1));
+}
 __device__ __forceinline__ double exp_c(double v) { return exp(v); }
 
 template <typename TC> __device__ __forceinline__ TC max_seed() { return TC(-1e30); }
@@ -362,17 +404,17 @@ __global__ void __launch_bounds__(256) rows_f16_resident_kernel(const Args a) {
         for (int q = 0; q < 4; ++q) m = fmaxf(m, fmaxf(__low2float(h[q]), __high2float(h[q])));
       }
       m = allreduce(m, true);
-      float s = 0.f;
+      const uint64_t c2 = pk2(1.4426950408889634f, 1.4426950408889634f), m2 = pk2(m, m);
+      uint64_t s2[2] = {0ull, 0ull};
 #pragma unroll
       for (int k = 0; k < CH; ++k) {
         const __half2 *h = reinterpret_cast<const __half2 *>(&v[k]);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          s += exp_c(__low2float(h[q]) - m);
-          s += exp_c(__high2float(h[q]) - m);
-        }
+        for (int q = 0; q < 4; ++q) s2[q & 1] = add2(s2[q & 1], exp_pair(h[q], m2, c2));
       }
-      s = allreduce(s, false);
+      float s0, s1;
+      upk2(add2(s2[0], s2[1]), s0, s1);
+      const float s = allreduce(s0 + s1, false);
       sc = 1.0f / s;
       sh = m;                                         // softmax: e^(x - sh) * sc
     } else if constexpr (MODE == M_RMS) {
@@ -427,8 +469,13 @@ __global__ void __launch_bounds__(256) rows_f16_resident_kernel(const Args a) {
         for (int q = 0; q < 4; ++q) {
           const float lo = __low2float(h[q]), hi = __high2float(h[q]);
           if constexpr (MODE == M_SOFTMAX) {
-            o[2 * q] = exp_c(lo - sh) * sc;
-            o[2 * q + 1] = exp_c(hi - sh) * sc;
+            float p0, p1;
+            upk2(exp_pair(h[q], pk2(sh, sh), pk2(1.4426950408889634f, 1.4426950408889634f)), p0,
+                 p1);
+            o[2 * q] = p0 * sc;
+            o[2 * q + 1] = p1 * sc;
+            (void)lo;
+            (void)hi;
           } else if constexpr (MODE == M_RMS) {
             o[2 * q] = lo * sc;
             o[2 * q + 1] = hi * sc;
