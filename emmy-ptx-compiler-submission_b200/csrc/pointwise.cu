@@ -871,8 +871,9 @@ static int pointwise_impl(const void *const *inputs, const int *input_dtypes,
     const bool has_bc = q.kind[0] == 3 || q.kind[1] == 3 || q.kind[2] == 3;
     if (compiled(op) && !f32io && op == PW_GELU_TANH && n % 8 == 0 && aligned16(q.ptr[0]) &&
         aligned16(out)) {
-      // gelu on whole 8-element groups: 16-byte loads and stores, packed pairs
-      constexpr int GS = 2;
+      // gelu on whole 8-element groups: 16-byte loads and stores, packed pairs;
+      // eight groups (128 bytes) in flight per thread before any compute
+      constexpr int GS = 8;
       const int64_t n8 = n / 8;
       int64_t blocks = (n8 + 256LL * GS - 1) / (256LL * GS);
       if (blocks > INT32_MAX) blocks = INT32_MAX;
