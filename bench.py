@@ -505,6 +505,10 @@ def family_cases():
             16384 * 4096, ("relu", ("add", "x0", ("bcast", "b", 4096, 1, 4096))), "f32",
             shape=[16384, 4096]),
         "X_softmax_f16_16384x4096": synth.retype(*synth.softmax([16384, 4096]), "f16", acc="f32"),
+        # integer programs (the reference's integer Assign path)
+        "F8d_pointwise_int_add_i32_2^26": synth.pointwise(1 << 26, ("add", "x0", "x1"), "i32"),
+        "F8e_pointwise_int_u8_sub_clamp_2^26": synth.pointwise(
+            1 << 26, ("maximum", ("subtract", "x0", "x1"), ("imm", 0)), "u8"),
     }
 
 
@@ -781,11 +785,12 @@ def reference_ptx_families():
              "K4a_splitk_f32": "K4a_splitk_f32_256x65536x256",
              "K3a_gemm_f16": "K3a_gemm_f16_4096x2048x8192_bias_relu",
              "K3b_bmm_f16": "K3b_bmm_f16_64x512", "K5_attention_f16": "K5_attention_f16_8x32x512x128",
-             "F8a_pointwise_add": "F8a_pointwise_add_f32_2^26"}
+             "F8a_pointwise_add": "F8a_pointwise_add_f32_2^26",
+             "F8d_pointwise_int": "F8d_pointwise_int_add_i32_2^26"}
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     flush = L2Flush(dev)
-    dts = {"f32": torch.float32, "f16": torch.float16, "f64": torch.float64}
+    from ptxc.launch import torch_dtype
     out = {}
     for name, make in BENCH_CASES.items():
         if not ref_ptx.available(name):
@@ -793,7 +798,8 @@ def reference_ptx_families():
         kop, meta = make(synth)
         k = ref_ptx.RefKernel(name)
         nbytes = sum((math.prod(a["shape"]) if a["shape"] else 1) *
-                     torch.empty((), dtype=dts[a["dtype"]]).element_size() for a in meta["args"])
+                     torch.empty((), dtype=torch_dtype(a["dtype"])).element_size()
+                     for a in meta["args"])
         # the harness zeroes these before every launch (atomic split-K outputs)
         zero = k.k.get("zero_outputs") or []
 
@@ -801,10 +807,10 @@ def reference_ptx_families():
             ts = {}
             for a in meta["args"]:
                 n = math.prod(a["shape"]) if a["shape"] else 1
-                t = torch.empty(n, dtype=dts[a["dtype"]], device=dev)
+                t = torch.empty(n, dtype=torch_dtype(a["dtype"]), device=dev)
                 if "data" in a:
-                    t.fill_(float(a["data"][0]))
-                elif a.get("output"):
+                    t.fill_(a["data"][0])
+                elif a.get("output") or not t.is_floating_point():
                     t.zero_()
                 else:
                     t.normal_()

@@ -19,6 +19,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "pw_index.cuh"
 
 namespace emmy {
 
@@ -31,32 +32,6 @@ enum PwOp {
   PW_WHERE, PW_ROUND_F16, PW_FMA, PW_LOG2, PW_LOG10, PW_COS, PW_SIN, PW_TAN, PW_ERF, PW_GELU,
   PW_GELU_TANH, PW_SOFTPLUS, PW_EXP2, PW_SILU, PW_POW, PW_FLOOR, PW_CEIL, PW_SIGN, PW_NE, PW_NOPS
 };
-
-// A broadcast input is read at ((first + e) / div) % mod for element e (mod
-// 0: no modulo).  The quotients use the round-up multiply-shift method for
-// division by an invariant integer (Granlund & Montgomery, PLDI 1994, fig.
-// 4.1): q = (t + ((x - t) >> 1)) >> (l - 1), t = mulhi(magic, x), l =
-// ceil(log2 d), magic = floor(2^64 (2^l - d) / d) + 1; exact for all 64-bit x.
-struct PwDiv {
-  unsigned long long d, magic;
-  int shift;                       // l - 1; -1 when d == 1
-};
-
-struct PwIndex {
-  PwDiv div, mod;
-  int bcast;                       // 0: input read at e (contiguous)
-  int has_mod;
-};
-
-__host__ __device__ inline unsigned long long pw_div(const PwDiv &v, unsigned long long x) {
-#ifdef __CUDA_ARCH__
-  if (v.shift < 0) return x;
-  const unsigned long long t = __umul64hi(v.magic, x);
-  return (t + ((x - t) >> 1)) >> v.shift;
-#else
-  return x / v.d;
-#endif
-}
 
 struct PwProgram {
   PwIndex idx[kPwMaxIn];
@@ -666,22 +641,6 @@ void dispatch_inputs(const PwProgram &p, int nregs, void *out, int out_dtype, in
     case 4: launch_pointwise<T, VEC, 4, 1>(p, nregs, out, out_dtype, n, st); break;
     default: launch_pointwise<T, VEC, -1, 1>(p, nregs, out, out_dtype, n, st); break;
   }
-}
-
-// Host: the multiply-shift constants for division by d (1 <= d < 2^62).
-static PwDiv make_div(unsigned long long d) {
-  PwDiv v{};
-  v.d = d;
-  if (d == 1) {
-    v.shift = -1;
-    return v;
-  }
-  int l = 0;
-  while ((1ull << l) < d) ++l;
-  const unsigned __int128 num = ((unsigned __int128)((1ull << l) - d)) << 64;
-  v.magic = (unsigned long long)(num / d) + 1;
-  v.shift = l - 1;
-  return v;
 }
 
 }  // namespace emmy

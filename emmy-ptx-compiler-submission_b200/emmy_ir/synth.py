@@ -37,8 +37,14 @@ DT = {
     "f16": DataType(name="f16", np=NpDType("float16"), nbytes=2),
     "f64": DataType(name="f64", np=NpDType("float64"), nbytes=8),
 }
-C_NAME = {"f32": "float", "f16": "half", "f64": "double"}
-NP = {"f32": np.float32, "f16": np.float16, "f64": np.float64}
+# integer buffers (the reference's dtype table, ptxc/ops.py:12-25)
+INT_NP = {"i8": np.int8, "u8": np.uint8, "i16": np.int16, "u16": np.uint16, "i32": np.int32,
+          "u32": np.uint32, "i64": np.int64, "u64": np.uint64}
+for _k, _t in INT_NP.items():
+    DT[_k] = DataType(name=_k, np=NpDType(np.dtype(_t).name), nbytes=np.dtype(_t).itemsize)
+C_NAME = {"f32": "float", "f16": "half", "f64": "double", "i32": "int", "u32": "unsigned",
+          "i64": "long", "i16": "short", "i8": "char"}
+NP = {"f32": np.float32, "f16": np.float16, "f64": np.float64, **INT_NP}
 
 
 def V(name):
@@ -367,7 +373,11 @@ def matvec(rows, cols, dtype="f64", block=128, entry="k_matvec"):
 
 
 def make_inputs(meta: dict, seed_offset: int = 0, only=None) -> dict:
-    """Seeded host inputs (numpy) for every argument, outputs zero-filled."""
+    """Seeded host inputs (numpy) for every argument, outputs zero-filled.
+
+    Integer arguments draw uniformly from the dtype's range (or from
+    ``{"dist": "int", "low": a, "high": b}``); a float ``init`` on an integer
+    argument is drawn as floats and truncated toward zero."""
     out = {}
     for a in meta["args"]:
         if only is not None and a["name"] not in only:
@@ -381,6 +391,14 @@ def make_inputs(meta: dict, seed_offset: int = 0, only=None) -> dict:
         else:
             rng = np.random.default_rng(a.get("seed", 0) + seed_offset)
             init = a.get("init")
+            if np.dtype(dt).kind in "iu" and (init is None or init.get("dist") == "int"):
+                # integers: the dtype's whole range, or {"dist": "int", "low", "high"}
+                # (both ends included)
+                info = np.iinfo(dt)
+                lo = info.min if init is None else max(int(init["low"]), int(info.min))
+                hi = info.max if init is None else min(int(init["high"]), int(info.max))
+                out[a["name"]] = rng.integers(lo, hi, size=n, endpoint=True, dtype=dt)
+                continue
             if init is None:
                 v = rng.standard_normal(n)
             elif init.get("dist") == "normal":
@@ -583,6 +601,9 @@ def attention(B, H, S, D, dtype="f16", out_dtype=None, scale_div=None, entry="k_
 
 BOOL = DataType(name="bool", np=NpDType("bool"), nbytes=1)
 _COMPARE = {"greater", "less", "greater_equal", "less_equal", "equal", "not_equal"}
+# predicate-valued ops of the reference's Assign (ptxc/stmts.py:516-518, ptxc/common.py:20-23)
+_LOGICAL = {"logical_and", "logical_or", "logical_not", "bitwise_and", "bitwise_or",
+            "bitwise_not", "and", "or", "not"}
 
 
 def pointwise(n, expr, dtype="f32", shape=None, block=256, unroll=None, entry="k_pointwise",
@@ -624,7 +645,7 @@ def pointwise(n, expr, dtype="f32", shape=None, block=256, unroll=None, entry="k
             if e not in inputs:
                 inputs.append(e)
         elif e[0] == "const":
-            consts[e[1]] = float(e[2])
+            consts[e[1]] = int(e[2]) if dtype in INT_NP else float(e[2])
         elif e[0] == "bcast":
             if e[1] not in inputs:
                 inputs.append(e[1])
@@ -696,12 +717,13 @@ def pointwise(n, expr, dtype="f32", shape=None, block=256, unroll=None, entry="k
             if e[0] == "imm":
                 nm = f"k{counter[0]}__u{u}"
                 counter[0] += 1
-                body.append(Let(name=nm, value=L(float(e[1])), dtype=DT[dtype]))
+                body.append(Let(name=nm, value=L(int(e[1]) if dtype in INT_NP else float(e[1])),
+                                dtype=DT[dtype]))
                 return nm
             args = [emit(a) for a in e[1:]]
             nm = f"v{counter[0]}__u{u}"
             counter[0] += 1
-            dt = BOOL if e[0] in _COMPARE else DT[dtype]
+            dt = BOOL if e[0] in _COMPARE or e[0] in _LOGICAL else DT[dtype]
             body.append(Assign(name=nm, op=E(e[0]), args=tuple(args), dtype=dt))
             return nm
         results.append(emit(expr))

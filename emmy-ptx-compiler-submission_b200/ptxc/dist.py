@@ -106,7 +106,7 @@ def shard_plan(plan: dict, rank: int, world: int):
         set_shape(a["k"], [hi - lo, g["d"], g["sk"]] if g["k_transposed"] else [hi - lo, g["sk"], g["d"]])
         set_shape(a["v"], [hi - lo, g["sk"], g["dv"]])
         set_shape(a["o"], [hi - lo, g["sq"], g["dv"]])
-    elif fam == "pointwise":
+    elif fam in ("pointwise", "pointwise_int"):
         g = plan["pointwise"]
         lo, hi = shard_ranges(g["n"], world)[rank]
         sub["pointwise"]["n"] = hi - lo

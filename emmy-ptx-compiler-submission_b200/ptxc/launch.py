@@ -52,13 +52,16 @@ SIGNATURES = {
                        _i64, _vp],
     "emmy_pointwise_indexed": [_vp, _vp, _vp, _int, _vp, _vp, _int, _vp, _int, _vp, _int, _int, _int,
                                _vp, _int, _i64, _i64, _vp],
+    "emmy_pointwise_int": [_vp, _vp, _vp, _int, _vp, _vp, _int, _vp, _int, _vp, _int, _int, _vp,
+                           _int, _i64, _i64, _vp],
 }
 RESTYPES = {"emmy_reduce_workspace_bytes": _sz}
 
 REDUCE_OP = {"sum": 0, "max": 1, "min": 2}
 REDUCE_PRE = {"identity": 0, "square": 1, "abs": 2}
 NORM_MODE = {"rms": 0, "l2": 1, "layer": 2}
-DT_CODE = {"f32": 0, "f16": 1, "f64": 2}
+DT_CODE = {"f32": 0, "f16": 1, "f64": 2, "i8": 3, "u8": 4, "i16": 5, "u16": 6, "i32": 7,
+           "u32": 8, "i64": 9, "u64": 10}
 
 
 class LibraryError(RuntimeError):
@@ -121,7 +124,8 @@ def torch_dtype(dt: str):
     if _TORCH_DT is None:
         _TORCH_DT = {"f32": torch.float32, "f16": torch.float16, "f64": torch.float64,
                      "i32": torch.int32, "i64": torch.int64, "i8": torch.int8,
-                     "u8": torch.uint8, "bool": torch.bool, "i16": torch.int16}
+                     "u8": torch.uint8, "bool": torch.bool, "i16": torch.int16,
+                     "u16": torch.uint16, "u32": torch.uint32, "u64": torch.uint64}
     return _TORCH_DT[dt]
 
 
@@ -252,6 +256,27 @@ def run(plan: dict, tensors: dict, stream=None, workspace=None, check: bool = Tr
                                       len(imms), prog, len(g["program"]), g["result_reg"],
                                       int(g["compute"] == "f64"), _ptr(T("out")),
                                       DT_CODE[g["out_dtype"]], g["n"], st), "emmy_pointwise")
+        launches += 1
+    elif fam == "pointwise_int":
+        g = plan["pointwise"]
+        ins, scs, imms = g["inputs"], g["scalars"], g["immediates"]
+        in_ptrs = (_vp * max(1, len(ins)))(*[_ptr(tensors[n]) for n in ins])
+        in_dts = (_int * max(1, len(ins)))(*[DT_CODE[plan["tensors"][n]["dtype"]] for n in ins])
+        sc_ptrs = (_vp * max(1, len(scs)))(*[_ptr(tensors[n]) for n in scs])
+        sc_dts = (_int * max(1, len(scs)))(*[DT_CODE[plan["tensors"][n]["dtype"]] for n in scs])
+        imm = (ctypes.c_int64 * max(1, len(imms)))(*[int(v) for v in imms])
+        flat = [int(x) for row in g["program"] for x in row]
+        prog = (_int * len(flat))(*flat)
+        idx_arr = None
+        if "input_index" in g:
+            idx = []
+            for n, (d, m) in zip(ins, g["input_index"]):
+                idx += [int(d), int(m), tensors[n].numel()]
+            idx_arr = (ctypes.c_int64 * len(idx))(*idx)
+        _check(lib.emmy_pointwise_int(in_ptrs, in_dts, idx_arr, len(ins), sc_ptrs, sc_dts, len(scs),
+                                      imm, len(imms), prog, len(g["program"]), g["result_reg"],
+                                      _ptr(T("out")), DT_CODE[g["out_dtype"]],
+                                      int(g.get("first", 0)), g["n"], st), "emmy_pointwise_int")
         launches += 1
     else:
         raise ValueError(f"plan family {fam!r} has no launcher")

@@ -86,12 +86,12 @@ def match_pointwise(kop, tile, meta) -> dict:
                 a2[""] = a2.get("", 0) + i
                 defs[nm] = ("load", st.input, a2)
         elif k == "Let":
-            defs[st.name] = ("let", float(getattr(st.value, "value", st.value)))
+            v = getattr(st.value, "value", st.value)
+            need(isinstance(v, (int, float)) and not isinstance(v, bool), "Let of a non-literal")
+            defs[st.name] = ("let", v, norm_dtype(st.dtype) if st.dtype else "f32")
         elif k == "Assign":
-            op = ALIASES.get(op_name(st.op), op_name(st.op))
-            need(op in OPCODES, f"no pointwise kernel op for {op!r}")
-            need(len(st.args) == ARITY.get(op, 1 if op in UNARY else 2), f"{op} arity")
-            defs[st.name] = ("op", op, tuple(st.args), norm_dtype(st.dtype) if st.dtype else None)
+            defs[st.name] = ("op", op_name(st.op), tuple(st.args),
+                             norm_dtype(st.dtype) if st.dtype else None)
 
     # written elements: (offset affine, value name)
     elems = []
@@ -125,7 +125,7 @@ def match_pointwise(kop, tile, meta) -> dict:
         d = defs.get(name)
         need(d is not None, f"undefined value {name!r}")
         if d[0] == "let":
-            r = ("imm", d[1])
+            r = ("imm", d[1], d[2])
         elif d[0] == "load":
             tensor, aff = d[1], d[2]
             tn = math.prod(shapes[tensor]) if shapes[tensor] else 1
@@ -155,6 +155,8 @@ def match_pointwise(kop, tile, meta) -> dict:
     forms = [canon(v, a, {}) for a, v in elems]
     need(all(f == forms[0] for f in forms), "elements compute different expressions")
     form = forms[0]
+    if _is_integer_program(form, dtypes, out):
+        return _lower_integer(form, dtypes, out, numel)
 
     # lower the expression tree to a register program
     prog = []
@@ -167,9 +169,14 @@ def match_pointwise(kop, tile, meta) -> dict:
         return (kind, key)
 
     def emit(node):
-        if node[0] in ("input", "scalar", "imm"):
+        if node[0] == "imm":
+            return leaf_reg("imm", float(node[1]))
+        if node[0] in ("input", "scalar"):
             return leaf_reg(node[0], node[1])
         _, op, args, dt = node
+        op = ALIASES.get(op, op)
+        need(op in OPCODES, f"no pointwise kernel op for {op!r}")
+        need(len(args) == ARITY.get(op, 1 if op in UNARY else 2), f"{op} arity")
         srcs = [emit(a) for a in args]
         prog.append([op, srcs])
         ref = ("tmp", len(prog) - 1)
@@ -217,4 +224,180 @@ def match_pointwise(kop, tile, meta) -> dict:
                       **({"input_index": in_index, "first": 0}
                          if any(D for D, _ in in_index) else {})},
         "params": {}, "dtypes": {"out": dtypes[out]},
+    }
+
+
+# ---------------------------------------------------------------------------
+# Integer programs (reference ptxc/stmts.py:509-560 Assign, ptxc/ops.py:98-117
+# INT_BINARY, ptxc/expr.py:815-877 predicates / where, :233-280 the store).
+# The reference types each Assign by its dtype (or, untyped, by its first
+# operand's kind): comparisons, and / or (``bitwise_and`` / ``bitwise_or``
+# too) and typed-bool ops give predicates, float types go to the float path,
+# every other op runs on s64.  A program with any integer value runs on the
+# integer kernel (``emmy_pointwise_int``), whose opcodes are these:
+
+INT_KINDS = {"i8", "u8", "i16", "u16", "i32", "u32", "i64", "u64"}
+FLOAT_KINDS = {"f16", "f32", "f64"}
+INT_OPCODES = {
+    "copy": 0, "add": 1, "subtract": 2, "multiply": 3, "divide": 4, "remainder": 5,
+    "left_shift": 6, "right_shift": 7, "bitwise_xor": 8, "maximum": 9, "minimum": 10,
+    "equal": 11, "not_equal": 12, "greater": 13, "less": 14, "greater_equal": 15,
+    "less_equal": 16, "and": 17, "or": 18, "not": 19, "where": 20,
+}
+INT_ALIASES = {"sum": "add", "sub": "subtract", "prod": "multiply", "floor_divide": "divide",
+               "true_divide": "divide", "mod": "remainder", "amax": "maximum"}
+CMP_ALIASES = {"eq": "equal", "ne": "not_equal", "gt": "greater", "lt": "less",
+               "ge": "greater_equal", "le": "less_equal"}
+BOOL_BINARY = {"bitwise_and": "and", "logical_and": "and", "and": "and",
+               "bitwise_or": "or", "logical_or": "or", "or": "or"}
+BOOL_NOT = {"bitwise_not", "logical_not", "not"}
+
+
+def _leaf_kind(node, dtypes):
+    if node[0] == "input":
+        return dtypes[node[1][0]]
+    if node[0] == "scalar":
+        return dtypes[node[1]]
+    return node[2]                                     # imm: the Let's dtype
+
+
+def _kind(node, dtypes):
+    """The reference's kind of a value: a dtype name, "i64" or "pred"."""
+    if node[0] != "op":
+        return _leaf_kind(node, dtypes)
+    _, op, args, dt = node
+    dt = dt or _kind(args[0], dtypes)
+    if dt == "bool" or op in CMP_ALIASES or op in COMPARES or op in BOOL_BINARY:
+        return "pred"
+    if op == "where":
+        return "f32" if (dt in FLOAT_KINDS or _kind(args[1], dtypes) in FLOAT_KINDS
+                         or _kind(args[2], dtypes) in FLOAT_KINDS) else "i64"
+    if dt in FLOAT_KINDS:
+        return dt
+    if op in ("copy", "pad", "bitcast"):
+        return _kind(args[0], dtypes)
+    return "i64"
+
+
+def _is_integer_program(form, dtypes, out) -> bool:
+    seen = []
+
+    def walk(node):
+        seen.append(_kind(node, dtypes))
+        if node[0] == "op":
+            for a in node[2]:
+                walk(a)
+    walk(form)
+    return dtypes[out] in INT_KINDS or any(k in INT_KINDS or k == "i64" for k in seen)
+
+
+def _rzi_f32(v) -> int:
+    """A float literal as an s64 operand: its f32 value, truncated toward zero."""
+    import numpy as np
+    f = float(np.float32(v))
+    need(math.isfinite(f) and abs(f) < 2.0 ** 63, "integer immediate out of range")
+    return int(f)
+
+
+def _lower_integer(form, dtypes, out, numel) -> dict:
+    out_dt = dtypes[out]
+    need(out_dt in INT_KINDS or out_dt in FLOAT_KINDS, f"output dtype {out_dt!r}")
+    inputs, scalars, imms, prog = [], [], [], []
+
+    def leaf(node):
+        if node[0] == "imm":
+            v = node[1]
+            v = _rzi_f32(v) if isinstance(v, float) else int(v)
+            v = (v + (1 << 63)) % (1 << 64) - (1 << 63)            # mov.s64 of the literal
+            key, lst = ("imm", v), imms
+        elif node[0] == "scalar":
+            key, lst = ("scalar", node[1]), scalars
+        else:
+            key, lst = ("input", node[1]), inputs
+        need(_leaf_kind(node, dtypes) in INT_KINDS | FLOAT_KINDS, "leaf dtype")
+        if key[1] not in lst:
+            lst.append(key[1])
+        return key
+
+    def operand(node, what):
+        k = _kind(node, dtypes)
+        need(k != "pred", f"a predicate used as an integer operand ({what})")
+        need(node[0] != "op" or k not in FLOAT_KINDS, f"float arithmetic in an integer program ({what})")
+        return emit(node)
+
+    def cond(node):
+        k = _kind(node, dtypes)
+        need(node[0] != "op" or k not in FLOAT_KINDS, "float value as an integer predicate")
+        need(k not in FLOAT_KINDS, "a float value tested in an integer program")
+        return emit(node)
+
+    def emit(node):
+        if node[0] != "op":
+            return leaf(node)
+        _, op, args, dt = node
+        k = _kind(node, dtypes)
+        if op in ("copy", "pad", "bitcast"):
+            need(len(args) == 1, f"{op} arity")
+            return emit(args[0])                       # mov: the value, its kind kept
+        if k == "pred":
+            if op in BOOL_BINARY:
+                need(len(args) == 2, f"{op} arity")
+                name, srcs = BOOL_BINARY[op], [cond(args[0]), cond(args[1])]
+            elif op in BOOL_NOT:
+                need(len(args) == 1, f"{op} arity")
+                name, srcs = "not", [cond(args[0])]
+            else:
+                name = CMP_ALIASES.get(op, op)
+                need(name in COMPARES, f"unsupported boolean op {op!r}")
+                need(len(args) == 2, f"{op} arity")
+                need(not any(_kind(a, dtypes) in FLOAT_KINDS for a in args),
+                     "comparison of float values in an integer program")
+                srcs = [operand(args[0], op), operand(args[1], op)]
+        elif k in FLOAT_KINDS:
+            need(False, f"float arithmetic in an integer program ({op})")
+        elif op == "where":
+            need(len(args) == 3, "where arity")
+            name, srcs = "where", [cond(args[0]), operand(args[1], op), operand(args[2], op)]
+        else:
+            name = INT_ALIASES.get(op, op)
+            need(name in INT_OPCODES and name not in COMPARES and name not in ("and", "or", "not",
+                                                                                 "where", "copy"),
+                 f"unsupported integer op {op!r}")
+            need(len(args) == 2, f"{op} arity")
+            srcs = [operand(args[0], op), operand(args[1], op)]
+        prog.append([name, srcs])
+        return ("tmp", len(prog) - 1)
+
+    need(_kind(form, dtypes) != "pred", "cannot store a predicate value as a scalar")
+    result = emit(form)
+    if result[0] != "tmp":
+        prog.append(["copy", [result]])
+        result = ("tmp", len(prog) - 1)
+    in_keys = inputs
+    base = {"input": 0, "scalar": len(in_keys), "imm": len(in_keys) + len(scalars)}
+    ntmp0 = len(in_keys) + len(scalars) + len(imms)
+
+    def reg_of(ref):
+        if ref[0] == "tmp":
+            return ntmp0 + ref[1]
+        lst = {"input": in_keys, "scalar": scalars, "imm": imms}[ref[0]]
+        return base[ref[0]] + lst.index(ref[1])
+
+    program = []
+    for i, (name, srcs) in enumerate(prog):
+        rs = [reg_of(x) for x in srcs] + [0] * (3 - len(srcs))
+        program.append([INT_OPCODES[name], ntmp0 + i] + rs)
+    need(ntmp0 + len(prog) <= MAX_REGS and len(prog) <= MAX_INSTR, "pointwise program too large")
+    need(len(in_keys) <= 8 and len(scalars) <= 8 and len(imms) <= 8, "pointwise program too large")
+    in_index = [[D, M] for _, D, M in in_keys]
+    names = [t for t, _, _ in in_keys]
+    return {
+        "family": "pointwise_int", "symbol": "emmy_pointwise_int",
+        "args": {"out": out},
+        "pointwise": {"n": numel, "inputs": names, "scalars": scalars, "immediates": imms,
+                      "program": program, "result_reg": ntmp0 + len(prog) - 1,
+                      "compute": "i64", "out_dtype": out_dt,
+                      **({"input_index": in_index, "first": 0}
+                         if any(D for D, _ in in_index) else {})},
+        "params": {}, "dtypes": {"out": out_dt},
     }

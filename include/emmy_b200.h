@@ -55,6 +55,15 @@ extern "C" {
 #define EMMY_DT_F32 0
 #define EMMY_DT_F16 1
 #define EMMY_DT_F64 2
+/* integer buffers (emmy_pointwise_int only) */
+#define EMMY_DT_I8 3
+#define EMMY_DT_U8 4
+#define EMMY_DT_I16 5
+#define EMMY_DT_U16 6
+#define EMMY_DT_I32 7
+#define EMMY_DT_U32 8
+#define EMMY_DT_I64 9
+#define EMMY_DT_U64 10
 
 /* GEMM epilogue bits, applied in this order: round the f32 product to f16
  * (ROUND_F16; emmy_gemm_f16 only: the f16 intermediate of a matmul kernel
@@ -300,6 +309,37 @@ int emmy_pointwise_indexed(const void *const *inputs, const int *input_dtypes,
                            const double *immediates, int n_imm, const int *program, int n_instr,
                            int result_reg, int compute_f64, void *out, int out_dtype,
                            int64_t first, int64_t n, void *stream);
+
+/*
+ * Integer pointwise program: out[e] = program(inputs at e, scalars, immediates)
+ * for e < n, evaluated on signed 64-bit values.  Replaces the entry the
+ * reference emits for a pointwise IR whose Assigns are integer-typed
+ * (ptxc/stmts.py:509-560, INT_BINARY in ptxc/ops.py:98-117, operand widening
+ * ptxc/expr.py:157-165 and 211-223, div / rem :697-716, predicates and where
+ * :815-877, the converting store :233-280).
+ * Inputs, scalars and the output may be any EMMY_DT_* type.  An integer
+ * element is sign- or zero-extended to s64, a float one truncated toward zero
+ * (cvt.rzi.s64: clamped to the s64 range, NaN to -2^63); the result is stored as
+ * its low bits (integer output) or rounded to nearest (float output; f16 via
+ * f32).  input_index: NULL, or per input three int64 [div, mod, numel] --
+ * div 0: contiguous, else the input is read at ((first + e) / div) % mod
+ * (mod 0: no modulo) and every read must stay below numel.
+ * program: n_instr rows of five ints [opcode, dst, a, b, c] over registers
+ * 0..n_inputs-1 (inputs), then the scalars, the immediates and the
+ * temporaries (dst must be a temporary; at most 32 registers, 48 steps, 8
+ * inputs / scalars / immediates).  Opcodes: 0 copy, 1 add, 2 sub, 3 mul
+ * (wrapping), 4 div, 5 rem (toward zero, as div.s64 / rem.s64; a zero divisor
+ * gives an unspecified value), 6 shl, 7 shr (arithmetic; by the low 32 bits of
+ * b, 64 or more: 0 / the sign), 8 xor, 9 max, 10 min, 11-16 eq ne gt lt ge le
+ * (signed, 0 or 1), 17 and, 18 or (of b != 0 and a != 0), 19 not, 20 where
+ * (a != 0 ? b : c).
+ */
+int emmy_pointwise_int(const void *const *inputs, const int *input_dtypes,
+                       const int64_t *input_index, int n_inputs,
+                       const void *const *scalars, const int *scalar_dtypes, int n_scalars,
+                       const int64_t *immediates, int n_imm, const int *program, int n_instr,
+                       int result_reg, void *out, int out_dtype, int64_t first, int64_t n,
+                       void *stream);
 
 /*
  * Long-row reduction that allocates nothing: y[0] = fold_op(pre(x[0..n))) [* 1/count].

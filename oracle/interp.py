@@ -66,11 +66,19 @@ from emmy_ir.nodes import (  # noqa: E402
     BinaryExpr, Builtin, CastExpr, Dim, Literal, TernaryExpr, Var, dtype_name, iter_stmts,
 )
 
+# u16 / u32 / u64 buffers are held as the signed tensor of the same width (the
+# same bits; ``run_ir`` views them so) and widened with a mask on load
 TORCH_DT = {"f32": torch.float32, "f16": torch.float16, "f64": torch.float64,
             "i32": torch.int32, "i64": torch.int64, "u8": torch.uint8, "i8": torch.int8,
+            "i16": torch.int16, "u16": torch.int16, "u32": torch.int32, "u64": torch.int64,
             "bool": torch.bool}
 NP_DT = {"f32": np.float32, "f16": np.float16, "f64": np.float64, "i32": np.int32,
-         "i64": np.int64, "u8": np.uint8, "i8": np.int8, "bool": np.bool_}
+         "i64": np.int64, "u8": np.uint8, "i8": np.int8, "i16": np.int16, "u16": np.uint16,
+         "u32": np.uint32, "u64": np.uint64, "bool": np.bool_}
+INT_DT = {"i8", "u8", "i16", "u16", "i32", "u32", "i64", "u64"}
+_UNSIGNED_MASK = {"u16": 0xFFFF, "u32": 0xFFFFFFFF}
+_SIGNED_VIEW = {np.dtype(np.uint16): np.int16, np.dtype(np.uint32): np.int32,
+                np.dtype(np.uint64): np.int64}
 
 IDENTITY = {"add": 0.0, "sum": 0.0, "multiply": 1.0, "prod": 1.0,
             "maximum": -1e30, "amax": -1e30, "minimum": 1e30}
@@ -366,6 +374,9 @@ class IRInterpreter:
         dt = dtype_name(st.dtype)
         kind = _compute_kind(dt)
         value = getattr(st.value, "value", st.value)
+        if dt in INT_DT and isinstance(value, float):
+            # a float literal in an integer Let: its f32 value, truncated (cvt.rzi.s64.f32)
+            value = int(_rzi_s64(torch.tensor([value], dtype=torch.float32))[0])
         self._set(st.name, self._const(value, kind).expand(self.L), kind, mask)
 
     def s_Init(self, st, mask):
@@ -407,16 +418,26 @@ class IRInterpreter:
             elif kind == "f64":
                 raw = raw.to(torch.float64)
             else:
+                # ld.s8 / ld.u8 ... widen with sign or zero extension
                 raw = raw.to(torch.int64)
+                if dt in _UNSIGNED_MASK:
+                    raw = raw & _UNSIGNED_MASK[dt]
             self._set(name, raw, kind, mask)
 
     def _convert(self, v, kind, dt):
+        """The store conversion (reference ``_cast_reg``, ptxc/expr.py:233-280)."""
         tdt = TORCH_DT[dt]
         if dt in ("f32", "f16", "f64"):
+            if kind not in ("f32", "f64", "f16", "pred"):
+                # an s64 value: cvt.rn.f64.s64, or cvt.rn.f32.s64 (then cvt.rn.f16.f32)
+                if dt == "f64":
+                    return v.to(torch.float64)
+                return v.to(torch.float32).to(tdt)
             return v.to(tdt)
         if kind in ("f32", "f64"):
-            return torch.trunc(v).to(tdt)
-        return v.to(tdt)
+            v = _rzi_s64(v)
+        # the low bits of the s64 value (st.u8 / cvt.s32.s64 ...)
+        return v.to(torch.int64).to(tdt)
 
     def s_Write(self, st, mask):
         if st.output in self.smem:
@@ -461,6 +482,12 @@ class IRInterpreter:
         vals = [self._value(a) for a in st.args]
         dt = dtype_name(st.dtype) if st.dtype is not None else None
         kinds = [k for _, k in vals]
+        if dt is None or dt in INT_DT or dt == "bool" or any(k in INT_DT or k == "pred"
+                                                              for k in kinds):
+            res = _int_assign(opname, dt, vals)
+            if res is not None:
+                self._set(st.name, res[0], res[1], mask)
+                return
         if dt is None:
             kind = "f64" if "f64" in kinds else ("f32" if any(k in ("f32", "f16") for k in kinds) else kinds[0])
         else:
@@ -658,6 +685,132 @@ def _fma_rn(a, b, c, tdt):
     return torch.tensor(out, dtype=torch.float64).reshape(a.shape).to(tdt)
 
 
+# ---------------------------------------------------------------------------
+# Integer Assigns, as the reference lowers them (ptxc/stmts.py:509-560,
+# ptxc/expr.py:157-165, 211-223, 697-716, 815-877, ptxc/ops.py:98-117): every
+# operand becomes an s64 value (cvt.s64.<int type> widens; cvt.rzi.s64.<float
+# type> truncates a float toward zero, saturating, NaN to -2^63), the op runs on
+# s64 (add / sub / mul.lo wrap modulo 2^64, div.s64 / rem.s64 truncate toward
+# zero, max / min and the comparisons are signed), a comparison or
+# and / or / not gives a predicate (``bitwise_and`` / ``bitwise_or`` included:
+# the reference sends them down its predicate path), ``where`` selects s64
+# values.  Shifts take the low 32 bits of the count as unsigned (the PTX
+# operand type) with shl.b64 / shr.s64 semantics past 63.
+
+_INT_OPS = {"add", "sum", "subtract", "sub", "multiply", "prod", "divide", "floor_divide",
+            "true_divide", "remainder", "mod", "left_shift", "right_shift", "bitwise_xor",
+            "maximum", "amax", "minimum"}
+_CMP_OPS = {"equal": "eq", "eq": "eq", "not_equal": "ne", "ne": "ne", "greater": "gt",
+            "gt": "gt", "less": "lt", "lt": "lt", "greater_equal": "ge", "ge": "ge",
+            "less_equal": "le", "le": "le"}
+_BOOL_BINARY = {"bitwise_and", "logical_and", "and", "bitwise_or", "logical_or", "or"}
+_BOOL_NOT = {"bitwise_not", "logical_not", "not"}
+_I64_MIN, _I64_MAX = -(1 << 63), (1 << 63) - 1
+
+
+def _rzi_s64(v):
+    """cvt.rzi.s64.f32 / .f64: toward zero, clamped to the s64 range, NaN -> -2^63
+    (the B200 running the reference's own PTX gives that)."""
+    a = v.double().numpy() if isinstance(v, torch.Tensor) else np.asarray(v, np.float64)
+    with np.errstate(invalid="ignore"):
+        t = np.trunc(a)
+    out = np.full(a.shape, _I64_MIN, np.int64)                 # NaN stays here
+    inside = np.isfinite(t) & (t >= -9.223372036854775808e18) & (t < 9.223372036854775808e18)
+    out[inside] = t[inside].astype(np.int64)
+    out[t >= 9.223372036854775808e18] = _I64_MAX
+    out[t < -9.223372036854775808e18] = _I64_MIN
+    return torch.from_numpy(out)
+
+
+def _s64_operand(v, kind):
+    """The reference's ``iexpr_operand`` / ``_to_s64`` for one value."""
+    if kind == "pred":
+        raise OracleError("a predicate used as an integer operand")
+    if kind in ("f32", "f64", "f16"):
+        return _rzi_s64(v)
+    return v.to(torch.int64)
+
+
+def _pred_operand(v, kind):
+    """The reference's ``pred_operand``: a predicate, else v != 0 (unordered for floats)."""
+    if kind == "pred":
+        return v.to(torch.bool)
+    return v != 0
+
+
+def _int_binary(op, a, b):
+    a, b = torch.broadcast_tensors(a.to(torch.int64), b.to(torch.int64))
+    x = a.contiguous().numpy()
+    y = b.contiguous().numpy()
+    ux, uy = x.view(np.uint64), y.view(np.uint64)
+    if op in ("add", "sum"):
+        r = (ux + uy).view(np.int64)
+    elif op in ("subtract", "sub"):
+        r = (ux - uy).view(np.int64)
+    elif op in ("multiply", "prod"):
+        r = (ux * uy).view(np.int64)
+    elif op in ("divide", "floor_divide", "true_divide", "remainder", "mod"):
+        if (y == 0).any():
+            raise OracleError("integer division by zero (div.s64 leaves it unspecified)")
+        if ((x == _I64_MIN) & (y == -1)).any():
+            raise OracleError("s64 division overflow (div.s64 leaves it unspecified)")
+        q = np.floor_divide(x, y)
+        rem = x - q * y
+        q = q + ((rem != 0) & ((x < 0) != (y < 0)))            # toward zero
+        if op in ("remainder", "mod"):
+            r = (ux - (q.view(np.uint64) * uy)).view(np.int64)
+        else:
+            r = q
+    elif op in ("left_shift", "right_shift"):
+        c = (uy & np.uint64(0xFFFFFFFF)).astype(np.uint64)
+        cc = np.minimum(c, np.uint64(63))
+        if op == "left_shift":
+            r = np.where(c >= 64, np.uint64(0), ux << cc).view(np.int64)
+        else:
+            r = np.where(c >= 64, np.where(x < 0, -1, 0), x >> cc.astype(np.int64))
+    elif op == "bitwise_xor":
+        r = x ^ y
+    elif op in ("maximum", "amax"):
+        r = np.maximum(x, y)
+    else:
+        r = np.minimum(x, y)
+    return torch.from_numpy(np.ascontiguousarray(r, dtype=np.int64))
+
+
+def _int_assign(opname, dt, vals):
+    """One Assign the reference lowers on its integer / predicate paths, or
+    None when it lowers it as float arithmetic.  Returns (tensor, kind)."""
+    kinds = [k for _, k in vals]
+    ref_dt = dt if dt is not None else kinds[0]      # ``_infer_kind``: the first argument's
+    floats = ("f32", "f64", "f16")
+    if ref_dt == "bool" or opname in _CMP_OPS or opname in _BOOL_BINARY:
+        if opname in _BOOL_BINARY:
+            return _pred_operand(*vals[0]) & _pred_operand(*vals[1]) if "and" in opname else \
+                _pred_operand(*vals[0]) | _pred_operand(*vals[1]), "pred"
+        if opname in _BOOL_NOT:
+            return ~_pred_operand(*vals[0]), "pred"
+        if opname not in _CMP_OPS:
+            raise OracleError(f"unsupported boolean op {opname!r}")
+        if any(k in floats for k in kinds[:2]):
+            return None
+        a, b = _s64_operand(*vals[0]), _s64_operand(*vals[1])
+        rel = _CMP_OPS[opname]
+        return {"eq": a == b, "ne": a != b, "gt": a > b, "lt": a < b, "ge": a >= b,
+                "le": a <= b}[rel], "pred"
+    if opname == "where":
+        if ref_dt in floats or kinds[1] in floats or kinds[2] in floats:
+            return None
+        c = _pred_operand(*vals[0])
+        return torch.where(c, _s64_operand(*vals[1]), _s64_operand(*vals[2])), "i64"
+    if ref_dt in floats:
+        return None
+    if opname in ("copy", "pad", "bitcast"):
+        return vals[0][0].clone(), vals[0][1]
+    if opname not in _INT_OPS:
+        raise OracleError(f"unsupported integer op {opname!r}")
+    return _int_binary(opname, _s64_operand(*vals[0]), _s64_operand(*vals[1])), "i64"
+
+
 def _elementwise(opname, args, kinds, kind):
     """One elementwise op in the compute kind (f32 or f64 tensors, int64 or bool)."""
     fl = kind in ("f32", "f64")
@@ -798,10 +951,13 @@ def run_ir(kernel_op, meta: dict, inputs: dict, blocks=None, threads=None) -> di
     """Evaluate the IR on numpy inputs; returns every buffer as numpy (outputs filled)."""
     if threads:
         torch.set_num_threads(threads)
-    bufs = {k: torch.from_numpy(np.array(v, copy=True)) for k, v in inputs.items()}
+    arrays = {k: np.array(v, copy=True) for k, v in inputs.items()}
+    orig = {k: a.dtype for k, a in arrays.items()}
+    bufs = {k: torch.from_numpy(a.view(_SIGNED_VIEW[a.dtype]) if a.dtype in _SIGNED_VIEW else a)
+            for k, a in arrays.items()}
     with torch.no_grad():
         IRInterpreter(kernel_op, meta, bufs, blocks=blocks).run()
-    return {k: v.numpy() for k, v in bufs.items()}
+    return {k: v.numpy().view(orig[k]) for k, v in bufs.items()}
 
 
 def run_chain(pairs, host: dict, blocks=None) -> dict:

@@ -48,6 +48,44 @@ BENCH_CASES = {
                                       tm=128, tn=128, rm=8, rn=8),
     "K5_attention_f16": lambda s: s.attention(8, 32, 512, 128, dtype="f16"),
     "F8a_pointwise_add": lambda s: s.pointwise(1 << 26, ("add", "x0", "x1"), "f32"),
+    "F8d_pointwise_int": lambda s: s.pointwise(1 << 26, ("add", "x0", "x1"), "i32"),
+}
+
+# integer pointwise programs (the reference's integer Assign path): each one
+# assembles with ptxas for sm_100a; shifts and copies of 8/16-bit values do
+# not (the reference passes an s64 shift count where PTX wants .u32, and a
+# 32-bit register to mov.u16), so they are left out here
+_NZ = ("where", ("equal", "x1", ("imm", 0)), ("imm", 7), "x1")     # a divisor that is never 0
+INT_CASES = {
+    "I_add_i32": lambda s: s.pointwise(4099, ("add", "x0", "x1"), "i32"),
+    "I_mul_imm_u8": lambda s: s.pointwise(4099, ("multiply", "x0", ("imm", 3)), "u8"),
+    "I_div_i64": lambda s: s.pointwise(4099, ("divide", "x0", _NZ), "i64"),
+    "I_rem_i16": lambda s: s.pointwise(4099, ("remainder", "x0", _NZ), "i16"),
+    "I_div_u32": lambda s: s.pointwise(4099, ("floor_divide", "x0", _NZ), "u32"),
+    "I_xor_sub_u32": lambda s: s.pointwise(4099, ("subtract", ("bitwise_xor", "x0", "x1"), "x1"),
+                                           "u32"),
+    "I_max_min_u64": lambda s: s.pointwise(4099, ("minimum", ("maximum", "x0", "x1"), "x0"), "u64"),
+    "I_where_cmp_i32": lambda s: s.pointwise(
+        4099, ("where", ("greater", "x0", "x1"), "x0", ("imm", -7)), "i32"),
+    "I_and_or_i8": lambda s: s.pointwise(
+        4099, ("where", ("bitwise_or", ("bitwise_and", "x0", "x1"), ("less", "x0", ("imm", 0))),
+               "x0", "x1"), "i8"),
+    "I_i32_to_f32": lambda s: s.pointwise(4099, ("add", "x0", "x1"), "i32", out_dtype="f32"),
+    "I_i64_to_f16": lambda s: s.pointwise(
+        4099, ("multiply", "x0", "x1"), "i64", out_dtype="f16",
+        inits={"x0": {"dist": "int", "low": -300, "high": 300},
+               "x1": {"dist": "int", "low": -300, "high": 300}}),
+    "I_u16_to_f64": lambda s: s.pointwise(4099, ("add", "x0", ("imm", 1)), "u16", out_dtype="f64"),
+    "I_float_in_i32": lambda s: s.pointwise(
+        4099, ("add", "x0", "x1"), "i32", dtypes={"x1": "f32"},
+        inits={"x1": {"dist": "uniform", "low": -1e9, "high": 1e9}}),
+    "I_f16_f64_in_i64": lambda s: s.pointwise(
+        4099, ("subtract", "x0", "x1"), "i64", dtypes={"x0": "f16", "x1": "f64"},
+        inits={"x0": {"dist": "normal", "std": 300.0}, "x1": {"dist": "normal", "std": 1e12}}),
+    "I_const_i8": lambda s: s.pointwise(4099, ("subtract", "x0", ("const", "c", -5)), "i8"),
+    "I_chain_mixed": lambda s: s.pointwise(
+        4099, ("add", ("multiply", "x0", "x1"), ("remainder", "x0", _NZ)), "i32",
+        dtypes={"x0": "u8", "x1": "i16"}, out_dtype="i16"),
 }
 
 
@@ -68,7 +106,7 @@ def main(ref: Path) -> int:
     for d in sorted(p for p in (ref / "tests" / "variants").iterdir() if (p / "meta.json").exists()):
         jobs.append((d.name, next(d.glob("*.ir.json")), d / "meta.json"))
     tmp = Path(tempfile.mkdtemp(prefix="emmy_ref_"))
-    for name, make in BENCH_CASES.items():
+    for name, make in {**BENCH_CASES, **INT_CASES}.items():
         kop, meta = make(synth)
         ir = write_package(tmp / name, kop, meta)
         jobs.append((name, ir, tmp / name / "meta.json"))

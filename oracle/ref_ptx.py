@@ -82,7 +82,10 @@ class RefKernel:
         out = {}
         for a in self.k["args"]:
             n = math.prod(a["shape"]) if a["shape"] else 1
-            dt = {"f32": torch.float32, "f16": torch.float16, "f64": torch.float64}[a["dtype"]]
+            dt = {"f32": torch.float32, "f16": torch.float16, "f64": torch.float64,
+                  "i8": torch.int8, "u8": torch.uint8, "i16": torch.int16, "u16": torch.uint16,
+                  "i32": torch.int32, "u32": torch.uint32, "i64": torch.int64,
+                  "u64": torch.uint64}[a["dtype"]]
             if a.get("output"):
                 out[a["name"]] = torch.zeros(n, dtype=dt, device=device)
             else:
