@@ -498,6 +498,8 @@ def family_cases():
            for D in (16, 32, 64, 96, 256) for S in (16, 128, 512)},
         "X_gemm_f64_2048x2048x2048": synth.matmul(2048, 2048, 2048, dtype="f64", tm=128, tn=128,
                                                   rm=8, rn=8, bk=16),
+        "X_gemm_f16_8192x8192x8192": synth.matmul(8192, 8192, 8192, dtype="f16", out_dtype="f16",
+                                                  tm=128, tn=128, rm=8, rn=8),
         "F8a_pointwise_add_f32_2^26": synth.pointwise(1 << 26, ("add", "x0", "x1"), "f32"),
         "F8b_pointwise_gelu_tanh_f16_16384x4096": synth.pointwise(
             16384 * 4096, ("gelu_tanh", "x0"), "f16", shape=[16384, 4096]),

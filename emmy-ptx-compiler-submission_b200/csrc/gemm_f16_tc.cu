@@ -274,21 +274,37 @@ gemm_f16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constan
 //                        handed back on CTA 0's barrier (8 arrivals)
 
 namespace gemm16p {
-constexpr int BM = 256, BMH = 128, BN = 256, BNH = 128, BK = 64, STAGES = 6, THREADS = 192;
+constexpr int BM = 256, BMH = 128, BN = 256, BNH = 128, BK = 64, THREADS = 192;
 constexpr int A_BYTES = BMH * BK * 2;                // 16 KB: this CTA's rows
 constexpr int B_BOX_BYTES = BK * 64 * 2;             // 8 KB
-constexpr int B_BYTES = BK * BNH * 2;                // 16 KB: this CTA's columns
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int B_BYTES = BK * BNH * 2;                // 16 KB: this CTA's columns of one N half
 constexpr int OUT_BOX_BYTES = 32 * 128;              // one warp's 32 rows x 128 B of C
 constexpr int OUT_BYTES = 4 * 2 * OUT_BOX_BYTES;     // 4 epilogue warps, double-buffered
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + 1024;
-constexpr uint32_t TMEM_COLS = 512;                  // two 256-column accumulators
-constexpr int GROUP_N = 8;
+constexpr uint32_t TMEM_COLS = 512;
 constexpr int kStatusGemmTimeout = 0x1102;
+// NH: 256-column N halves per tile.  NH = 1: 256 x 256 tiles, two 256-column
+// accumulators (the epilogue of one tile overlaps the next tile's products).
+// NH = 2: 256 x 512 tiles, one 512-column accumulator; each stage carries the
+// CTA's A rows once for two N = 256 products, so 24 KB of operands per
+// product reach shared memory instead of 32 KB.
+template <int NH>
+struct PairCfg {
+  static constexpr int TBN = BN * NH;                          // tile columns
+  static constexpr int STAGE_BYTES = A_BYTES + NH * B_BYTES;
+  static constexpr int STAGES = NH == 1 ? 6 : 4;
+  static constexpr int NACC = 2 / NH;                          // accumulators
+  static constexpr int ACC_COLS = BN * NH;
+  static constexpr int GROUP_N = 8 / NH;                       // raster group width in tiles
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + 1024;
+  static_assert(NACC * ACC_COLS <= (int)TMEM_COLS, "tensor memory");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+};
 }  // namespace gemm16p
 
+template <int NH>
 __device__ __forceinline__ TileCoord gemm16p_tile(int t, int mt, int nt) {
   using namespace gemm16p;
+  constexpr int GROUP_N = PairCfg<NH>::GROUP_N, BN = PairCfg<NH>::TBN;
   const int per_batch = mt * nt;
   const int b = t / per_batch;
   int r = t - b * per_batch;
@@ -300,13 +316,13 @@ __device__ __forceinline__ TileCoord gemm16p_tile(int t, int mt, int nt) {
   return {m * BM, n * BN, b};
 }
 
-// One epilogue warp's 32 accumulator rows (TMEM lanes), 256 columns: bias,
+// One epilogue warp's 32 accumulator rows (TMEM lanes), ncols columns: bias,
 // ReLU, convert, then stage 128-byte row pieces (64 f16 or 32 f32 columns) in
 // shared memory with the 128-byte swizzle and write each 32-row box with one
 // TMA store.  Coalesced writes, and TMA drops rows and columns outside C.
 // Two staging buffers per warp: a buffer is refilled once the store issued
 // from it two chunks earlier has finished reading it.
-__device__ __forceinline__ void gemm16_drain_warp_tma(uint32_t tbase, int lane, int row0,
+__device__ __forceinline__ void gemm16_drain_warp_tma(uint32_t tbase, int ncols, int lane, int row0,
                                                       TileCoord tc, int N,
                                                       const float *__restrict__ bias,
                                                       bool add_bias, bool relu, bool round16,
@@ -314,7 +330,7 @@ __device__ __forceinline__ void gemm16_drain_warp_tma(uint32_t tbase, int lane, 
                                                       unsigned char *stage, int &seq) {
   const int step = out_f16 ? 64 : 32;                // columns per 128-byte row piece
 #pragma unroll 1
-  for (int c0 = 0; c0 < 256; c0 += step, ++seq) {
+  for (int c0 = 0; c0 < ncols; c0 += step, ++seq) {
     unsigned char *buf = stage + (seq & 1) * gemm16p::OUT_BOX_BYTES;
     if (seq >= 2 && lane == 0) bulk_wait_group_read<1>();
     __syncwarp();
@@ -378,6 +394,7 @@ __device__ __forceinline__ void gemm16_drain_warp_tma(uint32_t tbase, int lane, 
   }
 }
 
+template <int NH>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm16p::THREADS, 1)
 gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB,
@@ -385,20 +402,22 @@ gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                      void *__restrict__ C, int M, int N, int K, int batch, int64_t c_batch_stride,
                      int out_f16, int epilogue, int *status) {
   using namespace gemm16p;
+  using P = PairCfg<NH>;
+  constexpr int STAGES = P::STAGES, STAGE_BYTES = P::STAGE_BYTES, NACC = P::NACC;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full[STAGES];
   __shared__ __align__(8) uint64_t empty[STAGES];
-  __shared__ __align__(8) uint64_t acc_full[2];
-  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ __align__(8) uint64_t acc_full[NACC];
+  __shared__ __align__(8) uint64_t acc_empty[NACC];
   __shared__ __align__(8) uint64_t mma_done;
   __shared__ uint32_t tmem_holder;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
-  const int mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
+  const int mt = (M + BM - 1) / BM, nt = (N + P::TBN - 1) / P::TBN;
   const int tiles = mt * nt * batch;
   const int ktiles = (K + BK - 1) / BK;
 
@@ -410,7 +429,7 @@ gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < NACC; ++a) {
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 8);      // four epilogue warps in each CTA
     }
@@ -429,7 +448,7 @@ gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
       int g = 0;
       bool ok = true;
       for (int t = cluster; ok && t < tiles; t += nclusters) {
-        const TileCoord tc = gemm16p_tile(t, mt, nt);
+        const TileCoord tc = gemm16p_tile<NH>(t, mt, nt);
         for (int kt = 0; kt < ktiles; ++kt, ++g) {
           const int s = g % STAGES;
           if (g >= STAGES &&
@@ -442,10 +461,13 @@ gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
           if (rank == 0) mbar_expect_tx(&full[s], 2 * STAGE_BYTES);
           const uint32_t leader_full = mapa_shared(smem_u32(&full[s]), 0);
           tma_load_3d_pair(sa, &tmA, leader_full, kt * BK, tc.m0 + BMH * (int)rank, tc.b);
+          // per N half h: this CTA's 128 columns, as two 64-column boxes
 #pragma unroll
-          for (int j = 0; j < BNH / 64; ++j)
-            tma_load_3d_pair(sb + j * B_BOX_BYTES, &tmB, leader_full,
-                             tc.n0 + BNH * (int)rank + 64 * j, kt * BK, tc.b);
+          for (int h = 0; h < NH; ++h)
+#pragma unroll
+            for (int j = 0; j < BNH / 64; ++j)
+              tma_load_3d_pair(sb + h * B_BYTES + j * B_BOX_BYTES, &tmB, leader_full,
+                               tc.n0 + BN * h + BNH * (int)rank + 64 * j, kt * BK, tc.b);
         }
       }
     }
@@ -456,11 +478,12 @@ gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
       int g = 0, i = 0;
       bool ok = true;
       for (int t = cluster; ok && t < tiles; t += nclusters, ++i) {
-        const int a = i & 1;
-        if (i >= 2 && !mbar_wait(&acc_empty[a], ((i >> 1) - 1) & 1, status, kStatusGemmTimeout))
+        const int a = i % NACC;
+        if (i >= NACC &&
+            !mbar_wait(&acc_empty[a], ((i / NACC) - 1) & 1, status, kStatusGemmTimeout))
           break;
         tc_fence_after();
-        const uint32_t acc = tmem + a * BN;
+        const uint32_t acc = tmem + a * P::ACC_COLS;
         // two stages per barrier wait, then eight MMAs back to back; each stage
         // is released to both CTAs' producers as soon as its own four are done
         for (int kt = 0; kt < ktiles; kt += 2) {
@@ -476,11 +499,14 @@ gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
             const int s = g % STAGES;
             const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
             const uint64_t da = sw128_desc(sa, 16, 1024);
-            const uint64_t db = sw128_desc(sa + A_BYTES, B_BOX_BYTES, 1024);
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk)
-              mma_f16_pair(acc, da + ((kk * 32) >> 4), db + ((kk * 2048) >> 4), idesc,
-                           (kt + h > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+              for (int nh = 0; nh < NH; ++nh)
+                mma_f16_pair(acc + nh * BN, da + ((kk * 32) >> 4),
+                             sw128_desc(sa + A_BYTES + nh * B_BYTES, B_BOX_BYTES, 1024) +
+                                 ((kk * 2048) >> 4),
+                             idesc, (kt + h > 0 || kk > 0) ? 1u : 0u);
             mma_commit_pair(smem_u32(&empty[s]));
             mma_commit_pair(mapa_shared(smem_u32(&empty[s]), 1));
           }
@@ -503,13 +529,14 @@ gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA,
     unsigned char *stage = smem + STAGES * STAGE_BYTES + q * 2 * OUT_BOX_BYTES;
     int i = 0, seq = 0;
     for (int t = cluster; t < tiles; t += nclusters, ++i) {
-      const int a = i & 1;
-      const TileCoord tc = gemm16p_tile(t, mt, nt);
-      if (!mbar_wait(&acc_full[a], (i >> 1) & 1, status, kStatusGemmTimeout)) break;
+      const int a = i % NACC;
+      const TileCoord tc = gemm16p_tile<NH>(t, mt, nt);
+      if (!mbar_wait(&acc_full[a], (i / NACC) & 1, status, kStatusGemmTimeout)) break;
       __syncwarp();
       tc_fence_after();
-      gemm16_drain_warp_tma(tmem + lane_off + a * BN, lane, tc.m0 + BMH * (int)rank + q * 32, tc,
-                            N, bias, add_bias, relu, round16, out_f16, &tmC, stage, seq);
+      gemm16_drain_warp_tma(tmem + lane_off + a * P::ACC_COLS, P::ACC_COLS, lane,
+                            tc.m0 + BMH * (int)rank + q * 32, tc, N, bias, add_bias, relu,
+                            round16, out_f16, &tmC, stage, seq);
       // the accumulator's TMEM reads are complete (tcgen05.wait::ld)
       tc_fence_before();
       __syncwarp();
@@ -577,6 +604,43 @@ gemm_f16_plain_kernel(const __half *__restrict__ A, const __half *__restrict__ B
 
 using namespace emmy;
 
+namespace {
+
+// One launch of the CTA-pair kernel: one cluster of two CTAs per two SMs,
+// persistent over the tiles; C written by TMA stores of 32-row x 128-byte boxes.
+template <int NH>
+int launch_gemm16_pair(const CUtensorMap &ta, const CUtensorMap &tb, const float *bias, void *C,
+                       int64_t M, int64_t N, int64_t K, int64_t batch, int out_f16, int epilogue,
+                       cudaStream_t st) {
+  using P = gemm16p::PairCfg<NH>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaFuncSetAttribute(gemm_f16_pair_kernel<NH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         P::SMEM_BYTES);
+    attr_set[dev] = true;
+  }
+  const int64_t ptiles = ((M + gemm16p::BM - 1) / gemm16p::BM) * ((N + P::TBN - 1) / P::TBN) * batch;
+  const int64_t pairs = sm_count() / 2;
+  const int clusters = (int)(ptiles < pairs ? ptiles : pairs);
+  const uint64_t esize = out_f16 ? 2 : 4;
+  CUtensorMap tc_map;
+  const uint64_t cdims[3] = {(uint64_t)N, (uint64_t)M, (uint64_t)batch};
+  const uint64_t cstr[2] = {(uint64_t)N * esize, (uint64_t)M * N * esize};
+  const uint32_t cbox[3] = {(uint32_t)(128 / esize), 32, 1};
+  const int rc = make_tensor_map(&tc_map, out_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                  : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                                 3, C, cdims, cstr, cbox, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  gemm_f16_pair_kernel<NH><<<2 * clusters, gemm16p::THREADS, P::SMEM_BYTES, st>>>(
+      ta, tb, tc_map, bias, C, (int)M, (int)N, (int)K, (int)batch, M * N, out_f16, epilogue,
+      device_status_ptr());
+  return check_launch("emmy_gemm_f16 (tcgen05 pair)");
+}
+
+}  // namespace
+
 extern "C" int emmy_gemm_f16(const void *A, const void *B, const float *bias, void *C,
                              int64_t batch, int64_t M, int64_t N, int64_t K, int out_dtype,
                              int epilogue, int accumulate, void *stream) {
@@ -620,30 +684,19 @@ extern "C" int emmy_gemm_f16(const void *A, const void *B, const float *bias, vo
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
       cudaFuncSetAttribute(gemm_f16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            SMEM_BYTES);
-      cudaFuncSetAttribute(gemm_f16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           gemm16p::SMEM_BYTES);
       attr_set[dev] = true;
     }
     if (M >= gemm16p::BM) {
-      // CTA pairs: 256 x 256 tiles, one cluster of two CTAs per two SMs; C is
-      // written by TMA stores of 32-row x 128-byte boxes
-      const int64_t ptiles = ((M + gemm16p::BM - 1) / gemm16p::BM) *
-                             ((N + gemm16p::BN - 1) / gemm16p::BN) * batch;
+      // CTA pairs: 256 x 512 tiles when their rounds over the clusters take no
+      // longer than those of 256 x 256 tiles (counted in 256 x 256 tile times),
+      // else 256 x 256 tiles
       const int64_t pairs = sm_count() / 2;
-      const int clusters = (int)(ptiles < pairs ? ptiles : pairs);
-      const uint64_t esize = out_f16 ? 2 : 4;
-      CUtensorMap tc_map;
-      const uint64_t cdims[3] = {(uint64_t)N, (uint64_t)M, (uint64_t)batch};
-      const uint64_t cstr[2] = {(uint64_t)N * esize, (uint64_t)M * N * esize};
-      const uint32_t cbox[3] = {(uint32_t)(128 / esize), 32, 1};
-      rc = make_tensor_map(&tc_map, out_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                           3, C, cdims, cstr, cbox, CU_TENSOR_MAP_SWIZZLE_128B);
-      if (rc) return rc;
-      gemm_f16_pair_kernel<<<2 * clusters, gemm16p::THREADS, gemm16p::SMEM_BYTES, st>>>(
-          ta, tb, tc_map, bias, C, (int)M, (int)N, (int)K, (int)batch, M * N, out_f16, epilogue,
-          device_status_ptr());
-      return check_launch("emmy_gemm_f16 (tcgen05 pair)");
+      const int64_t mt = (M + gemm16p::BM - 1) / gemm16p::BM;
+      const int64_t t1 = mt * ((N + 255) / 256) * batch, t2 = mt * ((N + 511) / 512) * batch;
+      const int64_t r1 = (t1 + pairs - 1) / pairs, r2 = 2 * ((t2 + pairs - 1) / pairs);
+      if (N > 256 && r2 <= r1)
+        return launch_gemm16_pair<2>(ta, tb, bias, C, M, N, K, batch, out_f16, epilogue, st);
+      return launch_gemm16_pair<1>(ta, tb, bias, C, M, N, K, batch, out_f16, epilogue, st);
     }
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
     gemm_f16_tc_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, bias, C, (int)M, (int)N, (int)K,

@@ -21,13 +21,12 @@
 // The conversions are the PTX instructions the reference emits, written as
 // inline PTX, so the two agree bit for bit.
 //
-// A chain program (each step reads leaves and at most the step before it) runs
-// with every value in registers (pointwise_int_chain_kernel); any other
-// program runs on the general kernel, whose register file is in shared memory
-// (lane j of register r of thread t at [(r*VEC + j)*THREADS + t]) like the
-// float pointwise kernel's.  Both decode each instruction once per four
-// elements and move inputs and the output as vectors of four elements (4 to
-// 32 bytes) when the pointers allow.
+// The program layout follows the float pointwise kernel: registers in shared
+// memory (lane j of register r of thread t at [(r*VEC + j)*THREADS + t]),
+// each instruction decoded once per four elements, inputs and the output
+// moved as vectors of four elements (4 to 32 bytes) when the pointers allow.
+// (Holding the s64 values in registers instead was measured slower: 70-122
+// registers a thread leave too few warps to keep the loads in flight.)
 
 #include <algorithm>
 
@@ -345,99 +344,6 @@ pointwise_int_kernel(const PiProgram p, void *out, int out_dtype, int64_t n) {
   }
 }
 
-// ---- chain programs: every value in registers -------------------------------
-//
-// Most programs are chains: each step reads leaves (inputs, scalars,
-// immediates) and at most the step just before it, and the last step is the
-// result.  Those run here with no shared register file: the leaves and the
-// running value stay in registers, each step picks its operands with a
-// uniform select, and every thread loads its G groups before any arithmetic.
-
-constexpr int kPcMaxLeaf = 4, kPcPrev = 15;
-
-struct PiChain {
-  const void *ptr[kPcMaxLeaf];
-  int dtype[kPcMaxLeaf];
-  int kind[kPcMaxLeaf];                    // 0 input, 1 one-element scalar, 2 immediate
-  PwIndex idx[kPcMaxLeaf];
-  long long imm[kPcMaxLeaf];
-  signed char op[kPiMaxInstr];
-  signed char src[kPiMaxInstr][3];         // leaf index, or kPcPrev: the previous step
-  long long first;
-  int n_leaf, n_steps;
-};
-
-template <int VEC>
-__device__ __forceinline__ void pc_pick(int s, const long long (&L)[kPcMaxLeaf][VEC],
-                                        const long long (&T)[VEC], long long (&X)[VEC]) {
-#pragma unroll
-  for (int j = 0; j < VEC; ++j)
-    X[j] = s == kPcPrev ? T[j] : s == 0 ? L[0][j] : s == 1 ? L[1][j] : s == 2 ? L[2][j] : L[3][j];
-}
-
-template <bool VIO, bool BC, int G>
-__global__ void __launch_bounds__(kPiThreads)
-pointwise_int_chain_kernel(const PiChain p, void *out, int out_dtype, int64_t n) {
-  constexpr int VEC = kPiVec, S = kPiThreads;
-  const int64_t groups = (n + VEC - 1) / VEC;
-  const int64_t stride = (int64_t)gridDim.x * S;
-  long long konst[kPcMaxLeaf];                       // scalars and immediates, once
-#pragma unroll
-  for (int q = 0; q < kPcMaxLeaf; ++q)
-    konst[q] = q < p.n_leaf ? (p.kind[q] == 2 ? p.imm[q]
-                               : p.kind[q] == 1 ? pi_load1(p.ptr[q], p.dtype[q], 0) : 0) : 0;
-  for (int64_t g0 = (int64_t)blockIdx.x * S + threadIdx.x; g0 < groups; g0 += stride * G) {
-    long long L[G][kPcMaxLeaf][VEC];
-#pragma unroll
-    for (int u = 0; u < G; ++u) {
-      const int64_t base = (g0 + u * stride) * VEC;
-      const bool full = base + VEC <= n;
-#pragma unroll
-      for (int q = 0; q < kPcMaxLeaf; ++q) {
-        if (q >= p.n_leaf || base >= n) continue;
-        if (p.kind[q] != 0) {
-#pragma unroll
-          for (int j = 0; j < VEC; ++j) L[u][q][j] = konst[q];
-        } else if (BC && p.idx[q].bcast) {
-          const PwIndex &x = p.idx[q];
-#pragma unroll
-          for (int j = 0; j < VEC; ++j) {
-            unsigned long long r = pw_div(x.div, (unsigned long long)(p.first + base + j));
-            if (x.has_mod) r -= pw_div(x.mod, r) * x.mod.d;
-            L[u][q][j] = base + j < n ? pi_load1(p.ptr[q], p.dtype[q], (int64_t)r) : 0;
-          }
-        } else if (VIO && full) {
-          pi_load4(p.ptr[q], p.dtype[q], base, L[u][q]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < VEC; ++j)
-            L[u][q][j] = base + j < n ? pi_load1(p.ptr[q], p.dtype[q], base + j) : 0;
-        }
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < G; ++u) {
-      const int64_t base = (g0 + u * stride) * VEC;
-      if (base >= n) break;
-      long long T[VEC] = {};
-      for (int k = 0; k < p.n_steps; ++k) {
-        long long A[VEC], B[VEC], C[VEC];
-        pc_pick<VEC>(p.src[k][0], L[u], T, A);
-        pc_pick<VEC>(p.src[k][1], L[u], T, B);
-        pc_pick<VEC>(p.src[k][2], L[u], T, C);
-        pi_step<VEC, 1>(p.op[k], T, A, B, C);
-      }
-      if (VIO && base + VEC <= n) {
-        pi_store4(out, out_dtype, base, T);
-      } else {
-#pragma unroll
-        for (int j = 0; j < VEC; ++j)
-          if (base + j < n) pi_store1(out, out_dtype, base + j, T[j]);
-      }
-    }
-  }
-}
-
 }  // namespace emmy
 
 using namespace emmy;
@@ -539,49 +445,6 @@ extern "C" int emmy_pointwise_int(const void *const *inputs, const int *input_dt
   }
   const int64_t groups = (n + kPiVec - 1) / kPiVec;
   cudaStream_t st = as_stream(stream);
-  // a chain (every step reads leaves and at most the step before it; the last
-  // step is the result) runs with all values in registers
-  const int nleaf = n_inputs + n_scalars + n_imm;
-  bool chain = nleaf >= 1 && nleaf <= kPcMaxLeaf && result_reg == nregs - 1;
-  for (int k = 0; chain && k < n_instr; ++k)
-    for (int j = 2; j < 5; ++j) {
-      const int r = program[5 * k + j];
-      chain = chain && (r < nleaf || (k > 0 && r == nleaf + k - 1));
-    }
-  if (chain) {
-    PiChain c{};
-    c.n_leaf = nleaf;
-    c.n_steps = n_instr;
-    c.first = first;
-    for (int q = 0; q < nleaf; ++q) {
-      if (q < n_inputs) {
-        c.kind[q] = 0; c.ptr[q] = p.inputs[q]; c.dtype[q] = p.in_dtype[q]; c.idx[q] = p.idx[q];
-      } else if (q < n_inputs + n_scalars) {
-        c.kind[q] = 1; c.ptr[q] = p.scalars[q - n_inputs]; c.dtype[q] = p.sc_dtype[q - n_inputs];
-      } else {
-        c.kind[q] = 2; c.imm[q] = p.imm[q - n_inputs - n_scalars];
-      }
-    }
-    for (int k = 0; k < n_instr; ++k) {
-      c.op[k] = (signed char)program[5 * k];
-      for (int j = 0; j < 3; ++j) {
-        const int r = program[5 * k + 2 + j];
-        c.src[k][j] = (signed char)(r < nleaf ? r : kPcPrev);
-      }
-    }
-    constexpr int G = 2;
-    int64_t cblocks = (groups + (int64_t)kPiThreads * G - 1) / ((int64_t)kPiThreads * G);
-    if (cblocks > INT32_MAX) cblocks = INT32_MAX;
-    auto go = [&](auto kern) { kern<<<(unsigned)cblocks, kPiThreads, 0, st>>>(c, out, out_dtype, n); };
-    if (bcast) {
-      if (vio) go(pointwise_int_chain_kernel<true, true, G>);
-      else go(pointwise_int_chain_kernel<false, true, G>);
-    } else {
-      if (vio) go(pointwise_int_chain_kernel<true, false, G>);
-      else go(pointwise_int_chain_kernel<false, false, G>);
-    }
-    return check_launch("emmy_pointwise_int (chain)");
-  }
   const size_t smem = (size_t)nregs * kPiVec * kPiThreads * sizeof(long long);
   int64_t blocks = (groups + kPiThreads - 1) / kPiThreads;
   if (blocks > INT32_MAX) blocks = INT32_MAX;             // the grid-stride loop covers the rest

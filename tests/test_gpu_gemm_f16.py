@@ -54,6 +54,18 @@ IR_CASES = [
                                         out_dtype="f32", tm=128, tn=128, rm=8, rn=8,
                                         a_init={"dist": "normal", "std": STD},
                                         b_init={"dist": "normal", "std": STD})),
+    # 256 x 512 pair tiles (chosen: 144 of them take as many rounds as 288 of
+    # 256 x 256): ragged in M (520), N (1000: the second half of the last
+    # tile partial) and K (136), with bias + ReLU, f16 and f32 output
+    ("wide_pair_tiles_ragged_24x520x1000x136", dict(M=520, N=1000, K=136, batch=24, dtype="f16",
+                                                    out_dtype="f16", bias=True, relu=True, tm=8,
+                                                    tn=8, rm=1, rn=1, bk=8,
+                                                    a_init={"dist": "normal", "std": STD},
+                                                    b_init={"dist": "normal", "std": STD})),
+    ("wide_pair_tiles_ragged_f32out", dict(M=520, N=1000, K=136, batch=24, dtype="f16",
+                                           out_dtype="f32", bias=True, tm=8, tn=8, rm=1, rn=1,
+                                           bk=8, a_init={"dist": "normal", "std": STD},
+                                           b_init={"dist": "normal", "std": STD})),
 ]
 
 

@@ -159,15 +159,15 @@ def test_bench_program_full_size_matches_reference_ptx():
 
 
 @pytest.mark.parametrize("expr", [
-    # step 3 reads steps 1 and 2: not a chain, the shared-memory register file
+    # step 3 reads steps 1 and 2
     ("multiply", ("add", "x0", "x1"), ("subtract", "x0", "x1")),
-    # five leaves: more than the chain kernel holds
+    # five inputs
     ("add", ("add", ("add", ("add", "x0", "x1"), "x2"), "x3"), "x4"),
-    # a chain of compare, where and remainder over three leaves
+    # compare, where and remainder over three leaves
     ("remainder", ("where", ("less", "x0", "x1"), "x1", "x0"), NZ),
 ])
 @pytest.mark.parametrize("dt", ["i16", "u32", "i64"])
-def test_chain_and_general_programs_match_oracle(expr, dt):
+def test_program_shapes_match_oracle(expr, dt):
     kop, meta = synth.pointwise(4099, expr, dt)
     host = synth.make_inputs(meta)
     _, _, out = run_on_gpu(kop, meta, host)
