@@ -1088,6 +1088,11 @@ PROFILE_CASES = {
     "rowop_softmax_f16_16384x4096": lambda s: s.retype(*s.softmax([16384, 4096]), "f16", acc="f32"),
     "rowop_layernorm_f16_16384x1024": lambda s: s.retype(*s.layernorm(16384, 1024), "f16",
                                                          acc="f32"),
+    "pointwise_int_add_i32_2^26": lambda s: s.pointwise(1 << 26, ("add", "x0", "x1"), "i32"),
+    "pointwise_int_u8_sub_clamp_2^26": lambda s: s.pointwise(
+        1 << 26, ("maximum", ("subtract", "x0", "x1"), ("imm", 0)), "u8"),
+    "gemm_f16_4096_wide_tiles": lambda s: s.matmul(4096, 4096, 4096, dtype="f16", out_dtype="f16",
+                                                   tm=128, tn=128, rm=8, rn=8),
 }
 
 
