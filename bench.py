@@ -103,6 +103,9 @@ PROFILE_OF = {
     "F8a_pointwise_add_f32_2^26": "pointwise_F8.md",
     "F8c_pointwise_bias_relu_f32_16384x4096": "pointwise_broadcast.md",
     "X_softmax_f16_16384x4096": "rowop_softmax_f16.md",
+    "F8b_pointwise_gelu_tanh_f16_16384x4096": "pointwise_gelu_f16_F8b.md",
+    "F8d_pointwise_int_add_i32_2^26": "pointwise_int_F8d_F8e.md#F8d",
+    "F8e_pointwise_int_u8_sub_clamp_2^26": "pointwise_int_F8d_F8e.md#F8e",
 }
 
 
@@ -131,14 +134,17 @@ def tensor_peak():
 
 
 def profile_traffic(name):
-    """dram bytes per launch recorded from an ncu capture in profiles/<name>."""
+    """dram bytes per launch recorded from an ncu capture in profiles/<name>
+    (``file.md#TAG`` reads the line ``dram_bytes_per_launch (TAG):``)."""
     if not name:
         return None
+    name, _, tag = name.partition("#")
+    key = f"dram_bytes_per_launch ({tag}):" if tag else "dram_bytes_per_launch:"
     p = ROOT / "profiles" / name
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
-        if line.strip().startswith("dram_bytes_per_launch:"):
+        if line.strip().startswith(key):
             try:
                 return int(line.split(":", 1)[1].strip().split()[0])
             except ValueError:
