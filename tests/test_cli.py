@@ -167,3 +167,19 @@ def test_invalid_ir_statement_is_a_compile_error(package, tmp_path):
     (root / "meta.json").write_text((package.parent / "meta.json").read_text())
     r = run(str(root / "k.ir.json"))
     assert r.returncode == 1 and "invalid IR" in r.stderr and "Traceback" not in r.stderr
+
+
+def test_integer_program_prints_its_plan_and_refusals_exit_1(tmp_path):
+    """An integer pointwise package compiles to the pointwise_int plan; an
+    integer op the reference cannot lower exits 1 with its message."""
+    kop, meta = synth.pointwise(1000, ("maximum", ("subtract", "x0", "x1"), ("imm", 0)), "u8",
+                                entry="k_int_cli")
+    r = run(str(write_package(tmp_path / "ok", kop, meta)))
+    assert r.returncode == 0, r.stderr
+    plan = json.loads(r.stdout)
+    assert plan["family"] == "pointwise_int" and plan["symbol"] == "emmy_pointwise_int"
+    assert plan["pointwise"]["immediates"] == [0] and plan["pointwise"]["out_dtype"] == "u8"
+    kop, meta = synth.pointwise(1000, ("negative", "x0"), "i32", entry="k_int_neg")
+    r = run(str(write_package(tmp_path / "neg", kop, meta)))
+    assert r.returncode == 1 and r.stdout == ""
+    assert "unsupported integer op 'negative'" in r.stderr and "Traceback" not in r.stderr
