@@ -29,6 +29,7 @@
 // registers a thread leave too few warps to keep the loads in flight.)
 
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "pw_index.cuh"
@@ -247,22 +248,45 @@ __device__ __forceinline__ long long pi_shr(long long a, long long b) {
   asm("shr.s64 %0, %1, %2;" : "=l"(r) : "l"(a), "r"((unsigned int)b));
   return r;
 }
+// the same on 32-bit values (programs whose values the matcher proved to fit)
+__device__ __forceinline__ int pi_div(int a, int b) {
+  int r;
+  asm("div.s32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ int pi_rem(int a, int b) {
+  int r;
+  asm("rem.s32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ int pi_shl(int a, int b) {
+  int r;
+  asm("shl.b32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"((unsigned int)b));
+  return r;
+}
+__device__ __forceinline__ int pi_shr(int a, int b) {
+  int r;
+  asm("shr.s32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"((unsigned int)b));
+  return r;
+}
 
-template <int VEC, int S>
-__device__ __forceinline__ void pi_step(int op, long long *RD, const long long *RA,
-                                        const long long *RB, const long long *RC) {
+// T: long long (s64, the reference's registers) or int (a program whose
+// values the matcher proved to give the same bits on 32 bits).
+template <typename T, int VEC, int S>
+__device__ __forceinline__ void pi_step(int op, T *RD, const T *RA, const T *RB, const T *RC) {
+  using U = typename std::make_unsigned<T>::type;
 #define PI_LANES(EXPR)                                                            \
   _Pragma("unroll") for (int j = 0; j < VEC; ++j) {                               \
-    const long long a = RA[j * S], b = RB[j * S], c = RC[j * S];                  \
+    const T a = RA[j * S], b = RB[j * S], c = RC[j * S];                          \
     (void)b; (void)c;                                                             \
     RD[j * S] = (EXPR);                                                           \
   }                                                                               \
   break;
   switch (op) {
     case PI_COPY: PI_LANES(a)
-    case PI_ADD: PI_LANES((long long)((unsigned long long)a + (unsigned long long)b))
-    case PI_SUB: PI_LANES((long long)((unsigned long long)a - (unsigned long long)b))
-    case PI_MUL: PI_LANES((long long)((unsigned long long)a * (unsigned long long)b))
+    case PI_ADD: PI_LANES((T)((U)a + (U)b))
+    case PI_SUB: PI_LANES((T)((U)a - (U)b))
+    case PI_MUL: PI_LANES((T)((U)a * (U)b))
     case PI_DIV: PI_LANES(pi_div(a, b))
     case PI_REM: PI_LANES(pi_rem(a, b))
     case PI_SHL: PI_LANES(pi_shl(a, b))
@@ -270,36 +294,39 @@ __device__ __forceinline__ void pi_step(int op, long long *RD, const long long *
     case PI_XOR: PI_LANES(a ^ b)
     case PI_MAX: PI_LANES(a > b ? a : b)
     case PI_MIN: PI_LANES(a < b ? a : b)
-    case PI_EQ: PI_LANES((long long)(a == b))
-    case PI_NE: PI_LANES((long long)(a != b))
-    case PI_GT: PI_LANES((long long)(a > b))
-    case PI_LT: PI_LANES((long long)(a < b))
-    case PI_GE: PI_LANES((long long)(a >= b))
-    case PI_LE: PI_LANES((long long)(a <= b))
-    case PI_LAND: PI_LANES((long long)((a != 0) & (b != 0)))
-    case PI_LOR: PI_LANES((long long)((a != 0) | (b != 0)))
-    case PI_LNOT: PI_LANES((long long)(a == 0))
+    case PI_EQ: PI_LANES((T)(a == b))
+    case PI_NE: PI_LANES((T)(a != b))
+    case PI_GT: PI_LANES((T)(a > b))
+    case PI_LT: PI_LANES((T)(a < b))
+    case PI_GE: PI_LANES((T)(a >= b))
+    case PI_LE: PI_LANES((T)(a <= b))
+    case PI_LAND: PI_LANES((T)((a != 0) & (b != 0)))
+    case PI_LOR: PI_LANES((T)((a != 0) | (b != 0)))
+    case PI_LNOT: PI_LANES((T)(a == 0))
     default: PI_LANES(a != 0 ? b : c)                  // PI_WHERE
   }
 #undef PI_LANES
 }
 
-// VIO: every contiguous input and the output take vector loads / stores.
-// BC: some input is a broadcast (read through PwIndex).
-template <bool VIO, bool BC>
+// T: the register type (above).  VIO: every contiguous input and the output
+// take vector loads / stores.  BC: some input is a broadcast (read through
+// PwIndex).  Operands are widened to s64 as they load (as the reference does)
+// and, for T = int, cut to their low 32 bits; results are sign-extended back
+// to s64 for the store.
+template <typename T, bool VIO, bool BC>
 __global__ void __launch_bounds__(kPiThreads)
 pointwise_int_kernel(const PiProgram p, void *out, int out_dtype, int64_t n) {
   constexpr int S = kPiThreads, VEC = kPiVec;
-  extern __shared__ __align__(16) long long pi_smem[];
-  long long *R = pi_smem + threadIdx.x;               // register r, lane j at R[(r*VEC+j)*S]
+  extern __shared__ __align__(16) unsigned char pi_smem[];
+  T *R = reinterpret_cast<T *>(pi_smem) + threadIdx.x;   // register r, lane j at R[(r*VEC+j)*S]
   for (int s = 0; s < p.n_sc; ++s) {
-    const long long v = pi_load1(p.scalars[s], p.sc_dtype[s], 0);
+    const T v = (T)pi_load1(p.scalars[s], p.sc_dtype[s], 0);
 #pragma unroll
     for (int j = 0; j < VEC; ++j) R[((p.n_in + s) * VEC + j) * S] = v;
   }
   for (int s = 0; s < p.n_imm; ++s) {
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) R[((p.n_in + p.n_sc + s) * VEC + j) * S] = p.imm[s];
+    for (int j = 0; j < VEC; ++j) R[((p.n_in + p.n_sc + s) * VEC + j) * S] = (T)p.imm[s];
   }
   const int64_t groups = (n + VEC - 1) / VEC;
   const int64_t stride = (int64_t)gridDim.x * S;
@@ -324,16 +351,16 @@ pointwise_int_kernel(const PiProgram p, void *out, int out_dtype, int64_t n) {
           v[j] = base + j < n ? pi_load1(p.inputs[k], p.in_dtype[k], base + j) : 0;
       }
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) R[(k * VEC + j) * S] = v[j];
+      for (int j = 0; j < VEC; ++j) R[(k * VEC + j) * S] = (T)v[j];
     }
     for (int k = 0; k < p.n_instr; ++k) {
       const signed char *c = p.code[k];
-      pi_step<VEC, S>(c[0], R + c[1] * VEC * S, R + c[2] * VEC * S, R + c[3] * VEC * S,
-                      R + c[4] * VEC * S);
+      pi_step<T, VEC, S>(c[0], R + c[1] * VEC * S, R + c[2] * VEC * S, R + c[3] * VEC * S,
+                         R + c[4] * VEC * S);
     }
     long long o[VEC];
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) o[j] = R[(p.result_reg * VEC + j) * S];
+    for (int j = 0; j < VEC; ++j) o[j] = (long long)R[(p.result_reg * VEC + j) * S];
     if (VIO && full) {
       pi_store4(out, out_dtype, base, o);
     } else {
@@ -374,9 +401,12 @@ extern "C" int emmy_pointwise_int(const void *const *inputs, const int *input_dt
                                   const void *const *scalars, const int *scalar_dtypes,
                                   int n_scalars, const int64_t *immediates, int n_imm,
                                   const int *program, int n_instr, int result_reg, void *out,
-                                  int out_dtype, int64_t first, int64_t n, void *stream) {
+                                  int out_dtype, int64_t first, int64_t n, int value_bits,
+                                  void *stream) {
   clear_error();
   if (n < 0 || first < 0) return set_error(EMMY_ERR_INVALID, "emmy_pointwise_int: negative size");
+  if (value_bits != 64 && value_bits != 32)
+    return set_error(EMMY_ERR_INVALID, "emmy_pointwise_int: value_bits must be 64 or 32");
   if (n == 0) return EMMY_OK;
   if (!out) return set_error(EMMY_ERR_INVALID, "emmy_pointwise_int: null output");
   if (n_inputs < 0 || n_inputs > kPiMaxIn || n_scalars < 0 || n_scalars > kPiMaxIn || n_imm < 0 ||
@@ -445,19 +475,27 @@ extern "C" int emmy_pointwise_int(const void *const *inputs, const int *input_dt
   }
   const int64_t groups = (n + kPiVec - 1) / kPiVec;
   cudaStream_t st = as_stream(stream);
-  const size_t smem = (size_t)nregs * kPiVec * kPiThreads * sizeof(long long);
+  const size_t smem = (size_t)nregs * kPiVec * kPiThreads * (value_bits / 8);
   int64_t blocks = (groups + kPiThreads - 1) / kPiThreads;
   if (blocks > INT32_MAX) blocks = INT32_MAX;             // the grid-stride loop covers the rest
   auto launch = [&](auto kern) {
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     kern<<<(unsigned)blocks, kPiThreads, smem, st>>>(p, out, out_dtype, n);
   };
-  if (bcast) {
-    if (vio) launch(pointwise_int_kernel<true, true>);
-    else launch(pointwise_int_kernel<false, true>);
+  if (value_bits == 32) {
+    if (bcast) {
+      if (vio) launch(pointwise_int_kernel<int, true, true>);
+      else launch(pointwise_int_kernel<int, false, true>);
+    } else {
+      if (vio) launch(pointwise_int_kernel<int, true, false>);
+      else launch(pointwise_int_kernel<int, false, false>);
+    }
+  } else if (bcast) {
+    if (vio) launch(pointwise_int_kernel<long long, true, true>);
+    else launch(pointwise_int_kernel<long long, false, true>);
   } else {
-    if (vio) launch(pointwise_int_kernel<true, false>);
-    else launch(pointwise_int_kernel<false, false>);
+    if (vio) launch(pointwise_int_kernel<long long, true, false>);
+    else launch(pointwise_int_kernel<long long, false, false>);
   }
   return check_launch("emmy_pointwise_int");
 }

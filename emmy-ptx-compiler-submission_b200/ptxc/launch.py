@@ -53,7 +53,7 @@ SIGNATURES = {
     "emmy_pointwise_indexed": [_vp, _vp, _vp, _int, _vp, _vp, _int, _vp, _int, _vp, _int, _int, _int,
                                _vp, _int, _i64, _i64, _vp],
     "emmy_pointwise_int": [_vp, _vp, _vp, _int, _vp, _vp, _int, _vp, _int, _vp, _int, _int, _vp,
-                           _int, _i64, _i64, _vp],
+                           _int, _i64, _i64, _int, _vp],
 }
 RESTYPES = {"emmy_reduce_workspace_bytes": _sz}
 
@@ -276,7 +276,8 @@ def run(plan: dict, tensors: dict, stream=None, workspace=None, check: bool = Tr
         _check(lib.emmy_pointwise_int(in_ptrs, in_dts, idx_arr, len(ins), sc_ptrs, sc_dts, len(scs),
                                       imm, len(imms), prog, len(g["program"]), g["result_reg"],
                                       _ptr(T("out")), DT_CODE[g["out_dtype"]],
-                                      int(g.get("first", 0)), g["n"], st), "emmy_pointwise_int")
+                                      int(g.get("first", 0)), g["n"], int(g.get("value_bits", 64)),
+                                      st), "emmy_pointwise_int")
         launches += 1
     else:
         raise ValueError(f"plan family {fam!r} has no launcher")

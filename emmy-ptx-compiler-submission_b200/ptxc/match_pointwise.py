@@ -374,6 +374,10 @@ def _lower_integer(form, dtypes, out, numel) -> dict:
         prog.append(["copy", [result]])
         result = ("tmp", len(prog) - 1)
     in_keys = inputs
+    leaf_dt = {("input", k): dtypes[k[0]] for k in in_keys}
+    leaf_dt.update({("scalar", k): dtypes[k] for k in scalars})
+    leaf_dt.update({("imm", v): v for v in imms})
+    bits = value_bits(prog, result, leaf_dt, out_dt)
     base = {"input": 0, "scalar": len(in_keys), "imm": len(in_keys) + len(scalars)}
     ntmp0 = len(in_keys) + len(scalars) + len(imms)
 
@@ -396,8 +400,122 @@ def _lower_integer(form, dtypes, out, numel) -> dict:
         "args": {"out": out},
         "pointwise": {"n": numel, "inputs": names, "scalars": scalars, "immediates": imms,
                       "program": program, "result_reg": ntmp0 + len(prog) - 1,
-                      "compute": "i64", "out_dtype": out_dt,
+                      "compute": "i64", "out_dtype": out_dt, "value_bits": bits,
                       **({"input_index": in_index, "first": 0}
                          if any(D for D, _ in in_index) else {})},
         "params": {}, "dtypes": {"out": out_dt},
     }
+
+
+# ---------------------------------------------------------------------------
+# 32-bit evaluation of an integer program.  The reference computes on s64.
+# The same stored bits come out of 32-bit registers when every value that
+# must be exact fits in int32 and every other value is used only through its
+# low 32 bits:
+#   * add, sub, mul, xor, shl and copy: the low 32 bits of the result depend
+#     only on the low 32 bits of the operands (shl.b32 / shl.b64 both give 0
+#     past their width, and both read the count's low 32 bits);
+#   * comparisons, max, min, div, rem, shr's value, where's condition and the
+#     logical ops read the whole value: their operands must be exact;
+#   * the stored result must be exact for a float or 64-bit output, and only
+#     its low bits count for an integer output of 32 bits or fewer.
+# Exactness flows from the result and those operands down to the leaves;
+# ranges flow up from the leaves' types and the immediates by interval
+# arithmetic on unbounded integers.  A value that must be exact needs a range
+# inside int32 (then no s64 operation on the way wrapped either).  A division
+# or remainder counts as exact too: a zero divisor or INT32_MIN / -1 gives the
+# 32-bit and 64-bit instructions different (unspecified) bits.
+
+INT32_LO, INT32_HI = -(1 << 31), (1 << 31) - 1
+DT_RANGE = {"i8": (-128, 127), "u8": (0, 255), "i16": (-32768, 32767), "u16": (0, 65535),
+            "i32": (INT32_LO, INT32_HI), "u32": (0, (1 << 32) - 1),
+            "i64": (-(1 << 63), (1 << 63) - 1), "u64": (-(1 << 63), (1 << 63) - 1)}
+_LOW_BITS = {"add", "subtract", "multiply", "bitwise_xor", "copy", "left_shift"}
+
+
+def _range_of(name, rs):
+    """Interval of an instruction's result from its operands' intervals (None: unbounded)."""
+    if any(r is None for r in rs):
+        return None
+    a = rs[0]
+    b = rs[1] if len(rs) > 1 else None
+    if name == "copy":
+        return a
+    if name == "add":
+        return (a[0] + b[0], a[1] + b[1])
+    if name == "subtract":
+        return (a[0] - b[1], a[1] - b[0])
+    if name == "multiply":
+        p = [x * y for x in a for y in b]
+        return (min(p), max(p))
+    if name in ("divide", "remainder"):
+        if b[0] <= 0 <= b[1]:
+            return None                                    # a zero divisor is possible
+        m = max(abs(a[0]), abs(a[1]))
+        if name == "remainder":
+            m = min(m, max(abs(b[0]), abs(b[1])) - 1)
+        return (0 if a[0] >= 0 else -m, m)
+    if name == "left_shift":
+        if b[0] < 0 or b[1] > 62:
+            return None
+        p = [x << c for x in a for c in b]
+        return (min(p), max(p))
+    if name == "right_shift":
+        return (min(a[0], 0), max(a[1], 0))                # toward 0 / -1 for any count
+    if name == "bitwise_xor":
+        if a[0] >= 0 and b[0] >= 0:
+            return (0, (1 << max(a[1], b[1]).bit_length()) - 1)
+        k = max(abs(v) for v in a + b).bit_length()
+        return (-(1 << k), (1 << k) - 1)
+    if name == "maximum":
+        return (max(a[0], b[0]), max(a[1], b[1]))
+    if name == "minimum":
+        return (min(a[0], b[0]), min(a[1], b[1]))
+    if name == "where":
+        c = rs[2]
+        return (min(b[0], c[0]), max(b[1], c[1]))
+    return (0, 1)                                          # comparisons, and / or / not
+
+
+def value_bits(prog, result, leaf_dtypes, out_dt) -> int:
+    """32 when the program's stored bits are the same on 32-bit values, else 64.
+    ``prog``: [(name, [ref...])] with refs ("tmp", i) or leaf keys; ``result``:
+    the result ref; ``leaf_dtypes``: leaf ref -> dtype (ints, floats) or an int
+    (an immediate's value)."""
+    exact = set()
+    if out_dt in FLOAT_KINDS or out_dt in ("i64", "u64"):
+        exact.add(result)
+    for i in range(len(prog) - 1, -1, -1):
+        name, srcs = prog[i]
+        mine = ("tmp", i) in exact
+        if name in _LOW_BITS:
+            if mine:
+                exact.update(srcs[:1] if name == "left_shift" else srcs)
+        elif name == "right_shift":
+            exact.add(srcs[0])
+        elif name == "where":
+            exact.add(srcs[0])
+            if mine:
+                exact.update(srcs[1:])
+        else:
+            exact.update(srcs)
+    ranges = {}
+
+    def rng(ref):
+        if ref[0] == "tmp":
+            return ranges[ref]
+        d = leaf_dtypes[ref]
+        return (d, d) if isinstance(d, int) else DT_RANGE.get(d)
+
+    for i, (name, srcs) in enumerate(prog):
+        ranges[("tmp", i)] = _range_of(name, [rng(s) for s in srcs])
+        if name in ("divide", "remainder"):
+            # div.s32 / rem.s32 and the s64 forms agree only without a zero
+            # divisor or an overflowing quotient: the result's own range (None
+            # when the divisor may be 0) must lie inside int32
+            exact.add(("tmp", i))
+    for ref in exact:
+        r = rng(ref)
+        if r is None or r[0] < INT32_LO or r[1] > INT32_HI:
+            return 64
+    return 32

@@ -333,13 +333,21 @@ int emmy_pointwise_indexed(const void *const *inputs, const int *input_dtypes,
  * b, 64 or more: 0 / the sign), 8 xor, 9 max, 10 min, 11-16 eq ne gt lt ge le
  * (signed, 0 or 1), 17 and, 18 or (of b != 0 and a != 0), 19 not, 20 where
  * (a != 0 ? b : c).
+ * value_bits: 64, or 32 when the caller has shown that the program gives the
+ * same stored bits on 32-bit values: every value that must be exact (an
+ * operand of a comparison, max, min, div, rem, shr, where's condition, a
+ * logical op, or a result stored as a float or 64-bit integer) lies within
+ * the int32 range, and every other value is used only through its low 32
+ * bits (add, sub, mul, xor, shl, copy, a store to an integer of 32 bits or
+ * fewer).  The matcher proves it by interval arithmetic over the inputs'
+ * types and the immediates.
  */
 int emmy_pointwise_int(const void *const *inputs, const int *input_dtypes,
                        const int64_t *input_index, int n_inputs,
                        const void *const *scalars, const int *scalar_dtypes, int n_scalars,
                        const int64_t *immediates, int n_imm, const int *program, int n_instr,
                        int result_reg, void *out, int out_dtype, int64_t first, int64_t n,
-                       void *stream);
+                       int value_bits, void *stream);
 
 /*
  * Long-row reduction that allocates nothing: y[0] = fold_op(pre(x[0..n))) [* 1/count].

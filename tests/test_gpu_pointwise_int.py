@@ -172,3 +172,49 @@ def test_program_shapes_match_oracle(expr, dt):
     host = synth.make_inputs(meta)
     _, _, out = run_on_gpu(kop, meta, host)
     assert np.array_equal(_bits(out["out"]), _bits(run_ir(kop, meta, host)["out"]))
+
+
+WIDTH_CASES = [
+    (("add", "x0", "x1"), "i32", {}),
+    (("maximum", ("subtract", "x0", "x1"), ("imm", 0)), "u8", {}),
+    (("add", "x0", "x1"), "u16", {"out_dtype": "i64"}),
+    (("add", "x0", "x1"), "u16", {"out_dtype": "f16"}),
+    (("where", ("greater", ("multiply", "x0", "x1"), ("imm", 0)), "x0", "x1"), "i16", {}),
+    (("divide", "x0", ("imm", 3)), "i16", {}),
+    (("divide", "x0", ("imm", -1)), "i16", {}),
+    (("right_shift", "x0", "x1"), "i32", {}),
+    (("left_shift", "x0", "x1"), "i64", {"out_dtype": "i32"}),
+    (("multiply", ("add", "x0", "x1"), ("bitwise_xor", "x0", ("imm", -5))), "u32", {}),
+    (("add", "x0", "x1"), "i32", {"dtypes": {"x1": "f32"},
+                                  "inits": {"x1": {"dist": "uniform", "low": -3e9, "high": 3e9}}}),
+]
+
+
+@pytest.mark.parametrize("expr,dt,kw", WIDTH_CASES)
+def test_32_bit_programs_store_the_64_bit_bits(expr, dt, kw):
+    """Programs the matcher runs on 32-bit values: the same program forced to
+    64 bits gives the same stored bits, inputs at their types' extremes included."""
+    import copy
+    import torch
+    from ptxc import Lowerer
+    from ptxc.launch import Executor
+    kop, meta = synth.pointwise(4099, expr, dt, **kw)
+    plan = Lowerer(kop, meta).plan()
+    assert plan["pointwise"]["value_bits"] == 32
+    host = synth.make_inputs(meta)
+    for name, arr in host.items():
+        if arr.dtype.kind in "iu" and name != "out":
+            info = np.iinfo(arr.dtype)
+            arr[:6] = [info.min, info.max, 0, -1 if arr.dtype.kind == "i" else 1, info.min + 1,
+                       info.max - 1]
+    outs = []
+    for bits in (32, 64):
+        p = copy.deepcopy(plan)
+        p["pointwise"]["value_bits"] = bits
+        ex = Executor(p)
+        ex.upload(host)
+        ex.launch()
+        torch.cuda.synchronize()
+        outs.append(ex.download()["out"].numpy())
+    assert np.array_equal(_bits(outs[0]), _bits(outs[1]))
+    assert np.array_equal(_bits(outs[0]), _bits(run_ir(kop, meta, host)["out"]))

@@ -176,11 +176,12 @@ def lib():
     lib = ctypes.CDLL(str(PKG / "libemmyb200.so"))
     lib.emmy_last_error.restype = ctypes.c_char_p
     vp, i, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
-    lib.emmy_pointwise_int.argtypes = [vp, vp, vp, i, vp, vp, i, vp, i, vp, i, i, vp, i, i64, i64, vp]
+    lib.emmy_pointwise_int.argtypes = [vp, vp, vp, i, vp, vp, i, vp, i, vp, i, i, vp, i, i64, i64, i,
+                                       vp]
     return lib
 
 
-def _call(lib, program, *, n=64, in_dt=7, out_dt=7, index=None, result=None, imms=()):
+def _call(lib, program, *, n=64, in_dt=7, out_dt=7, index=None, result=None, imms=(), bits=64):
     ins = (ctypes.c_void_p * 2)(16, 32)
     dts = (ctypes.c_int * 2)(in_dt, in_dt)
     flat = [int(x) for row in program for x in row]
@@ -189,7 +190,7 @@ def _call(lib, program, *, n=64, in_dt=7, out_dt=7, index=None, result=None, imm
     idx = (ctypes.c_int64 * 6)(*index) if index else None
     res = result if result is not None else 2 + len(imms) + len(program) - 1
     return lib.emmy_pointwise_int(ins, dts, idx, 2, None, None, 0, imm, len(imms), prog,
-                                  len(program), res, ctypes.c_void_p(48), out_dt, 0, n, None)
+                                  len(program), res, ctypes.c_void_p(48), out_dt, 0, n, bits, None)
 
 
 def test_capi_host_checks_need_no_gpu(lib):
@@ -198,6 +199,8 @@ def test_capi_host_checks_need_no_gpu(lib):
     assert b"unknown opcode" in lib.emmy_last_error()
     assert _call(lib, [[1, 0, 0, 1, 0]]) == 1                      # writes an input register
     assert b"writes register" in lib.emmy_last_error()
+    assert _call(lib, [[1, 2, 0, 1, 0]], bits=16) == 1
+    assert b"value_bits" in lib.emmy_last_error()
     assert _call(lib, [[1, 2, 0, 1, 0]], out_dt=11) == 1
     assert b"bad output dtype" in lib.emmy_last_error()
     assert _call(lib, [[1, 2, 0, 1, 0]], in_dt=-1) == 1
@@ -217,3 +220,32 @@ def test_reference_compiled_every_integer_case():
     for name in INT_CASES:
         assert rep.get(name, {}).get("rc") == 0, (name, rep.get(name))
         assert (ROOT / "oracle" / "_ref" / name / "kernel.ptx").exists()
+
+
+@pytest.mark.parametrize("expr,dt,kw,bits", [
+    (("add", "x0", "x1"), "i32", {}, 32),                       # low bits only
+    (("maximum", ("subtract", "x0", "x1"), ("imm", 0)), "u8", {}, 32),   # exact, in range
+    (("add", "x0", "x1"), "i32", {"out_dtype": "f32"}, 64),     # exact, 2^32 wide
+    (("add", "x0", "x1"), "u16", {"out_dtype": "i64"}, 32),     # exact, in range
+    (("maximum", "x0", "x1"), "u32", {}, 64),                   # u32 does not fit int32
+    (("greater", ("multiply", "x0", "x1"), ("imm", 0)), "i16", {"out_dtype": "i8"}, None),
+    (("where", ("greater", ("multiply", "x0", "x1"), ("imm", 0)), "x0", "x1"), "i16", {}, 32),
+    (("where", ("greater", ("multiply", "x0", "x1"), ("imm", 0)), "x0", "x1"), "i32", {}, 64),
+    (("divide", "x0", ("imm", 3)), "i16", {}, 32),
+    (("divide", "x0", ("imm", -1)), "i32", {}, 64),              # INT32_MIN / -1
+    (("remainder", "x0", "x1"), "i16", {}, 64),                  # the divisor may be 0
+    (("right_shift", "x0", "x1"), "i32", {}, 32),
+    (("right_shift", "x0", "x1"), "u32", {}, 64),
+    (("left_shift", "x0", "x1"), "i64", {}, 64),                  # an i64 output is exact
+    (("left_shift", "x0", "x1"), "i64", {"out_dtype": "i32"}, 32),  # its low 32 bits only
+])
+def test_value_bits_proof(expr, dt, kw, bits):
+    """The matcher's choice of 32-bit evaluation on small programs."""
+    from ptxc import CompileError, Lowerer
+    kop, meta = synth.pointwise(64, expr, dt, **kw)
+    if bits is None:                                   # a predicate stored: refused
+        with pytest.raises(CompileError):
+            Lowerer(kop, meta).plan()
+        return
+    got = Lowerer(kop, meta).plan()["pointwise"]["value_bits"]
+    assert got == bits, (expr, dt, got)
