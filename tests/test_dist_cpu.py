@@ -81,6 +81,16 @@ def _family_result(plan, meta, full):
             x, y = regs[ra], regs[rb]
             regs.append({1: lambda: x + y, 3: lambda: x * y}[op]())
         return np.asarray(regs[g["result_reg"]], dtype=np.float64).reshape(-1)
+    if fam == "pointwise_int":
+        # s64 walk of the integer program (add / multiply only here), wrapping
+        g = plan["pointwise"]
+        regs = [full[n].astype(np.int64).view(np.uint64) for n in g["inputs"]] + \
+            [full[n].astype(np.int64).view(np.uint64) for n in g["scalars"]] + \
+            [np.array(v, np.int64).view(np.uint64) for v in g["immediates"]]
+        for op, _dst, ra, rb, _rc in g["program"]:
+            x, y = regs[ra], regs[rb]
+            regs.append({1: lambda: x + y, 3: lambda: x * y}[op]())
+        return np.asarray(regs[g["result_reg"]]).view(np.int64).astype(np.float64).reshape(-1)
     raise ValueError(fam)
 
 
@@ -95,6 +105,10 @@ CASES = {
     "attention_heads": lambda: synth.attention(2, 3, 16, 16, dtype="f32"),
     "pointwise_elements": lambda: synth.pointwise(
         1001, ("add", ("multiply", ("const", "c", 1.5), "x0"), "x1"), "f32"),
+    "pointwise_int_elements": lambda: synth.pointwise(
+        1001, ("add", ("multiply", ("const", "c", 3), "x0"), "x1"), "i32",
+        inits={"x0": {"dist": "int", "low": -1000, "high": 1000},
+               "x1": {"dist": "int", "low": -1000, "high": 1000}}),
 }
 
 
