@@ -371,6 +371,77 @@ pointwise_int_kernel(const PiProgram p, void *out, int out_dtype, int64_t n) {
   }
 }
 
+// One-step programs (one op over contiguous inputs and constants: the
+// commonest integer program) with the op fixed at compile time: operands in
+// registers, no shared register file, two 4-element groups loaded per thread
+// before any arithmetic.  Operand kinds: 0 contiguous input, 1 immediate,
+// 2 one-element scalar tensor.
+struct PiSimple {
+  const void *ptr[3];
+  int dtype[3];
+  int kind[3];
+  long long konst[3];
+  int nops;
+};
+
+// G: 4-element groups per thread -- two on 32-bit values when at most one
+// operand streams from memory, else one (s64 with two groups spills; two
+// streams run faster with one, as in the float kernel)
+template <typename T, int OP, bool VIO, int G>
+__global__ void __launch_bounds__(256)
+pointwise_int_simple_kernel(const PiSimple q, void *out, int out_dtype, int64_t n) {
+  constexpr int VEC = kPiVec;
+  const int64_t groups = (n + VEC - 1) / VEC;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  long long cval[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k)
+    cval[k] = k >= q.nops ? 0 : q.kind[k] == 1 ? q.konst[k]
+                              : q.kind[k] == 2 ? pi_load1(q.ptr[k], q.dtype[k], 0) : 0;
+  for (int64_t g0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g0 < groups;
+       g0 += stride * G) {
+    T v[G][3][VEC];
+#pragma unroll
+    for (int u = 0; u < G; ++u) {
+      const int64_t base = (g0 + u * stride) * VEC;
+      if (base >= n) break;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        long long w[VEC];
+        if (k >= q.nops || q.kind[k] != 0) {
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) w[j] = cval[k];
+        } else if (VIO && base + VEC <= n) {
+          pi_load4(q.ptr[k], q.dtype[k], base, w);
+        } else {
+#pragma unroll
+          for (int j = 0; j < VEC; ++j)
+            w[j] = base + j < n ? pi_load1(q.ptr[k], q.dtype[k], base + j) : 0;
+        }
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) v[u][k][j] = (T)w[j];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < G; ++u) {
+      const int64_t base = (g0 + u * stride) * VEC;
+      if (base >= n) break;
+      T r[VEC];
+      pi_step<T, VEC, 1>(OP, r, v[u][0], v[u][1], v[u][2]);
+      long long o[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) o[j] = (long long)r[j];
+      if (VIO && base + VEC <= n) {
+        pi_store4(out, out_dtype, base, o);
+      } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j)
+          if (base + j < n) pi_store1(out, out_dtype, base + j, o[j]);
+      }
+    }
+  }
+}
+
 }  // namespace emmy
 
 using namespace emmy;
@@ -475,6 +546,56 @@ extern "C" int emmy_pointwise_int(const void *const *inputs, const int *input_dt
   }
   const int64_t groups = (n + kPiVec - 1) / kPiVec;
   cudaStream_t st = as_stream(stream);
+  // one step over contiguous inputs and constants: the op-specialised kernel
+  const int nleaf = n_inputs + n_scalars + n_imm;
+  auto arity = [](int op) { return op == PI_WHERE ? 3 : (op == PI_COPY || op == PI_LNOT) ? 1 : 2; };
+  bool simple = !bcast && n_instr == 1 && result_reg == nleaf;
+  for (int j = 0; simple && j < arity(program[0]); ++j) simple = program[2 + j] < nleaf;
+  if (simple) {
+    const int op = program[0];
+    PiSimple q{};
+    q.nops = arity(op);
+    for (int j = 0; j < q.nops; ++j) {
+      const int r = program[2 + j];
+      if (r < n_inputs) {
+        q.kind[j] = 0; q.ptr[j] = p.inputs[r]; q.dtype[j] = p.in_dtype[r];
+      } else if (r < n_inputs + n_scalars) {
+        q.kind[j] = 2; q.ptr[j] = p.scalars[r - n_inputs]; q.dtype[j] = p.sc_dtype[r - n_inputs];
+      } else {
+        q.kind[j] = 1; q.konst[j] = p.imm[r - n_inputs - n_scalars];
+      }
+    }
+    int streams = 0;
+    for (int j = 0; j < q.nops; ++j) streams += q.kind[j] == 0;
+    const bool two = value_bits == 32 && streams <= 1;
+    const int64_t G = two ? 2 : 1;
+    int64_t sblocks = (groups + 256LL * G - 1) / (256LL * G);
+    if (sblocks > INT32_MAX) sblocks = INT32_MAX;
+    const unsigned sb = (unsigned)sblocks;
+#define EMMY_PI_SIMPLE(OPC)                                                                          \
+  case OPC:                                                                                          \
+    if (value_bits == 32 && two) {                                                                   \
+      if (vio) pointwise_int_simple_kernel<int, OPC, true, 2><<<sb, 256, 0, st>>>(q, out, out_dtype, n); \
+      else pointwise_int_simple_kernel<int, OPC, false, 2><<<sb, 256, 0, st>>>(q, out, out_dtype, n); \
+    } else if (value_bits == 32) {                                                                   \
+      if (vio) pointwise_int_simple_kernel<int, OPC, true, 1><<<sb, 256, 0, st>>>(q, out, out_dtype, n); \
+      else pointwise_int_simple_kernel<int, OPC, false, 1><<<sb, 256, 0, st>>>(q, out, out_dtype, n); \
+    } else {                                                                                         \
+      if (vio) pointwise_int_simple_kernel<long long, OPC, true, 1><<<sb, 256, 0, st>>>(q, out, out_dtype, n); \
+      else pointwise_int_simple_kernel<long long, OPC, false, 1><<<sb, 256, 0, st>>>(q, out, out_dtype, n); \
+    }                                                                                                \
+    break;
+    switch (op) {
+      EMMY_PI_SIMPLE(PI_COPY) EMMY_PI_SIMPLE(PI_ADD) EMMY_PI_SIMPLE(PI_SUB) EMMY_PI_SIMPLE(PI_MUL)
+      EMMY_PI_SIMPLE(PI_DIV) EMMY_PI_SIMPLE(PI_REM) EMMY_PI_SIMPLE(PI_SHL) EMMY_PI_SIMPLE(PI_SHR)
+      EMMY_PI_SIMPLE(PI_XOR) EMMY_PI_SIMPLE(PI_MAX) EMMY_PI_SIMPLE(PI_MIN) EMMY_PI_SIMPLE(PI_EQ)
+      EMMY_PI_SIMPLE(PI_NE) EMMY_PI_SIMPLE(PI_GT) EMMY_PI_SIMPLE(PI_LT) EMMY_PI_SIMPLE(PI_GE)
+      EMMY_PI_SIMPLE(PI_LE) EMMY_PI_SIMPLE(PI_LAND) EMMY_PI_SIMPLE(PI_LOR) EMMY_PI_SIMPLE(PI_LNOT)
+      default: EMMY_PI_SIMPLE(PI_WHERE)
+    }
+#undef EMMY_PI_SIMPLE
+    return check_launch("emmy_pointwise_int (one step)");
+  }
   const size_t smem = (size_t)nregs * kPiVec * kPiThreads * (value_bits / 8);
   int64_t blocks = (groups + kPiThreads - 1) / kPiThreads;
   if (blocks > INT32_MAX) blocks = INT32_MAX;             // the grid-stride loop covers the rest

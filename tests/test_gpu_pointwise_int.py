@@ -218,3 +218,19 @@ def test_32_bit_programs_store_the_64_bit_bits(expr, dt, kw):
         outs.append(ex.download()["out"].numpy())
     assert np.array_equal(_bits(outs[0]), _bits(outs[1]))
     assert np.array_equal(_bits(outs[0]), _bits(run_ir(kop, meta, host)["out"]))
+
+
+@pytest.mark.parametrize("expr,dt", [
+    # one op over inputs, then steps with a constant (clamps, scales, offsets)
+    (("add", ("multiply", "x0", "x1"), ("imm", 3)), "i32"),
+    (("subtract", ("imm", 100), ("bitwise_xor", "x0", "x1")), "i16"),            # swapped tail
+    (("maximum", ("minimum", ("subtract", "x0", "x1"), ("const", "hi", 100)), ("imm", -100)), "i32"),
+    (("remainder", ("add", ("multiply", "x0", ("imm", 5)), ("imm", -7)), ("imm", 9)), "i64"),
+    (("divide", ("add", "x0", "x1"), ("imm", 3)), "u8"),
+    (("left_shift", ("add", "x0", "x1"), ("imm", 3)), "u16"),
+])
+def test_op_then_constant_steps_match_oracle(expr, dt):
+    kop, meta = synth.pointwise(4099, expr, dt)
+    host = synth.make_inputs(meta)
+    _, _, out = run_on_gpu(kop, meta, host)
+    assert np.array_equal(_bits(out["out"]), _bits(run_ir(kop, meta, host)["out"]))
