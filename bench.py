@@ -634,13 +634,17 @@ def splitk_across_gpus(world, rank, device, reps=10):
     Each rank multiplies its K slice (65536 / N, 64 / N partitions) into a full
     partial C; then (a) the NCCL reduce-scatter leaves each rank its 256 / N
     rows of C, or (b) the fused kernel stores each partial row straight into
-    its owner's slot over NVLink and the owner sums its slots.  Device times,
-    max over ranks, median of ``reps``.  The two forms' results are compared.
+    its owner's slot over NVLink and the owner sums its slots, or (c) with no
+    host barrier, every rank publishes its step into the others' flag words
+    and sums its rows of every partial over NVLink (``splitk_pull_step``).
+    Device times, max over ranks, median of ``reps``.  The forms' results are
+    compared.
     """
     import ctypes
     import torch
     import torch.distributed as dist
-    from ptxc.dist import PeerRows, reduce_scatter_rows, shard_ranges, splitk_to_peers, sum_slots
+    from ptxc.dist import (PeerPartials, PeerRows, reduce_scatter_rows, shard_ranges,
+                           splitk_pull_gemm, splitk_pull_reduce, splitk_to_peers, sum_slots)
     from ptxc.launch import _check, _stream_handle, load_library
     lib = load_library()
     M, N, K = 256, 256, 65536
@@ -709,7 +713,39 @@ def splitk_across_gpus(world, rank, device, reps=10):
         torch.cuda.synchronize()
         dist.barrier()
         peers.close()
-    med = torch.tensor([statistics.median(x) for x in (t_g, t_r, t_t, t_k, t_s, t_f)] + [diff],
+    # pull: GEMM into this step's partial buffer, then the exchange over peer memory
+    pp = PeerPartials(M, N, device)
+    t_p, t_pg, t_px = [], [], []
+    try:
+        mine_p = None
+        for i in range(3 + reps):
+            flush()
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = _event_pair()
+            em = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            splitk_pull_gemm(A, B, pp, splits=splits)
+            em.record()
+            mine_p = splitk_pull_reduce(pp)
+            e1.record()
+            e1.synchronize()
+            if i >= 3:
+                t_p.append(e0.elapsed_time(e1) * 1e3)
+                t_pg.append(e0.elapsed_time(em) * 1e3)
+                t_px.append(em.elapsed_time(e1) * 1e3)
+        code = ctypes.c_int(0)
+        lib.emmy_get_device_status(ctypes.byref(code), None)
+        if code.value:
+            raise RuntimeError(f"emmy_peer_reduce_rows: device status {code.value:#x}")
+        diff_p = float((mine_p - rows).abs().max()) / max(float(rows.abs().max()), 1e-30)
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier()
+        pp.close()
+    med = torch.tensor([statistics.median(x) for x in (t_g, t_r, t_t, t_k, t_s, t_f)] +
+                       [max(diff, diff_p), statistics.median(t_p), statistics.median(t_pg),
+                        statistics.median(t_px)],
                        device=device, dtype=torch.float64)
     dist.all_reduce(med, op=dist.ReduceOp.MAX)
     v = [float(x) for x in med.tolist()]
@@ -720,6 +756,8 @@ def splitk_across_gpus(world, rank, device, reps=10):
             "total_us": round(v[2], 2), "total_tflops": round(flops / v[2] / 1e6, 2),
             "fused_kernel_us": round(v[3], 2), "fused_slot_sum_us": round(v[4], 2),
             "fused_total_us": round(v[5], 2), "fused_tflops": round(flops / v[5] / 1e6, 2),
+            "pull_gemm_us": round(v[8], 2), "pull_exchange_us": round(v[9], 2),
+            "pull_total_us": round(v[7], 2), "pull_tflops": round(flops / v[7] / 1e6, 2),
             "forms_agree_max_rel": v[6],
             "timing": "device events per rank, max over ranks, median of 10; L2 flushed"}
 

@@ -303,3 +303,118 @@ def splitk_step(a_slice, b_slice, peers, M, N, splits=0, bias=None, out=None):
     torch.cuda.synchronize()
     dist.barrier(group=peers.group)
     return sum_slots(peers, out)
+
+
+class PeerPartials:
+    """Every rank's double-buffered split-K partials and flag words, mapped
+    into this rank's address space (CUDA IPC, as ``PeerRows``).
+
+    Each rank owns ``parts``, a CUDA tensor ``[2, M, N]`` (step s writes
+    buffer ``s % 2``), and ``flags``, ``world`` int64 words that the other
+    ranks set to the step they have finished.  ``emmy_peer_reduce_rows``
+    reads every rank's buffer of the step for this rank's rows once all flags
+    show the step (``splitk_pull_step``).  ``close()`` unmaps the peers'
+    buffers; call it on every rank before the process group goes away.
+    """
+
+    def __init__(self, M, N, device, group=None):
+        import ctypes
+        import torch
+        import torch.distributed as dist
+        from .launch import LibraryError, load_library
+        self.lib = load_library()
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.M, self.N = M, N
+        self.parts = torch.zeros(2, M, N, dtype=torch.float32, device=device)
+        self.flags = torch.zeros(self.world, dtype=torch.int64, device=device)
+        self.seq = 0
+        mine = []
+        for t in (self.parts, self.flags):
+            handle = (ctypes.c_ubyte * 64)()
+            offset = ctypes.c_int64()
+            rc = self.lib.emmy_ipc_export(ctypes.c_void_p(t.data_ptr()), handle,
+                                          ctypes.byref(offset))
+            if rc:
+                raise LibraryError("emmy_ipc_export: " + self.lib.emmy_last_error().decode())
+            mine.append((bytes(handle), int(offset.value)))
+        allh = [None] * self.world
+        torch.cuda.synchronize(device)
+        dist.all_gather_object(allh, mine, group=group)
+        self.part_ptrs, self.flag_ptrs, self._bases = [], [], []
+        for r, handles in enumerate(allh):
+            if r == self.rank:
+                self.part_ptrs.append(self.parts.data_ptr())
+                self.flag_ptrs.append(self.flags.data_ptr())
+                continue
+            got = []
+            for h, off in handles:
+                hb = (ctypes.c_ubyte * 64).from_buffer_copy(h)
+                p, base = ctypes.c_void_p(), ctypes.c_void_p()
+                rc = self.lib.emmy_ipc_import(hb, ctypes.c_int64(off), ctypes.byref(p),
+                                              ctypes.byref(base))
+                if rc:
+                    self.close()
+                    raise LibraryError("emmy_ipc_import: " + self.lib.emmy_last_error().decode())
+                got.append(p.value)
+                self._bases.append(base.value)
+            self.part_ptrs.append(got[0])
+            self.flag_ptrs.append(got[1])
+
+    def close(self):
+        import ctypes
+        for b in self._bases:
+            self.lib.emmy_ipc_close(ctypes.c_void_p(b))
+        self._bases = []
+
+
+def splitk_pull_gemm(a_slice, b_slice, peers, splits=0, bias=None, stream=None):
+    """The first half of ``splitk_pull_step``: start the next step and run this
+    rank's K slice into its partial buffer of the step (the f32 GEMM with
+    in-GPU atomic split-K; the bias on rank 0 only)."""
+    import ctypes
+    import torch
+    from .launch import _check, _stream_handle
+    lib = peers.lib
+    M, N, rank = peers.M, peers.N, peers.rank
+    K = a_slice.shape[-1]
+    st = stream if stream is not None else torch.cuda.current_stream()
+    peers.seq += 1
+    c = peers.parts[peers.seq % 2]
+    use_bias = bias is not None and rank == 0
+    _check(lib.emmy_gemm_f32(ctypes.c_void_p(a_slice.data_ptr()), ctypes.c_void_p(b_slice.data_ptr()),
+                             ctypes.c_void_p(bias.data_ptr()) if use_bias else None,
+                             ctypes.c_void_p(c.data_ptr()), 1, M, N, K, 0, 0, 0, splits, 0,
+                             1 if use_bias else 0, _stream_handle(st)), "emmy_gemm_f32")
+
+
+def splitk_pull_reduce(peers, out=None, stream=None):
+    """The second half: ``emmy_peer_reduce_rows`` publishes the step, waits for
+    every rank's, and sums every rank's partial of this rank's rows."""
+    import ctypes
+    import torch
+    from .launch import _check, _stream_handle
+    lib = peers.lib
+    M, N, world, rank = peers.M, peers.N, peers.world, peers.rank
+    st = stream if stream is not None else torch.cuda.current_stream()
+    buf = peers.seq % 2
+    c = peers.parts[buf]
+    lo, hi = shard_ranges(M, world)[rank]
+    if out is None:
+        out = torch.empty(hi - lo, N, dtype=torch.float32, device=c.device)
+    off = buf * M * N * 4
+    parts = (ctypes.c_void_p * world)(*[ctypes.c_void_p(p + off) for p in peers.part_ptrs])
+    flags = (ctypes.c_void_p * world)(*[ctypes.c_void_p(p) for p in peers.flag_ptrs])
+    _check(lib.emmy_peer_reduce_rows(parts, flags, world, rank, peers.seq, lo, hi - lo, N,
+                                     ctypes.c_void_p(out.data_ptr()), _stream_handle(st)),
+           "emmy_peer_reduce_rows")
+    return out
+
+
+def splitk_pull_step(a_slice, b_slice, peers, splits=0, bias=None, out=None, stream=None):
+    """One split-K step with the exchange over peer memory, no host barrier:
+    ``splitk_pull_gemm`` then ``splitk_pull_reduce``.  Returns this rank's
+    rows of ``A @ B`` (+ bias), ``[rows, N]``."""
+    splitk_pull_gemm(a_slice, b_slice, peers, splits, bias, stream)
+    return splitk_pull_reduce(peers, out, stream)

@@ -45,6 +45,7 @@ SIGNATURES = {
     "emmy_ipc_export": [_vp, _vp, _vp],
     "emmy_ipc_import": [_vp, _i64, _vp, _vp],
     "emmy_ipc_close": [_vp],
+    "emmy_peer_reduce_rows": [_vp, _vp, _int, _int, _i64, _i64, _i64, _i64, _vp, _vp],
     "emmy_gemm_f16": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _int, _vp],
     "emmy_attention_f32": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _int, _vp],
     "emmy_attention_f16": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _vp],

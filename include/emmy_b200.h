@@ -224,6 +224,26 @@ int emmy_ipc_import(const void *handle, int64_t offset, void **peer_ptr, void **
 int emmy_ipc_close(void *peer_base);
 
 /*
+ * Reduce-scatter of split-K partials over peer memory (the exchange after a
+ * matmul whose K is split across GPUs; the multi-GPU form of the reference's
+ * atomic split-K writes, ptxc/stmts.py:456-461).  parts[r]: rank r's full-size
+ * [M, n] f32 partial of this step (mapped with emmy_ipc_import; this rank's
+ * own at parts[me]); flags[r]: rank r's int64 flag words [world], zero before
+ * the first step.  The kernel stores `seq` into flags[r][me] for every r
+ * (system-scope release), waits until flags[me][q] >= seq for every q
+ * (system-scope acquire, bounded: after the wait limit it records status 0x1301
+ * in the device status word and writes nothing), then writes
+ * out[i][:] = sum_r parts[r][row0 + i][:] for i < rows.  Launch it after the
+ * GEMM that filled parts[me], on the same stream; seq starts at 1 and grows by
+ * one per step, and each rank alternates two partial buffers by step parity
+ * (a buffer of step s is rewritten at step s + 2, after every rank has passed
+ * its wait of step s + 1, so no rank still reads it).  world <= 8.
+ */
+int emmy_peer_reduce_rows(const float *const *parts, long long *const *flags, int world, int me,
+                          long long seq, int64_t row0, int64_t rows, int64_t n, float *out,
+                          void *stream);
+
+/*
  * f16 GEMM with f32 accumulation on the tcgen05 tensor cores:
  * C[b] = A[b] @ B[b] (+ bias[n]) (ReLU), A [M,K] f16, B [K,N] f16 row-major,
  * C [M,N] f32 or f16 (out_dtype), bias f32 (nullable), dense batches.

@@ -7,7 +7,9 @@
   a full partial C, and ``reduce_scatter_rows`` sums the partials over NCCL;
   then the fused form: the GEMM stores its partial rows straight into their
   owner's slot over NVLink and each owner sums its slots (``PeerRows`` +
-  ``splitk_step``).
+  ``splitk_step``); then the exchange over peer memory with no host
+  barrier (``PeerPartials`` + ``splitk_pull_step``: step flags in each
+  rank's memory, bounded waits, double-buffered partials; three steps).
 
 Tolerances as in the single-GPU tests (``tests/parity.py``): softmax 1e-5
 relative, attention 1e-3 of ``sum_j p_j |v_j|``, split-K 1e-5 of ``|A| @ |B|``.  NVLS is off (``NCCL_NVLS_ENABLE=0``).
@@ -52,7 +54,8 @@ def _worker(rank, world, port, q):
     from emmy_ir import synth
     from oracle import formulas as F
     from ptxc import Lowerer
-    from ptxc.dist import PeerRows, reduce_scatter_rows, shard_plan, splitk_plan, splitk_step
+    from ptxc.dist import (PeerPartials, PeerRows, reduce_scatter_rows, shard_plan, splitk_plan,
+                           splitk_pull_step, splitk_step)
     from ptxc.launch import Executor, load_library
     import ctypes
     torch.cuda.set_device(rank)
@@ -129,6 +132,29 @@ def _worker(rank, world, port, q):
             torch.cuda.synchronize()
             dist.barrier()
             peers.close()
+        # --- the exchange over peer memory with no host barrier: each rank's
+        # partial into its buffer of the step, then every rank sums its rows
+        # of every partial once all have published the step.  Three steps in
+        # a row (both buffers and the step flags turn over), a bias on rank 0.
+        bias = torch.linspace(-1.0, 1.0, 256, device="cuda")
+        pp = PeerPartials(256, 256, torch.device("cuda"))
+        try:
+            for _ in range(3):
+                mine3 = splitk_pull_step(a_loc, b_loc, pp, splits=g["splits"], bias=bias)
+            torch.cuda.synchronize()
+            code = ctypes.c_int(0)
+            lib.emmy_get_device_status(ctypes.byref(code), None)
+            ok &= code.value == 0
+            full3 = torch.empty(256, 256, device="cuda")
+            dist.all_gather_into_tensor(full3, mine3)
+            if rank == 0:
+                refb = ref + bias.double().cpu().numpy()
+                scaleb = scale + np.abs(bias.double().cpu().numpy())
+                ok &= bool(np.all(np.abs(full3.cpu().numpy() - refb) <= 1e-5 * scaleb))
+        finally:
+            torch.cuda.synchronize()
+            dist.barrier()
+            pp.close()
         torch.cuda.synchronize()
     finally:
         dist.barrier()
