@@ -448,18 +448,21 @@ def time_launches(make_launch, nbytes, flush, reps=10, warmup=3):
     return statistics.median(samples), copies
 
 
-def roofline_block(name, nbytes, flops, us, pipe, n_exp=0):
+def roofline_block(name, nbytes, flops, us, pipe, n_exp=0, gpus=1):
     """The binding roof of one configuration: t_roof = max(bytes / HBM peak,
     flops / peak of the pipe the kernel uses, exponentials / MUFU rate);
     frac = t_roof / measured time.  The exponential term (attention: one per
     score, B*H*Sq*Sk) uses the nominal MUFU rate, 16 ex2 per SM per clock at
-    148 SMs and 1.965 GHz."""
+    148 SMs and 1.965 GHz.  With ``gpus`` > 1 the problem is split over that
+    many GPUs and every peak is the single-GPU one times ``gpus``."""
     hbm, hsrc = hbm_peak()
+    hbm = round(hbm * gpus, 1)
     t_hbm = nbytes / (hbm * 1e9)
     pipe_peak = {"tensor": tensor_peak()[0], "fp32": FP32_MEASURED_TFLOPS,
                  "fp64": FP64_MEASURED_TFLOPS}.get(pipe)
+    pipe_peak = round(pipe_peak * gpus, 2) if pipe_peak else None
     t_pipe = flops / (pipe_peak * 1e12) if pipe_peak else 0.0
-    t_exp = n_exp / MUFU_EXP_PER_S
+    t_exp = n_exp / (MUFU_EXP_PER_S * gpus)
     t = us * 1e-6
     if t_hbm >= max(t_pipe, t_exp):
         blk = {"bound": "hbm", "achieved": round(nbytes / t / 1e9, 1), "peak": hbm, "unit": "GB/s",
@@ -473,9 +476,13 @@ def roofline_block(name, nbytes, flops, us, pipe, n_exp=0):
                "unit": "TFLOP/s",
                "peak_source": ("measured bf16_tflops (burst)" if pipe == "tensor"
                                else f"measured {pipe} FMA chains")}
+    if blk["bound"] == "mufu":
+        blk["peak"] = round(MUFU_EXP_PER_S * gpus / 1e12, 3)
+    if gpus > 1:
+        blk["peak_source"] += f" x {gpus} GPUs"
     blk["frac"] = round(max(t_hbm, t_pipe, t_exp) / t, 4)
     blk["algorithmic_bytes"] = int(nbytes)
-    blk["traffic"] = profile_traffic(PROFILE_OF.get(name))
+    blk["traffic"] = profile_traffic(PROFILE_OF.get(name)) if gpus == 1 else None
     blk["profile"] = PROFILE_OF.get(name) if blk["traffic"] is not None else None
     return blk
 
@@ -625,6 +632,64 @@ def family_extras(device, only=None):
     del graph, exs
     del flush
     torch.cuda.empty_cache()
+    return out
+
+
+def family_extras_sharded(device, world, rank, max_over_ranks, barrier):
+    """Every benchmark configuration split over the ``world`` GPUs of the run.
+
+    Each rank launches its ``ptxc.dist.shard_plan`` shard (rows, batches or
+    elements; no collective on the data path) and times it alone as
+    ``time_launches`` does at one GPU; the configuration's time is the max over
+    ranks, its throughput the whole problem's bytes or flops over that time,
+    and its roofline is against ``world`` times the single-GPU peaks.  K4a is
+    left out (its K split is the ``splitk_across_gpus`` key) and so is the
+    attention shape sweep.  Every rank takes the same collective steps: a
+    barrier and one max per configuration, in ``family_cases`` order.
+    """
+    import torch
+    from ptxc import Lowerer
+    from ptxc.dist import shard_plan
+    from ptxc.launch import Executor
+    out = {}
+    flush = L2Flush(device)
+    for name, (kop, meta) in family_cases().items():
+        if name.startswith(("K4a", "K5_sweep")):
+            continue
+        plan = Lowerer(kop, meta).plan()
+        try:
+            sub, _ = shard_plan(plan, rank, world)
+        except ValueError as e:
+            out[name] = {"unsharded": str(e)}
+            continue
+        nbytes, flops = plan_bytes(plan), plan_flops(plan)
+
+        def make():
+            ex = Executor(sub, device=device)
+            for t in ex.tensors.values():
+                if t.is_floating_point():
+                    t.normal_()
+            for a in meta["args"]:
+                if "data" in a:
+                    ex.tensors[a["name"]].fill_(float(a["data"][0]))
+            return ex.launch
+        barrier()
+        us, copies = time_launches(make, plan_bytes(sub), flush)
+        us = max_over_ranks(us)
+        row = {"us": round(us, 2), "gbs": round(nbytes / us / 1e3, 1), "bytes": nbytes,
+               "launches_per_sample": copies, "kernel_family": plan["family"],
+               "gpus": world, "shard_bytes_rank0": plan_bytes(sub)}
+        if flops:
+            row["tflops"] = round(flops / us / 1e6, 2)
+        n_exp = 0
+        if "attention" in plan:
+            at = plan["attention"]
+            n_exp = at["batch"] * at["sq"] * at["sk"]
+        row["roofline"] = roofline_block(name, nbytes, flops, us, _pipe_of(plan), n_exp,
+                                         gpus=world)
+        out[name] = row
+        torch.cuda.empty_cache()
+    del flush
     return out
 
 
@@ -1068,7 +1133,10 @@ def run_b200_arm(args):
     torch.cuda.empty_cache()
 
     splitk = splitk_across_gpus(world, rank, device) if world > 1 else None
-    extras = family_extras(device) if (world == 1 and not args.no_families) else None
+    extras = None
+    if not args.no_families:
+        extras = (family_extras(device) if world == 1 else
+                  family_extras_sharded(device, world, rank, max_over_ranks, barrier))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

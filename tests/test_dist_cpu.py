@@ -199,3 +199,30 @@ def test_shard_ranges_cover_exactly_once():
             assert r[0][0] == 0 and r[-1][1] == n
             assert all(a[1] == b[0] for a, b in zip(r, r[1:]))
             assert max(e - s for s, e in r) - min(e - s for s, e in r) <= 1
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_every_bench_configuration_shards(world):
+    """The per-family bench key at N > 1 times each rank's ``shard_plan`` shard:
+    every configuration it names has one, and the shards of each sliced tensor
+    cover it exactly once."""
+    import math
+    import bench
+    for name, (kop, meta) in bench.family_cases().items():
+        if name.startswith(("K4a", "K5_sweep")):
+            continue
+        plan = Lowerer(kop, meta).plan()
+        covered = {}
+        for rank in range(world):
+            sub, slices = shard_plan(plan, rank, world)
+            assert sub["shard"] == {"rank": rank, "world": world}
+            for t, (off, cnt) in slices.items():
+                covered.setdefault(t, []).append((off, cnt))
+        for t, parts in covered.items():
+            full = math.prod(plan["tensors"][t]["shape"])
+            if all(p == (0, full) for p in parts):
+                continue                                  # replicated on every rank
+            parts.sort()
+            assert parts[0][0] == 0, (name, t)
+            assert all(a[0] + a[1] == b[0] for a, b in zip(parts, parts[1:])), (name, t)
+            assert parts[-1][0] + parts[-1][1] == full, (name, t)
