@@ -33,6 +33,7 @@
 
 #include "common.cuh"
 #include "pw_index.cuh"
+#include "tma.cuh"
 
 namespace emmy {
 
@@ -106,60 +107,119 @@ __device__ __forceinline__ long long pi_load1(const void *p, int dt, int64_t i) 
   }
 }
 
-// elements base .. base + 3 (aligned for one or two vector loads)
-__device__ __forceinline__ void pi_load4(const void *p, int dt, int64_t base, long long v[4]) {
+// a vector load: read-only global (GLOBAL) or shared memory
+template <bool GLOBAL, typename V>
+__device__ __forceinline__ V pi_ld(const V *q) {
+  if constexpr (GLOBAL) return __ldg(q);
+  else return *q;
+}
+
+// U groups of four elements of global (GLOBAL) or shared memory, group u at
+// elements base + u * gstride .. + 3 (each group aligned for one or two vector
+// loads), as values of type T (s64 values cut to T); lane 4u + j of v.  One
+// switch on the type for all groups.
+template <bool GLOBAL, int U, typename T, typename CONV>
+__device__ __forceinline__ void pi_load_bytes(const void *p, int64_t base, int64_t gstride,
+                                              T v[4 * U], const CONV &conv) {
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const unsigned int w = pi_ld<GLOBAL>(reinterpret_cast<const unsigned int *>(
+        static_cast<const unsigned char *>(p) + base + u * gstride));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[4 * u + j] = conv((w >> (8 * j)) & 0xffu);
+  }
+}
+template <bool GLOBAL, int U, typename T, typename CONV>
+__device__ __forceinline__ void pi_load_halves(const void *p, int64_t base, int64_t gstride,
+                                               T v[4 * U], const CONV &conv) {
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const uint2 w = pi_ld<GLOBAL>(reinterpret_cast<const uint2 *>(
+        static_cast<const unsigned short *>(p) + base + u * gstride));
+    const unsigned int h[4] = {w.x & 0xffffu, w.x >> 16, w.y & 0xffffu, w.y >> 16};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[4 * u + j] = conv(h[j]);
+  }
+}
+template <bool GLOBAL, int U, typename T, typename CONV>
+__device__ __forceinline__ void pi_load_words(const void *p, int64_t base, int64_t gstride,
+                                              T v[4 * U], const CONV &conv) {
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const uint4 w = pi_ld<GLOBAL>(reinterpret_cast<const uint4 *>(
+        static_cast<const int *>(p) + base + u * gstride));
+    const unsigned int x[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[4 * u + j] = conv(x[j]);
+  }
+}
+
+// U groups of four elements of global (GLOBAL) or shared memory, group u at
+// elements base + u * gstride .. + 3 (each group aligned for one or two vector
+// loads), as values of type T (s64 values cut to T); lane 4u + j of v.  One
+// switch on the type for all groups, each type's widening fixed in its case.
+template <bool GLOBAL, int U, typename T>
+__device__ __forceinline__ void pi_loadv(const void *p, int dt, int64_t base, int64_t gstride,
+                                         T v[4 * U]) {
   switch (dt) {
     case EMMY_DT_I8:
-    case EMMY_DT_U8: {
-      const unsigned int w = __ldg(reinterpret_cast<const unsigned int *>(
-          static_cast<const unsigned char *>(p) + base));
+      pi_load_bytes<GLOBAL, U>(p, base, gstride, v, [](unsigned int b) { return (T)(signed char)b; });
+      break;
+    case EMMY_DT_U8:
+      pi_load_bytes<GLOBAL, U>(p, base, gstride, v, [](unsigned int b) { return (T)b; });
+      break;
+    case EMMY_DT_I16:
+      pi_load_halves<GLOBAL, U>(p, base, gstride, v, [](unsigned int h) { return (T)(short)h; });
+      break;
+    case EMMY_DT_U16:
+      pi_load_halves<GLOBAL, U>(p, base, gstride, v, [](unsigned int h) { return (T)h; });
+      break;
+    case EMMY_DT_F16:
+      pi_load_halves<GLOBAL, U>(p, base, gstride, v,
+                                [](unsigned int h) { return (T)pi_rzi_f16((unsigned short)h); });
+      break;
+    case EMMY_DT_I32:
+      pi_load_words<GLOBAL, U>(p, base, gstride, v, [](unsigned int x) { return (T)(int)x; });
+      break;
+    case EMMY_DT_U32:
+      pi_load_words<GLOBAL, U>(p, base, gstride, v, [](unsigned int x) { return (T)(long long)x; });
+      break;
+    case EMMY_DT_F32:
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const unsigned int b = (w >> (8 * j)) & 0xffu;
-        v[j] = dt == EMMY_DT_I8 ? (long long)(signed char)b : (long long)b;
+      for (int u = 0; u < U; ++u) {
+        const float4 w = pi_ld<GLOBAL>(reinterpret_cast<const float4 *>(
+            static_cast<const float *>(p) + base + u * gstride));
+        v[4 * u + 0] = (T)pi_rzi_f32(w.x); v[4 * u + 1] = (T)pi_rzi_f32(w.y);
+        v[4 * u + 2] = (T)pi_rzi_f32(w.z); v[4 * u + 3] = (T)pi_rzi_f32(w.w);
       }
       break;
-    }
-    case EMMY_DT_I16:
-    case EMMY_DT_U16:
-    case EMMY_DT_F16: {
-      const uint2 w = __ldg(reinterpret_cast<const uint2 *>(
-          static_cast<const unsigned short *>(p) + base));
-      const unsigned int h[4] = {w.x & 0xffffu, w.x >> 16, w.y & 0xffffu, w.y >> 16};
+    case EMMY_DT_F64:
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        v[j] = dt == EMMY_DT_I16   ? (long long)(short)h[j]
-               : dt == EMMY_DT_U16 ? (long long)h[j]
-                                   : pi_rzi_f16((unsigned short)h[j]);
+      for (int u = 0; u < U; ++u) {
+        const double2 *q = reinterpret_cast<const double2 *>(
+            static_cast<const double *>(p) + base + u * gstride);
+        const double2 a = pi_ld<GLOBAL>(q), b = pi_ld<GLOBAL>(q + 1);
+        v[4 * u + 0] = (T)pi_rzi_f64(a.x); v[4 * u + 1] = (T)pi_rzi_f64(a.y);
+        v[4 * u + 2] = (T)pi_rzi_f64(b.x); v[4 * u + 3] = (T)pi_rzi_f64(b.y);
+      }
       break;
-    }
-    case EMMY_DT_I32:
-    case EMMY_DT_U32: {
-      const uint4 w = __ldg(reinterpret_cast<const uint4 *>(static_cast<const int *>(p) + base));
-      const unsigned int u[4] = {w.x, w.y, w.z, w.w};
+    default:                                           // I64, U64
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        v[j] = dt == EMMY_DT_I32 ? (long long)(int)u[j] : (long long)u[j];
+      for (int u = 0; u < U; ++u) {
+        const longlong2 *q = reinterpret_cast<const longlong2 *>(
+            static_cast<const long long *>(p) + base + u * gstride);
+        const longlong2 a = pi_ld<GLOBAL>(q), b = pi_ld<GLOBAL>(q + 1);
+        v[4 * u + 0] = (T)a.x; v[4 * u + 1] = (T)a.y; v[4 * u + 2] = (T)b.x; v[4 * u + 3] = (T)b.y;
+      }
       break;
-    }
-    case EMMY_DT_F32: {
-      const float4 w = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(p) + base));
-      v[0] = pi_rzi_f32(w.x); v[1] = pi_rzi_f32(w.y); v[2] = pi_rzi_f32(w.z); v[3] = pi_rzi_f32(w.w);
-      break;
-    }
-    case EMMY_DT_F64: {
-      const double2 *q = reinterpret_cast<const double2 *>(static_cast<const double *>(p) + base);
-      const double2 a = __ldg(q), b = __ldg(q + 1);
-      v[0] = pi_rzi_f64(a.x); v[1] = pi_rzi_f64(a.y); v[2] = pi_rzi_f64(b.x); v[3] = pi_rzi_f64(b.y);
-      break;
-    }
-    default: {                                         // I64, U64
-      const longlong2 *q = reinterpret_cast<const longlong2 *>(static_cast<const long long *>(p) + base);
-      const longlong2 a = __ldg(q), b = __ldg(q + 1);
-      v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
-      break;
-    }
   }
+}
+
+// elements base .. base + 3 (aligned for one or two vector loads) of global
+// (GLOBAL) or shared memory
+template <bool GLOBAL = true>
+__device__ __forceinline__ void pi_load4(const void *p, int dt, int64_t base, long long v[4]) {
+  pi_loadv<GLOBAL, 1, long long>(p, dt, base, 0, v);
 }
 
 // ---- stores: the output's type decides (reference _cast_reg) ----------------
@@ -180,50 +240,82 @@ __device__ __forceinline__ void pi_store1(void *p, int dt, int64_t i, long long 
   }
 }
 
-__device__ __forceinline__ void pi_store4(void *p, int dt, int64_t base, const long long v[4]) {
-  unsigned long long u[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) u[j] = (unsigned long long)v[j];
+// U groups of four elements, group u at base + u * gstride (each aligned for
+// one or two vector stores); lane 4u + j of v (s64 values, or T values that
+// stand for them).  One switch on the type for all groups.
+template <int U, typename T>
+__device__ __forceinline__ void pi_storev(void *p, int dt, int64_t base, int64_t gstride,
+                                          const T v[4 * U]) {
   switch (dt) {
     case EMMY_DT_I8:
     case EMMY_DT_U8:
-      *reinterpret_cast<unsigned int *>(static_cast<unsigned char *>(p) + base) =
-          (unsigned int)(u[0] & 0xff) | (unsigned int)(u[1] & 0xff) << 8 |
-          (unsigned int)(u[2] & 0xff) << 16 | (unsigned int)(u[3] & 0xff) << 24;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const T *x = v + 4 * u;
+        *reinterpret_cast<unsigned int *>(static_cast<unsigned char *>(p) + base + u * gstride) =
+            ((unsigned int)x[0] & 0xffu) | ((unsigned int)x[1] & 0xffu) << 8 |
+            ((unsigned int)x[2] & 0xffu) << 16 | ((unsigned int)x[3] & 0xffu) << 24;
+      }
       break;
     case EMMY_DT_I16:
     case EMMY_DT_U16:
-      *reinterpret_cast<uint2 *>(static_cast<unsigned short *>(p) + base) =
-          make_uint2((unsigned int)(u[0] & 0xffff) | (unsigned int)(u[1] & 0xffff) << 16,
-                     (unsigned int)(u[2] & 0xffff) | (unsigned int)(u[3] & 0xffff) << 16);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const T *x = v + 4 * u;
+        *reinterpret_cast<uint2 *>(static_cast<unsigned short *>(p) + base + u * gstride) =
+            make_uint2(((unsigned int)x[0] & 0xffffu) | ((unsigned int)x[1] & 0xffffu) << 16,
+                       ((unsigned int)x[2] & 0xffffu) | ((unsigned int)x[3] & 0xffffu) << 16);
+      }
       break;
     case EMMY_DT_F16:
-      *reinterpret_cast<uint2 *>(static_cast<unsigned short *>(p) + base) =
-          make_uint2((unsigned int)pi_f16_of(v[0]) | (unsigned int)pi_f16_of(v[1]) << 16,
-                     (unsigned int)pi_f16_of(v[2]) | (unsigned int)pi_f16_of(v[3]) << 16);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const T *x = v + 4 * u;
+        *reinterpret_cast<uint2 *>(static_cast<unsigned short *>(p) + base + u * gstride) =
+            make_uint2((unsigned int)pi_f16_of(x[0]) | (unsigned int)pi_f16_of(x[1]) << 16,
+                       (unsigned int)pi_f16_of(x[2]) | (unsigned int)pi_f16_of(x[3]) << 16);
+      }
       break;
     case EMMY_DT_I32:
     case EMMY_DT_U32:
-      *reinterpret_cast<uint4 *>(static_cast<unsigned int *>(p) + base) =
-          make_uint4((unsigned int)u[0], (unsigned int)u[1], (unsigned int)u[2], (unsigned int)u[3]);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const T *x = v + 4 * u;
+        *reinterpret_cast<uint4 *>(static_cast<unsigned int *>(p) + base + u * gstride) =
+            make_uint4((unsigned int)x[0], (unsigned int)x[1], (unsigned int)x[2], (unsigned int)x[3]);
+      }
       break;
     case EMMY_DT_F32:
-      *reinterpret_cast<float4 *>(static_cast<float *>(p) + base) =
-          make_float4(pi_f32_of(v[0]), pi_f32_of(v[1]), pi_f32_of(v[2]), pi_f32_of(v[3]));
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const T *x = v + 4 * u;
+        *reinterpret_cast<float4 *>(static_cast<float *>(p) + base + u * gstride) =
+            make_float4(pi_f32_of(x[0]), pi_f32_of(x[1]), pi_f32_of(x[2]), pi_f32_of(x[3]));
+      }
       break;
-    case EMMY_DT_F64: {
-      double2 *q = reinterpret_cast<double2 *>(static_cast<double *>(p) + base);
-      q[0] = make_double2(pi_f64_of(v[0]), pi_f64_of(v[1]));
-      q[1] = make_double2(pi_f64_of(v[2]), pi_f64_of(v[3]));
+    case EMMY_DT_F64:
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const T *x = v + 4 * u;
+        double2 *q = reinterpret_cast<double2 *>(static_cast<double *>(p) + base + u * gstride);
+        q[0] = make_double2(pi_f64_of(x[0]), pi_f64_of(x[1]));
+        q[1] = make_double2(pi_f64_of(x[2]), pi_f64_of(x[3]));
+      }
       break;
-    }
-    default: {                                         // I64, U64
-      longlong2 *q = reinterpret_cast<longlong2 *>(static_cast<long long *>(p) + base);
-      q[0] = make_longlong2(v[0], v[1]);
-      q[1] = make_longlong2(v[2], v[3]);
+    default:                                           // I64, U64
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const T *x = v + 4 * u;
+        longlong2 *q = reinterpret_cast<longlong2 *>(static_cast<long long *>(p) + base + u * gstride);
+        q[0] = make_longlong2((long long)x[0], (long long)x[1]);
+        q[1] = make_longlong2((long long)x[2], (long long)x[3]);
+      }
       break;
-    }
   }
+}
+
+__device__ __forceinline__ void pi_store4(void *p, int dt, int64_t base, const long long v[4]) {
+  pi_storev<1, long long>(p, dt, base, 0, v);
 }
 
 // ---- one instruction over VEC lanes (lane stride S) -------------------------
@@ -270,16 +362,20 @@ __device__ __forceinline__ int pi_shr(int a, int b) {
   return r;
 }
 
-// T: long long (s64, the reference's registers) or int (a program whose
-// values the matcher proved to give the same bits on 32 bits).
-template <typename T, int VEC, int S>
-__device__ __forceinline__ void pi_step(int op, T *RD, const T *RA, const T *RB, const T *RC) {
+// One instruction over L lanes.  T: long long (s64, the reference's
+// registers) or int (a program whose values the matcher proved to give the
+// same bits on 32 bits).  Operand lane l is fa(l) / fb(l) / fc(l) and the
+// result goes to put(l, value): the callers' operands are register arrays,
+// shared-memory slots or one broadcast constant, all resolved at compile time.
+template <typename T, int L, typename PUT, typename FA, typename FB, typename FC>
+__device__ __forceinline__ void pi_apply(int op, const PUT &put, const FA &fa, const FB &fb,
+                                         const FC &fc) {
   using U = typename std::make_unsigned<T>::type;
 #define PI_LANES(EXPR)                                                            \
-  _Pragma("unroll") for (int j = 0; j < VEC; ++j) {                               \
-    const T a = RA[j * S], b = RB[j * S], c = RC[j * S];                          \
+  _Pragma("unroll") for (int j = 0; j < L; ++j) {                                 \
+    const T a = fa(j), b = fb(j), c = fc(j);                                      \
     (void)b; (void)c;                                                             \
-    RD[j * S] = (EXPR);                                                           \
+    put(j, (T)(EXPR));                                                            \
   }                                                                               \
   break;
   switch (op) {
@@ -306,6 +402,14 @@ __device__ __forceinline__ void pi_step(int op, T *RD, const T *RA, const T *RB,
     default: PI_LANES(a != 0 ? b : c)                  // PI_WHERE
   }
 #undef PI_LANES
+}
+
+// the same over register slots laid out with lane stride S
+template <typename T, int VEC, int S>
+__device__ __forceinline__ void pi_step(int op, T *RD, const T *RA, const T *RB, const T *RC) {
+  pi_apply<T, VEC>(
+      op, [&](int j, T v) { RD[j * S] = v; }, [&](int j) { return RA[j * S]; },
+      [&](int j) { return RB[j * S]; }, [&](int j) { return RC[j * S]; });
 }
 
 // T: the register type (above).  VIO: every contiguous input and the output
@@ -367,6 +471,170 @@ pointwise_int_kernel(const PiProgram p, void *out, int out_dtype, int64_t n) {
 #pragma unroll
       for (int j = 0; j < VEC; ++j)
         if (base + j < n) pi_store1(out, out_dtype, base + j, o[j]);
+    }
+  }
+}
+
+// Chain programs: every step reads the step before it (if it reads a step
+// at all) plus inputs and constants -- max(x0 - x1, 0), ((x0 * x1) >> 3) ^ x2
+// and the like.  The running value stays in registers (4 * U lanes a thread),
+// so no shared register file; the inputs stream into shared memory by bulk
+// copies (cp.async.bulk, no multicast) through a ring of `stages` chunks per
+// CTA, which keeps many bytes in flight whatever the element width, and every
+// step reads its input operands from the staged chunk.  Each step is decoded
+// once per chunk and applied to all of the thread's lanes.  Persistent CTAs
+// walk chunks of kPcThreads * 4 * U elements (group u of thread t: elements
+// (u * kPcThreads + t) * 4 .. + 3); a last partial chunk is read from global
+// memory directly.  Operand codes: -1 the previous step's value, 0..7 input
+// k, 8 + j constant j (scalars, then immediates).
+#ifndef EMMY_PC_GROUPS32
+#define EMMY_PC_GROUPS32 4
+#endif
+#ifndef EMMY_PC_GROUPS64
+#define EMMY_PC_GROUPS64 2
+#endif
+#ifndef EMMY_PC_RING_KB
+#define EMMY_PC_RING_KB 72
+#endif
+constexpr int kPcThreads = 256, kPcMaxStages = 16;
+constexpr int kStatusPcWait = 0x1401;
+
+struct PiChain {
+  const void *inputs[kPiMaxIn];
+  int in_dtype[kPiMaxIn];
+  int in_off[kPiMaxIn];                  // byte offset of input k in a staged chunk
+  int in_bytes[kPiMaxIn];                // bytes of one chunk of input k
+  const void *scalars[kPiMaxIn];
+  int sc_dtype[kPiMaxIn];
+  long long imm[kPiMaxIn];
+  signed char code[kPiMaxInstr][4];      // op, then up to three operand codes
+  int64_t n, nfull;                      // elements, full chunks
+  int n_in, n_sc, n_imm, n_instr, stages, chunk_bytes;
+};
+
+__device__ __forceinline__ int pi_arity(int op) {
+  return op == PI_WHERE ? 3 : (op == PI_COPY || op == PI_LNOT) ? 1 : 2;
+}
+
+template <typename T, int U, bool VO>
+__global__ void __launch_bounds__(kPcThreads)
+pointwise_int_chain_kernel(const __grid_constant__ PiChain p, void *out, int out_dtype,
+                           int *status) {
+  constexpr int L = kPiVec * U;                      // lanes a thread per chunk
+  constexpr int CH = kPcThreads * L;                 // elements a chunk
+  constexpr int GS = kPcThreads * kPiVec;            // element stride between groups
+  extern __shared__ __align__(128) unsigned char pc_smem[];
+  __shared__ uint64_t full[kPcMaxStages];
+  __shared__ T kc[2 * kPiMaxIn];
+  const int tid = threadIdx.x;
+  if (tid < p.n_sc) kc[tid] = (T)pi_load1(p.scalars[tid], p.sc_dtype[tid], 0);
+  else if (tid < p.n_sc + p.n_imm) kc[tid] = (T)p.imm[tid - p.n_sc];
+  if (tid == 0) {
+    for (int s = 0; s < p.stages; ++s) mbar_init(&full[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int64_t nchunks = (p.n + CH - 1) / CH;
+  auto issue = [&](int64_t c, int s) {               // thread 0: chunk c into stage s
+    unsigned char *dst = pc_smem + (size_t)s * p.chunk_bytes;
+    mbar_expect_tx(&full[s], (uint32_t)p.chunk_bytes);
+    for (int k = 0; k < p.n_in; ++k)
+      bulk_load_1d(dst + p.in_off[k], static_cast<const unsigned char *>(p.inputs[k]) +
+                   c * p.in_bytes[k], (uint32_t)p.in_bytes[k], &full[s]);
+  };
+  if (tid == 0)
+    for (int s = 0; s < p.stages; ++s) {
+      const int64_t c = blockIdx.x + (int64_t)s * gridDim.x;
+      if (c < p.nfull) issue(c, s);
+    }
+  bool ok = true;
+  int64_t i = 0;
+  int s = 0;                                         // stage of chunk i, and its phase
+  uint32_t phase = 0;
+  for (;; ++i) {
+    const int64_t c = blockIdx.x + i * gridDim.x;
+    if (c >= nchunks) break;
+    const bool staged = c < p.nfull;
+    if (staged) ok = mbar_wait(&full[s], phase, status, kStatusPcWait);
+    const int64_t base = c * CH + (int64_t)tid * kPiVec;   // the thread's first group
+    if (ok && base < p.n) {
+      const unsigned char *stage = pc_smem + (size_t)s * p.chunk_bytes;
+      T acc[L];
+#pragma unroll
+      for (int l = 0; l < L; ++l) acc[l] = 0;
+      // input d of this chunk into buf (from the stage, or global memory for
+      // the partial chunk)
+      auto fetch = [&](int d, T *buf) {
+        if (staged) {
+          pi_loadv<false, U, T>(stage + p.in_off[d], p.in_dtype[d], (int64_t)tid * kPiVec, GS, buf);
+        } else {
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int j = 0; j < kPiVec; ++j) {
+              const int64_t e = base + (int64_t)u * GS + j;
+              buf[kPiVec * u + j] = e < p.n ? (T)pi_load1(p.inputs[d], p.in_dtype[d], e) : 0;
+            }
+        }
+      };
+      for (int k = 0; k < p.n_instr; ++k) {
+        const int op = p.code[k][0];
+        T a[3][L];
+#pragma unroll
+        for (int q = 0; q < 3; ++q) {
+          if (q >= pi_arity(op)) {
+#pragma unroll
+            for (int l = 0; l < L; ++l) a[q][l] = 0;
+            continue;
+          }
+          const int d = p.code[k][1 + q];
+          if (d < 0) {
+#pragma unroll
+            for (int l = 0; l < L; ++l) a[q][l] = acc[l];
+          } else if (d >= kPiMaxIn) {
+            const T v = kc[d - kPiMaxIn];
+#pragma unroll
+            for (int l = 0; l < L; ++l) a[q][l] = v;
+          } else {
+            fetch(d, a[q]);
+          }
+        }
+        pi_step<T, L, 1>(op, acc, a[0], a[1], a[2]);
+      }
+      if (VO && staged) {
+        pi_storev<U, T>(out, out_dtype, base, GS, acc);
+      } else {
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+          for (int j = 0; j < kPiVec; ++j) {
+            const int64_t e = base + (int64_t)u * GS + j;
+            if (e < p.n) pi_store1(out, out_dtype, e, (long long)acc[kPiVec * u + j]);
+          }
+      }
+    }
+    // every thread is done with stage s (and agrees whether a wait gave up)
+    if (__syncthreads_or(!ok)) break;
+    if (tid == 0) {
+      const int64_t cn = blockIdx.x + (i + p.stages) * gridDim.x;
+      if (cn < p.nfull) issue(cn, s);
+    }
+    if (++s == p.stages) {
+      s = 0;
+      phase ^= 1;
+    }
+  }
+  if (!ok && tid == 0) {
+    // a wait gave up: let the copies still in flight into this CTA's shared
+    // memory land (each wait bounded) before the CTA exits
+    for (int64_t j = i; j < i + p.stages; ++j) {
+      const int64_t c = blockIdx.x + j * gridDim.x;
+      if (c >= p.nfull) break;
+      mbar_wait(&full[s], phase, nullptr, 0);
+      if (++s == p.stages) {
+        s = 0;
+        phase ^= 1;
+      }
     }
   }
 }
@@ -595,6 +863,84 @@ extern "C" int emmy_pointwise_int(const void *const *inputs, const int *input_dt
     }
 #undef EMMY_PI_SIMPLE
     return check_launch("emmy_pointwise_int (one step)");
+  }
+  // a chain program over 16-byte aligned contiguous inputs: the staged kernel
+  // (four groups of four lanes a thread on 32-bit values, two on s64 ones)
+  const int pc_groups = value_bits == 32 ? EMMY_PC_GROUPS32 : EMMY_PC_GROUPS64;
+  const int64_t pc_chunk = (int64_t)kPcThreads * kPiVec * pc_groups;
+  if (!bcast && n_inputs > 0 && n_instr >= 2 && n >= pc_chunk) {
+    PiChain c{};
+    bool chain = true;
+    int writer[kPiMaxRegs];
+    for (int r = 0; r < kPiMaxRegs; ++r) writer[r] = -1;
+    int chunk_bytes = 0;
+    for (int k = 0; k < n_inputs; ++k) {
+      chain = chain && ((uintptr_t)inputs[k] % 16) == 0;
+      c.inputs[k] = p.inputs[k];
+      c.in_dtype[k] = p.in_dtype[k];
+      c.in_off[k] = chunk_bytes;
+      c.in_bytes[k] = (int)pc_chunk * pi_elem_bytes(p.in_dtype[k]);
+      chunk_bytes += c.in_bytes[k];
+    }
+    for (int k = 0; chain && k < n_instr; ++k) {
+      const int *ins = program + 5 * k;
+      c.code[k][0] = (signed char)ins[0];
+      for (int q = 0; q < 3; ++q) {
+        int d = 0;
+        if (q < arity(ins[0])) {
+          const int r = ins[2 + q];
+          if (r < n_inputs) d = r;
+          else if (r < nleaf) d = kPiMaxIn + (r - n_inputs);
+          else if (k > 0 && writer[r] == k - 1) d = -1;
+          else chain = false;                       // reads an older step: not a chain
+        }
+        c.code[k][1 + q] = (signed char)d;
+      }
+      writer[ins[1]] = k;
+    }
+    chain = chain && result_reg >= nleaf && writer[result_reg] == n_instr - 1 &&
+            2 * chunk_bytes <= 192 * 1024;                 // two stages fit shared memory
+    if (chain) {
+      c.n = n;
+      c.nfull = n / pc_chunk;
+      c.n_in = n_inputs;
+      c.n_sc = n_scalars;
+      c.n_imm = n_imm;
+      c.n_instr = n_instr;
+      for (int k = 0; k < n_scalars; ++k) {
+        c.scalars[k] = p.scalars[k];
+        c.sc_dtype[k] = p.sc_dtype[k];
+      }
+      for (int k = 0; k < n_imm; ++k) c.imm[k] = p.imm[k];
+      c.chunk_bytes = chunk_bytes;
+      const int64_t nchunks = (n + pc_chunk - 1) / pc_chunk;
+      const bool vo = pi_vec_aligned(out, out_dtype);
+      auto go = [&](auto kern) {
+        // the CTAs that the registers let reside on an SM share EMMY_PC_RING_KB
+        // of staged chunks, two to sixteen stages each (72 KB measured as good
+        // as 200 KB: past a few chunks in flight the issue rate bounds it)
+        int per_sm = 1;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kPcThreads, 0);
+        per_sm = std::max(per_sm, 1);
+        c.stages = std::max(2, std::min(kPcMaxStages, (EMMY_PC_RING_KB * 1024 / per_sm) / chunk_bytes));
+        const size_t smem = (size_t)c.stages * chunk_bytes;
+        // (the kernel's own barriers and constants take the static part)
+        if (smem + 1024 > 48 * 1024)
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kPcThreads, smem);
+        const unsigned grid =
+            (unsigned)std::min<int64_t>(nchunks, (int64_t)std::max(per_sm, 1) * sm_count());
+        kern<<<grid, kPcThreads, smem, st>>>(c, out, out_dtype, device_status_ptr());
+      };
+      if (value_bits == 32) {
+        if (vo) go(pointwise_int_chain_kernel<int, EMMY_PC_GROUPS32, true>);
+        else go(pointwise_int_chain_kernel<int, EMMY_PC_GROUPS32, false>);
+      } else {
+        if (vo) go(pointwise_int_chain_kernel<long long, EMMY_PC_GROUPS64, true>);
+        else go(pointwise_int_chain_kernel<long long, EMMY_PC_GROUPS64, false>);
+      }
+      return check_launch("emmy_pointwise_int (chain)");
+    }
   }
   const size_t smem = (size_t)nregs * kPiVec * kPiThreads * (value_bits / 8);
   int64_t blocks = (groups + kPiThreads - 1) / kPiThreads;

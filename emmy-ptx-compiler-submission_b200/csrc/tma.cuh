@@ -117,6 +117,18 @@ __device__ __forceinline__ void tma_load_3d_pair(void *dst, const CUtensorMap *m
       : "memory");
 }
 
+// Untiled bulk copy of `bytes` contiguous bytes from global memory into this
+// CTA's shared memory, completing on `bar`.  Both addresses 16-byte aligned,
+// `bytes` a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_load_1d(void *dst, const void *src, uint32_t bytes,
+                                             uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 3-D tiled TMA store from this CTA's shared memory (bulk-group completion).
 // Parts of the box outside the tensor are not written.
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *src, int c0,

@@ -361,6 +361,11 @@ int emmy_pointwise_indexed(const void *const *inputs, const int *input_dtypes,
  * bits (add, sub, mul, xor, shl, copy, a store to an integer of 32 bits or
  * fewer).  The matcher proves it by interval arithmetic over the inputs'
  * types and the immediates.
+ * A chain program (each step reads only the step before it besides inputs
+ * and constants; contiguous inputs on 16-byte boundaries; n >= 1024) runs
+ * with its inputs staged in shared memory by bulk copies; a staging wait that
+ * passes the library's wait limit records device status 0x1401
+ * (emmy_get_device_status) and leaves the output incomplete.
  */
 int emmy_pointwise_int(const void *const *inputs, const int *input_dtypes,
                        const int64_t *input_index, int n_inputs,

@@ -234,3 +234,78 @@ def test_op_then_constant_steps_match_oracle(expr, dt):
     host = synth.make_inputs(meta)
     _, _, out = run_on_gpu(kop, meta, host)
     assert np.array_equal(_bits(out["out"]), _bits(run_ir(kop, meta, host)["out"]))
+
+
+# ---- chain programs (the staged kernel) ---------------------------------------
+
+def _is_chain(pw):
+    """The library's rule for the staged chain kernel: each step reads only the
+    step before it besides inputs and constants, and the last step is the result."""
+    nleaf = len(pw["inputs"]) + len(pw["scalars"]) + len(pw["immediates"])
+    writer = {}
+    prog = pw["program"]
+    if len(prog) < 2 or not pw["inputs"]:
+        return False
+    for k, (op, dst, *ops) in enumerate(prog):
+        arity = 3 if op == 20 else 1 if op in (0, 19) else 2
+        for r in ops[:arity]:
+            if r >= nleaf and writer.get(r) != k - 1:
+                return False
+        writer[dst] = k
+    return pw["result_reg"] >= nleaf and writer.get(pw["result_reg"]) == len(prog) - 1
+
+
+CHAIN_CASES = [
+    # (expr, dtype, kwargs)
+    (("maximum", ("subtract", "x0", "x1"), ("imm", 0)), "u8", {}),
+    (("bitwise_xor", ("right_shift", ("multiply", "x0", "x1"), ("imm", 3)), "x2"), "i32", {}),
+    (("where", ("greater", ("subtract", "x0", "x1"), ("const", "t", 5)), "x1", "x0"), "i16", {}),
+    (("add", ("multiply", "x0", ("imm", 3)), "x1"), "i64", {}),
+    (("minimum", ("add", "x0", "x1"), ("imm", 1000)), "i32",
+     {"dtypes": {"x1": "f32"}, "inits": {"x1": {"dist": "uniform", "low": -3e9, "high": 3e9}}}),
+    (("left_shift", ("add", "x0", "x1"), ("imm", 2)), "u16", {"out_dtype": "f16"}),
+    (("remainder", ("add", ("multiply", "x0", ("imm", 5)), ("imm", -7)), ("imm", 9)), "i64", {}),
+    (("add", ("add", ("add", ("add", "x0", "x1"), "x2"), "x3"), "x4"), "u32", {}),
+]
+
+
+@pytest.mark.parametrize("n", [1024, 4096 * 3 + 5, (1 << 21) + 3])
+@pytest.mark.parametrize("expr,dt,kw", CHAIN_CASES)
+def test_chain_programs_match_oracle(expr, dt, kw, n):
+    kop, meta = synth.pointwise(n, expr, dt, unroll=1, **kw)
+    from ptxc import Lowerer
+    assert _is_chain(Lowerer(kop, meta).plan()["pointwise"])
+    host = synth.make_inputs(meta)
+    _, _, out = run_on_gpu(kop, meta, host)
+    assert np.array_equal(_bits(out["out"]), _bits(run_ir(kop, meta, host)["out"])), (expr, dt, n)
+
+
+def test_chain_bench_program_full_size():
+    """F8e (u8 max(x0 - x1, 0), 2^26 + 3 elements): many chunks per CTA, a tail."""
+    n = (1 << 26) + 3
+    kop, meta = synth.pointwise(n, ("maximum", ("subtract", "x0", "x1"), ("imm", 0)), "u8",
+                                unroll=1)
+    host = synth.make_inputs(meta)
+    _, _, out = run_on_gpu(kop, meta, host)
+    want = np.maximum(host["x0"].astype(np.int64) - host["x1"].astype(np.int64), 0).astype(np.uint8)
+    assert np.array_equal(out["out"], want)
+
+
+def test_chain_with_unaligned_output():
+    """Inputs on 16-byte boundaries (staged), the output one element off (scalar stores)."""
+    import torch
+    from ptxc import Lowerer
+    from ptxc.launch import run
+    n = 3 * 1024 + 7
+    kop, meta = synth.pointwise(n, ("maximum", ("subtract", "x0", "x1"), ("imm", 0)), "i32",
+                                unroll=1)
+    plan = Lowerer(kop, meta).plan()
+    host = synth.make_inputs(meta)
+    dev = torch.device("cuda:0")
+    ins = {k: torch.from_numpy(host[k]).to(dev) for k in ("x0", "x1")}
+    obuf = torch.full((n + 1,), -1, dtype=torch.int32, device=dev)
+    run(plan, {**ins, "out": obuf[1:]})
+    torch.cuda.synchronize()
+    want = np.maximum(host["x0"].astype(np.int64) - host["x1"].astype(np.int64), 0).astype(np.int32)
+    assert np.array_equal(obuf[1:].cpu().numpy(), want)
+    assert int(obuf[0]) == -1
