@@ -819,7 +819,7 @@ extern "C" int emmy_pointwise_int(const void *const *inputs, const int *input_dt
   auto arity = [](int op) { return op == PI_WHERE ? 3 : (op == PI_COPY || op == PI_LNOT) ? 1 : 2; };
   bool simple = !bcast && n_instr == 1 && result_reg == nleaf;
   for (int j = 0; simple && j < arity(program[0]); ++j) simple = program[2 + j] < nleaf;
-  if (simple) {
+  auto launch_simple = [&]() -> int {
     const int op = program[0];
     PiSimple q{};
     q.nops = arity(op);
@@ -863,12 +863,17 @@ extern "C" int emmy_pointwise_int(const void *const *inputs, const int *input_dt
     }
 #undef EMMY_PI_SIMPLE
     return check_launch("emmy_pointwise_int (one step)");
-  }
+  };
+  // narrow streams (1- and 2-byte elements) go to the staged kernel below,
+  // where bulk copies keep enough bytes in flight
+  bool narrow = false;
+  for (int i = 0; i < n_inputs; ++i) narrow = narrow || pi_elem_bytes(input_dtypes[i]) < 4;
+  if (simple && !narrow) return launch_simple();
   // a chain program over 16-byte aligned contiguous inputs: the staged kernel
   // (four groups of four lanes a thread on 32-bit values, two on s64 ones)
   const int pc_groups = value_bits == 32 ? EMMY_PC_GROUPS32 : EMMY_PC_GROUPS64;
   const int64_t pc_chunk = (int64_t)kPcThreads * kPiVec * pc_groups;
-  if (!bcast && n_inputs > 0 && n_instr >= 2 && n >= pc_chunk) {
+  if (!bcast && n_inputs > 0 && (n_instr >= 2 || simple) && n >= pc_chunk) {
     PiChain c{};
     bool chain = true;
     int writer[kPiMaxRegs];
@@ -942,6 +947,7 @@ extern "C" int emmy_pointwise_int(const void *const *inputs, const int *input_dt
       return check_launch("emmy_pointwise_int (chain)");
     }
   }
+  if (simple) return launch_simple();
   const size_t smem = (size_t)nregs * kPiVec * kPiThreads * (value_bits / 8);
   int64_t blocks = (groups + kPiThreads - 1) / kPiThreads;
   if (blocks > INT32_MAX) blocks = INT32_MAX;             // the grid-stride loop covers the rest

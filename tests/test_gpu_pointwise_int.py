@@ -309,3 +309,15 @@ def test_chain_with_unaligned_output():
     want = np.maximum(host["x0"].astype(np.int64) - host["x1"].astype(np.int64), 0).astype(np.int32)
     assert np.array_equal(obuf[1:].cpu().numpy(), want)
     assert int(obuf[0]) == -1
+
+
+@pytest.mark.parametrize("n", [1001, 4096 * 2 + 9])
+@pytest.mark.parametrize("dt", ["i8", "u8", "i16", "u16"])
+def test_narrow_one_step_programs(dt, n):
+    """One-step programs over 1- and 2-byte elements: the staged kernel from one
+    chunk up, the one-step kernel below it."""
+    for expr in (("add", "x0", "x1"), ("maximum", "x0", ("imm", 7)), ("bitwise_xor", "x0", "x1")):
+        kop, meta = synth.pointwise(n, expr, dt, unroll=1)
+        host = synth.make_inputs(meta)
+        _, _, out = run_on_gpu(kop, meta, host)
+        assert np.array_equal(_bits(out["out"]), _bits(run_ir(kop, meta, host)["out"])), (expr, dt, n)
