@@ -561,7 +561,12 @@ def family_extras(device, only=None):
                 if "data" in a:
                     ex.tensors[a["name"]].fill_(float(a["data"][0]))
             return ex.launch
-        us, copies = time_launches(make, nbytes, flush)
+        try:
+            us, copies = time_launches(make, nbytes, flush)
+        except Exception as e:                # a configuration that fails is reported, not fatal
+            out[name] = {"error": f"{type(e).__name__}: {e}"[:300]}
+            torch.cuda.empty_cache()
+            continue
         flops = plan_flops(plan)
         row = {"us": round(us, 2), "gbs": round(nbytes / us / 1e3, 1), "bytes": nbytes,
                "launches_per_sample": copies, "kernel_family": plan["family"]}
@@ -674,8 +679,18 @@ def family_extras_sharded(device, world, rank, max_over_ranks, barrier):
                     ex.tensors[a["name"]].fill_(float(a["data"][0]))
             return ex.launch
         barrier()
-        us, copies = time_launches(make, plan_bytes(sub), flush)
+        # a rank whose configuration fails still takes the same collective
+        # steps (its time counts as infinite), so the ranks stay in step
+        err = None
+        try:
+            us, copies = time_launches(make, plan_bytes(sub), flush)
+        except Exception as e:
+            us, copies, err = float("inf"), 0, f"{type(e).__name__}: {e}"[:300]
         us = max_over_ranks(us)
+        if not math.isfinite(us):
+            out[name] = {"error": err or "failed on another rank"}
+            torch.cuda.empty_cache()
+            continue
         row = {"us": round(us, 2), "gbs": round(nbytes / us / 1e3, 1), "bytes": nbytes,
                "launches_per_sample": copies, "kernel_family": plan["family"],
                "gpus": world, "shard_bytes_rank0": plan_bytes(sub)}
