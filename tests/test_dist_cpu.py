@@ -226,3 +226,25 @@ def test_every_bench_configuration_shards(world):
             assert parts[0][0] == 0, (name, t)
             assert all(a[0] + a[1] == b[0] for a, b in zip(parts, parts[1:])), (name, t)
             assert parts[-1][0] + parts[-1][1] == full, (name, t)
+
+
+def test_roofline_over_several_gpus_scales_every_peak():
+    """The per-family roofline at N > 1: every peak is N times the single-GPU
+    one, so the fraction of a time that scales as 1/N stays the same."""
+    import bench
+    nbytes, us = 1 << 30, 200.0
+    one = bench.roofline_block("K2a_softmax_32x16x512x512", nbytes, 0.0, us, None)
+    four = bench.roofline_block("K2a_softmax_32x16x512x512", nbytes, 0.0, us / 4, None, gpus=4)
+    assert four["bound"] == one["bound"] == "hbm"
+    assert abs(four["peak"] - 4 * one["peak"]) < 0.5
+    assert abs(four["frac"] - one["frac"]) < 1e-3
+    assert four["traffic"] is None and four["peak_source"].endswith("x 4 GPUs")
+    flops = 2.0 * 4096 * 8192 * 2048
+    t1 = bench.roofline_block("K3a_gemm_f16_4096x2048x8192_bias_relu", 117_440_512, flops, 110.0,
+                              "tensor")
+    t2 = bench.roofline_block("K3a_gemm_f16_4096x2048x8192_bias_relu", 117_440_512, flops, 55.0,
+                              "tensor", gpus=2)
+    assert t1["bound"] == t2["bound"] == "tensor"
+    assert abs(t2["frac"] - t1["frac"]) < 1e-3
+    att = bench.roofline_block("K5", 1 << 27, 1.0, 30.0, "tensor", n_exp=1 << 40, gpus=2)
+    assert att["bound"] == "mufu" and abs(att["peak"] - 2 * bench.MUFU_EXP_PER_S / 1e12) < 1e-3
